@@ -1,0 +1,312 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path: the dequant-GEMM of BASELINE config 2 (M=4608 tokens, K=3072,
+N=12288; bf16 activations, fp8 e4m3 weights with per-output-channel scales) on B200.
+
+One step = one linear layer forward through the public operator API (ops.linear -> activation
+split + tcgen05 GEMM) on one batch of synthetic inputs that are already resident in HBM. L2 is
+flushed (256 MB write) between timed steps, outside the timed events. Multi-GPU: one process per
+GPU (torchrun), each rank runs its own batch (data-parallel images, no data-path collective:
+weak scaling); time = max over ranks of the summed per-step CUDA-event time.
+
+Also reported on the same line: the GEMM kernel alone (roofline), the one-term fp8 mode and the
+int4 group-64 variant, an end-to-end number with host buffers (pinned H2D of x, D2H of y inside
+the timed region), SM clocks sampled during the timed region, and (rank 0, N=1) the CPU oracle on a
+bounded sample. ``--impl reference`` times the reference's CPU path instead: the reference is
+TypeScript (no Node here), so its arm is the C restatement of its float64 matmul reference
+(oracle/), run on all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+M, K, N = 4608, 3072, 12288
+FLOPS = 2.0 * M * N * K
+METRIC = "dequant-GEMM TFLOPS (config 2: M=4608 K=3072 N=12288, bf16 x fp8 e4m3 per-channel)"
+
+
+def load_package():
+    pkg_dir = os.path.join(ROOT, "web-engine_b200")
+    spec = importlib.util.spec_from_file_location("web_engine_b200", os.path.join(pkg_dir, "__init__.py"),
+                                                  submodule_search_locations=[pkg_dir])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["web_engine_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks() -> dict:
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "fallback": True}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons of one GPU every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self) -> dict:
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": float(rows[0][2]), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None,
+                "reasons": sorted(reasons)}
+
+
+def cpu_baseline(threads: int | None, target_s: float = 12.0) -> dict:
+    """The oracle's float64 matmul (the reference tests' CPU reference) on a bounded row sample of config 2."""
+    sys.path.insert(0, ROOT)
+    import numpy as np
+
+    from oracle import oracle as O  # the CPU baseline leg: the checker timed as the reference's CPU path
+
+    rng = np.random.default_rng(0)
+    w = rng.integers(0, 256, N * K, dtype=np.uint8)
+    w[(w & 0x7F) == 0x7F] = 0
+    cs = np.full(N, 0.002, np.float32)
+    nthreads = threads or os.cpu_count() or 1
+    rows = 2
+    while True:
+        x = O.bf16_round(rng.standard_normal(rows * K, dtype=np.float32))
+        t0 = time.perf_counter()
+        O.matmul(x, O.FP8, w, rows, N, K, chan_scale=cs, threads=nthreads)
+        dt = time.perf_counter() - t0
+        if dt > target_s / 4 or rows >= 4096:
+            break
+        rows = min(4096, max(rows * 2, int(rows * (target_s / 4) / max(dt, 1e-3))))
+    return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": "TFLOPS", "cores": nthreads, "kind": "port",
+            "sample": f"{rows} of {M} rows of config 2 (float64 oracle, OpenMP {nthreads} threads), {dt:.1f} s"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per_step = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = cpu_baseline(threads, target_s=max(2.0, 60.0 / max(1, args.steps + args.warmup)))
+        if i >= args.warmup:
+            per_step.append(info["value"])
+    value = sum(per_step) / len(per_step)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": FLOPS / (value * 1e12) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": config_dict(args),
+            "cpu_baseline": {**info, "value": value},
+            "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference path is TypeScript/WGSL (no Node or WebGPU on this box); this arm is the C "
+                    "restatement of its float64 CPU matmul reference (tests/gpu/matmul.test.ts:26-35)"}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args) -> dict:
+    return {"workload": "config 2: dequant-GEMM M=4608 K=3072 N=12288, bf16 activations ~N(0,1), fp8 e4m3 weights "
+                        "~N(0,0.02) with per-output-channel absmax scales, exact two-term e4m3 activation split",
+            "m": M, "k": K, "n": N, "parallelism": f"dp{args.gpus}", "l2": "flushed (256 MB write) between steps"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-variants", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    we = load_package()
+    g = we.Graph(local)
+    dev = torch.device("cuda", local)
+    # one stream for torch's plumbing (flush, copies, events) and the library's kernels
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    g.set_stream(stream.cuda_stream)
+
+    # ---- synthetic inputs, resident in HBM (seeded per rank: each rank is its own image batch) ----
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x = torch.randn(M, K, generator=gen, device=dev).to(torch.bfloat16)
+    w32 = torch.randn(N, K, generator=gen, device=dev) * 0.02
+    wq = torch.empty(N, K, dtype=torch.uint8, device=dev)
+    ws = torch.empty(N, dtype=torch.float32, device=dev)
+    we.kernels.quantize_fp8(g, w32, N, K, wq, ws, per_channel=True, w_dtype="f32")
+    w4 = torch.empty(N, K // 2, dtype=torch.uint8, device=dev)
+    w4s = torch.empty(N, K // 64, dtype=torch.int16, device=dev)
+    we.kernels.quantize_int4(g, w32, N, K, w4, w4s, w_dtype="f32")
+    del w32
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    lin = we.Linear(wq, "fp8", 1.0, N, K, chan_scale=ws)
+    lin4 = we.Linear(w4, "int4", 1.0, N, K, group_scale=w4s)
+    hi = torch.empty(M, K, dtype=torch.uint8, device=dev)
+    lo = torch.empty(M, K, dtype=torch.uint8, device=dev)
+    rs = torch.empty(M, dtype=torch.float32, device=dev)
+    yk = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize()
+
+    wall_ms = [0.0]
+
+    def timed(step, steps, warmup, sampler=None):
+        """Sum of per-step CUDA-event times (ms) with an L2 flush before each step, outside the events."""
+        for _ in range(warmup):
+            flush.zero_()
+            step()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for a, b in ev:
+            flush.zero_()
+            a.record(stream)
+            step()
+            b.record(stream)
+        torch.cuda.synchronize()
+        wall_ms[0] = (time.perf_counter() - t0) * 1e3
+        total = sum(a.elapsed_time(b) for a, b in ev)
+        if world > 1:
+            t = torch.tensor([total], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total = float(t.item())
+        return total
+
+    def step_linear():
+        mark = g.mark()
+        we.linear(g, x, lin, M, x_dtype="bf16", y_dtype="bf16")
+        g.release(mark)
+
+    # ---- headline: the linear layer (activation split + tcgen05 GEMM), inputs resident ----
+    launches0 = g.stats["launches"]
+    with ClockSampler(local) as clocks:
+        total_ms = timed(step_linear, args.steps, args.warmup)
+    launches = (g.stats["launches"] - launches0) // (args.steps + args.warmup) * args.steps
+    wall_headline_ms = wall_ms[0]
+    assert g.device_error() == 0, "device error word set"
+    ms = total_ms / args.steps
+    value = world * FLOPS / (ms * 1e-3) / 1e12
+
+    # ---- the GEMM kernel alone (roofline) and the activation split alone ----
+    we.kernels.quantize_act(g, x, M, K, hi, lo, rs, terms=2)
+    gemm_ms = timed(lambda: we.kernels.gemm_fp8(g, hi, lo, rs, wq, yk, M, N, K, chan_scale=ws, y_dtype="bf16"),
+                    args.steps, 2) / args.steps
+    split_ms = timed(lambda: we.kernels.quantize_act(g, x, M, K, hi, lo, rs, terms=2), args.steps, 2) / args.steps
+    peaks = measured_peaks()
+    bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
+    gemm_tflops = FLOPS / (gemm_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": gemm_tflops, "peak": bf16_peak, "unit": "TFLOP/s",
+                "frac": gemm_tflops / bf16_peak, "traffic": None,
+                "kernel": "gemm_tc_kernel<BT=128|256, TERMS=2, kind::f8f6f4>",
+                "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; two e4m3 MMAs per K step = bf16 rate)"
+                if "fallback" not in peaks else "fallback 1.59 PFLOP/s",
+                "algorithmic_flop_per_launch": FLOPS, "split_ms": split_ms, "gemm_ms": gemm_ms}
+
+    variants = {}
+    if not args.no_variants:
+        fast_ms = timed(lambda: we.kernels.gemm_fp8(g, hi, None, rs, wq, yk, M, N, K, chan_scale=ws,
+                                                    y_dtype="bf16"), args.steps, 2) / args.steps
+        variants["fp8_one_term_gemm"] = {"tflops": FLOPS / (fast_ms * 1e-3) / 1e12, "ms": fast_ms,
+                                         "note": "one e4m3 activation term (fp8 tensor-peak mode, ~3% rms act error)"}
+
+        def step_int4():
+            mark = g.mark()
+            we.linear(g, x, lin4, M, x_dtype="bf16", y_dtype="bf16")
+            g.release(mark)
+
+        i4_ms = timed(step_int4, args.steps, 2) / args.steps
+        variants["int4_g64_linear"] = {"tflops": FLOPS / (i4_ms * 1e-3) / 1e12, "ms": i4_ms,
+                                       "note": "int4 group-64 decode to bf16 + tcgen05 kind::f16"}
+
+    # ---- end to end through the public API with host buffers ----
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+
+    def step_e2e():
+        xd.copy_(xh, non_blocking=True)  # pinned host -> HBM on the library's stream
+        mark = g.mark()
+        y = we.linear(g, xd, lin, M, x_dtype="bf16", y_dtype="bf16")
+        g.read_into(y, yh.data_ptr(), M * N * 2)  # HBM -> pinned host, then wait for the stream
+        g.release(mark)
+
+    e2e_ms = timed(step_e2e, args.steps, 2) / args.steps
+    e2e = {"value": world * FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": M * K * 2,
+           "d2h_bytes_per_step": M * N * 2, "ms_per_step": e2e_ms}
+
+    line = None
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp8 e4m3 x2 (bf16 activations split exactly) -> f32 accumulate",
+                "data": "synthetic (seeded torch.randn on device; weights quantised by we_quantize_fp8)",
+                "config": config_dict(args), "roofline": roofline, "e2e": e2e, "gpu_launches": launches,
+                "clocks": clocks.summary(), "variants": variants,
+                "host_wall_ms_timed_region": wall_headline_ms}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(None)
+    g.destroy()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,223 @@
+/*
+ * web-engine B200: the C ABI of the quantized-linear / RMSNorm / RoPE hot path.
+ *
+ * This is the drop-in boundary for the operator layer of dotstories/web-engine:
+ * src/model/ops.ts (linear, norm, noMod, rotate) on top of src/gpu/graph.ts (Graph),
+ * and the kernel-level entry points of src/kernels/{matmul,fp8,rmsnorm,rope}.ts.
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, and returns an int
+ * status (WE_OK or an error code); the message of the last error of a context is
+ * we_last_error(ctx). The reference's synchronous `throw new Error(...)` cases map to
+ * WE_EINVAL with the same message text.
+ *
+ * Memory: device buffers are plain device pointers. Buffers made by we_buffer() belong
+ * to the context's pool (the Graph analog) and are freed by we_free / we_release /
+ * we_destroy. Pointers from elsewhere (cudaMalloc, torch) may be passed to every op.
+ *
+ * Ordering: all work of a context runs in order on its stream (we_set_stream); the
+ * calls are asynchronous except we_read and we_sync. A context is used by one host
+ * thread at a time (the reference is single-threaded JS).
+ */
+#ifndef WE_B200_H
+#define WE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------- status codes ---------------- */
+enum {
+  WE_OK = 0,
+  WE_EINVAL = 1,      /* bad shape/format/layout: the reference's throw cases */
+  WE_ENOMEM = 2,      /* device allocation failed */
+  WE_ECUDA = 3,       /* a CUDA runtime/driver call failed */
+  WE_ENCCL = 4,       /* a collective failed */
+  WE_ETIMEOUT = 5,    /* a bounded device-side wait gave up (see we_device_error) */
+  WE_EUNSUPPORTED = 6 /* valid request that this build does not implement */
+};
+
+/* ---------------- element types ---------------- */
+enum {
+  WE_F32 = 0,
+  WE_BF16 = 1,
+  WE_FP8 = 2,     /* float8_e4m3fn, 1 byte per value (src/kernels/fp8.ts: 4 per u32, little-endian) */
+  WE_INT4G64 = 3, /* symmetric int4, 2 per byte (low nibble = even k), f16 scale per 64 values of K */
+  WE_F16 = 4
+};
+
+typedef struct we_ctx we_ctx;
+
+/* ---------------- context (src/gpu/compute.ts getDevice; src/gpu/graph.ts constructor) ---------------- */
+/* Makes a context on CUDA device `device` with its own stream. flags: reserved, pass 0. */
+int we_init(int device, uint32_t flags, we_ctx** out);
+/* Frees every buffer of the context (Graph.destroy, src/gpu/graph.ts:148-154) and the context. */
+int we_destroy(we_ctx* ctx);
+const char* we_last_error(const we_ctx* ctx);
+/* Runs later work on `stream` (a cudaStream_t; NULL = the context's own stream). Waits for the old one. */
+int we_set_stream(we_ctx* ctx, void* stream);
+void* we_get_stream(const we_ctx* ctx);
+/* Waits for all queued work (device.queue.onSubmittedWorkDone). */
+int we_sync(we_ctx* ctx);
+/* Device-side error word of the context: 0, or the code a kernel's bounded wait recorded. Cleared on read. */
+int we_device_error(we_ctx* ctx, uint32_t* code);
+/* Number of streaming multiprocessors of the context's device. */
+int we_num_sms(const we_ctx* ctx);
+
+/* ---------------- memory: the Graph analog (src/gpu/graph.ts:26-155) ---------------- */
+/* Graph.buffer(data | bytes) (graph.ts:38-54): a device buffer of `bytes` (rounded up to 4),
+   filled with `host` when non-NULL, else zeroed. Reuses a pooled buffer of the same size. */
+int we_buffer(we_ctx* ctx, size_t bytes, const void* host, void** out);
+/* queue.writeBuffer: copy `bytes` from host to device (in order with the queued work). */
+int we_write(we_ctx* ctx, void* dst, const void* host, size_t bytes);
+/* Graph.read (graph.ts:109-119): runs everything queued, then copies `bytes` back. Synchronous. */
+int we_read(we_ctx* ctx, const void* src, void* host, size_t bytes);
+/* Graph.copy (graph.ts:93-98): device-to-device copy, in order with the queued work. */
+int we_copy(we_ctx* ctx, const void* src, size_t src_offset, void* dst, size_t dst_offset, size_t bytes);
+/* Graph.mark (graph.ts:122): how many buffers the context owns now. */
+size_t we_mark(we_ctx* ctx);
+/* Graph.release (graph.ts:127-132): frees every buffer made since `mark`, except `keep`. */
+int we_release(we_ctx* ctx, size_t mark, void* const* keep, size_t nkeep);
+/* Graph.free (graph.ts:135-139): frees one buffer made by we_buffer. */
+int we_free(we_ctx* ctx, void* buf);
+/* Graph.stats (graph.ts:33): buffers created vs taken from the pool, bytes created; plus the number of
+   kernels this context launched, and how many matmuls ran on the tcgen05 and CUDA-core kernels. */
+typedef struct {
+  uint64_t created, reused, created_bytes;
+  uint64_t launches, tc_gemms, simt_gemms;
+} we_stats;
+int we_get_stats(const we_ctx* ctx, we_stats* out);
+
+/* ---------------- matmul: matmulWgsl + matmulParams (src/kernels/matmul.ts:118-214) ---------------- */
+enum {
+  WE_MM_ACCUMULATE = 1u << 0, /* y += x . W^T * scale instead of y = (matmul.ts:145) */
+  WE_MM_FP8_FAST = 1u << 1,   /* bf16 x with fp8 W: one e4m3 term per activation (fp8 tensor peak, ~3% rms
+                                 per-element activation error) instead of the exact two-term split */
+  WE_MM_FORCE_SIMT = 1u << 2  /* use the CUDA-core kernel even where the tensor-core kernel applies */
+};
+typedef struct {
+  int64_t m, n, k;
+  /* Row strides and offsets in values (matmul.ts:185-195). 0 stride = contiguous (k, k, n). */
+  int64_t x_stride, w_stride, y_stride, x_offset, w_offset, y_offset;
+  int64_t k_split;          /* > 1: K slices, partials [k_split, m, y_stride] (matmul.ts:155-159) */
+  float scale;              /* per-tensor weight scale (the reference's scalar weight_scale) */
+  const float* chan_scale;  /* optional device [n]: per-output-channel scale, replaces `scale` */
+  const uint16_t* group_scale; /* WE_INT4G64: device f16 [n, k/64] */
+  const float* bias;        /* optional device f32 [n], added after scaling (ops.ts:65) */
+  int32_t x_dtype;          /* WE_F32 | WE_BF16 */
+  int32_t w_dtype;          /* WE_F32 | WE_BF16 | WE_FP8 | WE_INT4G64 */
+  int32_t y_dtype;          /* WE_F32 | WE_BF16 */
+  uint32_t flags;           /* WE_MM_* */
+} we_matmul_desc;
+/* y[m, n] = x[m, k] . W^T * scale (+ bias) with W [n, k] like nn.Linear. Validation as matmulParams
+   (matmul.ts:205-207): "K must be a multiple of 4, got 6" etc. Replaces matmulWgsl/matmulParams/
+   matmulWorkgroups and the one-shots matmulFp8/matmulBf16/matmulF32 (matmul.ts:223-265). */
+int we_matmul(we_ctx* ctx, const we_matmul_desc* desc, const void* x, const void* w, void* y);
+/* The matmulParams validation alone (throws in the reference): WE_OK or WE_EINVAL with the message. */
+int we_matmul_check(we_ctx* ctx, const we_matmul_desc* desc);
+/* The tcgen05 GEMM on activations already split into e4m3 terms (we_quantize_act, or a producer that
+   writes the split directly): y = (x_hi + x_lo) . W^T * row_scale[m] * (chan_scale[n] | scale) (+ bias)
+   (+ y with WE_MM_ACCUMULATE). x_lo NULL = one term. K % 16 == 0, rows 16-byte aligned. The matmul
+   of matmulWgsl (src/kernels/matmul.ts:118-178) with its activation quantisation hoisted out. */
+typedef struct {
+  int64_t m, n, k;
+  const uint8_t* x_hi;
+  const uint8_t* x_lo;
+  const float* row_scale;
+  const uint8_t* w;
+  float scale;
+  const float* chan_scale;
+  const float* bias;
+  void* y;
+  int64_t y_stride; /* values; 0 = n */
+  int32_t y_dtype;  /* WE_F32 | WE_BF16 */
+  uint32_t flags;   /* WE_MM_ACCUMULATE */
+} we_gemm_fp8_desc;
+int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* desc);
+/* kSplitFor (src/model/ops.ts:42-45). */
+int64_t we_ksplit_for(int64_t m, int64_t n, int64_t k);
+
+/* ---------------- the operator API: src/model/ops.ts ---------------- */
+/* Linear (ops.ts:24-32): W [n, k] as stored, scalar or per-channel scale, optional bias and LoRA. */
+typedef struct we_linear {
+  const void* weight;
+  int32_t dtype;               /* WE_FP8 | WE_BF16 | WE_F32 | WE_INT4G64 */
+  float scale;
+  const float* chan_scale;     /* optional [n] */
+  const uint16_t* group_scale; /* WE_INT4G64 */
+  int64_t n, k;
+  const float* bias;           /* optional [n] */
+  const struct we_linear* lora_down; /* optional [rank, k] */
+  const struct we_linear* lora_up;   /* optional [n, rank], scale = strength * alpha / rank */
+} we_linear;
+/* linear (ops.ts:61-73): y = x . W^T (+ bias) (+ up.scale (x . down^T) . up^T), a new pooled buffer
+   [m, n] of y_dtype. LoRA shape errors: "LoRA shapes do not fit the linear layer". */
+int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m,
+                      int32_t y_dtype, uint32_t flags, void** y);
+/* Mod (ops.ts:75): scale/shift device vectors of length d (NULL = zeros). */
+typedef struct {
+  const float* scale;
+  const float* shift;
+} we_mod;
+/* noMod (ops.ts:85): two zeroed pooled buffers of d floats. */
+int we_no_mod(we_ctx* ctx, int64_t d, we_mod* out);
+/* norm (ops.ts:78-82): RMSNorm rows of length d with modulation, a new pooled buffer. */
+int we_norm(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, int64_t rows, int64_t d,
+            const we_mod* mod, float eps, float offset, int32_t out_dtype, void** out);
+/* Rope (ops.ts:87): tables [tokens, pairs]. */
+typedef struct {
+  const float* cos;
+  const float* sin;
+  int64_t pairs, tokens;
+} we_rope;
+enum { WE_ROPE_INTERLEAVED = 0, WE_ROPE_HALF = 1 };
+/* rotate (ops.ts:89-93): x [tokens, heads, 2 pairs] -> a new pooled buffer. */
+int we_rotate(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t heads, const we_rope* rope, int32_t pairing,
+              int32_t out_dtype, void** out);
+
+/* ---------------- kernel-level entry points ---------------- */
+/* rmsnormWgsl (src/kernels/rmsnorm.ts:13-48):
+   out = x / sqrt(mean(x^2) + eps) * (offset + weight) * (1 + scale) + shift, per row of d. */
+int we_rmsnorm(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, const float* scale,
+               const float* shift, int64_t rows, int64_t d, float eps, float offset, void* out, int32_t out_dtype);
+/* ropeKernel (src/kernels/rope.ts:59-77), interleaved or half pairing. */
+int we_rope_apply(we_ctx* ctx, const void* x, int32_t x_dtype, const float* cos, const float* sin, int64_t tokens,
+                  int64_t heads, int64_t pairs, int32_t pairing, void* out, int32_t out_dtype);
+/* The block's q/k path in one pass (src/model/block.ts:53-56, norm then rotate): per head row of
+   2*pairs values, RMSNorm (offset, eps) with `weight` [2 pairs], then RoPE. */
+int we_qknorm_rope(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, float eps, float offset,
+                   const float* cos, const float* sin, int64_t tokens, int64_t heads, int64_t pairs,
+                   int32_t pairing, void* out, int32_t out_dtype);
+/* ropeTables (src/kernels/rope.ts:20-36) on the host in float64: pos [tokens, naxes], axes (even),
+   cos/sin [tokens, pairs] f32. Returns pairs, or -1 ("Every RoPE axis needs an even number of dims"). */
+int64_t we_rope_tables(const int64_t* pos, int64_t tokens, int32_t naxes, const int64_t* axes, double theta,
+                       float* cos, float* sin);
+/* positions (src/kernels/rope.ts:14-18): text tokens at (0,0,0), then image tokens (0, row, col). */
+int we_positions(int64_t text, int64_t rows, int64_t cols, int64_t* pos);
+
+/* unpackFp8 (src/kernels/fp8.ts:24-36): out[i] = e4m3(bytes[i]) * scale, f32. */
+int we_unpack_fp8(we_ctx* ctx, const uint8_t* bytes, int64_t n, float scale, float* out);
+/* The same decode to bf16 (exact: every e4m3 value is a bf16 value), scale 1. */
+int we_unpack_fp8_bf16(we_ctx* ctx, const uint8_t* bytes, int64_t n, uint16_t* out);
+/* int4 group-64 operand decode: out[n, k] = bf16_rne(q * f16 scale). */
+int we_unpack_int4(we_ctx* ctx, const uint8_t* packed, const uint16_t* scales, int64_t n, int64_t k,
+                   uint16_t* out);
+
+/* Weight quantisers (load-time helpers; no reference counterpart beyond the per-tensor fp8 format):
+   fp8 per output channel (per_channel = 1: s_n = max|W[n,:]| / 448) or per tensor (s = max|W| / 448),
+   q = e4m3 round-to-nearest-even, saturating. scales: [n] (or [1]) f32. */
+int we_quantize_fp8(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int64_t k, int32_t per_channel,
+                    uint8_t* q, float* scales);
+/* int4 group 64: s = f16_rne(max|W_group| / 7), q = clamp(rint(W / s), -8, 7). */
+int we_quantize_int4(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int64_t k, uint8_t* packed,
+                     uint16_t* scales);
+/* Activation split for the fp8 tensor-core path: per row a power-of-two scale 2^e (e smallest with
+   max|x| 2^-e <= 448), hi = e4m3(x 2^-e), lo = e4m3(x 2^-e - hi) (terms = 2; exact for bf16 input),
+   row_scale[m] = 2^e. lo may be NULL when terms = 1. */
+int we_quantize_act(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t m, int64_t k, int64_t x_stride,
+                    int32_t terms, uint8_t* hi, uint8_t* lo, float* row_scale);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -33,3 +33,11 @@ def pytest_configure(config):
 @pytest.fixture(scope="session")
 def we():
     return load_package()
+
+
+@pytest.fixture(scope="session")
+def graph(we):
+    """One library context on cuda:0 for the GPU tests."""
+    g = we.Graph(0)
+    yield g
+    g.destroy()

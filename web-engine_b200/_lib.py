@@ -1,0 +1,139 @@
+"""ctypes binding of the C ABI in include/we_b200.h (libwe_b200.so, built in this directory).
+
+There is no CPU fallback: when the library is missing, or there is no B200, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libwe_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "we_b200.h")
+
+WE_OK, WE_EINVAL, WE_ENOMEM, WE_ECUDA, WE_ENCCL, WE_ETIMEOUT, WE_EUNSUPPORTED = range(7)
+F32, BF16, FP8, INT4G64, F16 = 0, 1, 2, 3, 4
+MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT = 1, 2, 4
+ROPE_INTERLEAVED, ROPE_HALF = 0, 1
+
+DTYPES = {"f32": F32, "bf16": BF16, "fp8": FP8, "int4": INT4G64, "f16": F16}
+DTYPE_BYTES = {F32: 4, BF16: 2, FP8: 1, F16: 2}
+
+
+class WeError(RuntimeError):
+    """A non-OK status from the library; `code` is the WE_* status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+class Stats(C.Structure):
+    _fields_ = [("created", C.c_uint64), ("reused", C.c_uint64), ("created_bytes", C.c_uint64),
+                ("launches", C.c_uint64), ("tc_gemms", C.c_uint64), ("simt_gemms", C.c_uint64)]
+
+
+class MatmulDesc(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in ("m", "n", "k", "x_stride", "w_stride", "y_stride", "x_offset", "w_offset",
+                                         "y_offset", "k_split")] + [
+        ("scale", C.c_float), ("chan_scale", C.c_void_p), ("group_scale", C.c_void_p), ("bias", C.c_void_p),
+        ("x_dtype", C.c_int32), ("w_dtype", C.c_int32), ("y_dtype", C.c_int32), ("flags", C.c_uint32)]
+
+
+class GemmFp8Desc(C.Structure):
+    _fields_ = [("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64), ("x_hi", C.c_void_p), ("x_lo", C.c_void_p),
+                ("row_scale", C.c_void_p), ("w", C.c_void_p), ("scale", C.c_float), ("chan_scale", C.c_void_p),
+                ("bias", C.c_void_p), ("y", C.c_void_p), ("y_stride", C.c_int64), ("y_dtype", C.c_int32),
+                ("flags", C.c_uint32)]
+
+
+class LinearDesc(C.Structure):
+    pass
+
+
+LinearDesc._fields_ = [("weight", C.c_void_p), ("dtype", C.c_int32), ("scale", C.c_float), ("chan_scale", C.c_void_p),
+                       ("group_scale", C.c_void_p), ("n", C.c_int64), ("k", C.c_int64), ("bias", C.c_void_p),
+                       ("lora_down", C.POINTER(LinearDesc)), ("lora_up", C.POINTER(LinearDesc))]
+
+
+class ModDesc(C.Structure):
+    _fields_ = [("scale", C.c_void_p), ("shift", C.c_void_p)]
+
+
+class RopeDesc(C.Structure):
+    _fields_ = [("cos", C.c_void_p), ("sin", C.c_void_p), ("pairs", C.c_int64), ("tokens", C.c_int64)]
+
+
+_P = C.c_void_p
+_I64 = C.c_int64
+_SIGS = {
+    "we_init": (C.c_int, [C.c_int, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "we_destroy": (C.c_int, [_P]),
+    "we_last_error": (C.c_char_p, [_P]),
+    "we_set_stream": (C.c_int, [_P, _P]),
+    "we_get_stream": (_P, [_P]),
+    "we_sync": (C.c_int, [_P]),
+    "we_device_error": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "we_num_sms": (C.c_int, [_P]),
+    "we_buffer": (C.c_int, [_P, C.c_size_t, _P, C.POINTER(C.c_void_p)]),
+    "we_write": (C.c_int, [_P, _P, _P, C.c_size_t]),
+    "we_read": (C.c_int, [_P, _P, _P, C.c_size_t]),
+    "we_copy": (C.c_int, [_P, _P, C.c_size_t, _P, C.c_size_t, C.c_size_t]),
+    "we_mark": (C.c_size_t, [_P]),
+    "we_release": (C.c_int, [_P, C.c_size_t, C.POINTER(C.c_void_p), C.c_size_t]),
+    "we_free": (C.c_int, [_P, _P]),
+    "we_get_stats": (C.c_int, [_P, C.POINTER(Stats)]),
+    "we_matmul": (C.c_int, [_P, C.POINTER(MatmulDesc), _P, _P, _P]),
+    "we_matmul_check": (C.c_int, [_P, C.POINTER(MatmulDesc)]),
+    "we_gemm_fp8": (C.c_int, [_P, C.POINTER(GemmFp8Desc)]),
+    "we_ksplit_for": (_I64, [_I64, _I64, _I64]),
+    "we_linear_forward": (C.c_int, [_P, _P, C.c_int32, C.POINTER(LinearDesc), _I64, C.c_int32, C.c_uint32,
+                                    C.POINTER(C.c_void_p)]),
+    "we_no_mod": (C.c_int, [_P, _I64, C.POINTER(ModDesc)]),
+    "we_norm": (C.c_int, [_P, _P, C.c_int32, _P, _I64, _I64, C.POINTER(ModDesc), C.c_float, C.c_float, C.c_int32,
+                          C.POINTER(C.c_void_p)]),
+    "we_rotate": (C.c_int, [_P, _P, C.c_int32, _I64, C.POINTER(RopeDesc), C.c_int32, C.c_int32,
+                            C.POINTER(C.c_void_p)]),
+    "we_rmsnorm": (C.c_int, [_P, _P, C.c_int32, _P, _P, _P, _I64, _I64, C.c_float, C.c_float, _P, C.c_int32]),
+    "we_rope_apply": (C.c_int, [_P, _P, C.c_int32, _P, _P, _I64, _I64, _I64, C.c_int32, _P, C.c_int32]),
+    "we_qknorm_rope": (C.c_int, [_P, _P, C.c_int32, _P, C.c_float, C.c_float, _P, _P, _I64, _I64, _I64, C.c_int32, _P,
+                                 C.c_int32]),
+    "we_rope_tables": (_I64, [_P, _I64, C.c_int32, _P, C.c_double, _P, _P]),
+    "we_positions": (C.c_int, [_I64, _I64, _I64, _P]),
+    "we_unpack_fp8": (C.c_int, [_P, _P, _I64, C.c_float, _P]),
+    "we_unpack_fp8_bf16": (C.c_int, [_P, _P, _I64, _P]),
+    "we_unpack_int4": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
+    "we_quantize_fp8": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, C.c_int32, _P, _P]),
+    "we_quantize_int4": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _P, _P]),
+    "we_quantize_act": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, C.c_int32, _P, _P, _P]),
+}
+
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Every entry point declared in include/we_b200.h."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(we_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"web-engine B200 library not built ({LIB_PATH}); run __graft_entry__.build()")
+        lib_ = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(lib_, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib_
+    return _lib
+
+
+def check(ctx, rc: int) -> None:
+    if rc != WE_OK:
+        msg = lib().we_last_error(ctx)
+        raise WeError(rc, (msg.decode() if msg else "") or f"web-engine error {rc}")

@@ -1,0 +1,98 @@
+// Shared device helpers for the web-engine B200 kernels (sm_100a only).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/we_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "web-engine B200 kernels target sm_100a only"
+#endif
+
+namespace we {
+
+// Device error word codes (written by bounded waits; read by we_device_error).
+enum : uint32_t {
+  DEV_ERR_NONE = 0,
+  DEV_ERR_TIMEOUT_PRODUCER = 1,
+  DEV_ERR_TIMEOUT_MMA = 2,
+  DEV_ERR_TIMEOUT_EPILOGUE = 3,
+  DEV_ERR_TIMEOUT_DRAIN = 4,
+};
+
+// ---- element decode / encode ----
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+// e4m3fn byte -> f32 (exact). Same decode as src/kernels/fp8.ts:12-20 (NaN codes not special-cased).
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  uint32_t e = (b >> 3) & 0xfu, m = b & 7u;
+  float normal = __uint_as_float(((e + 120u) << 23) | (m << 20));
+  float sub = float(m) * 0.001953125f;  // m/8 * 2^-6
+  float v = e == 0 ? sub : normal;
+  return (b & 0x80u) ? -v : v;
+}
+
+// two e4m3 values (low byte first) -> two f32, by the hardware converter (exact)
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint16_t two) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(two, __NV_E4M3);
+  __half2 hh = *reinterpret_cast<__half2*>(&h);
+  return __half22float2(hh);
+}
+
+// f32 -> e4m3, round to nearest even, saturating to +-448 (NaN -> 0x7f)
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+  return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {
+  return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
+  __nv_bfloat16 b = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+template <int DT>
+__device__ __forceinline__ float load_act(const void* p, int64_t i) {
+  if constexpr (DT == WE_F32) return static_cast<const float*>(p)[i];
+  else return bf16_bits_to_f32(static_cast<const uint16_t*>(p)[i]);
+}
+template <int DT>
+__device__ __forceinline__ void store_out(void* p, int64_t i, float v) {
+  if constexpr (DT == WE_F32) static_cast<float*>(p)[i] = v;
+  else static_cast<uint16_t*>(p)[i] = f32_to_bf16_bits(v);
+}
+
+// int4 group-64 operand: bf16_rne(q * float(s)), q two's complement nibble
+__device__ __forceinline__ float int4_operand(uint32_t nib, float s) {
+  int q = int(nib ^ 8u) - 8;
+  return bf16_bits_to_f32(f32_to_bf16_bits(float(q) * s));
+}
+
+// ---- warp reductions ----
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+}  // namespace we

@@ -1,0 +1,460 @@
+// tcgen05 GEMM for the weight-quantized linear layers (sm_100a).
+//
+// Computes y[m, n] = (sum_t X_t[m, :] . W[n, :]) * row_scale[m] * (chan_scale[n] | scale) (+ bias) (+ y),
+// the tensor-core form of matmulWgsl (src/kernels/matmul.ts:118-178) for bf16 activations:
+//   * fp8 weights: kind::f8f6f4 with e4m3 W and e4m3 activation terms. The activation split
+//     (k_quant.cu quant_act_kernel) writes X = 2^e (hi + lo) per row with hi, lo e4m3: for bf16 x the
+//     two terms are exact, so the product equals the bf16 x fp8 dequant GEMM up to fp32 accumulation.
+//     One term (hi only) is the fp8-peak mode.
+//   * bf16 weights (and int4 weights decoded to bf16): kind::f16 with bf16 X, one term.
+//
+// Tile: 128 weight rows (UMMA M, TMEM lanes = output channels) x BT tokens (UMMA N, TMEM columns),
+// K in 128-byte stages (one SWIZZLE_128B row: 128 e4m3 or 64 bf16). Warp-specialised, persistent:
+//   warp 0     one thread issues TMA loads (no multicast) into a STAGES-deep shared-memory ring,
+//   warp 1     allocates TMEM and one thread issues tcgen05.mma, committing to the ring's empty
+//              barriers and, per tile, to a double-buffered TMEM accumulator's full barrier,
+//   warps 2-5  epilogue: tcgen05.ld 32 lanes x 32 columns, scale, bias, store (consecutive lanes =
+//              consecutive output channels, so each store instruction is coalesced).
+// Every mbarrier wait is bounded (2 s of %globaltimer); on timeout the kernel records a code in the
+// device error word, the other roles stop at their next wait, in-flight TMA loads and MMAs are
+// drained with bounded waits, TMEM is freed and the kernel returns.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace we {
+namespace tc {
+
+constexpr int BM = 128;           // weight rows per tile (UMMA M)
+constexpr int KB_BYTES = 128;     // K bytes per stage
+constexpr int THREADS = 192;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;
+constexpr int SMEM_BUDGET = 200 * 1024;
+
+struct Params {
+  int64_t m, n;
+  int num_kb;
+  const float* row_scale;
+  const float* chan_scale;
+  float scale;
+  const float* bias;
+  void* y;
+  int64_t y_stride;
+  int y_dtype;
+  int accumulate;
+  uint32_t* err;
+};
+
+template <int BT, int TERMS>
+struct Layout {
+  static constexpr int W_BYTES = BM * KB_BYTES;
+  static constexpr int X_BYTES = BT * KB_BYTES;
+  static constexpr int STAGE_BYTES = W_BYTES + TERMS * X_BYTES;
+  static constexpr int STAGES = (SMEM_BUDGET / STAGE_BYTES) > 8 ? 8 : (SMEM_BUDGET / STAGE_BYTES);
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int TOTAL = BAR_OFFSET + NUM_BARS * 8 + 16;
+  static constexpr int ALLOC = TOTAL + 1024;      // slack to align the base to 1024 bytes
+  static_assert(STAGES >= 2, "shared-memory ring needs at least 2 stages");
+};
+
+// ---------------- PTX wrappers ----------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: true when the phase of `parity` completed; false on timeout (records `code`, raises the
+// CTA's abort flag) or when another role already aborted (if watch_abort).
+__device__ __noinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint32_t* err,
+                                          uint32_t code, uint64_t limit_ns, bool watch_abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (watch_abort && *abort_flag) return false;
+      if (global_timer_ns() - t0 > limit_ns) {
+        atomicCAS(err, 0u, code);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// K-major operand in shared memory written by TMA with SWIZZLE_128B: rows of 128 bytes, 8-row groups
+// 1024 bytes apart (SBO), LBO unused (1), descriptor version 1 (sm_100), layout type 2 (128B swizzle).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B formats (f8f6f4: 0 = E4M3; f16: 1 = BF16), both K-major,
+// N = BT (bits 17-22, N >> 3), M = 128 (bits 24-28, M >> 4).
+template <int BT, bool F16>
+__host__ __device__ constexpr uint32_t make_idesc() {
+  return (1u << 4) | ((F16 ? 1u : 0u) << 7) | ((F16 ? 1u : 0u) << 10) | ((uint32_t)(BT >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+template <bool F16>
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  }
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------- the kernel ----------------
+template <int BT, int TERMS, bool F16>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x0,
+                   const __grid_constant__ CUtensorMap tm_x1, const Params p) {
+  using L = Layout<BT, TERMS>;
+  constexpr int STAGES = L::STAGES;
+  constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BT;
+  constexpr uint32_t IDESC = make_idesc<BT, F16>();
+  constexpr int MMAS_PER_KB = KB_BYTES / 32;  // 32 bytes of K per tcgen05.mma
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + L::BAR_OFFSET;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::BAR_OFFSET + L::NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+#define FULL(s) (bars + 8u * (s))
+#define EMPTY(s) (bars + 8u * (STAGES + (s)))
+#define TFULL(b) (bars + 8u * (2 * STAGES + (b)))
+#define TEMPTY(b) (bars + 8u * (2 * STAGES + 2 + (b)))
+#define DRAIN (bars + 8u * (2 * STAGES + 4))
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(FULL(s), 1);
+      mbar_init(EMPTY(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(TFULL(b), 1);
+      mbar_init(TEMPTY(b), 4);
+    }
+    mbar_init(DRAIN, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  const int64_t tiles_n = (p.n + BM - 1) / BM;
+  const int64_t tiles_m = (p.m + BT - 1) / BT;
+  const int64_t tiles = tiles_n * tiles_m;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x0)) : "memory");
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_ph[STAGES];
+      int issued = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int32_t row_w = (int32_t)((t % tiles_n) * BM), row_x = (int32_t)((t / tiles_n) * BT);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
+          mbar_expect_tx(FULL(s), L::STAGE_BYTES);
+          const int32_t kc = kb * KB_ELEMS;
+          tma_load_2d(st, &tm_w, FULL(s), kc, row_w);
+          tma_load_2d(st + L::W_BYTES, &tm_x0, FULL(s), kc, row_x);
+          if (TERMS > 1) tma_load_2d(st + L::W_BYTES + L::X_BYTES, &tm_x1, FULL(s), kc, row_x);
+          issued_ph[s] = ph;
+          issued++;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {  // let the loads already issued land before the CTA can exit
+        for (int i = 0; i < STAGES && i < issued; i++)
+          wait_bounded(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, aph = 0;
+      int ab = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!wait_bounded(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(ab * BT);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!wait_bounded(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
+          const uint64_t adesc = sw128_desc(st);
+#pragma unroll
+          for (int term = 0; term < TERMS; term++) {
+            const uint64_t bdesc = sw128_desc(st + L::W_BYTES + term * L::X_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < MMAS_PER_KB; kk++)
+              umma<F16>(d, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | term | kk) != 0);
+          }
+          umma_commit(EMPTY(s));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(TFULL(ab));
+        if (++ab == 2) {
+          ab = 0;
+          aph ^= 1u;
+        }
+      }
+      // all MMAs issued by this thread complete before TMEM can be freed
+      umma_commit(DRAIN);
+      wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int ab = 0;
+    uint32_t aph = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int64_t ch = (t % tiles_n) * BM + q * 32 + lane;
+      const int64_t tok_base = (t / tiles_n) * BT;
+      const bool ch_ok = ch < p.n;
+      const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
+      const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BT + c * 32), r);
+        const int64_t tok0 = tok_base + c * 32;
+        if (ch_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const int64_t tok = tok0 + j;
+            if (tok < p.m) {
+              float v = __uint_as_float(r[j]);
+              if (p.row_scale) v *= p.row_scale[tok];
+              v = v * cs + bias;
+              const int64_t o = tok * p.y_stride + ch;
+              if (p.y_dtype == WE_BF16) {
+                uint16_t* y = static_cast<uint16_t*>(p.y);
+                if (p.accumulate) v += bf16_bits_to_f32(y[o]);
+                y[o] = f32_to_bf16_bits(v);
+              } else {
+                float* y = static_cast<float*>(p.y);
+                if (p.accumulate) v += y[o];
+                y[o] = v;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(TEMPTY(ab));
+      if (++ab == 2) {
+        ab = 0;
+        aph ^= 1u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+#undef FULL
+#undef EMPTY
+#undef TFULL
+#undef TEMPTY
+#undef DRAIN
+}
+
+// ---------------- host side ----------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2D map over [rows, k] with 128-byte-wide boxes of box_rows rows, 128-byte swizzle, zero fill.
+static bool make_map(CUtensorMap* m, const void* base, bool f16, int64_t k, int64_t rows, int64_t stride_bytes,
+                     int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)stride_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(f16 ? KB_BYTES / 2 : KB_BYTES), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BT, int TERMS, bool F16>
+static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
+  using L = Layout<BT, TERMS>;
+  CUtensorMap mw, mx0, mx1;
+  if (!make_map(&mw, a.w, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
+  if (!make_map(&mx0, a.x[0], F16, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
+  if (TERMS > 1) {
+    if (!make_map(&mx1, a.x[1], F16, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
+  } else {
+    mx1 = mx0;
+  }
+  Params p;
+  p.m = a.m;
+  p.n = a.n;
+  const int64_t kbytes = a.k * (F16 ? 2 : 1);
+  p.num_kb = (int)((kbytes + KB_BYTES - 1) / KB_BYTES);
+  p.row_scale = a.row_scale;
+  p.chan_scale = a.chan_scale;
+  p.scale = a.scale;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.y_stride = a.y_stride;
+  p.y_dtype = a.y_dtype;
+  p.accumulate = a.accumulate;
+  p.err = a.dev_err;
+  auto kern = gemm_tc_kernel<BT, TERMS, F16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = ((a.n + BM - 1) / BM) * ((a.m + BT - 1) / BT);
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  kern<<<grid, THREADS, L::ALLOC, st>>>(mw, mx0, mx1, p);
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+bool gemm_tc_supported(const TcGemmArgs& a) {
+  const int es = a.kind_f16 ? 2 : 1;
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (a.m < 1 || a.n < 1 || a.k < 1) return false;
+  if ((a.k * es) % 16 != 0) return false;
+  if (a.w_stride_bytes % 16 != 0 || a.x_stride_bytes % 16 != 0) return false;
+  if (a.w_stride_bytes < a.k * es || a.x_stride_bytes < a.k * es) return false;
+  if (!al(a.w) || !al(a.x[0]) || (a.terms > 1 && !al(a.x[1]))) return false;
+  if (a.m > 0x7fffffffLL || a.n > 0x7fffffffLL || a.k > 0x7fffffffLL) return false;
+  return true;
+}
+
+// Token tile: the largest of 256 / 128 / 64 that still gives every SM a tile, else 64.
+cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
+  if (!gemm_tc_supported(a)) return cudaErrorNotSupported;
+  const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
+  auto tiles = [&](int bt) { return tn * ((a.m + bt - 1) / bt); };
+  int bt = tiles(256) >= sms ? 256 : (tiles(128) >= sms ? 128 : 64);
+  if (a.kind_f16) {
+    if (bt == 256) return tc::run<256, 1, true>(a, sms, st);
+    if (bt == 128) return tc::run<128, 1, true>(a, sms, st);
+    return tc::run<64, 1, true>(a, sms, st);
+  }
+  if (a.terms > 1) {
+    if (bt == 256) return tc::run<256, 2, false>(a, sms, st);
+    if (bt == 128) return tc::run<128, 2, false>(a, sms, st);
+    return tc::run<64, 2, false>(a, sms, st);
+  }
+  if (bt == 256) return tc::run<256, 1, false>(a, sms, st);
+  if (bt == 128) return tc::run<128, 1, false>(a, sms, st);
+  return tc::run<64, 1, false>(a, sms, st);
+}
+
+}  // namespace we

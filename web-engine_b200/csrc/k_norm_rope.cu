@@ -1,0 +1,299 @@
+// RMSNorm (+ Krea modulation), RoPE and the fused q/k-norm + RoPE.
+//
+// Reference: rmsnormWgsl (src/kernels/rmsnorm.ts:13-48), ropeKernel (src/kernels/rope.ts:59-77), and the
+// q/k path of attend() (src/model/block.ts:53-56: linear -> norm(qNorm, rows*heads, 128) -> rotate).
+// These are HBM-bandwidth kernels. Row sums of squares are accumulated in fp32 like the reference
+// shader (tree order differs; the result stays within the reference test's 1e-5).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace we {
+
+// 8 values of an activation row as floats: one 16-byte load for bf16, two for f32
+template <int DT>
+__device__ __forceinline__ void load8(const void* p, int64_t i, float v[8]) {
+  if constexpr (DT == WE_BF16) {
+    uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+  } else {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    float4 a = q[0], b = q[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+template <int DT>
+__device__ __forceinline__ void store8(void* p, int64_t i, const float v[8]) {
+  if constexpr (DT == WE_BF16) {
+    uint4 u = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = u;
+  } else {
+    float4* q = reinterpret_cast<float4*>(static_cast<float*>(p) + i);
+    q[0] = make_float4(v[0], v[1], v[2], v[3]);
+    q[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+__device__ __forceinline__ void load8f(const float* p, int64_t i, float v[8]) {
+  const float4* q = reinterpret_cast<const float4*>(p + i);
+  float4 a = q[0], b = q[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// One CTA per row (grid-stride over rows). VEC: 8 values per access (d % 8 == 0, aligned); the row
+// is read twice, the second time from L1/L2.
+template <int DT, int OT, bool VEC>
+__global__ void rmsnorm_kernel(const void* __restrict__ x, const float* __restrict__ w, const float* __restrict__ sc,
+                               const float* __restrict__ sh, int64_t rows, int64_t d, float eps, float offset,
+                               void* __restrict__ out) {
+  __shared__ float red[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    int64_t base = row * d;
+    float ss = 0.f;
+    if (VEC) {
+      for (int64_t i = 8 * threadIdx.x; i < d; i += 8 * blockDim.x) {
+        float v[8];
+        load8<DT>(x, base + i, v);
+#pragma unroll
+        for (int j = 0; j < 8; j++) ss = fmaf(v[j], v[j], ss);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < d; i += blockDim.x) {
+        float v = load_act<DT>(x, base + i);
+        ss = fmaf(v, v, ss);
+      }
+    }
+    float inv = rsqrtf(block_sum(ss, red) / (float)d + eps);
+    if (VEC) {
+      for (int64_t i = 8 * threadIdx.x; i < d; i += 8 * blockDim.x) {
+        float v[8], ww[8], s[8], h[8];
+        load8<DT>(x, base + i, v);
+        load8f(w, i, ww);
+        if (sc) load8f(sc, i, s); else for (int j = 0; j < 8; j++) s[j] = 0.f;
+        if (sh) load8f(sh, i, h); else for (int j = 0; j < 8; j++) h[j] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = v[j] * inv * (offset + ww[j]) * (1.f + s[j]) + h[j];
+        store8<OT>(out, base + i, v);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < d; i += blockDim.x) {
+        float v = load_act<DT>(x, base + i);
+        float s = sc ? sc[i] : 0.f, h = sh ? sh[i] : 0.f;
+        store_out<OT>(out, base + i, v * inv * (offset + w[i]) * (1.f + s) + h);
+      }
+    }
+  }
+}
+
+// RoPE, interleaved pairs (2j, 2j+1) or half pairs (j, j+P). One thread per (token, group of G pairs),
+// looping over heads so each cos/sin value is loaded once per token (like the reference kernel).
+template <int DT, int OT, int G, int PAIRING>
+__global__ void rope_kernel(const void* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
+                            int64_t tokens, int64_t heads, int64_t pairs, void* __restrict__ out) {
+  int64_t groups = pairs / G;
+  int64_t total = tokens * groups;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < total; it += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = it / groups, j0 = (it % groups) * G;
+    float c[G], s[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      c[g] = cs[t * pairs + j0 + g];
+      s[g] = sn[t * pairs + j0 + g];
+    }
+    for (int64_t h = 0; h < heads; h++) {
+      int64_t base = (t * heads + h) * pairs * 2;
+      if (PAIRING == WE_ROPE_INTERLEAVED) {
+        float v[2 * G];
+        if constexpr (2 * G == 8) load8<DT>(x, base + 2 * j0, v);
+        else for (int e = 0; e < 2 * G; e++) v[e] = load_act<DT>(x, base + 2 * j0 + e);
+        float o[2 * G];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          o[2 * g] = v[2 * g] * c[g] - v[2 * g + 1] * s[g];
+          o[2 * g + 1] = v[2 * g + 1] * c[g] + v[2 * g] * s[g];
+        }
+        if constexpr (2 * G == 8) store8<OT>(out, base + 2 * j0, o);
+        else for (int e = 0; e < 2 * G; e++) store_out<OT>(out, base + 2 * j0 + e, o[e]);
+      } else {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          float a = load_act<DT>(x, base + j0 + g), b = load_act<DT>(x, base + j0 + g + pairs);
+          store_out<OT>(out, base + j0 + g, a * c[g] - b * s[g]);
+          store_out<OT>(out, base + j0 + g + pairs, b * c[g] + a * s[g]);
+        }
+      }
+    }
+  }
+}
+
+// Fused q/k norm + RoPE: one warp per (token, head) row of D = 2 * pairs values; lane l holds the
+// contiguous values [l V, l V + V) with V = D / 32 (D = 64, 128 or 256). Interleaved pairs stay in a
+// lane; half pairing exchanges with lane l ^ 16.
+template <int DT, int OT, int V, int PAIRING>
+__global__ void qknorm_rope_kernel(const void* __restrict__ x, const float* __restrict__ w, float eps, float offset,
+                                   const float* __restrict__ cs, const float* __restrict__ sn, int64_t tokens,
+                                   int64_t heads, void* __restrict__ out) {
+  constexpr int D = 32 * V, P = D / 2;
+  int lane = threadIdx.x & 31;
+  int64_t rows = tokens * heads;
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  float ww[V];
+#pragma unroll
+  for (int e = 0; e < V; e++) ww[e] = offset + w[lane * V + e];
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    int64_t t = row / heads;
+    int64_t base = row * D + lane * V;
+    float v[V];
+    if constexpr (V == 8) load8<DT>(x, base, v);
+    else {
+#pragma unroll
+      for (int e = 0; e < V; e++) v[e] = load_act<DT>(x, base + e);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < V; e++) ss = fmaf(v[e], v[e], ss);
+    float inv = rsqrtf(warp_sum(ss) / (float)D + eps);
+#pragma unroll
+    for (int e = 0; e < V; e++) v[e] = v[e] * inv * ww[e];
+    float o[V];
+    if (PAIRING == WE_ROPE_INTERLEAVED) {
+#pragma unroll
+      for (int g = 0; g < V / 2; g++) {
+        int64_t j = lane * (V / 2) + g;
+        float c = cs[t * P + j], s = sn[t * P + j];
+        o[2 * g] = v[2 * g] * c - v[2 * g + 1] * s;
+        o[2 * g + 1] = v[2 * g + 1] * c + v[2 * g] * s;
+      }
+    } else {
+      bool first = lane < 16;
+#pragma unroll
+      for (int e = 0; e < V; e++) {
+        float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
+        int64_t j = (int64_t)(lane & 15) * V + e;  // pair index of this value
+        float c = cs[t * P + j], s = sn[t * P + j];
+        // first half: a = v, b = partner -> a c - b s ; second half: b = v, a = partner -> b c + a s
+        o[e] = first ? v[e] * c - partner * s : v[e] * c + partner * s;
+      }
+    }
+    if constexpr (V == 8) store8<OT>(out, base, o);
+    else {
+#pragma unroll
+      for (int e = 0; e < V; e++) store_out<OT>(out, base + e, o[e]);
+    }
+  }
+}
+
+static int capped(int64_t want, int sms, int per_sm) {
+  int64_t cap = (int64_t)sms * per_sm;
+  if (want > cap) want = cap;
+  return want < 1 ? 1 : (int)want;
+}
+
+template <int DT, int OT>
+static void rmsnorm_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
+                             float eps, float offset, void* out, bool vec, int sms, cudaStream_t st) {
+  int threads = d >= 2048 ? 256 : 128;
+  int g = capped(rows, sms, 2048 / threads * 2);
+  if (vec) rmsnorm_kernel<DT, OT, true><<<g, threads, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+  else rmsnorm_kernel<DT, OT, false><<<g, threads, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+}
+
+static bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+cudaError_t launch_rmsnorm(const void* x, int xdt, const float* w, const float* sc, const float* sh, int64_t rows,
+                           int64_t d, float eps, float offset, void* out, int odt, int sms, cudaStream_t st) {
+  bool vec = d % 8 == 0 && al16(x) && al16(out) && al16(w) && (!sc || al16(sc)) && (!sh || al16(sh));
+  if (xdt == WE_BF16 && odt == WE_BF16) rmsnorm_dispatch<WE_BF16, WE_BF16>(x, w, sc, sh, rows, d, eps, offset, out, vec, sms, st);
+  else if (xdt == WE_BF16) rmsnorm_dispatch<WE_BF16, WE_F32>(x, w, sc, sh, rows, d, eps, offset, out, vec, sms, st);
+  else if (odt == WE_BF16) rmsnorm_dispatch<WE_F32, WE_BF16>(x, w, sc, sh, rows, d, eps, offset, out, vec, sms, st);
+  else rmsnorm_dispatch<WE_F32, WE_F32>(x, w, sc, sh, rows, d, eps, offset, out, vec, sms, st);
+  return cudaGetLastError();
+}
+
+template <int DT, int OT>
+static void rope_dispatch(const void* x, const float* cs, const float* sn, int64_t tokens, int64_t heads, int64_t pairs,
+                          int pairing, void* out, bool vec, int sms, cudaStream_t st) {
+  int threads = 128;
+  if (pairing == WE_ROPE_INTERLEAVED) {
+    if (vec) {
+      int g = capped((tokens * (pairs / 4) + threads - 1) / threads, sms, 16);
+      rope_kernel<DT, OT, 4, WE_ROPE_INTERLEAVED><<<g, threads, 0, st>>>(x, cs, sn, tokens, heads, pairs, out);
+    } else {
+      int g = capped((tokens * pairs + threads - 1) / threads, sms, 16);
+      rope_kernel<DT, OT, 1, WE_ROPE_INTERLEAVED><<<g, threads, 0, st>>>(x, cs, sn, tokens, heads, pairs, out);
+    }
+  } else {
+    int g = capped((tokens * pairs + threads - 1) / threads, sms, 16);
+    rope_kernel<DT, OT, 1, WE_ROPE_HALF><<<g, threads, 0, st>>>(x, cs, sn, tokens, heads, pairs, out);
+  }
+}
+
+cudaError_t launch_rope(const void* x, int xdt, const float* cs, const float* sn, int64_t tokens, int64_t heads,
+                        int64_t pairs, int pairing, void* out, int odt, int sms, cudaStream_t st) {
+  bool vec = pairs % 4 == 0 && al16(x) && al16(out);
+  if (xdt == WE_BF16 && odt == WE_BF16) rope_dispatch<WE_BF16, WE_BF16>(x, cs, sn, tokens, heads, pairs, pairing, out, vec, sms, st);
+  else if (xdt == WE_BF16) rope_dispatch<WE_BF16, WE_F32>(x, cs, sn, tokens, heads, pairs, pairing, out, vec, sms, st);
+  else if (odt == WE_BF16) rope_dispatch<WE_F32, WE_BF16>(x, cs, sn, tokens, heads, pairs, pairing, out, vec, sms, st);
+  else rope_dispatch<WE_F32, WE_F32>(x, cs, sn, tokens, heads, pairs, pairing, out, vec, sms, st);
+  return cudaGetLastError();
+}
+
+template <int DT, int OT, int V>
+static void qk_dispatch2(const void* x, const float* w, float eps, float offset, const float* cs, const float* sn,
+                         int64_t tokens, int64_t heads, int pairing, void* out, int sms, cudaStream_t st) {
+  int threads = 256;
+  int64_t rows = tokens * heads;
+  int g = capped((rows + 7) / 8, sms, 8);
+  if (pairing == WE_ROPE_INTERLEAVED)
+    qknorm_rope_kernel<DT, OT, V, WE_ROPE_INTERLEAVED><<<g, threads, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+  else
+    qknorm_rope_kernel<DT, OT, V, WE_ROPE_HALF><<<g, threads, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+}
+
+template <int DT, int OT>
+static bool qk_dispatch(const void* x, const float* w, float eps, float offset, const float* cs, const float* sn,
+                        int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out, int sms, cudaStream_t st) {
+  switch (pairs * 2) {
+    case 64: qk_dispatch2<DT, OT, 2>(x, w, eps, offset, cs, sn, tokens, heads, pairing, out, sms, st); return true;
+    case 128: qk_dispatch2<DT, OT, 4>(x, w, eps, offset, cs, sn, tokens, heads, pairing, out, sms, st); return true;
+    case 256: qk_dispatch2<DT, OT, 8>(x, w, eps, offset, cs, sn, tokens, heads, pairing, out, sms, st); return true;
+    default: return false;
+  }
+}
+
+// Returns cudaErrorNotSupported when the head size has no fused variant (the caller then runs
+// rmsnorm + rope as two passes).
+cudaError_t launch_qknorm_rope(const void* x, int xdt, const float* w, float eps, float offset, const float* cs,
+                               const float* sn, int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out,
+                               int odt, int sms, cudaStream_t st) {
+  if (pairs * 2 == 256 && !(al16(x) && al16(out))) return cudaErrorNotSupported;
+  bool ok;
+  if (xdt == WE_BF16 && odt == WE_BF16) ok = qk_dispatch<WE_BF16, WE_BF16>(x, w, eps, offset, cs, sn, tokens, heads, pairs, pairing, out, sms, st);
+  else if (xdt == WE_BF16) ok = qk_dispatch<WE_BF16, WE_F32>(x, w, eps, offset, cs, sn, tokens, heads, pairs, pairing, out, sms, st);
+  else if (odt == WE_BF16) ok = qk_dispatch<WE_F32, WE_BF16>(x, w, eps, offset, cs, sn, tokens, heads, pairs, pairing, out, sms, st);
+  else ok = qk_dispatch<WE_F32, WE_F32>(x, w, eps, offset, cs, sn, tokens, heads, pairs, pairing, out, sms, st);
+  if (!ok) return cudaErrorNotSupported;
+  return cudaGetLastError();
+}
+
+}  // namespace we

@@ -1,0 +1,270 @@
+// Decode / quantise kernels: fp8 and int4 unpack (src/kernels/fp8.ts:24-36 unpackFp8 and the int4
+// group-64 operand), weight quantisers, and the activation split that feeds the fp8 tensor-core GEMM.
+// All are HBM-bandwidth kernels: 16-byte vector accesses where the layout allows, grid-stride
+// loops sized to a multiple of the SM count.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace we {
+
+// ---------------- unpack ----------------
+// n16: number of 16-value chunks done with vector accesses (0 when the pointers are not 16-byte aligned)
+__global__ void unpack_fp8_f32_kernel(const uint8_t* __restrict__ in, int64_t n, int64_t n16, float scale,
+                                      float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 v = reinterpret_cast<const uint4*>(in)[i];
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float r[16];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+#pragma unroll
+      for (int b = 0; b < 4; b++) r[4 * j + b] = e4m3_to_f32((w[j] >> (8 * b)) & 0xffu) * scale;
+    float4* o = reinterpret_cast<float4*>(out + 16 * i);
+#pragma unroll
+    for (int j = 0; j < 4; j++) o[j] = make_float4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+  }
+  // ragged tail (n not a multiple of 16): one thread per value
+  for (int64_t i = n16 * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = e4m3_to_f32(in[i]) * scale;
+}
+
+__global__ void unpack_fp8_bf16_kernel(const uint8_t* __restrict__ in, int64_t n, int64_t n8, uint16_t* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    uint2 v = reinterpret_cast<const uint2*>(in)[i];
+    uint32_t w[2] = {v.x, v.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      float2 a = e4m3x2_to_f32x2((uint16_t)(w[j] & 0xffffu));
+      float2 b = e4m3x2_to_f32x2((uint16_t)(w[j] >> 16));
+      o[2 * j] = pack_bf16x2(a.x, a.y);
+      o[2 * j + 1] = pack_bf16x2(b.x, b.y);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  for (int64_t i = n8 * 8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = f32_to_bf16_bits(e4m3_to_f32(in[i]));
+}
+
+// int4 g64 -> bf16 operand. One thread per 8 values (one u32 of packed nibbles), k % 64 == 0.
+__global__ void unpack_int4_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scales, int64_t n,
+                                   int64_t k, uint16_t* __restrict__ out) {
+  int64_t words = n * k / 8;
+  int64_t groups = k / 64;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < words; i += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t w = reinterpret_cast<const uint32_t*>(packed)[i];
+    int64_t e0 = i * 8;  // first value
+    int64_t row = e0 / k, col = e0 % k;
+    float s = __half2float(__ushort_as_half(scales[row * groups + col / 64]));
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float lo = int4_operand((w >> (8 * j)) & 0xfu, s);
+      float hi = int4_operand((w >> (8 * j + 4)) & 0xfu, s);
+      o[j] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------- weight quantisers ----------------
+template <int DT>
+__device__ float block_absmax_row(const void* w, int64_t base, int64_t k) {
+  float m = 0.f;
+  for (int64_t t = threadIdx.x; t < k; t += blockDim.x) m = fmaxf(m, fabsf(load_act<DT>(w, base + t)));
+  __shared__ float red[32];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+template <int DT>
+__global__ void quant_fp8_rows_kernel(const void* __restrict__ w, int64_t n, int64_t k, const float* __restrict__ tensor_amax,
+                                      uint8_t* __restrict__ q, float* __restrict__ scales) {
+  for (int64_t row = blockIdx.x; row < n; row += gridDim.x) {
+    float amax = tensor_amax ? *tensor_amax : block_absmax_row<DT>(w, row * k, k);
+    float s = amax > 0.f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+    if (threadIdx.x == 0 && (!tensor_amax || row == 0)) scales[tensor_amax ? 0 : row] = s;
+    for (int64_t t = threadIdx.x; t < k; t += blockDim.x) q[row * k + t] = f32_to_e4m3(__fdiv_rn(load_act<DT>(w, row * k + t), s));
+  }
+}
+
+template <int DT>
+__global__ void absmax_all_kernel(const void* __restrict__ w, int64_t total, unsigned int* __restrict__ out_bits) {
+  float m = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(load_act<DT>(w, i)));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(out_bits, __float_as_uint(m));  // non-negative floats order as ints
+}
+
+// one warp per (row, group of 64); lane l owns values 2l, 2l+1 (one packed byte)
+template <int DT>
+__global__ void quant_int4_kernel(const void* __restrict__ w, int64_t n, int64_t k, uint8_t* __restrict__ packed,
+                                  uint16_t* __restrict__ scales) {
+  int64_t groups = k / 64;
+  int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  int lane = threadIdx.x & 31;
+  for (int64_t gi = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); gi < n * groups; gi += warps) {
+    int64_t row = gi / groups, g = gi % groups;
+    int64_t base = row * k + g * 64 + 2 * lane;
+    float a = load_act<DT>(w, base), b = load_act<DT>(w, base + 1);
+    float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
+    __half s16 = __float2half_rn(__fdiv_rn(amax, 7.0f));
+    float s = __half2float(s16);
+    int qa = 0, qb = 0;
+    if (s != 0.f) {
+      qa = (int)fminf(fmaxf(rintf(__fdiv_rn(a, s)), -8.f), 7.f);
+      qb = (int)fminf(fmaxf(rintf(__fdiv_rn(b, s)), -8.f), 7.f);
+    }
+    packed[base / 2] = (uint8_t)((qa & 0xf) | ((qb & 0xf) << 4));
+    if (lane == 0) scales[gi] = __half_as_ushort(s16);
+  }
+}
+
+// ---------------- activation split (fp8 tensor-core path) ----------------
+// exponent e: smallest integer with amax * 2^-e <= 448 (amax = m 2^E, m in [1,2): e = E-8 if m <= 1.75 else E-7)
+__device__ __forceinline__ int act_exponent(float amax) {
+  if (!(amax > 0.f)) return 0;
+  int E;
+  float f = frexpf(amax, &E);  // amax = f 2^E, f in [0.5, 1)
+  float m = 2.f * f;
+  E -= 1;
+  return m <= 1.75f ? E - 8 : E - 7;
+}
+
+// one CTA per row (grid-stride); VEC = values per 16-byte load of x
+template <int DT, int TERMS>
+__global__ void quant_act_kernel(const void* __restrict__ x, int64_t m, int64_t k, int64_t stride, uint8_t* __restrict__ hi,
+                                 uint8_t* __restrict__ lo, float* __restrict__ row_scale, int vec_ok) {
+  __shared__ float red[32];
+  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+    int64_t base = row * stride;
+    float amax = 0.f;
+    for (int64_t t = threadIdx.x; t < k; t += blockDim.x) amax = fmaxf(amax, fabsf(load_act<DT>(x, base + t)));
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      v = warp_max(v);
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    int e = act_exponent(red[0]);
+    __syncthreads();
+    if (threadIdx.x == 0) row_scale[row] = ldexpf(1.0f, e);
+    if (vec_ok) {
+      // 8 values per step: 16 B of bf16 / 32 B of f32 in, 8 B per term out
+      for (int64_t t = 8 * threadIdx.x; t < k; t += 8 * blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = ldexpf(load_act<DT>(x, base + t + j), -e);
+        uint32_t h[2], l[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          uint16_t h0 = f32x2_to_e4m3x2(v[4 * j], v[4 * j + 1]);
+          uint16_t h1 = f32x2_to_e4m3x2(v[4 * j + 2], v[4 * j + 3]);
+          h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+          if (TERMS > 1) {
+            float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+            uint16_t l0 = f32x2_to_e4m3x2(v[4 * j] - d0.x, v[4 * j + 1] - d0.y);
+            uint16_t l1 = f32x2_to_e4m3x2(v[4 * j + 2] - d1.x, v[4 * j + 3] - d1.y);
+            l[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+          }
+        }
+        *reinterpret_cast<uint2*>(hi + row * k + t) = make_uint2(h[0], h[1]);
+        if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * k + t) = make_uint2(l[0], l[1]);
+      }
+    } else {
+      for (int64_t t = threadIdx.x; t < k; t += blockDim.x) {
+        float v = ldexpf(load_act<DT>(x, base + t), -e);
+        uint8_t h = f32_to_e4m3(v);
+        hi[row * k + t] = h;
+        if (TERMS > 1) lo[row * k + t] = f32_to_e4m3(v - e4m3_to_f32(h));
+      }
+    }
+  }
+}
+
+// ---------------- launchers ----------------
+static int grid_for(int64_t work, int threads, int sms, int per_sm = 8) {
+  int64_t g = (work + threads - 1) / threads;
+  int64_t cap = (int64_t)sms * per_sm;
+  if (g > cap) g = cap;
+  return g < 1 ? 1 : (int)g;
+}
+
+cudaError_t launch_unpack_fp8_f32(const uint8_t* in, int64_t n, float scale, float* out, int sms, cudaStream_t st) {
+  bool vec = ((uintptr_t)in % 16 == 0) && ((uintptr_t)out % 16 == 0);
+  int64_t n16 = vec ? n / 16 : 0;
+  unpack_fp8_f32_kernel<<<grid_for(n16 + (n - 16 * n16), 256, sms), 256, 0, st>>>(in, n, n16, scale, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_unpack_fp8_bf16(const uint8_t* in, int64_t n, uint16_t* out, int sms, cudaStream_t st) {
+  bool vec = ((uintptr_t)in % 8 == 0) && ((uintptr_t)out % 16 == 0);
+  int64_t n8 = vec ? n / 8 : 0;
+  unpack_fp8_bf16_kernel<<<grid_for(n8 + (n - 8 * n8), 256, sms), 256, 0, st>>>(in, n, n8, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_unpack_int4(const uint8_t* packed, const uint16_t* scales, int64_t n, int64_t k, uint16_t* out,
+                               int sms, cudaStream_t st) {
+  unpack_int4_kernel<<<grid_for(n * k / 8, 256, sms), 256, 0, st>>>(packed, scales, n, k, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_fp8(const void* w, int dt, int64_t n, int64_t k, bool per_channel, uint8_t* q, float* scales,
+                             unsigned int* amax_scratch, int sms, cudaStream_t st) {
+  int g = (int)((n < (int64_t)sms * 8) ? n : (int64_t)sms * 8);
+  if (g < 1) g = 1;
+  if (per_channel) {
+    if (dt == WE_F32) quant_fp8_rows_kernel<WE_F32><<<g, 256, 0, st>>>(w, n, k, nullptr, q, scales);
+    else quant_fp8_rows_kernel<WE_BF16><<<g, 256, 0, st>>>(w, n, k, nullptr, q, scales);
+  } else {
+    cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int), st);
+    if (dt == WE_F32) absmax_all_kernel<WE_F32><<<grid_for(n * k, 256, sms), 256, 0, st>>>(w, n * k, amax_scratch);
+    else absmax_all_kernel<WE_BF16><<<grid_for(n * k, 256, sms), 256, 0, st>>>(w, n * k, amax_scratch);
+    const float* am = reinterpret_cast<const float*>(amax_scratch);
+    if (dt == WE_F32) quant_fp8_rows_kernel<WE_F32><<<g, 256, 0, st>>>(w, n, k, am, q, scales);
+    else quant_fp8_rows_kernel<WE_BF16><<<g, 256, 0, st>>>(w, n, k, am, q, scales);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_int4(const void* w, int dt, int64_t n, int64_t k, uint8_t* packed, uint16_t* scales, int sms,
+                              cudaStream_t st) {
+  int64_t warps = n * (k / 64);
+  int g = grid_for(warps * 32, 256, sms);
+  if (dt == WE_F32) quant_int4_kernel<WE_F32><<<g, 256, 0, st>>>(w, n, k, packed, scales);
+  else quant_int4_kernel<WE_BF16><<<g, 256, 0, st>>>(w, n, k, packed, scales);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_act(const void* x, int dt, int64_t m, int64_t k, int64_t stride, int terms, uint8_t* hi,
+                             uint8_t* lo, float* row_scale, int sms, cudaStream_t st) {
+  int threads = 128;
+  int g = (int)((m < (int64_t)sms * 16) ? m : (int64_t)sms * 16);
+  if (g < 1) g = 1;
+  int vec_ok = (k % 8 == 0) && ((uintptr_t)hi % 8 == 0) && (!lo || (uintptr_t)lo % 8 == 0);
+  if (dt == WE_F32) {
+    if (terms > 1) quant_act_kernel<WE_F32, 2><<<g, threads, 0, st>>>(x, m, k, stride, hi, lo, row_scale, vec_ok);
+    else quant_act_kernel<WE_F32, 1><<<g, threads, 0, st>>>(x, m, k, stride, hi, lo, row_scale, vec_ok);
+  } else {
+    if (terms > 1) quant_act_kernel<WE_BF16, 2><<<g, threads, 0, st>>>(x, m, k, stride, hi, lo, row_scale, vec_ok);
+    else quant_act_kernel<WE_BF16, 1><<<g, threads, 0, st>>>(x, m, k, stride, hi, lo, row_scale, vec_ok);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace we

@@ -1,0 +1,67 @@
+// Host-side launch interfaces of the web-engine B200 kernels (internal to the library).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace we {
+
+// Resolved matmul arguments (values, not bytes; strides already defaulted).
+struct MatmulArgs {
+  int64_t m, n, k;
+  int64_t x_stride, w_stride, y_stride, x_offset, w_offset, y_offset;
+  int64_t k_split;
+  float scale;
+  const float* chan_scale;
+  const uint16_t* group_scale;
+  const float* bias;
+  int x_dtype, w_dtype, y_dtype;
+  int accumulate;
+};
+
+cudaError_t launch_gemm_simt(const void* x, const void* w, void* y, const MatmulArgs& a, cudaStream_t st);
+
+// tcgen05 GEMM: y[m, n] = (sum over terms of X_t[m, :] . W[n, :]) * row_scale[m] * (chan_scale[n] | scale)
+// (+ bias[n]) (+ y if accumulate). kind_f16: X and W bf16 (one term); else X terms and W e4m3.
+struct TcGemmArgs {
+  const void* w;            // [n, k] (fp8 bytes or bf16), rows w_stride_bytes apart
+  int64_t w_stride_bytes;
+  const void* x[2];         // terms, [m, k], rows x_stride_bytes apart
+  int64_t x_stride_bytes;
+  int terms;                // 1 or 2 (fp8 only)
+  int kind_f16;             // 1: bf16 x bf16 (kind::f16); 0: e4m3 x e4m3 (kind::f8f6f4)
+  int64_t m, n, k;          // k in elements
+  const float* row_scale;   // [m] or null
+  const float* chan_scale;  // [n] or null
+  float scale;
+  const float* bias;        // [n] or null
+  void* y;
+  int64_t y_stride;         // values
+  int y_dtype;
+  int accumulate;
+  uint32_t* dev_err;        // device error word
+};
+// Returns cudaErrorNotSupported when the layout cannot go through TMA (alignment) so the caller can
+// use the CUDA-core kernel instead.
+cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st);
+bool gemm_tc_supported(const TcGemmArgs& a);
+
+cudaError_t launch_unpack_fp8_f32(const uint8_t* in, int64_t n, float scale, float* out, int sms, cudaStream_t st);
+cudaError_t launch_unpack_fp8_bf16(const uint8_t* in, int64_t n, uint16_t* out, int sms, cudaStream_t st);
+cudaError_t launch_unpack_int4(const uint8_t* packed, const uint16_t* scales, int64_t n, int64_t k, uint16_t* out,
+                               int sms, cudaStream_t st);
+cudaError_t launch_quant_fp8(const void* w, int dt, int64_t n, int64_t k, bool per_channel, uint8_t* q, float* scales,
+                             unsigned int* amax_scratch, int sms, cudaStream_t st);
+cudaError_t launch_quant_int4(const void* w, int dt, int64_t n, int64_t k, uint8_t* packed, uint16_t* scales, int sms,
+                              cudaStream_t st);
+cudaError_t launch_quant_act(const void* x, int dt, int64_t m, int64_t k, int64_t stride, int terms, uint8_t* hi,
+                             uint8_t* lo, float* row_scale, int sms, cudaStream_t st);
+
+cudaError_t launch_rmsnorm(const void* x, int xdt, const float* w, const float* sc, const float* sh, int64_t rows,
+                           int64_t d, float eps, float offset, void* out, int odt, int sms, cudaStream_t st);
+cudaError_t launch_rope(const void* x, int xdt, const float* cs, const float* sn, int64_t tokens, int64_t heads,
+                        int64_t pairs, int pairing, void* out, int odt, int sms, cudaStream_t st);
+cudaError_t launch_qknorm_rope(const void* x, int xdt, const float* w, float eps, float offset, const float* cs,
+                               const float* sn, int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out,
+                               int odt, int sms, cudaStream_t st);
+
+}  // namespace we

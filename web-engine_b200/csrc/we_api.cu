@@ -1,0 +1,672 @@
+// The C ABI of the web-engine B200 hot path (include/we_b200.h): context, the Graph-style buffer
+// pool, argument validation with the reference's error messages, and dispatch to the kernels.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+struct we_ctx {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  // Graph analog (src/gpu/graph.ts:26-155): buffers in creation order, a free pool keyed by size
+  std::vector<void*> owned;
+  std::unordered_map<size_t, std::vector<void*>> pool;
+  std::unordered_map<void*, size_t> sizes;  // every buffer this context allocated
+  we_stats stats{0, 0, 0, 0, 0, 0};
+  uint32_t* dev_err = nullptr;  // device error word written by bounded waits
+  unsigned int* amax_word = nullptr;
+};
+
+namespace {
+
+int fail(we_ctx* c, int code, const std::string& msg) {
+  if (c) c->err = msg;
+  return code;
+}
+int cuda_fail(we_ctx* c, cudaError_t e, const char* what) {
+  return fail(c, e == cudaErrorMemoryAllocation ? WE_ENOMEM : WE_ECUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define CK(call, what)                      \
+  do {                                      \
+    cudaError_t e_ = (call);                \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, what); \
+  } while (0)
+// a kernel launch of this library: checked and counted in we_stats.launches
+#define LK(call, what)        \
+  do {                        \
+    CK(call, what);           \
+    ctx->stats.launches++;    \
+  } while (0)
+
+size_t round4(size_t b) { return std::max<size_t>(4, (b + 3) / 4 * 4); }
+
+// Takes a pooled buffer of exactly `size` bytes or allocates one (graph.ts:41-45).
+int pool_take(we_ctx* ctx, size_t size, void** out, bool* reused) {
+  auto it = ctx->pool.find(size);
+  if (it != ctx->pool.end() && !it->second.empty()) {
+    *out = it->second.back();
+    it->second.pop_back();
+    *reused = true;
+    return WE_OK;
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, size);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(ctx, WE_ENOMEM, "cudaMalloc of " + std::to_string(size) + " bytes failed: " + cudaGetErrorString(e));
+  }
+  ctx->sizes[p] = size;
+  *out = p;
+  *reused = false;
+  return WE_OK;
+}
+void pool_put(we_ctx* ctx, void* p) { ctx->pool[ctx->sizes[p]].push_back(p); }
+
+// A temporary of the library (activation split, decoded int4 weights): from the pool, not owned by
+// the caller, returned to the pool right after the work using it is queued (stream order keeps it safe).
+struct Scratch {
+  we_ctx* ctx;
+  std::vector<void*> bufs;
+  explicit Scratch(we_ctx* c) : ctx(c) {}
+  int take(size_t bytes, void** out) {
+    bool reused;
+    size_t size = (bytes + 255) / 256 * 256;
+    int rc = pool_take(ctx, size, out, &reused);
+    if (rc == WE_OK) bufs.push_back(*out);
+    return rc;
+  }
+  ~Scratch() {
+    for (void* p : bufs) pool_put(ctx, p);
+  }
+};
+
+// New output buffer of an op (ops.ts: graph.buffer(bytes)); contents are fully overwritten by the op.
+int op_output(we_ctx* ctx, size_t bytes, void** out) {
+  bool reused;
+  size_t size = round4(bytes);
+  int rc = pool_take(ctx, size, out, &reused);
+  if (rc != WE_OK) return rc;
+  if (reused) ctx->stats.reused++;
+  else {
+    ctx->stats.created++;
+    ctx->stats.created_bytes += size;
+  }
+  ctx->owned.push_back(*out);
+  return WE_OK;
+}
+
+size_t dsize(int dt) { return dt == WE_F32 ? 4 : (dt == WE_BF16 || dt == WE_F16) ? 2 : 1; }
+bool act_dtype_ok(int dt) { return dt == WE_F32 || dt == WE_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+// ---------------- context ----------------
+int we_init(int device, uint32_t flags, we_ctx** out) {
+  (void)flags;
+  if (!out) return WE_EINVAL;
+  *out = nullptr;
+  we_ctx* ctx = new we_ctx();
+  ctx->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return WE_ECUDA;
+  }
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (major != 10) {
+    delete ctx;
+    return WE_EUNSUPPORTED;  // sm_100a kernels only
+  }
+  ctx->sms = sms > 0 ? sms : 148;
+  if (cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ctx->dev_err, 16) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 16) != cudaSuccess) {
+    delete ctx;
+    return WE_ECUDA;
+  }
+  ctx->amax_word = reinterpret_cast<unsigned int*>(ctx->dev_err + 2);
+  ctx->stream = ctx->own;
+  *out = ctx;
+  return WE_OK;
+}
+
+int we_destroy(we_ctx* ctx) {
+  if (!ctx) return WE_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto& kv : ctx->sizes) cudaFree(kv.first);
+  cudaFree(ctx->dev_err);
+  cudaStreamDestroy(ctx->own);
+  delete ctx;
+  return WE_OK;
+}
+
+const char* we_last_error(const we_ctx* ctx) { return ctx ? ctx->err.c_str() : "no context"; }
+
+int we_set_stream(we_ctx* ctx, void* stream) {
+  if (!ctx) return WE_EINVAL;
+  CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own;
+  return WE_OK;
+}
+void* we_get_stream(const we_ctx* ctx) { return ctx ? ctx->stream : nullptr; }
+
+int we_sync(we_ctx* ctx) {
+  if (!ctx) return WE_EINVAL;
+  CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return WE_OK;
+}
+
+int we_device_error(we_ctx* ctx, uint32_t* code) {
+  if (!ctx || !code) return WE_EINVAL;
+  CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  CK(cudaMemcpy(code, ctx->dev_err, 4, cudaMemcpyDeviceToHost), "read device error word");
+  CK(cudaMemset(ctx->dev_err, 0, 4), "clear device error word");
+  return WE_OK;
+}
+
+int we_num_sms(const we_ctx* ctx) { return ctx ? ctx->sms : 0; }
+
+// ---------------- memory (Graph) ----------------
+int we_buffer(we_ctx* ctx, size_t bytes, const void* host, void** out) {
+  if (!ctx || !out) return WE_EINVAL;
+  int rc = op_output(ctx, bytes, out);
+  if (rc != WE_OK) return rc;
+  size_t size = ctx->sizes[*out];
+  if (host) {
+    CK(cudaMemcpyAsync(*out, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "upload");
+    if (size > bytes) CK(cudaMemsetAsync(static_cast<char*>(*out) + bytes, 0, size - bytes, ctx->stream), "pad");
+  } else {
+    CK(cudaMemsetAsync(*out, 0, size, ctx->stream), "zero buffer");
+  }
+  return WE_OK;
+}
+
+int we_write(we_ctx* ctx, void* dst, const void* host, size_t bytes) {
+  if (!ctx) return WE_EINVAL;
+  CK(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "we_write");
+  return WE_OK;
+}
+
+int we_read(we_ctx* ctx, const void* src, void* host, size_t bytes) {
+  if (!ctx) return WE_EINVAL;
+  CK(cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "we_read");
+  CK(cudaStreamSynchronize(ctx->stream), "we_read sync");
+  return WE_OK;
+}
+
+int we_copy(we_ctx* ctx, const void* src, size_t so, void* dst, size_t dof, size_t bytes) {
+  if (!ctx) return WE_EINVAL;
+  CK(cudaMemcpyAsync(static_cast<char*>(dst) + dof, static_cast<const char*>(src) + so, bytes,
+                     cudaMemcpyDeviceToDevice, ctx->stream),
+     "we_copy");
+  return WE_OK;
+}
+
+size_t we_mark(we_ctx* ctx) { return ctx ? ctx->owned.size() : 0; }
+
+int we_release(we_ctx* ctx, size_t mark, void* const* keep, size_t nkeep) {
+  if (!ctx) return WE_EINVAL;
+  if (mark > ctx->owned.size()) return fail(ctx, WE_EINVAL, "mark is beyond the buffers of this graph");
+  std::vector<void*> later(ctx->owned.begin() + mark, ctx->owned.end());
+  ctx->owned.resize(mark);
+  for (void* b : later) {
+    bool kept = false;
+    for (size_t i = 0; i < nkeep; i++) kept |= keep[i] == b;
+    if (kept) ctx->owned.push_back(b);
+    else pool_put(ctx, b);
+  }
+  return WE_OK;
+}
+
+int we_free(we_ctx* ctx, void* buf) {
+  if (!ctx) return WE_EINVAL;
+  auto it = std::find(ctx->owned.begin(), ctx->owned.end(), buf);
+  if (it == ctx->owned.end()) return fail(ctx, WE_EINVAL, "buffer is not owned by this graph");
+  ctx->owned.erase(it);
+  pool_put(ctx, buf);
+  return WE_OK;
+}
+
+int we_get_stats(const we_ctx* ctx, we_stats* out) {
+  if (!ctx || !out) return WE_EINVAL;
+  *out = ctx->stats;
+  return WE_OK;
+}
+
+// ---------------- matmul ----------------
+int64_t we_ksplit_for(int64_t m, int64_t n, int64_t k) {
+  const int64_t TILE = 128, BUSY = 256, MIN_SLICE = 256;
+  int64_t tiles = ((m + TILE - 1) / TILE) * ((n + TILE - 1) / TILE);
+  int64_t v = std::min((BUSY + tiles - 1) / tiles, k / MIN_SLICE);
+  return std::max<int64_t>(1, v);
+}
+
+int we_matmul_check(we_ctx* ctx, const we_matmul_desc* d) {
+  if (!d) return fail(ctx, WE_EINVAL, "no matmul description");
+  const int64_t xs = d->x_stride ? d->x_stride : d->k, ws = d->w_stride ? d->w_stride : d->k;
+  // matmulParams (src/kernels/matmul.ts:205-207)
+  const std::pair<const char*, int64_t> four[] = {{"K", d->k}, {"xStride", xs}, {"wStride", ws},
+                                                  {"xOffset", d->x_offset}, {"wOffset", d->w_offset}};
+  for (auto& kv : four)
+    if (kv.second % 4)
+      return fail(ctx, WE_EINVAL, std::string(kv.first) + " must be a multiple of 4, got " + std::to_string(kv.second));
+  if (d->m < 0 || d->n < 0 || d->k < 0) return fail(ctx, WE_EINVAL, "m, n and k must not be negative");
+  if (!act_dtype_ok(d->x_dtype)) return fail(ctx, WE_EINVAL, "x must be f32 or bf16");
+  if (!act_dtype_ok(d->y_dtype)) return fail(ctx, WE_EINVAL, "y must be f32 or bf16");
+  if (d->w_dtype < WE_F32 || d->w_dtype > WE_INT4G64) return fail(ctx, WE_EINVAL, "unknown weight format");
+  if (d->w_dtype == WE_INT4G64) {
+    if (d->k % 64) return fail(ctx, WE_EINVAL, "K must be a multiple of 64 for int4 group-64 weights, got " + std::to_string(d->k));
+    if (ws != d->k || d->w_offset) return fail(ctx, WE_EINVAL, "int4 group-64 weights must be contiguous [n, k]");
+    if (!d->group_scale) return fail(ctx, WE_EINVAL, "int4 group-64 weights need group scales");
+  }
+  if (d->k_split > 1 && d->bias) return fail(ctx, WE_EINVAL, "bias is not supported with kSplit");
+  return WE_OK;
+}
+
+static int matmul_impl(we_ctx* ctx, const we_matmul_desc* d, const void* x, const void* w, void* y) {
+  int rc = we_matmul_check(ctx, d);
+  if (rc != WE_OK) return rc;
+  if (d->m == 0 || d->n == 0) return WE_OK;
+  we::MatmulArgs a;
+  a.m = d->m;
+  a.n = d->n;
+  a.k = d->k;
+  a.x_stride = d->x_stride ? d->x_stride : d->k;
+  a.w_stride = d->w_stride ? d->w_stride : d->k;
+  a.y_stride = d->y_stride ? d->y_stride : d->n;
+  a.x_offset = d->x_offset;
+  a.w_offset = d->w_offset;
+  a.y_offset = d->y_offset;
+  a.k_split = d->k_split > 1 ? d->k_split : 1;
+  a.scale = d->scale;
+  a.chan_scale = d->chan_scale;
+  a.group_scale = d->group_scale;
+  a.bias = d->bias;
+  a.x_dtype = d->x_dtype;
+  a.w_dtype = d->w_dtype;
+  a.y_dtype = d->y_dtype;
+  a.accumulate = (d->flags & WE_MM_ACCUMULATE) ? 1 : 0;
+  cudaStream_t st = ctx->stream;
+
+  const bool tc_candidate = !(d->flags & WE_MM_FORCE_SIMT) && a.x_dtype == WE_BF16 && a.k_split == 1 && a.k > 0 &&
+                            a.w_dtype != WE_F32;
+  if (tc_candidate) {
+    Scratch scratch(ctx);
+    we::TcGemmArgs t{};
+    t.m = a.m;
+    t.n = a.n;
+    t.k = a.k;
+    t.scale = a.scale;
+    t.chan_scale = a.chan_scale;
+    t.bias = a.bias;
+    t.y = static_cast<char*>(y) + a.y_offset * dsize(a.y_dtype);
+    t.y_stride = a.y_stride;
+    t.y_dtype = a.y_dtype;
+    t.accumulate = a.accumulate;
+    t.dev_err = ctx->dev_err;
+    bool ready = false;
+    if (a.w_dtype == WE_FP8) {
+      t.kind_f16 = 0;
+      t.terms = (d->flags & WE_MM_FP8_FAST) ? 1 : 2;
+      t.w = static_cast<const uint8_t*>(w) + a.w_offset;
+      t.w_stride_bytes = a.w_stride;
+      t.x_stride_bytes = a.k;  // the split writes contiguous [m, k] rows (TMA needs k % 16 == 0)
+      t.x[0] = t.x[1] = reinterpret_cast<void*>(256);  // layout probe before doing the split
+      if (we::gemm_tc_supported(t)) {
+        void *hi, *lo = nullptr, *rs;
+        if ((rc = scratch.take((size_t)(a.m * a.k), &hi)) != WE_OK) return rc;
+        if (t.terms > 1 && (rc = scratch.take((size_t)(a.m * a.k), &lo)) != WE_OK) return rc;
+        if ((rc = scratch.take((size_t)a.m * 4, &rs)) != WE_OK) return rc;
+        const char* xp = static_cast<const char*>(x) + a.x_offset * 2;
+        LK(we::launch_quant_act(xp, WE_BF16, a.m, a.k, a.x_stride, t.terms, (uint8_t*)hi, (uint8_t*)lo, (float*)rs,
+                                ctx->sms, st),
+           "activation split");
+        t.x[0] = hi;
+        t.x[1] = lo ? lo : hi;
+        t.row_scale = (const float*)rs;
+        ready = true;
+      }
+    } else if (a.w_dtype == WE_BF16) {
+      t.kind_f16 = 1;
+      t.terms = 1;
+      t.w = static_cast<const uint16_t*>(w) + a.w_offset;
+      t.w_stride_bytes = a.w_stride * 2;
+      t.x[0] = t.x[1] = static_cast<const uint16_t*>(x) + a.x_offset;
+      t.x_stride_bytes = a.x_stride * 2;
+      ready = we::gemm_tc_supported(t);
+    } else if (a.w_dtype == WE_INT4G64) {
+      t.kind_f16 = 1;
+      t.terms = 1;
+      t.w_stride_bytes = a.k * 2;
+      t.x[0] = t.x[1] = static_cast<const uint16_t*>(x) + a.x_offset;
+      t.x_stride_bytes = a.x_stride * 2;
+      t.w = reinterpret_cast<void*>(256);
+      if (we::gemm_tc_supported(t)) {
+        void* wb;
+        if ((rc = scratch.take((size_t)(a.n * a.k * 2), &wb)) != WE_OK) return rc;
+        LK(we::launch_unpack_int4(static_cast<const uint8_t*>(w), a.group_scale, a.n, a.k, (uint16_t*)wb, ctx->sms, st),
+           "int4 decode");
+        t.w = wb;
+        ready = true;
+      }
+    }
+    if (ready) {
+      cudaError_t e = we::launch_gemm_tc(t, ctx->sms, st);
+      if (e == cudaSuccess) {
+        ctx->stats.launches++;
+        ctx->stats.tc_gemms++;
+        return WE_OK;
+      }
+      if (e != cudaErrorNotSupported) return cuda_fail(ctx, e, "tcgen05 gemm");
+    }
+  }
+  LK(we::launch_gemm_simt(x, w, y, a, st), "simt gemm");
+  ctx->stats.simt_gemms++;
+  return WE_OK;
+}
+
+int we_matmul(we_ctx* ctx, const we_matmul_desc* d, const void* x, const void* w, void* y) {
+  if (!ctx) return WE_EINVAL;
+  return matmul_impl(ctx, d, x, w, y);
+}
+
+int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
+  if (!ctx) return WE_EINVAL;
+  if (!d || !d->x_hi || !d->w || !d->y) return fail(ctx, WE_EINVAL, "we_gemm_fp8: missing operand");
+  if (!act_dtype_ok(d->y_dtype)) return fail(ctx, WE_EINVAL, "y must be f32 or bf16");
+  if (d->m == 0 || d->n == 0) return WE_OK;
+  we::TcGemmArgs t{};
+  t.m = d->m;
+  t.n = d->n;
+  t.k = d->k;
+  t.kind_f16 = 0;
+  t.terms = d->x_lo ? 2 : 1;
+  t.x[0] = d->x_hi;
+  t.x[1] = d->x_lo ? d->x_lo : d->x_hi;
+  t.x_stride_bytes = d->k;
+  t.w = d->w;
+  t.w_stride_bytes = d->k;
+  t.row_scale = d->row_scale;
+  t.scale = d->scale;
+  t.chan_scale = d->chan_scale;
+  t.bias = d->bias;
+  t.y = d->y;
+  t.y_stride = d->y_stride ? d->y_stride : d->n;
+  t.y_dtype = d->y_dtype;
+  t.accumulate = (d->flags & WE_MM_ACCUMULATE) ? 1 : 0;
+  t.dev_err = ctx->dev_err;
+  if (!we::gemm_tc_supported(t))
+    return fail(ctx, WE_EINVAL, "we_gemm_fp8 needs K a multiple of 16 and 16-byte aligned operands");
+  CK(we::launch_gemm_tc(t, ctx->sms, ctx->stream), "tcgen05 gemm");
+  ctx->stats.launches++;
+  ctx->stats.tc_gemms++;
+  return WE_OK;
+}
+
+// ---------------- ops ----------------
+static int sum_partials(we_ctx* ctx, const float* partials, int64_t split, int64_t count, float* out);
+
+int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m, int32_t y_dtype,
+                      uint32_t flags, void** y) {
+  if (!ctx || !w || !y) return WE_EINVAL;
+  if (w->lora_down || w->lora_up) {
+    const we_linear *down = w->lora_down, *up = w->lora_up;
+    if (!down || !up || down->k != w->k || up->n != w->n || up->k != down->n || down->n % 4)
+      return fail(ctx, WE_EINVAL, "LoRA shapes do not fit the linear layer");
+  }
+  int rc = op_output(ctx, (size_t)(m * w->n) * dsize(y_dtype), y);
+  if (rc != WE_OK) return rc;
+  we_matmul_desc d{};
+  d.m = m;
+  d.n = w->n;
+  d.k = w->k;
+  d.scale = w->scale;
+  d.chan_scale = w->chan_scale;
+  d.group_scale = w->group_scale;
+  d.bias = w->bias;
+  d.x_dtype = x_dtype;
+  d.w_dtype = w->dtype;
+  d.y_dtype = y_dtype;
+  d.flags = flags & (WE_MM_FP8_FAST | WE_MM_FORCE_SIMT);
+  if ((rc = matmul_impl(ctx, &d, x, w->weight, *y)) != WE_OK) return rc;
+  if (!w->lora_down) return WE_OK;
+  // narrowLinear (ops.ts:48-58): t = x . down^T, split over K when narrow, then y += up.scale t . up^T
+  const we_linear *down = w->lora_down, *up = w->lora_up;
+  Scratch scratch(ctx);
+  void* t;
+  if ((rc = scratch.take((size_t)(m * down->n) * 4, &t)) != WE_OK) return rc;
+  const int64_t split = we_ksplit_for(m, down->n, down->k);
+  we_matmul_desc dd{};
+  dd.m = m;
+  dd.n = down->n;
+  dd.k = down->k;
+  dd.scale = down->scale;
+  dd.chan_scale = down->chan_scale;
+  dd.group_scale = down->group_scale;
+  dd.x_dtype = x_dtype;
+  dd.w_dtype = down->dtype;
+  dd.y_dtype = WE_F32;
+  if (split == 1) {
+    if ((rc = matmul_impl(ctx, &dd, x, down->weight, t)) != WE_OK) return rc;
+  } else {
+    void* parts;
+    if ((rc = scratch.take((size_t)(split * m * down->n) * 4, &parts)) != WE_OK) return rc;
+    dd.k_split = split;
+    if ((rc = matmul_impl(ctx, &dd, x, down->weight, parts)) != WE_OK) return rc;
+    if ((rc = sum_partials(ctx, (const float*)parts, split, m * down->n, (float*)t)) != WE_OK) return rc;
+  }
+  we_matmul_desc du{};
+  du.m = m;
+  du.n = up->n;
+  du.k = up->k;
+  du.scale = up->scale;
+  du.chan_scale = up->chan_scale;
+  du.group_scale = up->group_scale;
+  du.x_dtype = WE_F32;
+  du.w_dtype = up->dtype;
+  du.y_dtype = y_dtype;
+  du.flags = WE_MM_ACCUMULATE;
+  return matmul_impl(ctx, &du, t, up->weight, *y);
+}
+
+int we_no_mod(we_ctx* ctx, int64_t d, we_mod* out) {
+  if (!ctx || !out) return WE_EINVAL;
+  void *s, *h;
+  int rc = we_buffer(ctx, (size_t)d * 4, nullptr, &s);
+  if (rc != WE_OK) return rc;
+  if ((rc = we_buffer(ctx, (size_t)d * 4, nullptr, &h)) != WE_OK) return rc;
+  out->scale = (const float*)s;
+  out->shift = (const float*)h;
+  return WE_OK;
+}
+
+int we_rmsnorm(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, const float* scale, const float* shift,
+               int64_t rows, int64_t d, float eps, float offset, void* out, int32_t out_dtype) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(out_dtype)) return fail(ctx, WE_EINVAL, "x and out must be f32 or bf16");
+  if (d <= 0 || rows < 0) return fail(ctx, WE_EINVAL, "rows and d must be positive");
+  if (rows == 0) return WE_OK;
+  LK(we::launch_rmsnorm(x, x_dtype, weight, scale, shift, rows, d, eps, offset, out, out_dtype, ctx->sms, ctx->stream),
+     "rmsnorm");
+  return WE_OK;
+}
+
+int we_norm(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, int64_t rows, int64_t d, const we_mod* mod,
+            float eps, float offset, int32_t out_dtype, void** out) {
+  if (!ctx || !out) return WE_EINVAL;
+  int rc = op_output(ctx, (size_t)(rows * d) * dsize(out_dtype), out);
+  if (rc != WE_OK) return rc;
+  return we_rmsnorm(ctx, x, x_dtype, weight, mod ? mod->scale : nullptr, mod ? mod->shift : nullptr, rows, d, eps,
+                    offset, *out, out_dtype);
+}
+
+int we_rope_apply(we_ctx* ctx, const void* x, int32_t x_dtype, const float* cos, const float* sin, int64_t tokens,
+                  int64_t heads, int64_t pairs, int32_t pairing, void* out, int32_t out_dtype) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(out_dtype)) return fail(ctx, WE_EINVAL, "x and out must be f32 or bf16");
+  if (pairing != WE_ROPE_INTERLEAVED && pairing != WE_ROPE_HALF) return fail(ctx, WE_EINVAL, "unknown pairing");
+  if (tokens < 0 || heads < 0 || pairs < 0) return fail(ctx, WE_EINVAL, "negative size");
+  if (tokens == 0 || heads == 0 || pairs == 0) return WE_OK;
+  LK(we::launch_rope(x, x_dtype, cos, sin, tokens, heads, pairs, pairing, out, out_dtype, ctx->sms, ctx->stream), "rope");
+  return WE_OK;
+}
+
+int we_rotate(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t heads, const we_rope* rope, int32_t pairing,
+              int32_t out_dtype, void** out) {
+  if (!ctx || !rope || !out) return WE_EINVAL;
+  int rc = op_output(ctx, (size_t)(rope->tokens * heads * rope->pairs * 2) * dsize(out_dtype), out);
+  if (rc != WE_OK) return rc;
+  return we_rope_apply(ctx, x, x_dtype, rope->cos, rope->sin, rope->tokens, heads, rope->pairs, pairing, *out,
+                       out_dtype);
+}
+
+int we_qknorm_rope(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, float eps, float offset,
+                   const float* cos, const float* sin, int64_t tokens, int64_t heads, int64_t pairs, int32_t pairing,
+                   void* out, int32_t out_dtype) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(x_dtype) || !act_dtype_ok(out_dtype)) return fail(ctx, WE_EINVAL, "x and out must be f32 or bf16");
+  if (pairing != WE_ROPE_INTERLEAVED && pairing != WE_ROPE_HALF) return fail(ctx, WE_EINVAL, "unknown pairing");
+  if (tokens == 0 || heads == 0 || pairs == 0) return WE_OK;
+  cudaError_t e = we::launch_qknorm_rope(x, x_dtype, weight, eps, offset, cos, sin, tokens, heads, pairs, pairing, out,
+                                         out_dtype, ctx->sms, ctx->stream);
+  if (e == cudaErrorNotSupported) {
+    // no fused variant for this head size: norm into `out` (f32 keeps the intermediate exact), rotate in place
+    Scratch scratch(ctx);
+    void* tmp;
+    int rc = scratch.take((size_t)(tokens * heads * pairs * 2) * 4, &tmp);
+    if (rc != WE_OK) return rc;
+    LK(we::launch_rmsnorm(x, x_dtype, weight, nullptr, nullptr, tokens * heads, pairs * 2, eps, offset, tmp, WE_F32,
+                          ctx->sms, ctx->stream),
+       "qk norm");
+    LK(we::launch_rope(tmp, WE_F32, cos, sin, tokens, heads, pairs, pairing, out, out_dtype, ctx->sms, ctx->stream),
+       "qk rope");
+    return WE_OK;
+  }
+  CK(e, "qknorm_rope");
+  ctx->stats.launches++;
+  return WE_OK;
+}
+
+int64_t we_rope_tables(const int64_t* pos, int64_t tokens, int32_t naxes, const int64_t* axes, double theta, float* cos,
+                       float* sin) {
+  int64_t pairs = 0;
+  for (int a = 0; a < naxes; a++) {
+    if (axes[a] % 2) return -1;
+    pairs += axes[a] / 2;
+  }
+  if (!cos || !sin) return pairs;
+  for (int64_t t = 0; t < tokens; t++) {
+    int64_t pair = 0;
+    for (int a = 0; a < naxes; a++) {
+      const int64_t dim = axes[a];
+      for (int64_t j = 0; j < dim / 2; j++, pair++) {
+        const double angle = (double)pos[t * naxes + a] * pow(theta, -(double)(2 * j) / (double)dim);
+        cos[t * pairs + pair] = (float)::cos(angle);
+        sin[t * pairs + pair] = (float)::sin(angle);
+      }
+    }
+  }
+  return pairs;
+}
+
+int we_positions(int64_t text, int64_t rows, int64_t cols, int64_t* pos) {
+  if (!pos || text < 0 || rows < 0 || cols < 0) return WE_EINVAL;
+  int64_t t = 0;
+  for (int64_t i = 0; i < text; i++, t++) pos[3 * t] = pos[3 * t + 1] = pos[3 * t + 2] = 0;
+  for (int64_t i = 0; i < rows * cols; i++, t++) {
+    pos[3 * t] = 0;
+    pos[3 * t + 1] = i / cols;
+    pos[3 * t + 2] = i % cols;
+  }
+  return WE_OK;
+}
+
+// ---------------- unpack / quantise ----------------
+int we_unpack_fp8(we_ctx* ctx, const uint8_t* bytes, int64_t n, float scale, float* out) {
+  if (!ctx) return WE_EINVAL;
+  if (n <= 0) return WE_OK;
+  LK(we::launch_unpack_fp8_f32(bytes, n, scale, out, ctx->sms, ctx->stream), "unpack fp8");
+  return WE_OK;
+}
+
+int we_unpack_fp8_bf16(we_ctx* ctx, const uint8_t* bytes, int64_t n, uint16_t* out) {
+  if (!ctx) return WE_EINVAL;
+  if (n <= 0) return WE_OK;
+  LK(we::launch_unpack_fp8_bf16(bytes, n, out, ctx->sms, ctx->stream), "unpack fp8 -> bf16");
+  return WE_OK;
+}
+
+int we_unpack_int4(we_ctx* ctx, const uint8_t* packed, const uint16_t* scales, int64_t n, int64_t k, uint16_t* out) {
+  if (!ctx) return WE_EINVAL;
+  if (k % 64) return fail(ctx, WE_EINVAL, "K must be a multiple of 64 for int4 group-64 weights, got " + std::to_string(k));
+  if (((uintptr_t)packed & 3) || ((uintptr_t)out & 15))
+    return fail(ctx, WE_EINVAL, "int4 decode needs 4-byte aligned input and 16-byte aligned output");
+  if (n <= 0) return WE_OK;
+  LK(we::launch_unpack_int4(packed, scales, n, k, out, ctx->sms, ctx->stream), "unpack int4");
+  return WE_OK;
+}
+
+int we_quantize_fp8(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int64_t k, int32_t per_channel, uint8_t* q,
+                    float* scales) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(w_dtype)) return fail(ctx, WE_EINVAL, "weights to quantise must be f32 or bf16");
+  if (n <= 0 || k <= 0) return WE_OK;
+  CK(we::launch_quant_fp8(w, w_dtype, n, k, per_channel != 0, q, scales, ctx->amax_word, ctx->sms, ctx->stream),
+     "quantise fp8");
+  ctx->stats.launches += per_channel ? 1 : 2;
+  return WE_OK;
+}
+
+int we_quantize_int4(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int64_t k, uint8_t* packed,
+                     uint16_t* scales) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(w_dtype)) return fail(ctx, WE_EINVAL, "weights to quantise must be f32 or bf16");
+  if (k % 64) return fail(ctx, WE_EINVAL, "K must be a multiple of 64 for int4 group-64 weights, got " + std::to_string(k));
+  if (n <= 0 || k <= 0) return WE_OK;
+  LK(we::launch_quant_int4(w, w_dtype, n, k, packed, scales, ctx->sms, ctx->stream), "quantise int4");
+  return WE_OK;
+}
+
+int we_quantize_act(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t m, int64_t k, int64_t x_stride, int32_t terms,
+                    uint8_t* hi, uint8_t* lo, float* row_scale) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(x_dtype)) return fail(ctx, WE_EINVAL, "x must be f32 or bf16");
+  if (terms != 1 && terms != 2) return fail(ctx, WE_EINVAL, "terms must be 1 or 2");
+  if (terms == 2 && !lo) return fail(ctx, WE_EINVAL, "two terms need a lo buffer");
+  if (m <= 0 || k <= 0) return WE_OK;
+  LK(we::launch_quant_act(x, x_dtype, m, k, x_stride ? x_stride : k, terms, hi, lo, row_scale, ctx->sms, ctx->stream),
+     "activation split");
+  return WE_OK;
+}
+
+}  // extern "C"
+
+// layerSum with unit weights (src/kernels/text.ts:67-84 as used by narrowLinear, ops.ts:55-57)
+__global__ void sum_partials_kernel(const float* __restrict__ p, int64_t split, int64_t count, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int64_t z = 0; z < split; z++) s += p[z * count + i];
+    out[i] = s;
+  }
+}
+static int sum_partials(we_ctx* ctx, const float* partials, int64_t split, int64_t count, float* out) {
+  int64_t g = std::min<int64_t>((count + 255) / 256, (int64_t)ctx->sms * 8);
+  sum_partials_kernel<<<(unsigned)std::max<int64_t>(g, 1), 256, 0, ctx->stream>>>(partials, split, count, out);
+  LK(cudaGetLastError(), "sum partials");
+  return WE_OK;
+}
