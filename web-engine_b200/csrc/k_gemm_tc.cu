@@ -19,6 +19,7 @@
 // device error word, the other roles stop at their next wait, in-flight TMA loads and MMAs are
 // drained with bounded waits, TMEM is freed and the kernel returns.
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -31,7 +32,9 @@ constexpr int KB_BYTES = 128;     // K bytes per stage
 constexpr int THREADS = 192;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;
-constexpr int SMEM_BUDGET = 200 * 1024;
+constexpr int EPI_LD = 36;  // floats per row of an epilogue warp's 32 x 32 staging tile (pad: no bank conflicts)
+constexpr int EPI_BYTES = 4 * 32 * EPI_LD * 4;
+constexpr int SMEM_BUDGET = 207 * 1024;  // for the stage ring; + epilogue staging + barriers <= 227 KB
 
 struct Params {
   int64_t m, n;
@@ -44,6 +47,7 @@ struct Params {
   int64_t y_stride;
   int y_dtype;
   int accumulate;
+  int vec_ok;  // y rows allow 16-byte stores (aligned base, stride a multiple of 16 bytes)
   uint32_t* err;
 };
 
@@ -53,7 +57,8 @@ struct Layout {
   static constexpr int X_BYTES = BT * KB_BYTES;
   static constexpr int STAGE_BYTES = W_BYTES + TERMS * X_BYTES;
   static constexpr int STAGES = (SMEM_BUDGET / STAGE_BYTES) > 8 ? 8 : (SMEM_BUDGET / STAGE_BYTES);
-  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], drain
   static constexpr int TOTAL = BAR_OFFSET + NUM_BARS * 8 + 16;
   static constexpr int ALLOC = TOTAL + 1024;      // slack to align the base to 1024 bytes
@@ -300,47 +305,89 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncwarp();
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    float* stage = reinterpret_cast<float*>(smem + L::EPI_OFFSET) + (warp - 2) * (32 * EPI_LD);
+    const int cg = (lane & 3) * 8;  // write-out: 8 channels of one token row per lane
     int ab = 0;
     uint32_t aph = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
       bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int64_t ch = (t % tiles_n) * BM + q * 32 + lane;
+      const int64_t ch_base = (t % tiles_n) * BM + q * 32;  // first output channel of this warp
+      const int64_t ch = ch_base + lane;
       const int64_t tok_base = (t / tiles_n) * BT;
       const bool ch_ok = ch < p.n;
       const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
       const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
 #pragma unroll 1
       for (int c = 0; c < BT / 32; c++) {
+        const int64_t tok0 = tok_base + c * 32;
+        if (tok0 >= p.m) break;  // warp-uniform: the rest of the tile is padding
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BT + c * 32), r);
-        const int64_t tok0 = tok_base + c * 32;
-        if (ch_ok) {
+        if (c == BT / 32 - 1 || tok0 + 32 >= p.m) {
+          // last TMEM read of this tile: hand the accumulator back to the MMA warp before the stores
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(TEMPTY(ab));
+        }
+        // the 32 row scales of this chunk: one coalesced load, then broadcast by shuffle
+        const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int64_t tok = tok0 + j;
-            if (tok < p.m) {
-              float v = __uint_as_float(r[j]);
-              if (p.row_scale) v *= p.row_scale[tok];
-              v = v * cs + bias;
-              const int64_t o = tok * p.y_stride + ch;
+        for (int j = 0; j < 32; j++)
+          stage[j * EPI_LD + lane] = __uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j) * cs + bias;
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 4; it++) {
+          const int tr = it * 8 + (lane >> 2);
+          const int64_t tok = tok0 + tr;
+          const float4 a = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg);
+          const float4 b = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg + 4);
+          float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+          const int64_t c0 = ch_base + cg;
+          if (tok >= p.m || c0 >= p.n) continue;
+          const int64_t o = tok * p.y_stride + c0;
+          if (p.vec_ok && c0 + 8 <= p.n) {
+            if (p.y_dtype == WE_BF16) {
+              uint4* y = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o);
+              if (p.accumulate) {
+                const uint4 old = *y;
+                const uint32_t w[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                  v[2 * e] += __uint_as_float(w[e] << 16);
+                  v[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+                }
+              }
+              *y = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                              pack_bf16x2(v[6], v[7]));
+            } else {
+              float4* y = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
+              if (p.accumulate) {
+                const float4 o0 = y[0], o1 = y[1];
+                v[0] += o0.x; v[1] += o0.y; v[2] += o0.z; v[3] += o0.w;
+                v[4] += o1.x; v[5] += o1.y; v[6] += o1.z; v[7] += o1.w;
+              }
+              y[0] = make_float4(v[0], v[1], v[2], v[3]);
+              y[1] = make_float4(v[4], v[5], v[6], v[7]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              if (c0 + e >= p.n) break;
               if (p.y_dtype == WE_BF16) {
                 uint16_t* y = static_cast<uint16_t*>(p.y);
-                if (p.accumulate) v += bf16_bits_to_f32(y[o]);
-                y[o] = f32_to_bf16_bits(v);
+                float val = v[e] + (p.accumulate ? bf16_bits_to_f32(y[o + e]) : 0.f);
+                y[o + e] = f32_to_bf16_bits(val);
               } else {
                 float* y = static_cast<float*>(p.y);
-                if (p.accumulate) v += y[o];
-                y[o] = v;
+                y[o + e] = v[e] + (p.accumulate ? y[o + e] : 0.f);
               }
             }
           }
         }
+        __syncwarp();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(TEMPTY(ab));
       if (++ab == 2) {
         ab = 0;
         aph ^= 1u;
@@ -412,6 +459,8 @@ static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
   p.y_stride = a.y_stride;
   p.y_dtype = a.y_dtype;
   p.accumulate = a.accumulate;
+  const int esz = a.y_dtype == WE_BF16 ? 2 : 4;
+  p.vec_ok = ((uintptr_t)a.y % 16 == 0) && ((a.y_stride * esz) % 16 == 0);
   p.err = a.dev_err;
   auto kern = gemm_tc_kernel<BT, TERMS, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
@@ -442,6 +491,10 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
   auto tiles = [&](int bt) { return tn * ((a.m + bt - 1) / bt); };
   int bt = tiles(256) >= sms ? 256 : (tiles(128) >= sms ? 128 : 64);
+  if (const char* env = getenv("WE_TC_BT")) {  // tuning override: 64, 128 or 256 tokens per tile
+    const int v = atoi(env);
+    if (v == 64 || v == 128 || v == 256) bt = v;
+  }
   if (a.kind_f16) {
     if (bt == 256) return tc::run<256, 1, true>(a, sms, st);
     if (bt == 128) return tc::run<128, 1, true>(a, sms, st);
