@@ -4,7 +4,8 @@ N=12288; bf16 activations, fp8 e4m3 weights with per-output-channel scales) on B
 
 One step = one linear layer forward through the public operator API (ops.linear -> activation
 split + tcgen05 GEMM) on one batch of synthetic inputs that are already resident in HBM. L2 is
-flushed (256 MB write) between timed steps, outside the timed events. Multi-GPU: one process per
+flushed between timed steps (256 MB write, then read back so no dirty lines remain), outside the
+timed events. Multi-GPU: one process per
 GPU (torchrun), each rank runs its own batch (data-parallel images, no data-path collective:
 weak scaling); time = max over ranks of the summed per-step CUDA-event time.
 
@@ -145,7 +146,7 @@ def run_reference(args, rank: int) -> None:
 def config_dict(args) -> dict:
     return {"workload": "config 2: dequant-GEMM M=4608 K=3072 N=12288, bf16 activations ~N(0,1), fp8 e4m3 weights "
                         "~N(0,0.02) with per-output-channel absmax scales, exact two-term e4m3 activation split",
-            "m": M, "k": K, "n": N, "parallelism": f"dp{args.gpus}", "l2": "flushed (256 MB write) between steps"}
+            "m": M, "k": K, "n": N, "parallelism": f"dp{args.gpus}", "l2": "flushed between steps (256 MB write, then read back), outside the timed events"}
 
 
 def main() -> None:
@@ -195,6 +196,13 @@ def main() -> None:
     we.kernels.quantize_int4(g, w32, N, K, w4, w4s, w_dtype="f32")
     del w32
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_sum = torch.empty((), dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        """Write 256 MB (> the 126 MB L2), then read it back so the evicted lines are clean: the timed
+        step starts from a cold L2 without the flush's dirty lines draining to HBM underneath it."""
+        flush.zero_()
+        torch.amax(flush.view(torch.float32), dim=0, out=flush_sum)
     lin = we.Linear(wq, "fp8", 1.0, N, K, chan_scale=ws)
     lin4 = we.Linear(w4, "int4", 1.0, N, K, group_scale=w4s)
     hi = torch.empty(M, K, dtype=torch.uint8, device=dev)
@@ -208,7 +216,7 @@ def main() -> None:
     def timed(step, steps, warmup, sampler=None):
         """Sum of per-step CUDA-event times (ms) with an L2 flush before each step, outside the events."""
         for _ in range(warmup):
-            flush.zero_()
+            flush_l2()
             step()
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         if world > 1:
@@ -216,7 +224,7 @@ def main() -> None:
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for a, b in ev:
-            flush.zero_()
+            flush_l2()
             a.record(stream)
             step()
             b.record(stream)
@@ -298,6 +306,54 @@ def main() -> None:
         i4_ms = timed(step_int4, args.steps, 2) / args.steps
         variants["int4_g64_linear"] = {"tflops": FLOPS / (i4_ms * 1e-3) / 1e12, "ms": i4_ms,
                                        "note": "int4 group-64 decode to bf16 + tcgen05 kind::f16"}
+
+    # ---- the bandwidth kernels around the GEMM at block size (config 3: 4608 tokens, hidden 3072, 24 heads) ----
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    wn = torch.randn(K, device=dev) * 0.1
+    sc_v, sh_v = torch.randn(K, device=dev) * 0.3, torch.randn(K, device=dev) * 0.3
+    qn = torch.randn(128, device=dev) * 0.1
+    cos_h, sin_h, pairs = we.kernels.rope_tables(we.kernels.positions(512, 64, 64), (16, 56, 56), 1e4)
+    cs_d, sn_d = torch.from_numpy(cos_h).to(dev), torch.from_numpy(sin_h).to(dev)
+    xn = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    act_bytes = M * K * 2
+    bw = {}
+    for name, fn, nbytes in [
+        ("rmsnorm_mod_bf16", lambda: we.kernels.rmsnorm(g, x, wn, M, K, xn, sc_v, sh_v, x_dtype="bf16", out_dtype="bf16"),
+         2 * act_bytes + 3 * K * 4),
+        ("qknorm_rope_bf16", lambda: we.kernels.qknorm_rope(g, x, qn, cs_d, sn_d, M, K // 128, pairs, xn,
+                                                            x_dtype="bf16", out_dtype="bf16"),
+         2 * act_bytes + 2 * M * pairs * 4 + 128 * 4),
+        ("rope_bf16", lambda: we.kernels.rope_apply(g, x, cs_d, sn_d, M, K // 128, pairs, xn, x_dtype="bf16",
+                                                    out_dtype="bf16"), 2 * act_bytes + 2 * M * pairs * 4),
+        ("act_split_2term", lambda: we.kernels.quantize_act(g, x, M, K, hi, lo, rs, terms=2),
+         act_bytes + 2 * M * K + M * 4),
+    ]:
+        t_ms = timed(fn, args.steps, 2) / args.steps
+        bw[name] = {"ms": t_ms, "gbs": nbytes / (t_ms * 1e-3) / 1e9, "frac_hbm": nbytes / (t_ms * 1e-3) / 1e9 / hbm,
+                    "bytes": nbytes}
+    roofline["bandwidth_kernels"] = bw
+
+    # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
+    if not args.no_variants:
+        try:
+            a8 = torch.randn(8192, 8192, device=dev).to(torch.float8_e4m3fn)
+            b8 = torch.randn(8192, 8192, device=dev).to(torch.float8_e4m3fn)
+            one = torch.ones((), device=dev)
+            best = 1e9
+            for _ in range(12):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                torch._scaled_mm(a8, b8.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            fp8_peak = 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+            variants["fp8_peak_cublas_tflops"] = fp8_peak
+            variants["fp8_one_term_gemm"]["frac_fp8_peak"] = variants["fp8_one_term_gemm"]["tflops"] / fp8_peak
+            roofline["frac_of_fp8_peak"] = gemm_tflops / fp8_peak
+            del a8, b8
+        except Exception as exc:  # noqa: BLE001
+            variants["fp8_peak_cublas_tflops"] = f"unmeasured: {exc}"
 
     # ---- end to end through the public API with host buffers ----
     xh = x.cpu().pin_memory()

@@ -77,6 +77,42 @@ __device__ __forceinline__ float int4_operand(uint32_t nib, float s) {
   return bf16_bits_to_f32(f32_to_bf16_bits(float(q) * s));
 }
 
+// 8 values of an activation row as floats: one 16-byte load for bf16, two for f32
+template <int DT>
+__device__ __forceinline__ void load8(const void* p, int64_t i, float v[8]) {
+  if constexpr (DT == WE_BF16) {
+    uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+  } else {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    float4 a = q[0], b = q[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+template <int DT>
+__device__ __forceinline__ void store8(void* p, int64_t i, const float v[8]) {
+  if constexpr (DT == WE_BF16) {
+    uint4 u = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = u;
+  } else {
+    float4* q = reinterpret_cast<float4*>(static_cast<float*>(p) + i);
+    q[0] = make_float4(v[0], v[1], v[2], v[3]);
+    q[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+__device__ __forceinline__ void load8f(const float* p, int64_t i, float v[8]) {
+  const float4* q = reinterpret_cast<const float4*>(p + i);
+  float4 a = q[0], b = q[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 // ---- warp reductions ----
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -9,42 +9,6 @@
 
 namespace we {
 
-// 8 values of an activation row as floats: one 16-byte load for bf16, two for f32
-template <int DT>
-__device__ __forceinline__ void load8(const void* p, int64_t i, float v[8]) {
-  if constexpr (DT == WE_BF16) {
-    uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
-    uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      v[2 * j] = __uint_as_float(w[j] << 16);
-      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
-    }
-  } else {
-    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
-    float4 a = q[0], b = q[1];
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-}
-template <int DT>
-__device__ __forceinline__ void store8(void* p, int64_t i, const float v[8]) {
-  if constexpr (DT == WE_BF16) {
-    uint4 u = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = u;
-  } else {
-    float4* q = reinterpret_cast<float4*>(static_cast<float*>(p) + i);
-    q[0] = make_float4(v[0], v[1], v[2], v[3]);
-    q[1] = make_float4(v[4], v[5], v[6], v[7]);
-  }
-}
-__device__ __forceinline__ void load8f(const float* p, int64_t i, float v[8]) {
-  const float4* q = reinterpret_cast<const float4*>(p + i);
-  float4 a = q[0], b = q[1];
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
@@ -101,6 +65,47 @@ __global__ void rmsnorm_kernel(const void* __restrict__ x, const float* __restri
         float s = sc ? sc[i] : 0.f, h = sh ? sh[i] : 0.f;
         store_out<OT>(out, base + i, v * inv * (offset + w[i]) * (1.f + s) + h);
       }
+    }
+  }
+}
+
+// Register-cached RMSNorm: one 128-thread CTA per row keeps its CH chunks of 8 values in registers,
+// so x is read from HBM once (d % 8 == 0, d <= 1024 CH, 16-byte aligned rows and vectors).
+template <int DT, int OT, int CH>
+__global__ void __launch_bounds__(128) rmsnorm_cached_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                             const float* __restrict__ sc, const float* __restrict__ sh,
+                                                             int64_t rows, int64_t d, float eps, float offset,
+                                                             void* __restrict__ out) {
+  __shared__ float red[4];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int64_t base = row * d;
+    float v[CH][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 128 + threadIdx.x) * 8;
+      if (i < d) {
+        load8<DT>(x, base + i, v[c]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) ss = fmaf(v[c][j], v[c][j], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / (float)d + eps);
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 128 + threadIdx.x) * 8;
+      if (i >= d) continue;
+      float ww[8], s[8], h[8];
+      load8f(w, i, ww);
+      if (sc) load8f(sc, i, s); else for (int j = 0; j < 8; j++) s[j] = 0.f;
+      if (sh) load8f(sh, i, h); else for (int j = 0; j < 8; j++) h[j] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[c][j] = v[c][j] * inv * (offset + ww[j]) * (1.f + s[j]) + h[j];
+      store8<OT>(out, base + i, v[c]);
     }
   }
 }
@@ -212,6 +217,13 @@ static int capped(int64_t want, int sms, int per_sm) {
 template <int DT, int OT>
 static void rmsnorm_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
                              float eps, float offset, void* out, bool vec, int sms, cudaStream_t st) {
+  if (vec && d >= 512) {
+    const int64_t chunks = (d / 8 + 127) / 128;
+    const int g = capped(rows, sms, 16);
+    if (chunks <= 4) { rmsnorm_cached_kernel<DT, OT, 4><<<g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out); return; }
+    if (chunks <= 6) { rmsnorm_cached_kernel<DT, OT, 6><<<g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out); return; }
+    if (chunks <= 8) { rmsnorm_cached_kernel<DT, OT, 8><<<g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out); return; }
+  }
   int threads = d >= 2048 ? 256 : 128;
   int g = capped(rows, sms, 2048 / threads * 2);
   if (vec) rmsnorm_kernel<DT, OT, true><<<g, threads, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);

@@ -196,6 +196,74 @@ __global__ void quant_act_kernel(const void* __restrict__ x, int64_t m, int64_t 
   }
 }
 
+// Register-cached variant: one 128-thread CTA per row, each thread keeps its CH chunks of 8 values
+// (16-byte loads) in registers, so x is read once. k % 8 == 0, k <= 1024 CH, 16-byte aligned rows.
+template <int DT, int TERMS, int CH>
+__global__ void __launch_bounds__(128) quant_act_cached_kernel(const void* __restrict__ x, int64_t m, int64_t k,
+                                                               int64_t stride, uint8_t* __restrict__ hi,
+                                                               uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
+  __shared__ float red[4];
+  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+    const int64_t base = row * stride;
+    float v[CH][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t t = (int64_t)(c * 128 + threadIdx.x) * 8;
+      if (t < k) {
+        load8<DT>(x, base + t, v[c]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[c][j]));
+      }
+    }
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    const int e = act_exponent(amax);
+    if (threadIdx.x == 0) row_scale[row] = ldexpf(1.0f, e);
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t t = (int64_t)(c * 128 + threadIdx.x) * 8;
+      if (t >= k) continue;
+      float s[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) s[j] = ldexpf(v[c][j], -e);
+      uint32_t h[2], l[2];
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const uint16_t h0 = f32x2_to_e4m3x2(s[4 * j], s[4 * j + 1]);
+        const uint16_t h1 = f32x2_to_e4m3x2(s[4 * j + 2], s[4 * j + 3]);
+        h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        if (TERMS > 1) {
+          const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+          const uint16_t l0 = f32x2_to_e4m3x2(s[4 * j] - d0.x, s[4 * j + 1] - d0.y);
+          const uint16_t l1 = f32x2_to_e4m3x2(s[4 * j + 2] - d1.x, s[4 * j + 3] - d1.y);
+          l[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        }
+      }
+      *reinterpret_cast<uint2*>(hi + row * k + t) = make_uint2(h[0], h[1]);
+      if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * k + t) = make_uint2(l[0], l[1]);
+    }
+  }
+}
+
+template <int DT, int TERMS>
+static bool quant_act_cached(const void* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo,
+                             float* rs, int sms, cudaStream_t st) {
+  const int g = (int)((m < (int64_t)sms * 16) ? m : (int64_t)sms * 16);
+  const int64_t chunks = (k / 8 + 127) / 128;
+  if (chunks <= 1) quant_act_cached_kernel<DT, TERMS, 1><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (chunks <= 2) quant_act_cached_kernel<DT, TERMS, 2><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (chunks <= 3) quant_act_cached_kernel<DT, TERMS, 3><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (chunks <= 4) quant_act_cached_kernel<DT, TERMS, 4><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (chunks <= 6) quant_act_cached_kernel<DT, TERMS, 6><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (chunks <= 8) quant_act_cached_kernel<DT, TERMS, 8><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else return false;
+  return true;
+}
+
 // ---------------- launchers ----------------
 static int grid_for(int64_t work, int threads, int sms, int per_sm = 8) {
   int64_t g = (work + threads - 1) / threads;
@@ -257,6 +325,15 @@ cudaError_t launch_quant_act(const void* x, int dt, int64_t m, int64_t k, int64_
   int g = (int)((m < (int64_t)sms * 16) ? m : (int64_t)sms * 16);
   if (g < 1) g = 1;
   int vec_ok = (k % 8 == 0) && ((uintptr_t)hi % 8 == 0) && (!lo || (uintptr_t)lo % 8 == 0);
+  const int esz = dt == WE_F32 ? 4 : 2;
+  if (vec_ok && (uintptr_t)x % 16 == 0 && (stride * esz) % 16 == 0) {
+    bool done;
+    if (dt == WE_F32) done = terms > 1 ? quant_act_cached<WE_F32, 2>(x, m, k, stride, hi, lo, row_scale, sms, st)
+                                       : quant_act_cached<WE_F32, 1>(x, m, k, stride, hi, lo, row_scale, sms, st);
+    else done = terms > 1 ? quant_act_cached<WE_BF16, 2>(x, m, k, stride, hi, lo, row_scale, sms, st)
+                          : quant_act_cached<WE_BF16, 1>(x, m, k, stride, hi, lo, row_scale, sms, st);
+    if (done) return cudaGetLastError();
+  }
   if (dt == WE_F32) {
     if (terms > 1) quant_act_kernel<WE_F32, 2><<<g, threads, 0, st>>>(x, m, k, stride, hi, lo, row_scale, vec_ok);
     else quant_act_kernel<WE_F32, 1><<<g, threads, 0, st>>>(x, m, k, stride, hi, lo, row_scale, vec_ok);
