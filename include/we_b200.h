@@ -217,6 +217,26 @@ int we_quantize_int4(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int
 int we_quantize_act(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t m, int64_t k, int64_t x_stride,
                     int32_t terms, uint8_t* hi, uint8_t* lo, float* row_scale);
 
+/* ---------------- allocation-free linear (no counterpart in the reference) ----------------
+   For callers that cannot allocate device memory: code inside someone else's CUDA-graph capture, a
+   serving loop with a fixed memory budget, or a runtime whose allocator owns all device memory.
+   y = x . W^T * scale (+ bias) for bf16 x [m, k] (row stride x_stride values, 0 = k) and e4m3 W [n, k]
+   with f32 scale or per-channel chan_scale [n]: the same activation split and tcgen05 GEMM as
+   we_matmul, but with no context and no allocation. The split lives in one static device array of
+   WE_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process exits; calls
+   needing more (2 m k + 4 m bytes, m k + 4 m with WE_MM_FP8_FAST) return WE_EINVAL. All calls on a
+   device share that array, so calls that overlap on the GPU (other streams, other threads) race:
+   serialise them. The first call on each device looks up the array's device address with that
+   device current; make that first call before any stream capture. `stream` is a cudaStream_t on the
+   current device. flags: WE_MM_FP8_FAST, WE_MM_ACCUMULATE, WE_NOALLOC_SYNC (wait for the stream and
+   return WE_ETIMEOUT if a bounded wait in the GEMM gave up). errbuf (may be NULL) receives a message
+   on failure. */
+#define WE_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+enum { WE_NOALLOC_SYNC = 1u << 3 };
+int we_matmul_fp8_noalloc(void* stream, const void* x, int64_t m, int64_t k, int64_t x_stride, const uint8_t* w,
+                          int64_t n, float scale, const float* chan_scale, const float* bias, void* y,
+                          int64_t y_stride, int32_t y_dtype, uint32_t flags, char* errbuf, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif

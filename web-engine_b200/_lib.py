@@ -14,7 +14,8 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "we_b200.h")
 
 WE_OK, WE_EINVAL, WE_ENOMEM, WE_ECUDA, WE_ENCCL, WE_ETIMEOUT, WE_EUNSUPPORTED = range(7)
 F32, BF16, FP8, INT4G64, F16 = 0, 1, 2, 3, 4
-MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT = 1, 2, 4
+MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT, NOALLOC_SYNC = 1, 2, 4, 8
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 ROPE_INTERLEAVED, ROPE_HALF = 0, 1
 
 DTYPES = {"f32": F32, "bf16": BF16, "fp8": FP8, "int4": INT4G64, "f16": F16}
@@ -107,6 +108,8 @@ _SIGS = {
     "we_quantize_fp8": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, C.c_int32, _P, _P]),
     "we_quantize_int4": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _P, _P]),
     "we_quantize_act": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, C.c_int32, _P, _P, _P]),
+    "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
+                                        C.c_uint32, C.c_char_p, C.c_size_t]),
 }
 
 _lib = None
