@@ -160,6 +160,41 @@ def test_tc_fp8_exact_split(we, graph, m, n, k):
     assert O.compare(y, want)["cosine"] > 0.99999
 
 
+@pytest.fixture
+def force_pair_kernel(monkeypatch):
+    """Runs the 2-SM (cta_group::2) kernel on every shape, not only where it fills the GPU."""
+    monkeypatch.setenv("WE_TC_2SM", "2")
+
+
+PAIR_SHAPES = [(256, 256, 128), (37, 70, 128), (300, 520, 384), (130, 65, 144), (1, 300, 512), (257, 513, 1024),
+               (512, 768, 3072)]
+
+
+@pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
+@pytest.mark.parametrize("terms", [2, 1])
+def test_tc_pair_kernel_fp8(we, graph, force_pair_kernel, m, n, k, terms):
+    x = bf16_round(randn(m * k, 21))
+    w = fast_fp8(n * k, 22)
+    y, path = run_tc(we, graph, x, w, m, n, k, "fp8", scale=0.002, fast=terms == 1)
+    assert path == "tc"
+    want = O.matmul(x, O.FP8, w, m, n, k, scale=0.002, threads=0)
+    if terms == 2:
+        assert O.rel_error(y, want) < EXACT_REL
+    else:
+        assert O.compare(y, want)["cosine"] >= FAST_COS and O.rel_error(y, want) < FAST_REL
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (200, 300, 264), (512, 512, 3072)])
+def test_tc_pair_kernel_bf16_and_epilogue(we, graph, force_pair_kernel, m, n, k):
+    x = bf16_round(randn(m * k, 23))
+    wf = bf16_round(randn(n * k, 24, 0.05))
+    bias = randn(n, 25)
+    y, path = run_tc(we, graph, x, bf16(wf), m, n, k, "bf16", scale=0.5, bias=bias, y_dtype="bf16")
+    assert path == "tc"
+    want = O.matmul(x, O.BF16, bf16(wf), m, n, k, scale=0.5).reshape(m, n) + bias.astype(np.float64)
+    assert np.all(np.abs(y.reshape(m, n) - want) <= np.abs(want) * 2.0 ** -8 + 1e-4 * np.abs(want).max())
+
+
 @pytest.mark.parametrize("m,n,k", [(128, 128, 128), (200, 260, 256), (256, 512, 3072)])
 def test_tc_fp8_fast_single_term(we, graph, m, n, k):
     x = bf16_round(randn(m * k, 3))

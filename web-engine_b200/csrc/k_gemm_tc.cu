@@ -175,6 +175,70 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Epilogue of one 32-token chunk of a warp's 32 channels: scale by the row scale (one coalesced load,
+// broadcast by shuffle), channel scale and bias, transpose through shared memory (row stride EPI_LD,
+// conflict-free), then 8 consecutive channels of one token per lane: one 16-byte bf16 store (or two
+// f32), scalar stores on ragged edges.
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], float* stage, int lane, int64_t tok0,
+                                               int64_t ch_base, float cs, float bias, const Params& p) {
+  const int cg = (lane & 3) * 8;
+  // the 32 row scales of this chunk: one coalesced load, then broadcast by shuffle
+  const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    stage[j * EPI_LD + lane] = __uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j) * cs + bias;
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 4; it++) {
+    const int tr = it * 8 + (lane >> 2);
+    const int64_t tok = tok0 + tr;
+    const float4 a = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg);
+    const float4 b = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg + 4);
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const int64_t c0 = ch_base + cg;
+    if (tok >= p.m || c0 >= p.n) continue;
+    const int64_t o = tok * p.y_stride + c0;
+    if (p.vec_ok && c0 + 8 <= p.n) {
+      if (p.y_dtype == WE_BF16) {
+        uint4* y = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o);
+        if (p.accumulate) {
+          const uint4 old = *y;
+          const uint32_t w[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            v[2 * e] += __uint_as_float(w[e] << 16);
+            v[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+          }
+        }
+        *y = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                        pack_bf16x2(v[6], v[7]));
+      } else {
+        float4* y = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
+        if (p.accumulate) {
+          const float4 o0 = y[0], o1 = y[1];
+          v[0] += o0.x; v[1] += o0.y; v[2] += o0.z; v[3] += o0.w;
+          v[4] += o1.x; v[5] += o1.y; v[6] += o1.z; v[7] += o1.w;
+        }
+        y[0] = make_float4(v[0], v[1], v[2], v[3]);
+        y[1] = make_float4(v[4], v[5], v[6], v[7]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        if (c0 + e >= p.n) break;
+        if (p.y_dtype == WE_BF16) {
+          uint16_t* y = static_cast<uint16_t*>(p.y);
+          float val = v[e] + (p.accumulate ? bf16_bits_to_f32(y[o + e]) : 0.f);
+          y[o + e] = f32_to_bf16_bits(val);
+        } else {
+          float* y = static_cast<float*>(p.y);
+          y[o + e] = v[e] + (p.accumulate ? y[o + e] : 0.f);
+        }
+      }
+    }
+  }
+}
+
 // ---------------- the kernel ----------------
 template <int BT, int TERMS, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -306,7 +370,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     float* stage = reinterpret_cast<float*>(smem + L::EPI_OFFSET) + (warp - 2) * (32 * EPI_LD);
-    const int cg = (lane & 3) * 8;  // write-out: 8 channels of one token row per lane
     int ab = 0;
     uint32_t aph = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -331,61 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(TEMPTY(ab));
         }
-        // the 32 row scales of this chunk: one coalesced load, then broadcast by shuffle
-        const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-          stage[j * EPI_LD + lane] = __uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j) * cs + bias;
-        __syncwarp();
-#pragma unroll
-        for (int it = 0; it < 4; it++) {
-          const int tr = it * 8 + (lane >> 2);
-          const int64_t tok = tok0 + tr;
-          const float4 a = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg);
-          const float4 b = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg + 4);
-          float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-          const int64_t c0 = ch_base + cg;
-          if (tok >= p.m || c0 >= p.n) continue;
-          const int64_t o = tok * p.y_stride + c0;
-          if (p.vec_ok && c0 + 8 <= p.n) {
-            if (p.y_dtype == WE_BF16) {
-              uint4* y = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o);
-              if (p.accumulate) {
-                const uint4 old = *y;
-                const uint32_t w[4] = {old.x, old.y, old.z, old.w};
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                  v[2 * e] += __uint_as_float(w[e] << 16);
-                  v[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
-                }
-              }
-              *y = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                              pack_bf16x2(v[6], v[7]));
-            } else {
-              float4* y = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
-              if (p.accumulate) {
-                const float4 o0 = y[0], o1 = y[1];
-                v[0] += o0.x; v[1] += o0.y; v[2] += o0.z; v[3] += o0.w;
-                v[4] += o1.x; v[5] += o1.y; v[6] += o1.z; v[7] += o1.w;
-              }
-              y[0] = make_float4(v[0], v[1], v[2], v[3]);
-              y[1] = make_float4(v[4], v[5], v[6], v[7]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-              if (c0 + e >= p.n) break;
-              if (p.y_dtype == WE_BF16) {
-                uint16_t* y = static_cast<uint16_t*>(p.y);
-                float val = v[e] + (p.accumulate ? bf16_bits_to_f32(y[o + e]) : 0.f);
-                y[o + e] = f32_to_bf16_bits(val);
-              } else {
-                float* y = static_cast<float*>(p.y);
-                y[o + e] = v[e] + (p.accumulate ? y[o + e] : 0.f);
-              }
-            }
-          }
-        }
+        epilogue_chunk(r, stage, lane, tok0, ch_base, cs, bias, p);
         __syncwarp();
       }
       if (++ab == 2) {
@@ -399,6 +408,282 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+  }
+#undef FULL
+#undef EMPTY
+#undef TFULL
+#undef TEMPTY
+#undef DRAIN
+}
+
+
+// ---------------- the 2-SM kernel (cta_group::2) ----------------
+// A CTA pair (cluster of 2, ranks 0 = leader and 1) computes 256 weight rows x BT tokens: each CTA
+// TMA-loads its own 128 weight rows and its own BT/2 token rows (plain loads, no multicast; the bytes
+// complete on the leader's barrier), the leader's MMA thread issues tcgen05.mma.cta_group::2 (M = 256,
+// N = BT) and its commits arrive on both CTAs' barriers (tcgen05.commit multicast), and each CTA's
+// epilogue drains its own 128-lane accumulator, releasing it on the leader's barrier (remote arrive).
+// Per SM this halves the token bytes per FLOP of the 1-SM kernel, so the same shared memory holds
+// twice the stages.
+template <int BT, int TERMS>
+struct Layout2 {
+  static constexpr int W_BYTES = BM * KB_BYTES;
+  static constexpr int X_BYTES = (BT / 2) * KB_BYTES;
+  static constexpr int STAGE_BYTES = W_BYTES + TERMS * X_BYTES;
+  static constexpr int STAGES = (SMEM_BUDGET / STAGE_BYTES) > 8 ? 8 : (SMEM_BUDGET / STAGE_BYTES);
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int TOTAL = BAR_OFFSET + NUM_BARS * 8 + 16;
+  static constexpr int ALLOC = TOTAL + 1024;
+  static_assert(STAGES >= 2, "shared-memory ring needs at least 2 stages");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// address of the same shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t c0,
+                                                 int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+template <bool F16>
+__device__ __forceinline__ void umma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  }
+}
+// arrive on the barrier at this offset in both CTAs of the pair once the leader's MMAs so far complete
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+               "h"((uint16_t)0x3)
+               : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+template <int BT, bool F16>
+__host__ __device__ constexpr uint32_t make_idesc_pair() {
+  return (1u << 4) | ((F16 ? 1u : 0u) << 7) | ((F16 ? 1u : 0u) << 10) | ((uint32_t)(BT >> 3) << 17) |
+         ((uint32_t)((2 * BM) >> 4) << 24);
+}
+
+template <int BT, int TERMS, bool F16>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x0,
+                    const __grid_constant__ CUtensorMap tm_x1, const Params p) {
+  using L = Layout2<BT, TERMS>;
+  constexpr int STAGES = L::STAGES;
+  constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BT;
+  constexpr uint32_t IDESC = make_idesc_pair<BT, F16>();
+  constexpr int MMAS_PER_KB = KB_BYTES / 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + L::BAR_OFFSET;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::BAR_OFFSET + L::NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+#define FULL(s) (bars + 8u * (s))
+#define EMPTY(s) (bars + 8u * (STAGES + (s)))
+#define TFULL(b) (bars + 8u * (2 * STAGES + (b)))
+#define TEMPTY(b) (bars + 8u * (2 * STAGES + 2 + (b)))
+#define DRAIN (bars + 8u * (2 * STAGES + 4))
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(FULL(s), 1);   // leader: one arrive.expect_tx of the pair's bytes per use
+      mbar_init(EMPTY(s), 1);  // both: the leader's multicast commit
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(TFULL(b), 1);   // both: the leader's multicast commit
+      mbar_init(TEMPTY(b), 8);  // leader: 4 epilogue warps of each CTA
+    }
+    mbar_init(DRAIN, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  const int64_t tiles_n = (p.n + 2 * BM - 1) / (2 * BM);  // pair tiles of 256 weight rows
+  const int64_t tiles_m = (p.m + BT - 1) / BT;
+  const int64_t tiles = tiles_n * tiles_m;
+  const int64_t cid = cluster_id(), ncl = cluster_count();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_w)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x0)) : "memory");
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_ph[STAGES];
+      int issued = 0;
+      bool ok = true;
+      for (int64_t t = cid; t < tiles && ok; t += ncl) {
+        const int32_t row_w = (int32_t)((t % tiles_n) * 2 * BM + rank * BM);
+        const int32_t row_x = (int32_t)((t / tiles_n) * BT + rank * (BT / 2));
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
+          if (leader) mbar_expect_tx(FULL(s), 2 * L::STAGE_BYTES);
+          const uint32_t bar = map_rank(FULL(s), 0);
+          const int32_t kc = kb * KB_ELEMS;
+          tma_load_2d_pair(st, &tm_w, bar, kc, row_w);
+          tma_load_2d_pair(st + L::W_BYTES, &tm_x0, bar, kc, row_x);
+          if (TERMS > 1) tma_load_2d_pair(st + L::W_BYTES + L::X_BYTES, &tm_x1, bar, kc, row_x);
+          issued_ph[s] = ph;
+          issued++;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok && leader) {  // the pair's loads already issued land before the CTAs can exit
+        for (int i = 0; i < STAGES && i < issued; i++)
+          wait_bounded(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int s = 0;
+      uint32_t ph = 0, aph = 0;
+      int ab = 0;
+      bool ok = true;
+      for (int64_t t = cid; t < tiles && ok; t += ncl) {
+        if (!wait_bounded(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(ab * BT);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!wait_bounded(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
+          const uint64_t adesc = sw128_desc(st);
+#pragma unroll
+          for (int term = 0; term < TERMS; term++) {
+            const uint64_t bdesc = sw128_desc(st + L::W_BYTES + term * L::X_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < MMAS_PER_KB; kk++)
+              umma_pair<F16>(d, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | term | kk) != 0);
+          }
+          umma_commit_pair_both(EMPTY(s));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_both(TFULL(ab));
+        if (++ab == 2) {
+          ab = 0;
+          aph ^= 1u;
+        }
+      }
+      umma_commit_pair_local(DRAIN);
+      wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    float* stage = reinterpret_cast<float*>(smem + L::EPI_OFFSET) + (warp - 2) * (32 * EPI_LD);
+    int ab = 0;
+    uint32_t aph = 0;
+    for (int64_t t = cid; t < tiles; t += ncl) {
+      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int64_t ch_base = (t % tiles_n) * 2 * BM + rank * BM + q * 32;
+      const int64_t ch = ch_base + lane;
+      const int64_t tok_base = (t / tiles_n) * BT;
+      const bool ch_ok = ch < p.n;
+      const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
+      const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; c++) {
+        const int64_t tok0 = tok_base + c * 32;
+        if (tok0 >= p.m) break;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BT + c * 32), r);
+        if (c == BT / 32 - 1 || tok0 + 32 >= p.m) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(map_rank(TEMPTY(ab), 0));
+        }
+        epilogue_chunk(r, stage, lane, tok0, ch_base, cs, bias, p);
+        __syncwarp();
+      }
+      if (++ab == 2) {
+        ab = 0;
+        aph ^= 1u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or exits while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TMEM_COLS);
   }
 #undef FULL
 #undef EMPTY
@@ -435,17 +720,8 @@ static bool make_map(CUtensorMap* m, const void* base, bool f16, int64_t k, int6
   return r == CUDA_SUCCESS;
 }
 
-template <int BT, int TERMS, bool F16>
-static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
-  using L = Layout<BT, TERMS>;
-  CUtensorMap mw, mx0, mx1;
-  if (!make_map(&mw, a.w, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
-  if (!make_map(&mx0, a.x[0], F16, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
-  if (TERMS > 1) {
-    if (!make_map(&mx1, a.x[1], F16, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
-  } else {
-    mx1 = mx0;
-  }
+template <bool F16>
+static Params make_params(const TcGemmArgs& a) {
   Params p;
   p.m = a.m;
   p.n = a.n;
@@ -462,6 +738,21 @@ static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
   const int esz = a.y_dtype == WE_BF16 ? 2 : 4;
   p.vec_ok = ((uintptr_t)a.y % 16 == 0) && ((a.y_stride * esz) % 16 == 0);
   p.err = a.dev_err;
+  return p;
+}
+
+template <int BT, int TERMS, bool F16>
+static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
+  using L = Layout<BT, TERMS>;
+  CUtensorMap mw, mx0, mx1;
+  if (!make_map(&mw, a.w, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
+  if (!make_map(&mx0, a.x[0], F16, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
+  if (TERMS > 1) {
+    if (!make_map(&mx1, a.x[1], F16, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
+  } else {
+    mx1 = mx0;
+  }
+  Params p = make_params<F16>(a);
   auto kern = gemm_tc_kernel<BT, TERMS, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
   if (e != cudaSuccess) return e;
@@ -471,6 +762,45 @@ static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+
+template <int BT, int TERMS, bool F16>
+static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
+  using L = Layout2<BT, TERMS>;
+  CUtensorMap mw, mx0, mx1;
+  if (!make_map(&mw, a.w, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
+  if (!make_map(&mx0, a.x[0], F16, a.k, a.m, a.x_stride_bytes, BT / 2)) return cudaErrorNotSupported;
+  if (TERMS > 1) {
+    if (!make_map(&mx1, a.x[1], F16, a.k, a.m, a.x_stride_bytes, BT / 2)) return cudaErrorNotSupported;
+  } else {
+    mx1 = mx0;
+  }
+  Params p = make_params<F16>(a);
+  auto kern = gemm_tc2_kernel<BT, TERMS, F16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int64_t tiles = ((a.n + 2 * BM - 1) / (2 * BM)) * ((a.m + BT - 1) / BT);
+  int clusters = sms / 2;
+  cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  int max_clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) == cudaSuccess && max_clusters > 0 &&
+      max_clusters < clusters)
+    clusters = max_clusters;
+  if (tiles < clusters) clusters = (int)tiles;
+  cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, mw, mx0, mx1, p);
+  return e == cudaSuccess ? cudaGetLastError() : e;
+}
 }  // namespace tc
 
 bool gemm_tc_supported(const TcGemmArgs& a) {
@@ -488,6 +818,18 @@ bool gemm_tc_supported(const TcGemmArgs& a) {
 // Token tile: the largest of 256 / 128 / 64 that still gives every SM a tile, else 64.
 cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (!gemm_tc_supported(a)) return cudaErrorNotSupported;
+  // 2-SM pairs (256 weight rows x 256 tokens per pair) when there are enough pair tiles to fill the
+  // GPU; otherwise 1-SM tiles with the largest token tile (256 / 128 / 64) that gives every SM a tile.
+  bool pair = ((a.n + 255) / 256) * ((a.m + 255) / 256) >= sms / 2;
+  if (const char* env = getenv("WE_TC_2SM")) {  // tuning / test override: 0 never, 2 always
+    const int v = atoi(env);
+    pair = v == 2 ? true : (v == 0 ? false : pair);
+  }
+  if (pair) {
+    if (a.kind_f16) return tc::run_pair<256, 1, true>(a, sms, st);
+    if (a.terms > 1) return tc::run_pair<256, 2, false>(a, sms, st);
+    return tc::run_pair<256, 1, false>(a, sms, st);
+  }
   const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
   auto tiles = [&](int bt) { return tn * ((a.m + bt - 1) / bt); };
   int bt = tiles(256) >= sms ? 256 : (tiles(128) >= sms ? 128 : 64);
