@@ -223,11 +223,30 @@ def test_rope_block_size_bf16(we, graph, pairing):
 
 
 # ---------------- fused q/k norm + RoPE (src/model/block.ts:53-56) ----------------
-@pytest.mark.parametrize("head_dim,pairing,axes", [(128, "interleaved", (32, 48, 48)), (128, "half", (32, 48, 48)),
-                                                   (64, "interleaved", (16, 24, 24)), (256, "interleaved", (64, 96, 96)),
-                                                   (96, "interleaved", (32, 32, 32))])
-def test_qknorm_rope_matches_norm_then_rotate(we, graph, head_dim, pairing, axes):
-    tokens, heads = 2 + 5 * 7, 4
+@pytest.mark.parametrize("pairing", ["interleaved", "half"])
+def test_qknorm_rope_block_size_bf16(we, graph, pairing):
+    """Config 3's q path in bf16: 4608 tokens x 24 heads x 128, axes 16/56/56, theta 1e4."""
+    tokens, heads = 512 + 64 * 64, 24
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(512, 64, 64), (16, 56, 56), 1e4)
+    x = bf16_round(randn(tokens * heads * 128, 41, 2.0))
+    w = randn(128, 42, 0.1)
+    mark = graph.mark()
+    xb, wb, cb, sb, ob = (graph.buffer(bf16(x)), graph.buffer(w), graph.buffer(cos), graph.buffer(sin),
+                          graph.buffer(x.size * 2))
+    we.kernels.qknorm_rope(graph, xb, wb, cb, sb, tokens, heads, pairs, ob, pairing=pairing, x_dtype="bf16",
+                           out_dtype="bf16")
+    got = O.bf16_to_f32(graph.read(ob, x.size * 2, np.uint16))
+    want = O.rope(O.rmsnorm(x, w, None, None, 1e-5, 1.0).astype(np.float32), tokens, heads, pairs, cos, sin, pairing)
+    assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -8 + 2e-5)
+    graph.release(mark)
+
+
+@pytest.mark.parametrize("head_dim,pairing,axes,heads", [
+    (128, "interleaved", (32, 48, 48), 4), (128, "half", (32, 48, 48), 4), (128, "interleaved", (32, 48, 48), 3),
+    (128, "half", (32, 48, 48), 3), (64, "interleaved", (16, 24, 24), 4), (256, "interleaved", (64, 96, 96), 4),
+    (96, "interleaved", (32, 32, 32), 4)])
+def test_qknorm_rope_matches_norm_then_rotate(we, graph, head_dim, pairing, axes, heads):
+    tokens = 2 + 5 * 7  # with 3 heads: an odd number of head rows
     cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(2, 5, 7), axes, 1000.0)
     assert 2 * pairs == head_dim
     x = lcg_floats(tokens * heads * head_dim, 5, 3.0)

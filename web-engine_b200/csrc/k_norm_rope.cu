@@ -110,6 +110,116 @@ __global__ void __launch_bounds__(128) rmsnorm_cached_kernel(const void* __restr
   }
 }
 
+// Warp-per-row RMSNorm for bf16 rows (d % 8 == 0, d <= 256 UMAX, 16-byte aligned): lane l holds the
+// row's 16-byte chunks l, l + 32, ... packed as bf16 in registers (4 registers per 8 values), so each
+// warp-wide load is 512 contiguous bytes, x is read once, and the reduction is shuffles only. With
+// ~2 KB of row per warp in flight, a full SM keeps the whole 4608-row block in one wave.
+template <int OT, int UMAX>
+__global__ void __launch_bounds__(128) rmsnorm_warp_kernel(const uint16_t* __restrict__ x, const float* __restrict__ w,
+                                                           const float* __restrict__ sc, const float* __restrict__ sh,
+                                                           int64_t rows, int64_t d, float eps, float offset,
+                                                           void* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * 4;
+  for (int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); row < rows; row += warps) {
+    const uint16_t* xr = x + row * d;
+    uint4 v[UMAX];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t i = (int64_t)(c * 32 + lane) * 8;
+      if (i < d) {
+        v[c] = *reinterpret_cast<const uint4*>(xr + i);
+        const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+          ss = fmaf(a, a, fmaf(b, b, ss));
+        }
+      }
+    }
+    const float inv = rsqrtf(warp_sum(ss) / (float)d + eps);
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t i = (int64_t)(c * 32 + lane) * 8;
+      if (i >= d) continue;
+      float f[8], ww[8], s[8], h[8];
+      const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        f[2 * j] = __uint_as_float(u[j] << 16);
+        f[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+      }
+      load8f(w, i, ww);
+      if (sc) load8f(sc, i, s); else for (int j = 0; j < 8; j++) s[j] = 0.f;
+      if (sh) load8f(sh, i, h); else for (int j = 0; j < 8; j++) h[j] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) f[j] = f[j] * inv * (offset + ww[j]) * (1.f + s[j]) + h[j];
+      store8<OT>(out, row * d + i, f);
+    }
+  }
+}
+
+// q/k norm + RoPE for 128-wide heads: 16 lanes per head row, 8 values (16 bytes of bf16) per lane,
+// two rows per warp. Interleaved pairs stay in a lane; half pairing exchanges with lane ^ 8.
+template <int DT, int OT, int PAIRING>
+__global__ void __launch_bounds__(256) qknorm_rope128_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                             float eps, float offset, const float* __restrict__ cs,
+                                                             const float* __restrict__ sn, int64_t tokens,
+                                                             int64_t heads, void* __restrict__ out) {
+  constexpr int D = 128, P = 64;
+  const int lane = threadIdx.x & 31, sub = lane & 15;
+  const int64_t rows = tokens * heads;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  float ww[8];
+  load8f(w, sub * 8, ww);
+#pragma unroll
+  for (int e = 0; e < 8; e++) ww[e] += offset;
+  // warp-uniform loop over row pairs: half-warp (lane >> 4) takes row 2 pr + (lane >> 4); a row beyond
+  // the end (odd row count) is computed on row rows - 1 and not stored, so the shuffles stay full-warp
+  for (int64_t pr = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); 2 * pr < rows; pr += warps) {
+    const int64_t row0 = 2 * pr + (lane >> 4);
+    const bool live = row0 < rows;
+    const int64_t row = live ? row0 : rows - 1;
+    const int64_t t = row / heads;
+    const int64_t base = row * D + sub * 8;
+    float v[8];
+    load8<DT>(x, base, v);
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] *= inv * ww[e];
+    float o8[8];
+    if (PAIRING == WE_ROPE_INTERLEAVED) {
+      float c4[4], s4[4];
+      const float4 cc = *reinterpret_cast<const float4*>(cs + t * P + sub * 4);
+      const float4 sv = *reinterpret_cast<const float4*>(sn + t * P + sub * 4);
+      c4[0] = cc.x; c4[1] = cc.y; c4[2] = cc.z; c4[3] = cc.w;
+      s4[0] = sv.x; s4[1] = sv.y; s4[2] = sv.z; s4[3] = sv.w;
+#pragma unroll
+      for (int g = 0; g < 4; g++) {
+        o8[2 * g] = v[2 * g] * c4[g] - v[2 * g + 1] * s4[g];
+        o8[2 * g + 1] = v[2 * g + 1] * c4[g] + v[2 * g] * s4[g];
+      }
+    } else {
+      const bool first = sub < 8;
+      float c8[8], s8[8];
+      load8f(cs, t * P + (sub & 7) * 8, c8);
+      load8f(sn, t * P + (sub & 7) * 8, s8);
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 8);
+        o8[e] = first ? v[e] * c8[e] - partner * s8[e] : v[e] * c8[e] + partner * s8[e];
+      }
+    }
+    if (live) store8<OT>(out, base, o8);
+  }
+}
+
 // RoPE, interleaved pairs (2j, 2j+1) or half pairs (j, j+P). One thread per (token, group of G pairs),
 // looping over heads so each cos/sin value is loaded once per token (like the reference kernel).
 template <int DT, int OT, int G, int PAIRING>
@@ -217,6 +327,18 @@ static int capped(int64_t want, int sms, int per_sm) {
 template <int DT, int OT>
 static void rmsnorm_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
                              float eps, float offset, void* out, bool vec, int sms, cudaStream_t st) {
+  if constexpr (DT == WE_BF16) {
+    if (vec && d <= 256 * 24) {
+      const int g = capped((rows + 3) / 4, sms, 16);
+      const uint16_t* xb = static_cast<const uint16_t*>(x);
+      if (d <= 256 * 4) rmsnorm_warp_kernel<OT, 4><<<g, 128, 0, st>>>(xb, w, sc, sh, rows, d, eps, offset, out);
+      else if (d <= 256 * 8) rmsnorm_warp_kernel<OT, 8><<<g, 128, 0, st>>>(xb, w, sc, sh, rows, d, eps, offset, out);
+      else if (d <= 256 * 12) rmsnorm_warp_kernel<OT, 12><<<g, 128, 0, st>>>(xb, w, sc, sh, rows, d, eps, offset, out);
+      else if (d <= 256 * 16) rmsnorm_warp_kernel<OT, 16><<<g, 128, 0, st>>>(xb, w, sc, sh, rows, d, eps, offset, out);
+      else rmsnorm_warp_kernel<OT, 24><<<g, 128, 0, st>>>(xb, w, sc, sh, rows, d, eps, offset, out);
+      return;
+    }
+  }
   if (vec && d >= 512) {
     const int64_t chunks = (d / 8 + 127) / 128;
     const int g = capped(rows, sms, 16);
@@ -285,6 +407,16 @@ static void qk_dispatch2(const void* x, const float* w, float eps, float offset,
 template <int DT, int OT>
 static bool qk_dispatch(const void* x, const float* w, float eps, float offset, const float* cs, const float* sn,
                         int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out, int sms, cudaStream_t st) {
+  if (pairs * 2 == 128 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0 && ((uintptr_t)cs & 15) == 0 &&
+      ((uintptr_t)sn & 15) == 0) {
+    const int64_t rows = tokens * heads;
+    const int g = capped((rows + 15) / 16, sms, 8);
+    if (pairing == WE_ROPE_INTERLEAVED)
+      qknorm_rope128_kernel<DT, OT, WE_ROPE_INTERLEAVED><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+    else
+      qknorm_rope128_kernel<DT, OT, WE_ROPE_HALF><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+    return true;
+  }
   switch (pairs * 2) {
     case 64: qk_dispatch2<DT, OT, 2>(x, w, eps, offset, cs, sn, tokens, heads, pairing, out, sms, st); return true;
     case 128: qk_dispatch2<DT, OT, 4>(x, w, eps, offset, cs, sn, tokens, heads, pairing, out, sms, st); return true;

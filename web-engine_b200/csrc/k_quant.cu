@@ -5,6 +5,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace we {
 
 // ---------------- unpack ----------------
@@ -142,6 +144,12 @@ __device__ __forceinline__ int act_exponent(float amax) {
   return m <= 1.75f ? E - 8 : E - 7;
 }
 
+// 2^-e as a float multiplier when it is a normal float (exact scaling), else 0 (callers use ldexpf)
+__device__ __forceinline__ float pow2_neg(int e) {
+  const int b = 127 - e;
+  return (b >= 1 && b <= 254) ? __int_as_float(b << 23) : 0.f;
+}
+
 // one CTA per row (grid-stride); VEC = values per 16-byte load of x
 template <int DT, int TERMS>
 __global__ void quant_act_kernel(const void* __restrict__ x, int64_t m, int64_t k, int64_t stride, uint8_t* __restrict__ hi,
@@ -249,6 +257,78 @@ __global__ void __launch_bounds__(128) quant_act_cached_kernel(const void* __res
   }
 }
 
+// Warp-per-row split for bf16 rows (k % 8 == 0, k <= 256 UMAX, 16-byte aligned rows): lane l keeps
+// the row's 16-byte chunks l, l + 32, ... packed in registers; the row max is a shuffle reduction.
+template <int TERMS, int UMAX>
+__global__ void __launch_bounds__(128, 6) quant_act_warp_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
+                                                             int64_t stride, uint8_t* __restrict__ hi,
+                                                             uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * 4;
+  for (int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); row < m; row += warps) {
+    const uint16_t* xr = x + row * stride;
+    uint4 v[UMAX];
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t t = (int64_t)(c * 32 + lane) * 8;
+      if (t < k) {
+        v[c] = *reinterpret_cast<const uint4*>(xr + t);
+        // |bf16| max on the bit patterns: clear the sign bits, compare as integers
+        const uint32_t a = v[c].x & 0x7fff7fffu, b = v[c].y & 0x7fff7fffu, cc = v[c].z & 0x7fff7fffu,
+                       dd = v[c].w & 0x7fff7fffu;
+        const uint32_t m1 = __vmaxu2(__vmaxu2(a, b), __vmaxu2(cc, dd));
+        amax = fmaxf(amax, fmaxf(__uint_as_float(m1 << 16), __uint_as_float(m1 & 0xffff0000u)));
+      }
+    }
+    amax = warp_max(amax);
+    const int e = act_exponent(amax);
+    if (lane == 0) row_scale[row] = ldexpf(1.0f, e);
+    const float mul = pow2_neg(e);  // exact: scaling by a power of two
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t t = (int64_t)(c * 32 + lane) * 8;
+      if (t >= k) continue;
+      const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+      float s[8];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+        s[2 * j] = mul != 0.f ? a * mul : ldexpf(a, -e);
+        s[2 * j + 1] = mul != 0.f ? b * mul : ldexpf(b, -e);
+      }
+      uint32_t h[2], l[2];
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const uint16_t h0 = f32x2_to_e4m3x2(s[4 * j], s[4 * j + 1]);
+        const uint16_t h1 = f32x2_to_e4m3x2(s[4 * j + 2], s[4 * j + 3]);
+        h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        if (TERMS > 1) {
+          const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+          const uint16_t l0 = f32x2_to_e4m3x2(s[4 * j] - d0.x, s[4 * j + 1] - d0.y);
+          const uint16_t l1 = f32x2_to_e4m3x2(s[4 * j + 2] - d1.x, s[4 * j + 3] - d1.y);
+          l[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        }
+      }
+      *reinterpret_cast<uint2*>(hi + row * k + t) = make_uint2(h[0], h[1]);
+      if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * k + t) = make_uint2(l[0], l[1]);
+    }
+  }
+}
+
+template <int TERMS>
+static bool quant_act_warp(const uint16_t* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo, float* rs,
+                           int sms, cudaStream_t st) {
+  const int g = (int)std::min<int64_t>((m + 3) / 4, (int64_t)sms * 16);
+  if (k <= 256 * 4) quant_act_warp_kernel<TERMS, 4><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (k <= 256 * 8) quant_act_warp_kernel<TERMS, 8><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (k <= 256 * 12) quant_act_warp_kernel<TERMS, 12><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (k <= 256 * 16) quant_act_warp_kernel<TERMS, 16><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (k <= 256 * 24) quant_act_warp_kernel<TERMS, 24><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else return false;
+  return true;
+}
+
 template <int DT, int TERMS>
 static bool quant_act_cached(const void* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo,
                              float* rs, int sms, cudaStream_t st) {
@@ -327,6 +407,12 @@ cudaError_t launch_quant_act(const void* x, int dt, int64_t m, int64_t k, int64_
   int vec_ok = (k % 8 == 0) && ((uintptr_t)hi % 8 == 0) && (!lo || (uintptr_t)lo % 8 == 0);
   const int esz = dt == WE_F32 ? 4 : 2;
   if (vec_ok && (uintptr_t)x % 16 == 0 && (stride * esz) % 16 == 0) {
+    if (dt == WE_BF16) {
+      const uint16_t* xb = static_cast<const uint16_t*>(x);
+      if (terms > 1 ? quant_act_warp<2>(xb, m, k, stride, hi, lo, row_scale, sms, st)
+                    : quant_act_warp<1>(xb, m, k, stride, hi, lo, row_scale, sms, st))
+        return cudaGetLastError();
+    }
     bool done;
     if (dt == WE_F32) done = terms > 1 ? quant_act_cached<WE_F32, 2>(x, m, k, stride, hi, lo, row_scale, sms, st)
                                        : quant_act_cached<WE_F32, 1>(x, m, k, stride, hi, lo, row_scale, sms, st);
