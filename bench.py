@@ -231,11 +231,7 @@ def main() -> None:
         torch.cuda.synchronize()
         wall_ms[0] = (time.perf_counter() - t0) * 1e3
         total = sum(a.elapsed_time(b) for a, b in ev)
-        if world > 1:
-            t = torch.tensor([total], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            total = float(t.item())
-        return total
+        return we.parallel.max_over_ranks(total, device=dev)
 
     if args.profile_case:
         # the activation split, the two-term and one-term GEMMs, the int4 decode + kind::f16 GEMM,
@@ -285,8 +281,12 @@ def main() -> None:
     bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
     gemm_tflops = FLOPS / (gemm_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": gemm_tflops, "peak": bf16_peak, "unit": "TFLOP/s",
-                "frac": gemm_tflops / bf16_peak, "traffic": None,
-                "kernel": "gemm_tc_kernel<BT=128|256, TERMS=2, kind::f8f6f4>",
+                "frac": gemm_tflops / bf16_peak,
+                # dram__bytes_read.sum + dram__bytes_write.sum of this kernel, one ncu --set full capture of
+                # `python bench.py --profile-case` (cold caches): 87.2 MB + 83.5 MB per launch
+                "traffic": 170.7e6, "traffic_unit": "bytes per launch",
+                "algorithmic_bytes_per_launch": N * K + 2 * M * K + 4 * M + 2 * M * N,
+                "kernel": "gemm_tc2_kernel<256, 2, kind::f8f6f4> (cta_group::2 pairs)",
                 "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; two e4m3 MMAs per K step = bf16 rate)"
                 if "fallback" not in peaks else "fallback 1.59 PFLOP/s",
                 "algorithmic_flop_per_launch": FLOPS, "split_ms": split_ms, "gemm_ms": gemm_ms}

@@ -6,7 +6,7 @@ mirror of the reference's operator API (src/model/ops.ts over src/gpu/graph.ts) 
 from . import _lib
 from .graph import Binding, Buffer, Graph
 from .ops import Linear, Mod, Rope, k_split_for, linear, no_mod, norm, qk_norm_rotate, rotate
-from . import kernels
+from . import kernels, parallel
 
 __all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "norm", "no_mod", "rotate",
            "qk_norm_rotate", "k_split_for", "kernels", "build"]
