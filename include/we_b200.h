@@ -217,6 +217,24 @@ int we_quantize_int4(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int
 int we_quantize_act(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t m, int64_t k, int64_t x_stride,
                     int32_t terms, uint8_t* hi, uint8_t* lo, float* row_scale);
 
+/* ---------------- layer streaming: src/model/weights.ts:94-131 (loadTransformer) ----------------
+   The reference uploads every block once and keeps it resident. A streamer instead keeps `slots` device
+   buffers and copies layer l (host[l], bytes[l]) into slot l % slots with cudaMemcpyAsync on its own copy
+   stream, overlapped with compute on the context stream. The host ranges are page-locked by the streamer
+   (cudaHostRegister) unless WE_STREAM_HOST_PINNED says they already are. */
+typedef struct we_streamer we_streamer;
+enum { WE_STREAM_HOST_PINNED = 1u };
+int we_streamer_create(we_ctx* ctx, const void* const* host, const size_t* bytes, int32_t layers, int32_t slots,
+                       uint32_t flags, we_streamer** out);
+/* Layer `layer`'s device copy: work queued on the context stream after this call sees its bytes. Also starts
+   copying the following layers (wrapping to layer 0) into slots that no acquired layer holds. A layer whose
+   slot is still held by another acquired layer is refused ("release it first"). */
+int we_streamer_acquire(we_streamer* s, int32_t layer, void** dev);
+/* The work using `layer` is queued: its slot may be refilled once that work has run. */
+int we_streamer_release(we_streamer* s, int32_t layer);
+int we_streamer_stats(const we_streamer* s, uint64_t* copies, uint64_t* bytes_copied);
+int we_streamer_destroy(we_streamer* s);
+
 /* ---------------- allocation-free linear (no counterpart in the reference) ----------------
    For callers that cannot allocate device memory: code inside someone else's CUDA-graph capture, a
    serving loop with a fixed memory budget, or a runtime whose allocator owns all device memory.

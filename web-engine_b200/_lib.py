@@ -16,6 +16,7 @@ WE_OK, WE_EINVAL, WE_ENOMEM, WE_ECUDA, WE_ENCCL, WE_ETIMEOUT, WE_EUNSUPPORTED = 
 F32, BF16, FP8, INT4G64, F16 = 0, 1, 2, 3, 4
 MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT, NOALLOC_SYNC = 1, 2, 4, 8
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
+STREAM_HOST_PINNED = 1
 ROPE_INTERLEAVED, ROPE_HALF = 0, 1
 
 DTYPES = {"f32": F32, "bf16": BF16, "fp8": FP8, "int4": INT4G64, "f16": F16}
@@ -108,6 +109,12 @@ _SIGS = {
     "we_quantize_fp8": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, C.c_int32, _P, _P]),
     "we_quantize_int4": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _P, _P]),
     "we_quantize_act": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, C.c_int32, _P, _P, _P]),
+    "we_streamer_create": (C.c_int, [_P, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t), C.c_int32, C.c_int32,
+                                     C.c_uint32, C.POINTER(C.c_void_p)]),
+    "we_streamer_acquire": (C.c_int, [_P, C.c_int32, C.POINTER(C.c_void_p)]),
+    "we_streamer_release": (C.c_int, [_P, C.c_int32]),
+    "we_streamer_stats": (C.c_int, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "we_streamer_destroy": (C.c_int, [_P]),
     "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
                                         C.c_uint32, C.c_char_p, C.c_size_t]),
 }

@@ -110,6 +110,10 @@ bool act_dtype_ok(int dt) { return dt == WE_F32 || dt == WE_BF16; }
 
 }  // namespace
 
+// helpers shared with the other translation units of the library (we_stream.cu)
+int we_ctx_fail(we_ctx* ctx, int code, const std::string& msg) { return fail(ctx, code, msg); }
+cudaStream_t we_ctx_stream(we_ctx* ctx) { return ctx->stream; }
+
 extern "C" {
 
 // ---------------- context ----------------
