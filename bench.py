@@ -333,6 +333,24 @@ def main() -> None:
                     "bytes": nbytes}
     roofline["bandwidth_kernels"] = bw
 
+    # ---- config 3's attention (4608 tokens, 24 heads x 128, bf16): tcgen05 flash attention ----
+    if not args.no_variants:
+        heads = K // 128
+        qa = torch.randn(M, heads, 128, generator=gen, device=dev).to(torch.bfloat16)
+        ka = torch.randn(M, heads, 128, generator=gen, device=dev).to(torch.bfloat16)
+        va = torch.randn(M, heads, 128, generator=gen, device=dev).to(torch.bfloat16)
+        oa = torch.empty(M, heads, 128, dtype=torch.bfloat16, device=dev)
+
+        def step_attn():
+            we.kernels.attention(g, qa, ka, va, M, heads, heads, 128, oa, dtype="bf16", out_dtype="bf16")
+
+        at_ms = timed(step_attn, args.steps, 2) / args.steps
+        at_flops = 4.0 * M * M * heads * 128
+        variants["flash_attention_config3"] = {"tflops": at_flops / (at_ms * 1e-3) / 1e12, "ms": at_ms,
+                                               "frac_bf16_peak": at_flops / (at_ms * 1e-3) / 1e12 / bf16_peak,
+                                               "note": "4 T^2 H D FLOP, T=4608, 24 heads x 128, incl. the V transpose"}
+        del qa, ka, va, oa
+
     # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
     if not args.no_variants:
         try:

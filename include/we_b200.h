@@ -217,6 +217,18 @@ int we_quantize_int4(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int
 int we_quantize_act(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t m, int64_t k, int64_t x_stride,
                     int32_t terms, uint8_t* hi, uint8_t* lo, float* row_scale);
 
+/* ---------------- attention: attention() (src/kernels/attention.ts:20-51) ----------------
+   softmax(q k^T / sqrt(dim)) v per head with grouped-query heads (query head h uses kv head
+   h / (heads / kv_heads)); q [tokens, heads, dim], k, v [tokens, kv_heads, dim] -> out [tokens, heads, dim].
+   causal = 1: query i sees keys 0..i (the text encoder). "heads must be a multiple of kvHeads" otherwise.
+   bf16 with dim 128 and no mask runs the tcgen05 flash-attention kernel; the rest runs on CUDA cores in
+   fp32 (the reference's exact semantics for f32 buffers). */
+int we_attention(we_ctx* ctx, const void* q, const void* k, const void* v, int32_t dtype, int64_t tokens,
+                 int64_t heads, int64_t kv_heads, int64_t dim, int32_t causal, void* out, int32_t out_dtype);
+/* The same as an op: out is a new pooled buffer [tokens, heads, dim] of out_dtype. */
+int we_attend(we_ctx* ctx, const void* q, const void* k, const void* v, int32_t dtype, int64_t tokens, int64_t heads,
+              int64_t kv_heads, int64_t dim, int32_t causal, int32_t out_dtype, void** out);
+
 /* ---------------- layer streaming: src/model/weights.ts:94-131 (loadTransformer) ----------------
    The reference uploads every block once and keeps it resident. A streamer instead keeps `slots` device
    buffers and copies layer l (host[l], bytes[l]) into slot l % slots with cudaMemcpyAsync on its own copy

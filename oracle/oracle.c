@@ -437,3 +437,34 @@ void or_rope(const float* x, long tokens, long heads, long pairs, const float* c
         out[ib] = b * c + a * s;
       }
 }
+
+/* ---------------- attention: tests/gpu/attention.test.ts:9-31 ---------------- */
+void or_attention(const float* q, const float* k, const float* v, long tokens, long heads, long kv_heads, long dim,
+                  int causal, double* out) {
+  long group = heads / kv_heads;
+#ifdef _OPENMP
+#pragma omp parallel for collapse(2) schedule(static)
+#endif
+  for (long h = 0; h < heads; h++)
+    for (long i = 0; i < tokens; i++) {
+      long g = h / group, n = causal ? i + 1 : tokens;
+      double* s = (double*)malloc(sizeof(double) * (size_t)n);
+      double m = -INFINITY, sum = 0;
+      for (long j = 0; j < n; j++) {
+        double dot = 0;
+        for (long d = 0; d < dim; d++) dot += (double)q[(i * heads + h) * dim + d] * k[(j * kv_heads + g) * dim + d];
+        s[j] = dot / sqrt((double)dim);
+        if (s[j] > m) m = s[j];
+      }
+      for (long j = 0; j < n; j++) {
+        s[j] = exp(s[j] - m);
+        sum += s[j];
+      }
+      for (long d = 0; d < dim; d++) {
+        double o = 0;
+        for (long j = 0; j < n; j++) o += (s[j] / sum) * v[(j * kv_heads + g) * dim + d];
+        out[(i * heads + h) * dim + d] = o;
+      }
+      free(s);
+    }
+}

@@ -115,6 +115,12 @@ long or_rope_tables(const long* pos, long tokens, int naxes, const long* axes, d
 void or_rope(const float* x, long tokens, long heads, long pairs, const float* cos_t, const float* sin_t,
              int pairing, double* out);
 
+/* ---- attention (tests/gpu/attention.test.ts:9-31): softmax(q k^T / sqrt(dim)) v per head, GQA kv head
+   = floor(h / (heads / kv_heads)); causal: query i sees keys j <= i. q [tokens, heads, dim], k, v
+   [tokens, kv_heads, dim] -> out [tokens, heads, dim]. */
+void or_attention(const float* q, const float* k, const float* v, long tokens, long heads, long kv_heads, long dim,
+                  int causal, double* out);
+
 #ifdef __cplusplus
 }
 #endif

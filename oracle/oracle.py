@@ -64,6 +64,7 @@ def _load() -> C.CDLL:
     lib.or_rope_tables.restype = C.c_long
     lib.or_rope_tables.argtypes = [p, C.c_long, C.c_int, p, C.c_double, p, p]
     lib.or_rope.argtypes = [p, C.c_long, C.c_long, C.c_long, p, p, C.c_int, p]
+    lib.or_attention.argtypes = [p, p, p, C.c_long, C.c_long, C.c_long, C.c_long, C.c_int, p]
     return lib
 
 
@@ -279,4 +280,12 @@ def rope(x, tokens: int, heads: int, pairs: int, cos, sin, pairing: str = "inter
     out = np.zeros(x.size, dtype=np.float64)
     lib.or_rope(_ptr(x), tokens, heads, pairs, _ptr(_c(cos, np.float32)), _ptr(_c(sin, np.float32)),
                 1 if pairing == "half" else 0, _ptr(out))
+    return out
+
+
+def attention(q, k, v, tokens: int, heads: int, kv_heads: int, dim: int, causal: bool = False) -> np.ndarray:
+    """float64 attention of the reference test (tests/gpu/attention.test.ts:9-31)."""
+    q, k, v = (_c(a, np.float32) for a in (q, k, v))
+    out = np.zeros(tokens * heads * dim, dtype=np.float64)
+    lib.or_attention(_ptr(q), _ptr(k), _ptr(v), tokens, heads, kv_heads, dim, int(causal), _ptr(out))
     return out

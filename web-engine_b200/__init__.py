@@ -5,7 +5,7 @@ mirror of the reference's operator API (src/model/ops.ts over src/gpu/graph.ts) 
 """
 from . import _lib
 from .graph import Binding, Buffer, Graph
-from .ops import Linear, Mod, Rope, k_split_for, linear, no_mod, norm, qk_norm_rotate, rotate
+from .ops import Linear, Mod, Rope, attention, k_split_for, linear, no_mod, norm, qk_norm_rotate, rotate
 from . import kernels, parallel
 from .stream import Streamer
 

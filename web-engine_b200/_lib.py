@@ -109,6 +109,9 @@ _SIGS = {
     "we_quantize_fp8": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, C.c_int32, _P, _P]),
     "we_quantize_int4": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _P, _P]),
     "we_quantize_act": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, C.c_int32, _P, _P, _P]),
+    "we_attention": (C.c_int, [_P, _P, _P, _P, C.c_int32, _I64, _I64, _I64, _I64, C.c_int32, _P, C.c_int32]),
+    "we_attend": (C.c_int, [_P, _P, _P, _P, C.c_int32, _I64, _I64, _I64, _I64, C.c_int32, C.c_int32,
+                            C.POINTER(C.c_void_p)]),
     "we_streamer_create": (C.c_int, [_P, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t), C.c_int32, C.c_int32,
                                      C.c_uint32, C.POINTER(C.c_void_p)]),
     "we_streamer_acquire": (C.c_int, [_P, C.c_int32, C.POINTER(C.c_void_p)]),

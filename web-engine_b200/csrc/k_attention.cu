@@ -1,0 +1,484 @@
+// Attention: softmax(q k^T / sqrt(dim)) v with grouped-query heads, the reference's attention()
+// (src/kernels/attention.ts:20-51: matmul -> softmax -> matmul per head and query chunk; GQA kv head
+// = floor(h / (heads / kvHeads)); optional causal mask for the text encoder).
+//
+// Two kernels:
+//  * attention_simt_kernel: CUDA cores, fp32, one warp per (query, head) with an online softmax over
+//    the keys. The exact path for the reference's f32 buffers (its tests hold 1e-5) and for head
+//    sizes / masks the tensor-core kernel does not take.
+//  * flash_attn_kernel: tcgen05 flash attention for bf16 q/k/v with 128-wide heads, no mask (the DiT
+//    blocks). One CTA = one head x 128 queries. Warp 0 TMA-loads Q once and K / V^T key tiles of 128
+//    into a 2-stage ring; warp 1 issues S = Q K^T into one of two TMEM score buffers and O += P V^T into
+//    a TMEM accumulator; warps 2-5 (one thread per query row) run the online softmax on the scores
+//    (tcgen05.ld), write P as bf16 into shared memory in the UMMA 128-byte-swizzled layout, and rescale
+//    O in TMEM only when a row's running maximum grows by more than 2^8 (the probabilities stay <= 256
+//    in between, which fp32 accumulation and bf16 P hold without loss of relative precision).
+//    V is transposed once per call into [kv_heads, dim, tokens] so both MMAs take K-major operands.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_ptx.cuh"
+
+namespace we {
+
+// ---------------- CUDA-core attention (fp32, exact reference semantics) ----------------
+template <int DT, int OT, int VPL>
+__global__ void __launch_bounds__(128) attention_simt_kernel(const void* __restrict__ q, const void* __restrict__ k,
+                                                             const void* __restrict__ v, int64_t tokens, int64_t heads,
+                                                             int64_t kv_heads, int64_t dim, int causal, float scale,
+                                                             void* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = tokens * heads;
+  const int64_t warps = (int64_t)gridDim.x * 4;
+  const int64_t group = heads / kv_heads;
+  for (int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t i = row / heads, h = row % heads, g = h / group;
+    float qv[VPL], acc[VPL];
+#pragma unroll
+    for (int e = 0; e < VPL; e++) {
+      const int64_t d = lane + 32 * e;
+      qv[e] = d < dim ? load_act<DT>(q, row * dim + d) * scale : 0.f;
+      acc[e] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    const int64_t n = causal ? i + 1 : tokens;
+    for (int64_t j = 0; j < n; j++) {
+      const int64_t kb = (j * kv_heads + g) * dim;
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < VPL; e++) {
+        const int64_t d = lane + 32 * e;
+        if (d < dim) dot = fmaf(qv[e], load_act<DT>(k, kb + d), dot);
+      }
+      const float s = warp_sum(dot);
+      const float mn = fmaxf(m, s);
+      const float corr = expf(m - mn);  // m = -inf on the first key: corr = 0
+      const float p = expf(s - mn);
+      l = l * corr + p;
+#pragma unroll
+      for (int e = 0; e < VPL; e++) {
+        const int64_t d = lane + 32 * e;
+        acc[e] = acc[e] * corr + (d < dim ? p * load_act<DT>(v, kb + d) : 0.f);
+      }
+      m = mn;
+    }
+#pragma unroll
+    for (int e = 0; e < VPL; e++) {
+      const int64_t d = lane + 32 * e;
+      if (d < dim) store_out<OT>(out, row * dim + d, acc[e] / l);
+    }
+  }
+}
+
+// ---------------- V transpose: [tokens, kv_heads, dim] -> [kv_heads, dim, tokens_padded] (bf16) ----------------
+__global__ void transpose_v_kernel(const uint16_t* __restrict__ v, int64_t tokens, int64_t kv_heads, int64_t dim,
+                                   int64_t tp, uint16_t* __restrict__ vt) {
+  __shared__ uint16_t tile[32][33];
+  const int64_t rows = kv_heads * dim;  // output rows
+  const int64_t tx = (int64_t)blockIdx.x * 32, ry = (int64_t)blockIdx.y * 32;
+  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
+    // read: token tx + threadIdx.x... as the fast index of the input is dim, read input rows = tokens
+    const int64_t t = tx + yy, r = ry + threadIdx.x;  // input element (token t, (g, d) = r)
+    uint16_t val = 0;
+    if (t < tokens && r < rows) val = v[t * rows + r];
+    tile[yy][threadIdx.x] = val;
+  }
+  __syncthreads();
+  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
+    const int64_t r = ry + yy, t = tx + threadIdx.x;
+    if (r < rows && t < tp) vt[r * tp + t] = tile[threadIdx.x][yy];
+  }
+}
+
+// ---------------- tcgen05 flash attention ----------------
+namespace fa {
+constexpr int BQ = 128, BK = 128, D = 128;
+constexpr int ATOM = 128 * 128;          // one 128-row x 128-byte swizzle-128B atom (64 bf16 per row)
+constexpr int Q_BYTES = 2 * ATOM;        // 128 queries x 128 dims
+constexpr int K_BYTES = 2 * ATOM;        // 128 keys x 128 dims
+constexpr int V_BYTES = 2 * ATOM;        // 128 dims x 128 keys (V^T)
+constexpr int P_BYTES = 2 * ATOM;        // 128 queries x 128 keys
+constexpr int STAGES = 2;
+constexpr int Q_OFF = 0;
+constexpr int KV_OFF = Q_OFF + Q_BYTES;
+constexpr int KV_STAGE = K_BYTES + V_BYTES;
+constexpr int P_OFF = KV_OFF + STAGES * KV_STAGE;
+constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
+// barriers: q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain
+constexpr int NUM_BARS = 1 + 2 * 6 + 1;
+constexpr int TOTAL = BAR_OFF + NUM_BARS * 8 + 16;
+constexpr int ALLOC = TOTAL + 1024;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+constexpr uint32_t O_COL = 256;
+// kind::f16, bf16 x bf16 -> f32, K-major A and B, N = 128, M = 128
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr float RESCALE_LOG2 = 8.f;  // rescale O only when a row maximum grows by more than 2^8
+
+struct Params {
+  int64_t tokens, heads, kv_heads;
+  float scale_log2;  // log2(e) / sqrt(dim)
+  void* out;
+  int out_dtype;
+  uint32_t* err;
+};
+}  // namespace fa
+
+__global__ void __launch_bounds__(fa::THREADS, 1)
+    flash_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_vt, const fa::Params p) {
+  using namespace tc;
+  using namespace fa;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + BAR_OFF;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + BAR_OFF + NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const uint32_t Q_FULL = bars;
+#define KV_FULL(s) (bars + 8u * (1 + (s)))
+#define KV_EMPTY(s) (bars + 8u * (3 + (s)))
+#define S_FULL(b) (bars + 8u * (5 + (b)))
+#define S_FREE(b) (bars + 8u * (7 + (b)))
+#define P_FULL(b) (bars + 8u * (9 + (b)))
+#define PV_DONE(b) (bars + 8u * (11 + (b)))
+#define DRAIN (bars + 8u * 13)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t q0 = (int64_t)blockIdx.x * BQ;
+  const int64_t h = blockIdx.y;
+  const int64_t g = h / (p.heads / p.kv_heads);
+  const int nt = (int)((p.tokens + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    mbar_init(Q_FULL, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(KV_FULL(i), 1);
+      mbar_init(KV_EMPTY(i), 1);
+      mbar_init(S_FULL(i), 1);
+      mbar_init(S_FREE(i), 4);
+      mbar_init(P_FULL(i), 4);
+      mbar_init(PV_DONE(i), 1);
+    }
+    mbar_init(DRAIN, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(Q_FULL, Q_BYTES);
+      tma_load_2d(sbase + Q_OFF, &tm_q, Q_FULL, (int32_t)(h * D), (int32_t)q0);
+      tma_load_2d(sbase + Q_OFF + ATOM, &tm_q, Q_FULL, (int32_t)(h * D + 64), (int32_t)q0);
+      int issued = 0;
+      for (int j = 0; j < nt && ok; j++) {
+        const int s = j & 1;
+        if (!wait_bounded(KV_EMPTY(s), ((j >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
+                          WAIT_LIMIT_NS, true)) {
+          ok = false;
+          break;
+        }
+        const uint32_t st = sbase + KV_OFF + s * KV_STAGE;
+        mbar_expect_tx(KV_FULL(s), KV_STAGE);
+        const int32_t j0 = j * BK;
+        tma_load_2d(st, &tm_k, KV_FULL(s), (int32_t)(g * D), j0);
+        tma_load_2d(st + ATOM, &tm_k, KV_FULL(s), (int32_t)(g * D + 64), j0);
+        tma_load_2d(st + K_BYTES, &tm_vt, KV_FULL(s), j0, (int32_t)(g * D));
+        tma_load_2d(st + K_BYTES + ATOM, &tm_vt, KV_FULL(s), j0 + 64, (int32_t)(g * D));
+        issued = j + 1;
+      }
+      if (!ok) {  // the copies already issued land before the CTA exits
+        wait_bounded(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+        for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; j++)
+          wait_bounded(KV_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = wait_bounded(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true);
+      tc_fence_after();
+      const uint64_t qdesc = sw128_desc(sbase + Q_OFF);
+      // O += P_j V_j^T for tile j (P in buffer j & 1, V^T in KV stage j & 1)
+      auto pv = [&](int j) -> bool {
+        const int b = j & 1;
+        if (!wait_bounded(P_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
+          return false;
+        tc_fence_after();
+        const uint64_t pdesc = sw128_desc(sbase + P_OFF + b * P_BYTES);
+        const uint64_t vdesc = sw128_desc(sbase + KV_OFF + (j & 1) * KV_STAGE + K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {  // K = 128 keys: two 64-key atoms, 4 MMAs of 16 each
+          const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
+          umma<true>(tmem + O_COL, pdesc + off, vdesc + off, IDESC, (j | kk) != 0);
+        }
+        umma_commit(KV_EMPTY(j & 1));
+        umma_commit(PV_DONE(b));
+        return true;
+      };
+      for (int j = 0; j < nt && ok; j++) {
+        const int s = j & 1, b = j & 1;
+        if (!wait_bounded(KV_FULL(s), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
+            !wait_bounded(S_FREE(b), ((j >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t kdesc = sw128_desc(sbase + KV_OFF + s * KV_STAGE);
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {  // K = 128 dims
+          const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
+          umma<true>(tmem + (uint32_t)(b * 128), qdesc + off, kdesc + off, IDESC, kk != 0);
+        }
+        umma_commit(S_FULL(b));
+        if (j > 0 && !pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && nt > 0) pv(nt - 1);
+      // every MMA this thread issued completes before TMEM is freed
+      umma_commit(DRAIN);
+      wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+    }
+    __syncwarp();
+  } else {
+    // softmax: thread = query row r of this CTA, TMEM lane r
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; j++) {
+      const int b = j & 1;
+      ok = wait_bounded(S_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float t[BK];
+#pragma unroll
+      for (int c = 0; c < BK / 32; c++) {
+        uint32_t u[32];
+        tmem_ld32(tmem + lane_addr + (uint32_t)(b * 128 + c * 32), u);
+#pragma unroll
+        for (int e = 0; e < 32; e++) t[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(S_FREE(b));
+      const int64_t valid = p.tokens - (int64_t)j * BK;  // keys of this tile that exist
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BK; c++) {
+        if (c >= valid) t[c] = -INFINITY;
+        mt = fmaxf(mt, t[c]);
+      }
+      float corr = 1.f;
+      const bool grow = mt > m_used + RESCALE_LOG2;
+      if (grow) {
+        corr = exp2f(m_used - mt);  // 0 on the first tile
+        l *= corr;
+        m_used = mt;
+      }
+      float sum = 0.f;
+      // P buffer b was last read by PV_{j-2}
+      if (j >= 2) {
+        ok = wait_bounded(PV_DONE(b), ((j - 2) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS,
+                          true);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+      }
+      uint8_t* prow = smem + P_OFF + b * P_BYTES + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 16; ch++) {  // 16 chunks of 8 keys; chunk ch lives in atom ch / 8
+        float e8[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          e8[e] = exp2f(t[ch * 8 + e] - m_used);
+          sum += e8[e];
+        }
+        const uint4 packed = make_uint4(pack_bf16x2(e8[0], e8[1]), pack_bf16x2(e8[2], e8[3]),
+                                        pack_bf16x2(e8[4], e8[5]), pack_bf16x2(e8[6], e8[7]));
+        *reinterpret_cast<uint4*>(prow + (ch >> 3) * ATOM + (((ch & 7) ^ (r & 7)) << 4)) = packed;
+      }
+      l += sum;
+      // O was scaled for the old maximum: bring it to the new one before PV_j adds to it
+      if (__any_sync(0xffffffffu, grow && j > 0)) {
+        ok = wait_bounded(PV_DONE((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE,
+                          WAIT_LIMIT_NS, true);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = (grow && j > 0) ? corr : 1.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; c++) {
+          uint32_t u[32];
+          tmem_ld32(tmem + lane_addr + O_COL + (uint32_t)(c * 32), u);
+#pragma unroll
+          for (int e = 0; e < 32; e++) u[e] = __float_as_uint(__uint_as_float(u[e]) * f);
+          tmem_st32(tmem + lane_addr + O_COL + (uint32_t)(c * 32), u);
+        }
+        tmem_st_wait();
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P stores -> visible to the tensor core
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(P_FULL(b));
+    }
+    if (ok && nt > 0) {
+      ok = wait_bounded(PV_DONE((nt - 1) & 1), ((nt - 1) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE,
+                        WAIT_LIMIT_NS, true);
+      if (__all_sync(0xffffffffu, ok)) {
+        tc_fence_after();
+        const int64_t qi = q0 + r;
+        const float inv = 1.f / l;
+#pragma unroll
+        for (int c = 0; c < D / 32; c++) {
+          uint32_t u[32];
+          tmem_ld32(tmem + lane_addr + O_COL + (uint32_t)(c * 32), u);
+          if (qi < p.tokens) {
+            const int64_t o = (qi * p.heads + h) * D + c * 32;
+            if (p.out_dtype == WE_BF16) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + o);
+#pragma unroll
+              for (int e = 0; e < 4; e++)
+                dst[e] = make_uint4(pack_bf16x2(__uint_as_float(u[8 * e]) * inv, __uint_as_float(u[8 * e + 1]) * inv),
+                                    pack_bf16x2(__uint_as_float(u[8 * e + 2]) * inv, __uint_as_float(u[8 * e + 3]) * inv),
+                                    pack_bf16x2(__uint_as_float(u[8 * e + 4]) * inv, __uint_as_float(u[8 * e + 5]) * inv),
+                                    pack_bf16x2(__uint_as_float(u[8 * e + 6]) * inv, __uint_as_float(u[8 * e + 7]) * inv));
+            } else {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + o);
+#pragma unroll
+              for (int e = 0; e < 8; e++)
+                dst[e] = make_float4(__uint_as_float(u[4 * e]) * inv, __uint_as_float(u[4 * e + 1]) * inv,
+                                     __uint_as_float(u[4 * e + 2]) * inv, __uint_as_float(u[4 * e + 3]) * inv);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+#undef KV_FULL
+#undef KV_EMPTY
+#undef S_FULL
+#undef S_FREE
+#undef P_FULL
+#undef PV_DONE
+#undef DRAIN
+}
+
+// ---------------- host side ----------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_attn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2D bf16 map over [rows, cols] (row stride in bytes) with 64 x 128 boxes and 128-byte swizzle
+static bool bf16_map(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int64_t stride_bytes) {
+  auto fn = encode_fn_attn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)stride_bytes};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool flash_attention_supported(const AttnArgs& a) {
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  return a.dtype == WE_BF16 && a.dim == 128 && !a.causal && a.tokens >= 1 && al(a.q) && al(a.k) && al(a.v) &&
+         al(a.out) && a.heads % a.kv_heads == 0 && a.tokens <= 0x7fffffffLL;
+}
+
+int64_t flash_attention_scratch_bytes(const AttnArgs& a) {
+  const int64_t tp = (a.tokens + 7) / 8 * 8;
+  return a.kv_heads * a.dim * tp * 2;
+}
+
+cudaError_t launch_flash_attention(const AttnArgs& a, void* vt_scratch, uint32_t* err, cudaStream_t st) {
+  const int64_t tp = (a.tokens + 7) / 8 * 8;
+  {
+    dim3 blk(32, 8), grd((unsigned)((tp + 31) / 32), (unsigned)((a.kv_heads * a.dim + 31) / 32));
+    transpose_v_kernel<<<grd, blk, 0, st>>>(static_cast<const uint16_t*>(a.v), a.tokens, a.kv_heads, a.dim, tp,
+                                            static_cast<uint16_t*>(vt_scratch));
+  }
+  CUtensorMap mq, mk, mv;
+  if (!bf16_map(&mq, a.q, a.heads * a.dim, a.tokens, a.heads * a.dim * 2) ||
+      !bf16_map(&mk, a.k, a.kv_heads * a.dim, a.tokens, a.kv_heads * a.dim * 2) ||
+      !bf16_map(&mv, vt_scratch, tp, a.kv_heads * a.dim, tp * 2))
+    return cudaErrorNotSupported;
+  fa::Params p;
+  p.tokens = a.tokens;
+  p.heads = a.heads;
+  p.kv_heads = a.kv_heads;
+  p.scale_log2 = 1.4426950408889634f / sqrtf((float)a.dim);
+  p.out = a.out;
+  p.out_dtype = a.out_dtype;
+  p.err = err;
+  cudaError_t e = cudaFuncSetAttribute(flash_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::ALLOC);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((a.tokens + fa::BQ - 1) / fa::BQ), (unsigned)a.heads);
+  flash_attn_kernel<<<grid, fa::THREADS, fa::ALLOC, st>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention_simt(const AttnArgs& a, int sms, cudaStream_t st) {
+  const int64_t rows = a.tokens * a.heads;
+  int64_t g = (rows + 3) / 4;
+  if (g > (int64_t)sms * 16) g = (int64_t)sms * 16;
+  const float scale = 1.f / sqrtf((float)a.dim);
+  const int vpl = (int)((a.dim + 31) / 32);
+#define ATT_CASE(V)                                                                                                 \
+  if (vpl <= V) {                                                                                                   \
+    if (a.dtype == WE_BF16 && a.out_dtype == WE_BF16)                                                               \
+      attention_simt_kernel<WE_BF16, WE_BF16, V><<<(unsigned)g, 128, 0, st>>>(a.q, a.k, a.v, a.tokens, a.heads,     \
+                                                                             a.kv_heads, a.dim, a.causal, scale, a.out); \
+    else if (a.dtype == WE_BF16)                                                                                    \
+      attention_simt_kernel<WE_BF16, WE_F32, V><<<(unsigned)g, 128, 0, st>>>(a.q, a.k, a.v, a.tokens, a.heads,      \
+                                                                            a.kv_heads, a.dim, a.causal, scale, a.out); \
+    else if (a.out_dtype == WE_BF16)                                                                                \
+      attention_simt_kernel<WE_F32, WE_BF16, V><<<(unsigned)g, 128, 0, st>>>(a.q, a.k, a.v, a.tokens, a.heads,      \
+                                                                            a.kv_heads, a.dim, a.causal, scale, a.out); \
+    else                                                                                                            \
+      attention_simt_kernel<WE_F32, WE_F32, V><<<(unsigned)g, 128, 0, st>>>(a.q, a.k, a.v, a.tokens, a.heads,       \
+                                                                           a.kv_heads, a.dim, a.causal, scale, a.out); \
+    return cudaGetLastError();                                                                                      \
+  }
+  ATT_CASE(1)
+  ATT_CASE(2)
+  ATT_CASE(4)
+  ATT_CASE(8)
+#undef ATT_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace we

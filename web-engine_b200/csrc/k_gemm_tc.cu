@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_ptx.cuh"
 
 namespace we {
 namespace tc {
@@ -30,8 +31,6 @@ namespace tc {
 constexpr int BM = 128;           // weight rows per tile (UMMA M)
 constexpr int KB_BYTES = 128;     // K bytes per stage
 constexpr int THREADS = 192;
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
-constexpr uint64_t DRAIN_LIMIT_NS = 200000000ull;
 constexpr int EPI_LD = 36;  // floats per row of an epilogue warp's 32 x 32 staging tile (pad: no bank conflicts)
 constexpr int EPI_BYTES = 4 * 32 * EPI_LD * 4;
 constexpr int SMEM_BUDGET = 207 * 1024;  // for the stage ring; + epilogue staging + barriers <= 227 KB
@@ -65,114 +64,10 @@ struct Layout {
   static_assert(STAGES >= 2, "shared-memory ring needs at least 2 stages");
 };
 
-// ---------------- PTX wrappers ----------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: true when the phase of `parity` completed; false on timeout (records `code`, raises the
-// CTA's abort flag) or when another role already aborted (if watch_abort).
-__device__ __noinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint32_t* err,
-                                          uint32_t code, uint64_t limit_ns, bool watch_abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31) == 0) {
-      if (watch_abort && *abort_flag) return false;
-      if (global_timer_ns() - t0 > limit_ns) {
-        atomicCAS(err, 0u, code);
-        *abort_flag = 1;
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t c0, int32_t c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t holder, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder), "r"(ncols) : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// K-major operand in shared memory written by TMA with SWIZZLE_128B: rows of 128 bytes, 8-row groups
-// 1024 bytes apart (SBO), LBO unused (1), descriptor version 1 (sm_100), layout type 2 (128B swizzle).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)(1024 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Instruction descriptor: D f32, A/B formats (f8f6f4: 0 = E4M3; f16: 1 = BF16), both K-major,
-// N = BT (bits 17-22, N >> 3), M = 128 (bits 24-28, M >> 4).
 template <int BT, bool F16>
 __host__ __device__ constexpr uint32_t make_idesc() {
   return (1u << 4) | ((F16 ? 1u : 0u) << 7) | ((F16 ? 1u : 0u) << 10) | ((uint32_t)(BT >> 3) << 17) |
          ((uint32_t)(BM >> 4) << 24);
-}
-
-template <bool F16>
-__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-  if constexpr (F16) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-  } else {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-  }
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Epilogue of one 32-token chunk of a warp's 32 channels: scale by the row scale (one coalesced load,

@@ -64,4 +64,19 @@ cudaError_t launch_qknorm_rope(const void* x, int xdt, const float* w, float eps
                                const float* sn, int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out,
                                int odt, int sms, cudaStream_t st);
 
+// attention(q [T, H, D], k, v [T, Hkv, D]) -> out [T, H, D]
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int64_t tokens, heads, kv_heads, dim;
+  int causal;
+  int dtype, out_dtype;
+};
+bool flash_attention_supported(const AttnArgs& a);
+int64_t flash_attention_scratch_bytes(const AttnArgs& a);
+cudaError_t launch_flash_attention(const AttnArgs& a, void* vt_scratch, uint32_t* err, cudaStream_t st);
+cudaError_t launch_attention_simt(const AttnArgs& a, int sms, cudaStream_t st);
+
 }  // namespace we

@@ -600,6 +600,40 @@ int we_positions(int64_t text, int64_t rows, int64_t cols, int64_t* pos) {
   return WE_OK;
 }
 
+// ---------------- attention ----------------
+int we_attention(we_ctx* ctx, const void* q, const void* k, const void* v, int32_t dtype, int64_t tokens, int64_t heads,
+                 int64_t kv_heads, int64_t dim, int32_t causal, void* out, int32_t out_dtype) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(dtype) || !act_dtype_ok(out_dtype)) return fail(ctx, WE_EINVAL, "q/k/v and out must be f32 or bf16");
+  if (kv_heads <= 0 || heads % kv_heads) return fail(ctx, WE_EINVAL, "heads must be a multiple of kvHeads");
+  if (dim <= 0 || dim > 256) return fail(ctx, WE_EINVAL, "dim must be in 1..256");
+  if (tokens <= 0 || heads <= 0) return WE_OK;
+  we::AttnArgs a{q, k, v, out, tokens, heads, kv_heads, dim, causal ? 1 : 0, dtype, out_dtype};
+  if (we::flash_attention_supported(a)) {
+    Scratch scratch(ctx);
+    void* vt;
+    int rc = scratch.take((size_t)we::flash_attention_scratch_bytes(a), &vt);
+    if (rc != WE_OK) return rc;
+    cudaError_t e = we::launch_flash_attention(a, vt, ctx->dev_err, ctx->stream);
+    if (e == cudaSuccess) {
+      ctx->stats.launches += 2;
+      return WE_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_fail(ctx, e, "flash attention");
+  }
+  LK(we::launch_attention_simt(a, ctx->sms, ctx->stream), "attention");
+  return WE_OK;
+}
+
+int we_attend(we_ctx* ctx, const void* q, const void* k, const void* v, int32_t dtype, int64_t tokens, int64_t heads,
+              int64_t kv_heads, int64_t dim, int32_t causal, int32_t out_dtype, void** out) {
+  if (!ctx || !out) return WE_EINVAL;
+  if (kv_heads <= 0 || heads % kv_heads) return fail(ctx, WE_EINVAL, "heads must be a multiple of kvHeads");
+  int rc = op_output(ctx, (size_t)(tokens * heads * dim) * dsize(out_dtype), out);
+  if (rc != WE_OK) return rc;
+  return we_attention(ctx, q, k, v, dtype, tokens, heads, kv_heads, dim, causal, *out, out_dtype);
+}
+
 // ---------------- unpack / quantise ----------------
 int we_unpack_fp8(we_ctx* ctx, const uint8_t* bytes, int64_t n, float scale, float* out) {
   if (!ctx) return WE_EINVAL;

@@ -221,3 +221,10 @@ def unpack_fp8_bf16(graph: Graph, data, n: int, out) -> None:
 
 def unpack_int4(graph: Graph, packed, scales, n: int, k: int, out) -> None:
     L.check(graph.ctx, L.lib().we_unpack_int4(graph.ctx, addr(packed), addr(scales), n, k, addr(out)))
+
+
+def attention(graph: Graph, q, k, v, tokens: int, heads: int, kv_heads: int, dim: int, out, causal: bool = False,
+              dtype: str = "f32", out_dtype: str = "f32") -> None:
+    """attention into a given output buffer (src/kernels/attention.ts:20-51)."""
+    L.check(graph.ctx, L.lib().we_attention(graph.ctx, addr(q), addr(k), addr(v), L.DTYPES[dtype], tokens, heads,
+                                            kv_heads, dim, int(causal), addr(out), L.DTYPES[out_dtype]))

@@ -131,3 +131,15 @@ def qk_norm_rotate(graph: Graph, x, weight, heads: int, rope: Rope, eps: float =
                                               addr(rope.cos), addr(rope.sin), rope.tokens, heads, rope.pairs, p,
                                               addr(out), L.DTYPES[out_dtype]))
     return out
+
+
+def attention(graph: Graph, q, k, v, tokens: int, heads: int, kv_heads: int, dim: int, causal: bool = False,
+              chunk: int | None = None, dtype: str = "f32", out_dtype: str | None = None) -> Buffer:
+    """attention(graph, q, k, v, shape) (src/kernels/attention.ts:20-51): softmax(q k^T / sqrt(dim)) v with
+    grouped-query heads; q [tokens, heads, dim], k, v [tokens, kv_heads, dim] -> a new [tokens, heads, dim].
+    `chunk` only bounded the reference's score memory; the kernels here keep no score matrix."""
+    od = out_dtype or dtype
+    out = C.c_void_p()
+    L.check(graph.ctx, L.lib().we_attend(graph.ctx, addr(q), addr(k), addr(v), L.DTYPES[dtype], tokens, heads,
+                                         kv_heads, dim, int(causal), L.DTYPES[od], C.byref(out)))
+    return Buffer(out.value, tokens * heads * dim * L.DTYPE_BYTES[L.DTYPES[od]])
