@@ -95,6 +95,23 @@ enum {
                                  per-element activation error) instead of the exact two-term split */
   WE_MM_FORCE_SIMT = 1u << 2  /* use the CUDA-core kernel even where the tensor-core kernel applies */
 };
+/* Epilogue operations fused into a matmul (the per-value steps of a block, src/kernels/elementwise.ts:38-84),
+   applied to v = x . W^T * scale + bias in this order:
+     act:    WE_ACT_GELU_TANH (geluTanh) | WE_ACT_SILU (silu) | WE_ACT_NONE
+     aux_op: WE_AUX_SIGMOID_GATE  v = aux * sigmoid(v)  (sigmoidGate with this matmul as the gate)
+             WE_AUX_SWIGLU        v = silu(aux) * v     (swiglu with this matmul as "up", aux = gate)
+             aux: [m, n] in aux_dtype with y's row stride
+     gate:   v = gate[col] * v                          (gatedAdd's g, with WE_MM_ACCUMULATE: y += g h)
+   A zero-initialised we_epilogue does nothing. */
+enum { WE_ACT_NONE = 0, WE_ACT_GELU_TANH = 1, WE_ACT_SILU = 2 };
+enum { WE_AUX_NONE = 0, WE_AUX_SIGMOID_GATE = 1, WE_AUX_SWIGLU = 2 };
+typedef struct {
+  int32_t act;
+  int32_t aux_op;
+  int32_t aux_dtype; /* WE_F32 | WE_BF16 */
+  const void* aux;
+  const float* gate;
+} we_epilogue;
 typedef struct {
   int64_t m, n, k;
   /* Row strides and offsets in values (matmul.ts:185-195). 0 stride = contiguous (k, k, n). */
@@ -108,6 +125,7 @@ typedef struct {
   int32_t w_dtype;          /* WE_F32 | WE_BF16 | WE_FP8 | WE_INT4G64 */
   int32_t y_dtype;          /* WE_F32 | WE_BF16 */
   uint32_t flags;           /* WE_MM_* */
+  we_epilogue epi;          /* fused per-value steps (zero = none) */
 } we_matmul_desc;
 /* y[m, n] = x[m, k] . W^T * scale (+ bias) with W [n, k] like nn.Linear. Validation as matmulParams
    (matmul.ts:205-207): "K must be a multiple of 4, got 6" etc. Replaces matmulWgsl/matmulParams/
@@ -132,6 +150,7 @@ typedef struct {
   int64_t y_stride; /* values; 0 = n */
   int32_t y_dtype;  /* WE_F32 | WE_BF16 */
   uint32_t flags;   /* WE_MM_ACCUMULATE */
+  we_epilogue epi;  /* fused per-value steps (zero = none) */
 } we_gemm_fp8_desc;
 int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* desc);
 /* kSplitFor (src/model/ops.ts:42-45). */
@@ -216,6 +235,30 @@ int we_quantize_int4(we_ctx* ctx, const void* w, int32_t w_dtype, int64_t n, int
    row_scale[m] = 2^e. lo may be NULL when terms = 1. */
 int we_quantize_act(we_ctx* ctx, const void* x, int32_t x_dtype, int64_t m, int64_t k, int64_t x_stride,
                     int32_t terms, uint8_t* hi, uint8_t* lo, float* row_scale);
+
+/* ---------------- elementwise (src/kernels/elementwise.ts:38-84, ops.ts:95-113) ----------------
+   out[i] = swiglu: silu(a) b | sigmoidGate: a sigmoid(b) | gatedAdd: a + g[i % d] b | addBias: a + g[i % d]
+          | geluTanh: GELU(a), tanh form | add: a + b | silu: a sigmoid(a), over n values (b, g unused where
+   the formula has none). */
+enum {
+  WE_EW_SWIGLU = 0,
+  WE_EW_SIGMOID_GATE = 1,
+  WE_EW_GATED_ADD = 2,
+  WE_EW_ADD_BIAS = 3,
+  WE_EW_GELU_TANH = 4,
+  WE_EW_ADD = 5,
+  WE_EW_SILU = 6
+};
+int we_elementwise(we_ctx* ctx, int32_t op, const void* a, const void* b, const float* g, int64_t n, int64_t d,
+                   int32_t dtype, void* out, int32_t out_dtype);
+/* The op form (ops.ts elementwise()): out is a new pooled buffer of n values. */
+int we_ew(we_ctx* ctx, int32_t op, const void* a, const void* b, const float* g, int64_t n, int64_t d, int32_t dtype,
+          int32_t out_dtype, void** out);
+/* norm() followed by the e4m3 activation split of its bf16-rounded output, in one pass: the planes and row
+   scales equal we_rmsnorm(out_dtype = bf16) then we_quantize_act. d % 8 == 0, d <= 6144, 16-byte aligned. */
+int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, const float* scale,
+                  const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
+                  uint8_t* lo, float* row_scale);
 
 /* ---------------- attention: attention() (src/kernels/attention.ts:20-51) ----------------
    softmax(q k^T / sqrt(dim)) v per head with grouped-query heads (query head h uses kv head

@@ -289,3 +289,62 @@ def attention(q, k, v, tokens: int, heads: int, kv_heads: int, dim: int, causal:
     out = np.zeros(tokens * heads * dim, dtype=np.float64)
     lib.or_attention(_ptr(q), _ptr(k), _ptr(v), tokens, heads, kv_heads, dim, int(causal), _ptr(out))
     return out
+
+
+def block_reference(x, w: dict, cfg: dict, temb, cos, sin) -> np.ndarray:
+    """float64 block of the reference test (tests/gpu/block.test.ts:26-100), restated with numpy from the
+    formulas: fp8 linears with a scalar or per-channel scale, zero-centred norms (offset 1), GQA attention
+    with an optional sigmoid gate, and a SwiGLU or tanh-GELU MLP. w holds host arrays: linears as dicts
+    {"bytes", "n", "k", "scale" | "chan_scale"}, norms f32, table f32 [6 hidden]."""
+    t, hid, heads, kvh, hd = x.shape[0], cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+    eps = cfg.get("eps", 1e-5)
+    e4 = e4m3_table()
+
+    def mm(a, lin):
+        wv = e4[lin["bytes"]].reshape(lin["n"], lin["k"])
+        y = a @ wv.T
+        return y * (lin["chan_scale"].astype(np.float64) if lin.get("chan_scale") is not None else lin["scale"])
+
+    def rms(a, wt, rows, d, sc=None, sh=None):
+        a = a.reshape(rows, d)
+        inv = 1.0 / np.sqrt((a * a).sum(1) / d + eps)
+        y = a * inv[:, None] * (1.0 + wt.astype(np.float64))
+        if sc is not None:
+            y = y * (1.0 + sc) + sh
+        return y
+
+    def rope_np(a, tokens, nh):
+        pairs = hd // 2
+        a = a.reshape(tokens, nh, pairs, 2)
+        c = cos.reshape(tokens, 1, pairs).astype(np.float64)
+        s = sin.reshape(tokens, 1, pairs).astype(np.float64)
+        out = np.empty_like(a)
+        out[..., 0] = a[..., 0] * c - a[..., 1] * s
+        out[..., 1] = a[..., 1] * c + a[..., 0] * s
+        return out.reshape(tokens, nh * hd)
+
+    x = x.astype(np.float64)
+    mod = [(temb[i * hid:(i + 1) * hid].astype(np.float64) + w["table"][i * hid:(i + 1) * hid]) for i in range(6)]
+    prescale, preshift, pregate, postscale, postshift, postgate = mod
+    h = rms(x, w["norm1"], t, hid, prescale, preshift)
+    q = rope_np(rms(mm(h, w["wq"]), w["norm_q"], t * heads, hd), t, heads).reshape(t, heads, hd)
+    k = rope_np(rms(mm(h, w["wk"]), w["norm_k"], t * kvh, hd), t, kvh).reshape(t, kvh, hd)
+    v = mm(h, w["wv"]).reshape(t, kvh, hd)
+    o = np.empty((t, heads, hd))
+    for hh in range(heads):
+        g = hh // (heads // kvh)
+        s = q[:, hh] @ k[:, g].T / np.sqrt(hd)
+        p = np.exp(s - s.max(1, keepdims=True))
+        o[:, hh] = (p / p.sum(1, keepdims=True)) @ v[:, g]
+    o = o.reshape(t, hid)
+    if cfg.get("attn_gate", True):
+        o = o / (1.0 + np.exp(-mm(h, w["gate"])))
+    x1 = x + pregate * mm(o, w["wo"])
+    h2 = rms(x1, w["norm2"], t, hid, postscale, postshift)
+    if cfg.get("mlp_act", "swiglu") == "swiglu":
+        gg = mm(h2, w["mlp_gate"])
+        m = gg / (1.0 + np.exp(-gg)) * mm(h2, w["mlp_up"])
+    else:
+        u = mm(h2, w["mlp_up"])
+        m = 0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))
+    return x1 + postgate * mm(m, w["mlp_down"])

@@ -1,0 +1,188 @@
+"""The per-value ops, the GEMM-epilogue fusions, RMSNorm + split, and a whole block on the GPU.
+
+Elementwise ops mirror tests/gpu/elementwise.test.ts (same tolerances). The block is checked against a
+float64 restatement of tests/gpu/block.test.ts:26-100: in f32 on its tiny GQA config with the reference's
+tolerance (cosine > 0.99999, relErr < 1e-4); in bf16 (fused B200 path: norm + split, fp8 tcgen05 GEMMs with
+fused epilogues, q/k norm + RoPE, flash attention) on 128-wide heads with SwiGLU and GELU MLPs, where the
+block's update (out - x) must reach cosine >= 0.9999 and max-abs-rel < 1e-2.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from util import bf16, bf16_round, fast_fp8, lcg_floats, randn
+
+pytestmark = pytest.mark.gpu
+
+
+def sigmoid(v):
+    return 1.0 / (1.0 + np.exp(-v.astype(np.float64)))
+
+
+def gelu(v):
+    v = v.astype(np.float64)
+    return 0.5 * v * (1.0 + np.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))
+
+
+def ew(we, graph, op, a, b=None, g=None, d=1, dtype="f32"):
+    mark = graph.mark()
+    try:
+        conv = bf16 if dtype == "bf16" else (lambda z: np.asarray(z, np.float32))
+        ab = graph.buffer(conv(a))
+        bb = graph.buffer(conv(b)) if b is not None else None
+        gb = graph.buffer(np.asarray(g, np.float32)) if g is not None else None
+        out = we.ops.elementwise(graph, op, ab, bb, a.size, g=gb, d=d, dtype=dtype, out_dtype="f32")
+        return graph.read(out, a.size * 4, np.float32).copy()
+    finally:
+        graph.release(mark)
+
+
+def test_elementwise_ops_match_the_reference_formulas(we, graph):  # tests/gpu/elementwise.test.ts:15-37
+    n, d = 1000, 40
+    a, b = lcg_floats(n, 1, 8.0), lcg_floats(n, 2, 8.0)
+    g = lcg_floats(d, 7, 1.0)
+    af, bf = a.astype(np.float64), b.astype(np.float64)
+    assert np.max(np.abs(ew(we, graph, "swiglu", a, b) - af * sigmoid(a) * bf)) < 1e-4
+    assert np.max(np.abs(ew(we, graph, "sigmoid_gate", a, b) - af * sigmoid(b))) < 1e-5
+    gi = g[np.arange(n) % d].astype(np.float64)
+    assert np.max(np.abs(ew(we, graph, "gated_add", a, b, g=g, d=d) - (af + gi * bf))) < 1e-5
+    assert np.max(np.abs(ew(we, graph, "add_bias", a, g=g, d=d) - (af + gi))) < 1e-5
+    assert np.max(np.abs(ew(we, graph, "add", a, b) - (af + bf))) < 1e-5
+    assert np.max(np.abs(ew(we, graph, "gelu_tanh", a) - gelu(a))) < 1e-5
+    assert np.max(np.abs(ew(we, graph, "silu", a) - af * sigmoid(a))) < 1e-5
+    # ragged length with bf16 inputs: the tail path and the 8-wide path agree
+    x = bf16_round(randn(1003, 3, 4.0))
+    y = bf16_round(randn(1003, 4, 4.0))
+    assert np.max(np.abs(ew(we, graph, "swiglu", x, y, dtype="bf16") - x * sigmoid(x) * y)) < 1e-4
+
+
+@pytest.mark.parametrize("rows,d,xdt", [(300, 3072, "bf16"), (64, 512, "f32"), (17, 136, "f32")])
+def test_norm_split_equals_norm_then_split(we, graph, rows, d, xdt):
+    x = randn(rows * d, 11, 2.0)
+    if xdt == "bf16":
+        x = bf16_round(x)
+    w, sc, sh = randn(d, 12, 0.1), randn(d, 13, 0.3), randn(d, 14, 0.3)
+    mark = graph.mark()
+    xb = graph.buffer(bf16(x) if xdt == "bf16" else x)
+    wb, scb, shb = graph.buffer(w), graph.buffer(sc), graph.buffer(sh)
+    h = graph.buffer(rows * d * 2)
+    we.kernels.rmsnorm(graph, xb, wb, rows, d, h, scb, shb, x_dtype=xdt, out_dtype="bf16")
+    a = [graph.buffer(rows * d), graph.buffer(rows * d), graph.buffer(rows * 4)]
+    we.kernels.quantize_act(graph, h, rows, d, *a, terms=2)
+    b = [graph.buffer(rows * d), graph.buffer(rows * d), graph.buffer(rows * 4)]
+    we.kernels.norm_split(graph, xb, wb, rows, d, *b, scale=scb, shift=shb, x_dtype=xdt)
+    planes = [graph.read(buf, nb).copy() for buf, nb in zip(a + b, (rows * d, rows * d, rows * 4) * 2)]
+    graph.release(mark)
+    e4 = O.e4m3_table()
+    recon = [(e4[hi] + e4[lo]).reshape(rows, d) * rs.view(np.float32)[:, None]
+             for hi, lo, rs in (planes[:3], planes[3:])]
+    if xdt == "bf16":  # same row reduction as the bf16 RMSNorm kernel: identical bits
+        for u, v in zip(planes[:3], planes[3:]):
+            assert np.array_equal(u, v)
+    else:  # f32 rows: the two kernels sum the squares in different orders; a rare 1-ulp bf16 difference
+        diff = np.abs(recon[0] - recon[1])
+        assert np.all(diff <= np.abs(recon[0]) * 2.0 ** -7 + 1e-30)
+        assert np.mean(diff == 0) > 0.999
+
+
+@pytest.mark.parametrize("path", ["tc", "simt"])
+def test_gemm_epilogue_fusions(we, graph, path):
+    m, n, k = 150, 264, 256
+    x = bf16_round(randn(m * k, 21))
+    w = fast_fp8(n * k, 22)
+    cs = (np.abs(randn(n, 23, 0.004)) + np.float32(1e-3)).astype(np.float32)
+    aux = bf16_round(randn(m * n, 24, 2.0))
+    gate = randn(n, 25)
+    start = randn(m * n, 26)
+    base = O.matmul(x, O.FP8, w, m, n, k, chan_scale=cs).reshape(m, n)
+    xd = "bf16" if path == "tc" else "f32"
+    mark = graph.mark()
+    xb = graph.buffer(bf16(x) if path == "tc" else x)
+    wb, csb, auxb, gb = graph.buffer(w), graph.buffer(cs), graph.buffer(bf16(aux)), graph.buffer(gate)
+    cases = {
+        "gelu": (dict(act="gelu_tanh"), gelu(base)),
+        "sigmoid_gate": (dict(aux_op="sigmoid_gate", aux=auxb, aux_dtype="bf16"),
+                         aux.reshape(m, n) * sigmoid(base)),
+        "swiglu": (dict(aux_op="swiglu", aux=auxb, aux_dtype="bf16"),
+                   aux.reshape(m, n) * sigmoid(aux.reshape(m, n)) * base),
+    }
+    for name, (epi, want) in cases.items():
+        yb = graph.buffer(m * n * 4)
+        before = graph.stats["tcGemms"]
+        we.kernels.matmul(graph, xb, wb, yb, m, n, k, 1.0, x_dtype=xd, w_dtype="fp8", chan_scale=csb,
+                          force_simt=path == "simt", **epi)
+        assert (graph.stats["tcGemms"] > before) == (path == "tc")
+        got = graph.read(yb, m * n * 4, np.float32).reshape(m, n)
+        assert O.rel_error(got, want) < 1e-5, name
+    # gated residual: y = start + gate[col] * (x W^T)
+    yb = graph.buffer(start)
+    we.kernels.matmul(graph, xb, wb, yb, m, n, k, 1.0, x_dtype=xd, w_dtype="fp8", chan_scale=csb,
+                      force_simt=path == "simt", accumulate=True, gate=gb)
+    got = graph.read(yb, m * n * 4, np.float32).reshape(m, n)
+    assert O.rel_error(got, start.reshape(m, n) + gate.astype(np.float64) * base) < 1e-5
+    graph.release(mark)
+
+
+def make_block(we, graph, cfg, seed, per_channel=False):
+    """Random fp8 block weights on the device plus their host copies for the float64 reference."""
+    hid, mlp, heads, kvh, hd = cfg.hidden, cfg.mlp, cfg.heads, cfg.kv_heads, cfg.head_dim
+    shapes = {"wq": (heads * hd, hid), "wk": (kvh * hd, hid), "wv": (kvh * hd, hid), "wo": (hid, hid),
+              "mlp_up": (mlp, hid), "mlp_down": (hid, mlp)}
+    if cfg.attn_gate:
+        shapes["gate"] = (hid, hid)
+    if cfg.mlp_act == "swiglu":
+        shapes["mlp_gate"] = (mlp, hid)
+    host, dev = {}, {}
+    for i, (name, (n, k)) in enumerate(sorted(shapes.items())):
+        if per_channel:
+            q, s = O.quant_fp8_channel(randn(n * k, seed + i, 0.02), n, k)
+            host[name] = {"bytes": q, "n": n, "k": k, "chan_scale": s}
+            dev[name] = we.Linear(graph.buffer(q), "fp8", 1.0, n, k, chan_scale=graph.buffer(s))
+        else:
+            q = fast_fp8(n * k, seed + i)
+            sc = 0.002 if k <= 512 else 0.002 * (512 / k) ** 0.5
+            host[name] = {"bytes": q, "n": n, "k": k, "scale": sc}
+            dev[name] = we.Linear(graph.buffer(q), "fp8", sc, n, k)
+    vec = {"norm1": randn(hid, seed + 50, 0.5), "norm2": randn(hid, seed + 51, 0.5), "norm_q": randn(hd, seed + 52, 0.5),
+           "norm_k": randn(hd, seed + 53, 0.5), "table": randn(6 * hid, seed + 54, 0.3)}
+    host.update(vec)
+    bw = we.blocks.BlockWeights(**dev, **{k: graph.buffer(v) for k, v in vec.items()})
+    return host, bw
+
+
+def test_block_f32_matches_the_float64_block(we, graph):  # tests/gpu/block.test.ts:102-136
+    cfg = we.blocks.BlockConfig(hidden=64, mlp=96, heads=4, kv_heads=2, head_dim=16)
+    tokens = 4 + 3 * 4
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(4, 3, 4), (4, 6, 6), 1000.0)
+    host, bw = make_block(we, graph, cfg, 100)
+    x, temb = randn(tokens * cfg.hidden, 1, 1.0), randn(6 * cfg.hidden, 2, 0.3)
+    want = O.block_reference(x.reshape(tokens, -1), host, vars(cfg), temb, cos, sin)
+    mark = graph.mark()
+    rope = we.Rope(graph.buffer(cos), graph.buffer(sin), pairs, tokens)
+    out = we.blocks.block(graph, bw, cfg, graph.buffer(x), graph.buffer(temb), rope, dtype="f32")
+    got = graph.read(out, tokens * cfg.hidden * 4, np.float32)
+    graph.release(mark)
+    c = O.compare(got, want.ravel())
+    assert c["cosine"] > 0.99999 and c["relativeError"] < 1e-4, c
+
+
+@pytest.mark.parametrize("mlp_act,kv_heads,per_channel", [("swiglu", 2, False), ("gelu", 4, True)])
+def test_block_bf16_fused_path(we, graph, mlp_act, kv_heads, per_channel):
+    cfg = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=kv_heads, head_dim=128, mlp_act=mlp_act,
+                                attn_gate=mlp_act == "swiglu")
+    text, side = 16, 20
+    tokens = text + side * side
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(text, side, side), (32, 48, 48), 1e4)
+    host, bw = make_block(we, graph, cfg, 200, per_channel)
+    x, temb = randn(tokens * cfg.hidden, 3, 1.0), randn(6 * cfg.hidden, 4, 0.3)
+    want = O.block_reference(x.reshape(tokens, -1), host, vars(cfg), temb, cos, sin)
+    mark = graph.mark()
+    rope = we.Rope(graph.buffer(cos), graph.buffer(sin), pairs, tokens)
+    out = we.blocks.block(graph, bw, cfg, graph.buffer(x), graph.buffer(temb), rope, dtype="bf16")
+    got = graph.read(out, tokens * cfg.hidden * 4, np.float32).reshape(tokens, -1)
+    assert graph.device_error() == 0
+    graph.release(mark)
+    delta, wdelta = got - x.reshape(tokens, -1), want - x.reshape(tokens, -1)
+    c = O.compare(delta.ravel(), wdelta.ravel())
+    rel = float(np.max(np.abs(delta - wdelta)) / np.max(np.abs(wdelta)))
+    assert c["cosine"] >= 0.9999 and rel < 1e-2, (c, rel)

@@ -8,6 +8,7 @@ from .graph import Binding, Buffer, Graph
 from .ops import Linear, Mod, Rope, attention, k_split_for, linear, no_mod, norm, qk_norm_rotate, rotate
 from . import kernels, parallel
 from .stream import Streamer
+from . import block as blocks
 
 __all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "norm", "no_mod", "rotate",
            "qk_norm_rotate", "k_split_for", "kernels", "build"]

@@ -18,6 +18,9 @@ MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT, NOALLOC_SYNC = 1, 2, 4, 8
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 STREAM_HOST_PINNED = 1
 ROPE_INTERLEAVED, ROPE_HALF = 0, 1
+EW = {"swiglu": 0, "sigmoid_gate": 1, "gated_add": 2, "add_bias": 3, "gelu_tanh": 4, "add": 5, "silu": 6}
+ACTS = {None: 0, "none": 0, "gelu_tanh": 1, "silu": 2}
+AUX_OPS = {None: 0, "none": 0, "sigmoid_gate": 1, "swiglu": 2}
 
 DTYPES = {"f32": F32, "bf16": BF16, "fp8": FP8, "int4": INT4G64, "f16": F16}
 DTYPE_BYTES = {F32: 4, BF16: 2, FP8: 1, F16: 2}
@@ -36,18 +39,24 @@ class Stats(C.Structure):
                 ("launches", C.c_uint64), ("tc_gemms", C.c_uint64), ("simt_gemms", C.c_uint64)]
 
 
+class Epilogue(C.Structure):
+    _fields_ = [("act", C.c_int32), ("aux_op", C.c_int32), ("aux_dtype", C.c_int32), ("aux", C.c_void_p),
+                ("gate", C.c_void_p)]
+
+
 class MatmulDesc(C.Structure):
     _fields_ = [(n, C.c_int64) for n in ("m", "n", "k", "x_stride", "w_stride", "y_stride", "x_offset", "w_offset",
                                          "y_offset", "k_split")] + [
         ("scale", C.c_float), ("chan_scale", C.c_void_p), ("group_scale", C.c_void_p), ("bias", C.c_void_p),
-        ("x_dtype", C.c_int32), ("w_dtype", C.c_int32), ("y_dtype", C.c_int32), ("flags", C.c_uint32)]
+        ("x_dtype", C.c_int32), ("w_dtype", C.c_int32), ("y_dtype", C.c_int32), ("flags", C.c_uint32),
+        ("epi", Epilogue)]
 
 
 class GemmFp8Desc(C.Structure):
     _fields_ = [("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64), ("x_hi", C.c_void_p), ("x_lo", C.c_void_p),
                 ("row_scale", C.c_void_p), ("w", C.c_void_p), ("scale", C.c_float), ("chan_scale", C.c_void_p),
                 ("bias", C.c_void_p), ("y", C.c_void_p), ("y_stride", C.c_int64), ("y_dtype", C.c_int32),
-                ("flags", C.c_uint32)]
+                ("flags", C.c_uint32), ("epi", Epilogue)]
 
 
 class LinearDesc(C.Structure):
@@ -109,6 +118,10 @@ _SIGS = {
     "we_quantize_fp8": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, C.c_int32, _P, _P]),
     "we_quantize_int4": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _P, _P]),
     "we_quantize_act": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, C.c_int32, _P, _P, _P]),
+    "we_elementwise": (C.c_int, [_P, C.c_int32, _P, _P, _P, _I64, _I64, C.c_int32, _P, C.c_int32]),
+    "we_ew": (C.c_int, [_P, C.c_int32, _P, _P, _P, _I64, _I64, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "we_norm_split": (C.c_int, [_P, _P, C.c_int32, _P, _P, _P, _I64, _I64, C.c_float, C.c_float, C.c_int32, _P, _P,
+                                _P]),
     "we_attention": (C.c_int, [_P, _P, _P, _P, C.c_int32, _I64, _I64, _I64, _I64, C.c_int32, _P, C.c_int32]),
     "we_attend": (C.c_int, [_P, _P, _P, _P, C.c_int32, _I64, _I64, _I64, _I64, C.c_int32, C.c_int32,
                             C.POINTER(C.c_void_p)]),

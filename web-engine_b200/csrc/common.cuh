@@ -113,6 +113,21 @@ __device__ __forceinline__ void load8f(const float* p, int64_t i, float v[8]) {
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// ---- the per-value steps of a block (src/kernels/elementwise.ts:22-29) ----
+__device__ __forceinline__ float sigmoid_ref(float v) { return 1.f / (1.f + expf(-v)); }
+// PyTorch GELU(approximate="tanh"), tanh written with exp and clamped like the reference shader
+__device__ __forceinline__ float gelu_tanh_ref(float v) {
+  const float u = fminf(fmaxf(0.7978845608028654f * (v + 0.044715f * v * v * v), -15.f), 15.f);
+  const float e = expf(2.f * u);
+  return 0.5f * v * (1.f + (e - 1.f) / (e + 1.f));
+}
+__device__ __forceinline__ float act_apply(int act, float v) {
+  return act == WE_ACT_GELU_TANH ? gelu_tanh_ref(v) : (act == WE_ACT_SILU ? v * sigmoid_ref(v) : v);
+}
+__device__ __forceinline__ float aux_apply(int op, float aux, float v) {
+  return op == WE_AUX_SIGMOID_GATE ? aux * sigmoid_ref(v) : (op == WE_AUX_SWIGLU ? aux * sigmoid_ref(aux) * v : v);
+}
+
 // ---- warp reductions ----
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

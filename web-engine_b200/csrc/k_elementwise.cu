@@ -1,0 +1,183 @@
+// The per-value steps of a block (src/kernels/elementwise.ts:38-84) as standalone bandwidth kernels, and
+// RMSNorm fused with the e4m3 activation split that feeds the fp8 tensor-core GEMM.
+//
+// Standalone ops keep the reference's exact formulas (sigmoid 1 / (1 + exp(-v)), tanh-form GELU written
+// with exp and clamped): swiglu silu(a) b, sigmoidGate a sigmoid(b), gatedAdd a + g[i % d] b, addBias
+// a + g[i % d], geluTanh, add a + b, silu. Inside a block they are usually fused into the epilogue of
+// the matmul that produces one of their inputs instead (we_epilogue).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace we {
+
+template <int OP>
+__device__ __forceinline__ float ew_apply(float a, float b, float g) {
+  if constexpr (OP == WE_EW_SWIGLU) return a * sigmoid_ref(a) * b;
+  else if constexpr (OP == WE_EW_SIGMOID_GATE) return a * sigmoid_ref(b);
+  else if constexpr (OP == WE_EW_GATED_ADD) return a + g * b;
+  else if constexpr (OP == WE_EW_ADD_BIAS) return a + g;
+  else if constexpr (OP == WE_EW_GELU_TANH) return gelu_tanh_ref(a);
+  else if constexpr (OP == WE_EW_ADD) return a + b;
+  else return a * sigmoid_ref(a);  // WE_EW_SILU
+}
+
+// grid-stride over n values; 8 per step when the pointers allow 16-byte (bf16) / 32-byte (f32) accesses
+template <int OP, int DT, int OT>
+__global__ void elementwise_kernel(const void* __restrict__ a, const void* __restrict__ b, const float* __restrict__ g,
+                                   int64_t n, int64_t d, void* __restrict__ out, int64_t n8) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+    float va[8], vb[8], o[8];
+    load8<DT>(a, 8 * i, va);
+    if (b) load8<DT>(b, 8 * i, vb);
+    else
+#pragma unroll
+      for (int e = 0; e < 8; e++) vb[e] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] = ew_apply<OP>(va[e], vb[e], g ? g[(8 * i + e) % d] : 0.f);
+    store8<OT>(out, 8 * i, o);
+  }
+  for (int64_t i = 8 * n8 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float vb = b ? load_act<DT>(b, i) : 0.f;
+    store_out<OT>(out, i, ew_apply<OP>(load_act<DT>(a, i), vb, g ? g[i % d] : 0.f));
+  }
+}
+
+template <int OP>
+static void ew_dispatch(const void* a, const void* b, const float* g, int64_t n, int64_t d, int dt, void* out, int ot,
+                        int sms, cudaStream_t st) {
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  const bool vec = al(a) && (!b || al(b)) && al(out);
+  const int64_t n8 = vec ? n / 8 : 0;
+  int64_t grid = (n8 + (n - 8 * n8) + 255) / 256;
+  if (grid > (int64_t)sms * 16) grid = (int64_t)sms * 16;
+  if (grid < 1) grid = 1;
+  if (dt == WE_BF16 && ot == WE_BF16) elementwise_kernel<OP, WE_BF16, WE_BF16><<<(unsigned)grid, 256, 0, st>>>(a, b, g, n, d, out, n8);
+  else if (dt == WE_BF16) elementwise_kernel<OP, WE_BF16, WE_F32><<<(unsigned)grid, 256, 0, st>>>(a, b, g, n, d, out, n8);
+  else if (ot == WE_BF16) elementwise_kernel<OP, WE_F32, WE_BF16><<<(unsigned)grid, 256, 0, st>>>(a, b, g, n, d, out, n8);
+  else elementwise_kernel<OP, WE_F32, WE_F32><<<(unsigned)grid, 256, 0, st>>>(a, b, g, n, d, out, n8);
+}
+
+cudaError_t launch_elementwise(int op, const void* a, const void* b, const float* g, int64_t n, int64_t d, int dt,
+                               void* out, int ot, int sms, cudaStream_t st) {
+  switch (op) {
+    case WE_EW_SWIGLU: ew_dispatch<WE_EW_SWIGLU>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    case WE_EW_SIGMOID_GATE: ew_dispatch<WE_EW_SIGMOID_GATE>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    case WE_EW_GATED_ADD: ew_dispatch<WE_EW_GATED_ADD>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    case WE_EW_ADD_BIAS: ew_dispatch<WE_EW_ADD_BIAS>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    case WE_EW_GELU_TANH: ew_dispatch<WE_EW_GELU_TANH>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    case WE_EW_ADD: ew_dispatch<WE_EW_ADD>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    case WE_EW_SILU: ew_dispatch<WE_EW_SILU>(a, b, g, n, d, dt, out, ot, sms, st); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------- RMSNorm + modulation fused with the e4m3 split ----------------
+// One warp per row: the normalised, modulated row is rounded to bf16 (the value the unfused path
+// would store), then split into hi / lo e4m3 planes under the row's power-of-two scale, exactly as
+// quant_act_kernel does on that bf16 row. So the planes equal norm(bf16 out) followed by the split.
+template <int DT, int TERMS, int UMAX>
+__global__ void __launch_bounds__(128) norm_split_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                         const float* __restrict__ sc, const float* __restrict__ sh,
+                                                         int64_t rows, int64_t d, float eps, float offset,
+                                                         uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
+                                                         float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * 4;
+  for (int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); row < rows; row += warps) {
+    float v[UMAX][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t i = (int64_t)(c * 32 + lane) * 8;
+      if (i < d) {
+        load8<DT>(x, row * d + i, v[c]);
+        // the summation order of rmsnorm_warp_kernel, so a bf16 row normalises to the same bits
+#pragma unroll
+        for (int j = 0; j < 4; j++) ss = fmaf(v[c][2 * j], v[c][2 * j], fmaf(v[c][2 * j + 1], v[c][2 * j + 1], ss));
+      }
+    }
+    const float inv = rsqrtf(warp_sum(ss) / (float)d + eps);
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t i = (int64_t)(c * 32 + lane) * 8;
+      if (i >= d) continue;
+      float ww[8], s8[8], h8[8];
+      load8f(w, i, ww);
+      if (sc) load8f(sc, i, s8); else for (int j = 0; j < 8; j++) s8[j] = 0.f;
+      if (sh) load8f(sh, i, h8); else for (int j = 0; j < 8; j++) h8[j] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float y = v[c][j] * inv * (offset + ww[j]) * (1.f + s8[j]) + h8[j];
+        v[c][j] = bf16_bits_to_f32(f32_to_bf16_bits(y));
+        amax = fmaxf(amax, fabsf(v[c][j]));
+      }
+    }
+    amax = warp_max(amax);
+    int e = 0;
+    if (amax > 0.f) {
+      int E;
+      const float f = frexpf(amax, &E);
+      e = (2.f * f <= 1.75f) ? E - 9 : E - 8;
+    }
+    if (lane == 0) row_scale[row] = ldexpf(1.0f, e);
+#pragma unroll
+    for (int c = 0; c < UMAX; c++) {
+      const int64_t i = (int64_t)(c * 32 + lane) * 8;
+      if (i >= d) continue;
+      float s[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) s[j] = ldexpf(v[c][j], -e);
+      uint32_t h2[2], l2[2];
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const uint16_t h0 = f32x2_to_e4m3x2(s[4 * j], s[4 * j + 1]);
+        const uint16_t h1 = f32x2_to_e4m3x2(s[4 * j + 2], s[4 * j + 3]);
+        h2[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        if (TERMS > 1) {
+          const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+          const uint16_t l0 = f32x2_to_e4m3x2(s[4 * j] - d0.x, s[4 * j + 1] - d0.y);
+          const uint16_t l1 = f32x2_to_e4m3x2(s[4 * j + 2] - d1.x, s[4 * j + 3] - d1.y);
+          l2[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        }
+      }
+      *reinterpret_cast<uint2*>(hi + row * d + i) = make_uint2(h2[0], h2[1]);
+      if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * d + i) = make_uint2(l2[0], l2[1]);
+    }
+  }
+}
+
+template <int DT, int TERMS>
+static bool norm_split_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
+                                int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs, int sms,
+                                cudaStream_t st) {
+  int64_t g = (rows + 3) / 4;
+  if (g > (int64_t)sms * 16) g = (int64_t)sms * 16;
+  if (d <= 256 * 4) norm_split_kernel<DT, TERMS, 4><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (d <= 256 * 8) norm_split_kernel<DT, TERMS, 8><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (d <= 256 * 12) norm_split_kernel<DT, TERMS, 12><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (d <= 256 * 16) norm_split_kernel<DT, TERMS, 16><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (d <= 256 * 24) norm_split_kernel<DT, TERMS, 24><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else return false;
+  return true;
+}
+
+cudaError_t launch_norm_split(const void* x, int xdt, const float* w, const float* sc, const float* sh, int64_t rows,
+                              int64_t d, float eps, float offset, int terms, uint8_t* hi, uint8_t* lo, float* rs,
+                              int sms, cudaStream_t st) {
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (d % 8 || !al(x) || !al(w) || (sc && !al(sc)) || (sh && !al(sh)) || ((uintptr_t)hi & 7) ||
+      (lo && ((uintptr_t)lo & 7)))
+    return cudaErrorNotSupported;
+  bool ok;
+  if (xdt == WE_BF16) ok = terms > 1 ? norm_split_dispatch<WE_BF16, 2>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st)
+                                     : norm_split_dispatch<WE_BF16, 1>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st);
+  else ok = terms > 1 ? norm_split_dispatch<WE_F32, 2>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st)
+                      : norm_split_dispatch<WE_F32, 1>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st);
+  if (!ok) return cudaErrorNotSupported;
+  return cudaGetLastError();
+}
+
+}  // namespace we

@@ -77,6 +77,13 @@ __global__ void __launch_bounds__(SB_T) gemm_simt_kernel(const void* __restrict_
       float v = acc[i][j] * sc;
       if (a.bias) v += a.bias[c];
       int64_t o = a.y_offset + (zrows + r) * a.y_stride + c;
+      v = act_apply(a.epi.act, v);
+      if (a.epi.aux_op) {
+        const int64_t oa = (zrows + r) * a.y_stride + c;  // aux is offset like y
+        const float ax = a.epi.aux_dtype == WE_BF16 ? load_act<WE_BF16>(a.epi.aux, oa) : load_act<WE_F32>(a.epi.aux, oa);
+        v = aux_apply(a.epi.aux_op, ax, v);
+      }
+      if (a.epi.gate) v *= a.epi.gate[c];
       if (a.accumulate) v += load_act<YT>(y, o);
       store_out<YT>(y, o, v);
     }

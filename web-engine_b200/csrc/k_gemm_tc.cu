@@ -47,6 +47,8 @@ struct Params {
   int y_dtype;
   int accumulate;
   int vec_ok;  // y rows allow 16-byte stores (aligned base, stride a multiple of 16 bytes)
+  EpiOps epi;
+  int epi_vec_ok;  // aux rows and the gate vector allow 16-byte loads
   uint32_t* err;
 };
 
@@ -93,6 +95,34 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], float* s
     const int64_t c0 = ch_base + cg;
     if (tok >= p.m || c0 >= p.n) continue;
     const int64_t o = tok * p.y_stride + c0;
+    const bool full8 = c0 + 8 <= p.n;
+    if (p.epi.act | p.epi.aux_op | (p.epi.gate != nullptr)) {
+      // fused per-value steps: activation, aux gate / swiglu, residual gate
+      float ax[8], gt[8];
+      if (p.epi.aux_op) {
+        if (p.epi_vec_ok && full8) {
+          if (p.epi.aux_dtype == WE_BF16) load8<WE_BF16>(p.epi.aux, o, ax);
+          else load8<WE_F32>(p.epi.aux, o, ax);
+        } else
+#pragma unroll
+          for (int e = 0; e < 8; e++)
+            ax[e] = (c0 + e < p.n) ? (p.epi.aux_dtype == WE_BF16 ? load_act<WE_BF16>(p.epi.aux, o + e)
+                                                                 : load_act<WE_F32>(p.epi.aux, o + e))
+                                   : 0.f;
+      }
+      if (p.epi.gate) {
+        if (p.epi_vec_ok && full8) load8f(p.epi.gate, c0, gt);
+        else
+#pragma unroll
+          for (int e = 0; e < 8; e++) gt[e] = (c0 + e < p.n) ? p.epi.gate[c0 + e] : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        v[e] = act_apply(p.epi.act, v[e]);
+        if (p.epi.aux_op) v[e] = aux_apply(p.epi.aux_op, ax[e], v[e]);
+        if (p.epi.gate) v[e] *= gt[e];
+      }
+    }
     if (p.vec_ok && c0 + 8 <= p.n) {
       if (p.y_dtype == WE_BF16) {
         uint4* y = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o);
@@ -632,6 +662,10 @@ static Params make_params(const TcGemmArgs& a) {
   p.accumulate = a.accumulate;
   const int esz = a.y_dtype == WE_BF16 ? 2 : 4;
   p.vec_ok = ((uintptr_t)a.y % 16 == 0) && ((a.y_stride * esz) % 16 == 0);
+  p.epi = a.epi;
+  const int asz = a.epi.aux_dtype == WE_BF16 ? 2 : 4;
+  p.epi_vec_ok = (!a.epi.aux || (((uintptr_t)a.epi.aux % 16 == 0) && ((a.y_stride * asz) % 16 == 0))) &&
+                 (!a.epi.gate || (uintptr_t)a.epi.gate % 16 == 0);
   p.err = a.dev_err;
   return p;
 }

@@ -5,6 +5,15 @@
 
 namespace we {
 
+// Fused epilogue steps after v = acc * scales + bias (see we_epilogue in the public header).
+struct EpiOps {
+  int act = 0;
+  int aux_op = 0;
+  int aux_dtype = 0;
+  const void* aux = nullptr;  // [m, n] with y's stride (already offset like y)
+  const float* gate = nullptr;
+};
+
 // Resolved matmul arguments (values, not bytes; strides already defaulted).
 struct MatmulArgs {
   int64_t m, n, k;
@@ -16,6 +25,7 @@ struct MatmulArgs {
   const float* bias;
   int x_dtype, w_dtype, y_dtype;
   int accumulate;
+  EpiOps epi;
 };
 
 cudaError_t launch_gemm_simt(const void* x, const void* w, void* y, const MatmulArgs& a, cudaStream_t st);
@@ -38,6 +48,7 @@ struct TcGemmArgs {
   int64_t y_stride;         // values
   int y_dtype;
   int accumulate;
+  EpiOps epi;
   uint32_t* dev_err;        // device error word
 };
 // Returns cudaErrorNotSupported when the layout cannot go through TMA (alignment) so the caller can
@@ -63,6 +74,12 @@ cudaError_t launch_rope(const void* x, int xdt, const float* cs, const float* sn
 cudaError_t launch_qknorm_rope(const void* x, int xdt, const float* w, float eps, float offset, const float* cs,
                                const float* sn, int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out,
                                int odt, int sms, cudaStream_t st);
+
+cudaError_t launch_elementwise(int op, const void* a, const void* b, const float* g, int64_t n, int64_t d, int dt,
+                               void* out, int ot, int sms, cudaStream_t st);
+cudaError_t launch_norm_split(const void* x, int xdt, const float* w, const float* sc, const float* sh, int64_t rows,
+                              int64_t d, float eps, float offset, int terms, uint8_t* hi, uint8_t* lo, float* rs,
+                              int sms, cudaStream_t st);
 
 // attention(q [T, H, D], k, v [T, Hkv, D]) -> out [T, H, D]
 struct AttnArgs {

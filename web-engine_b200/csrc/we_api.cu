@@ -279,6 +279,12 @@ int we_matmul_check(we_ctx* ctx, const we_matmul_desc* d) {
     if (!d->group_scale) return fail(ctx, WE_EINVAL, "int4 group-64 weights need group scales");
   }
   if (d->k_split > 1 && d->bias) return fail(ctx, WE_EINVAL, "bias is not supported with kSplit");
+  if (d->epi.act < WE_ACT_NONE || d->epi.act > WE_ACT_SILU) return fail(ctx, WE_EINVAL, "unknown activation");
+  if (d->epi.aux_op < WE_AUX_NONE || d->epi.aux_op > WE_AUX_SWIGLU) return fail(ctx, WE_EINVAL, "unknown aux op");
+  if (d->epi.aux_op && (!d->epi.aux || !act_dtype_ok(d->epi.aux_dtype)))
+    return fail(ctx, WE_EINVAL, "the aux op needs an f32 or bf16 aux tensor");
+  if (d->k_split > 1 && (d->epi.act || d->epi.aux_op || d->epi.gate))
+    return fail(ctx, WE_EINVAL, "fused epilogue steps are not supported with kSplit");
   return WE_OK;
 }
 
@@ -305,6 +311,11 @@ static int matmul_impl(we_ctx* ctx, const we_matmul_desc* d, const void* x, cons
   a.w_dtype = d->w_dtype;
   a.y_dtype = d->y_dtype;
   a.accumulate = (d->flags & WE_MM_ACCUMULATE) ? 1 : 0;
+  a.epi.act = d->epi.act;
+  a.epi.aux_op = d->epi.aux_op;
+  a.epi.aux_dtype = d->epi.aux_dtype;
+  a.epi.aux = d->epi.aux ? static_cast<const char*>(d->epi.aux) + a.y_offset * dsize(d->epi.aux_dtype) : nullptr;
+  a.epi.gate = d->epi.gate;
   cudaStream_t st = ctx->stream;
 
   const bool tc_candidate = !(d->flags & WE_MM_FORCE_SIMT) && a.x_dtype == WE_BF16 && a.k_split == 1 && a.k > 0 &&
@@ -322,6 +333,7 @@ static int matmul_impl(we_ctx* ctx, const we_matmul_desc* d, const void* x, cons
     t.y_stride = a.y_stride;
     t.y_dtype = a.y_dtype;
     t.accumulate = a.accumulate;
+    t.epi = a.epi;
     t.dev_err = ctx->dev_err;
     bool ready = false;
     if (a.w_dtype == WE_FP8) {
@@ -413,6 +425,11 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
   t.y_stride = d->y_stride ? d->y_stride : d->n;
   t.y_dtype = d->y_dtype;
   t.accumulate = (d->flags & WE_MM_ACCUMULATE) ? 1 : 0;
+  t.epi.act = d->epi.act;
+  t.epi.aux_op = d->epi.aux_op;
+  t.epi.aux_dtype = d->epi.aux_dtype;
+  t.epi.aux = d->epi.aux;
+  t.epi.gate = d->epi.gate;
   t.dev_err = ctx->dev_err;
   if (!we::gemm_tc_supported(t))
     return fail(ctx, WE_EINVAL, "we_gemm_fp8 needs K a multiple of 16 and 16-byte aligned operands");
@@ -597,6 +614,47 @@ int we_positions(int64_t text, int64_t rows, int64_t cols, int64_t* pos) {
     pos[3 * t + 1] = i / cols;
     pos[3 * t + 2] = i % cols;
   }
+  return WE_OK;
+}
+
+// ---------------- elementwise / norm + split ----------------
+int we_elementwise(we_ctx* ctx, int32_t op, const void* a, const void* b, const float* g, int64_t n, int64_t d,
+                   int32_t dtype, void* out, int32_t out_dtype) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(dtype) || !act_dtype_ok(out_dtype)) return fail(ctx, WE_EINVAL, "inputs and out must be f32 or bf16");
+  if (op < WE_EW_SWIGLU || op > WE_EW_SILU) return fail(ctx, WE_EINVAL, "unknown elementwise op");
+  const bool needs_b = op == WE_EW_SWIGLU || op == WE_EW_SIGMOID_GATE || op == WE_EW_GATED_ADD || op == WE_EW_ADD;
+  const bool needs_g = op == WE_EW_GATED_ADD || op == WE_EW_ADD_BIAS;
+  if ((needs_b && !b) || (needs_g && (!g || d <= 0))) return fail(ctx, WE_EINVAL, "missing input of the elementwise op");
+  if (n <= 0) return WE_OK;
+  LK(we::launch_elementwise(op, a, needs_b ? b : nullptr, needs_g ? g : nullptr, n, d > 0 ? d : 1, dtype, out, out_dtype,
+                            ctx->sms, ctx->stream),
+     "elementwise");
+  return WE_OK;
+}
+
+int we_ew(we_ctx* ctx, int32_t op, const void* a, const void* b, const float* g, int64_t n, int64_t d, int32_t dtype,
+          int32_t out_dtype, void** out) {
+  if (!ctx || !out) return WE_EINVAL;
+  int rc = op_output(ctx, (size_t)n * dsize(out_dtype), out);
+  if (rc != WE_OK) return rc;
+  return we_elementwise(ctx, op, a, b, g, n, d, dtype, *out, out_dtype);
+}
+
+int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, const float* scale,
+                  const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
+                  uint8_t* lo, float* row_scale) {
+  if (!ctx) return WE_EINVAL;
+  if (!act_dtype_ok(x_dtype)) return fail(ctx, WE_EINVAL, "x must be f32 or bf16");
+  if (terms != 1 && terms != 2) return fail(ctx, WE_EINVAL, "terms must be 1 or 2");
+  if (terms == 2 && !lo) return fail(ctx, WE_EINVAL, "two terms need a lo buffer");
+  if (rows <= 0) return WE_OK;
+  cudaError_t e = we::launch_norm_split(x, x_dtype, weight, scale, shift, rows, d, eps, offset, terms, hi, lo,
+                                        row_scale, ctx->sms, ctx->stream);
+  if (e == cudaErrorNotSupported)
+    return fail(ctx, WE_EINVAL, "norm + split needs d % 8 == 0, d <= 6144 and 16-byte aligned rows");
+  CK(e, "norm + split");
+  ctx->stats.launches++;
   return WE_OK;
 }
 

@@ -32,11 +32,20 @@ def matmul_params(m: int, n: int, k: int, scale: float, x_stride=None, w_stride=
                         L.F32, L.FP8, L.F32, 0)
 
 
+def epilogue(act=None, aux_op=None, aux=None, aux_dtype="f32", gate=None) -> L.Epilogue:
+    """Fused per-value steps after a matmul (see we_epilogue): act "gelu_tanh" | "silu"; aux_op
+    "sigmoid_gate" (aux * sigmoid(v)) | "swiglu" (silu(aux) * v); gate: per-column factor [n]."""
+    return L.Epilogue(L.ACTS[act], L.AUX_OPS[aux_op], L.DTYPES[aux_dtype], addr(aux).value, addr(gate).value)
+
+
 def matmul(graph: Graph, x, w, y, m: int, n: int, k: int, scale: float = 1.0, *, x_dtype="f32", w_dtype="fp8",
            y_dtype="f32", chan_scale=None, group_scale=None, bias=None, x_stride=None, w_stride=None, y_stride=None,
-           x_offset=0, w_offset=0, y_offset=0, k_split=1, accumulate=False, fast=False, force_simt=False) -> None:
-    """Queues y = x . W^T * scale (matmulWgsl, src/kernels/matmul.ts:118-178) on device buffers."""
+           x_offset=0, w_offset=0, y_offset=0, k_split=1, accumulate=False, fast=False, force_simt=False,
+           act=None, aux_op=None, aux=None, aux_dtype="f32", gate=None) -> None:
+    """Queues y = x . W^T * scale (matmulWgsl, src/kernels/matmul.ts:118-178) on device buffers, with optional
+    fused epilogue steps (act, aux_op/aux, gate; see `epilogue`)."""
     d = matmul_params(m, n, k, scale, x_stride, w_stride, y_stride, x_offset, w_offset, y_offset, k_split)
+    d.epi = epilogue(act, aux_op, aux, aux_dtype, gate)
     d.chan_scale = addr(chan_scale).value
     d.group_scale = addr(group_scale).value
     d.bias = addr(bias).value
@@ -207,11 +216,12 @@ def quantize_act(graph: Graph, x, m: int, k: int, hi, lo, row_scale, terms: int 
 
 
 def gemm_fp8(graph: Graph, x_hi, x_lo, row_scale, w, y, m: int, n: int, k: int, scale: float = 1.0,
-             chan_scale=None, bias=None, y_dtype="f32", y_stride: int = 0, accumulate: bool = False) -> None:
+             chan_scale=None, bias=None, y_dtype="f32", y_stride: int = 0, accumulate: bool = False,
+             act=None, aux_op=None, aux=None, aux_dtype="f32", gate=None) -> None:
     """The tcgen05 GEMM on an already-split activation (we_gemm_fp8); x_lo None = one term."""
     d = L.GemmFp8Desc(m, n, k, addr(x_hi).value, addr(x_lo).value, addr(row_scale).value, addr(w).value, scale,
                       addr(chan_scale).value, addr(bias).value, addr(y).value, y_stride, L.DTYPES[y_dtype],
-                      L.MM_ACCUMULATE if accumulate else 0)
+                      L.MM_ACCUMULATE if accumulate else 0, epilogue(act, aux_op, aux, aux_dtype, gate))
     L.check(graph.ctx, L.lib().we_gemm_fp8(graph.ctx, C.byref(d)))
 
 
@@ -228,3 +238,11 @@ def attention(graph: Graph, q, k, v, tokens: int, heads: int, kv_heads: int, dim
     """attention into a given output buffer (src/kernels/attention.ts:20-51)."""
     L.check(graph.ctx, L.lib().we_attention(graph.ctx, addr(q), addr(k), addr(v), L.DTYPES[dtype], tokens, heads,
                                             kv_heads, dim, int(causal), addr(out), L.DTYPES[out_dtype]))
+
+
+def norm_split(graph: Graph, x, weight, rows: int, d: int, hi, lo, row_scale, scale=None, shift=None, eps=1e-5,
+               offset=1.0, terms: int = 2, x_dtype: str = "f32") -> None:
+    """RMSNorm + modulation, rounded to bf16 and split into e4m3 planes for the fp8 GEMM, in one pass."""
+    L.check(graph.ctx, L.lib().we_norm_split(graph.ctx, addr(x), L.DTYPES[x_dtype], addr(weight), addr(scale),
+                                             addr(shift), rows, d, eps, offset, terms, addr(hi), addr(lo),
+                                             addr(row_scale)))

@@ -143,3 +143,43 @@ def attention(graph: Graph, q, k, v, tokens: int, heads: int, kv_heads: int, dim
     L.check(graph.ctx, L.lib().we_attend(graph.ctx, addr(q), addr(k), addr(v), L.DTYPES[dtype], tokens, heads,
                                          kv_heads, dim, int(causal), L.DTYPES[od], C.byref(out)))
     return Buffer(out.value, tokens * heads * dim * L.DTYPE_BYTES[L.DTYPES[od]])
+
+
+def elementwise(graph: Graph, op: str, a, b, n: int, g=None, d: int = 1, dtype: str = "f32",
+                out_dtype: str | None = None) -> Buffer:
+    """One per-value step as a graph op (ops.ts:95-99): a new buffer of n values."""
+    od = out_dtype or dtype
+    out = C.c_void_p()
+    L.check(graph.ctx, L.lib().we_ew(graph.ctx, L.EW[op], addr(a), addr(b), addr(g), n, d, L.DTYPES[dtype],
+                                     L.DTYPES[od], C.byref(out)))
+    return Buffer(out.value, n * L.DTYPE_BYTES[L.DTYPES[od]])
+
+
+def swiglu(graph: Graph, gate, up, n: int, dtype: str = "f32") -> Buffer:
+    """silu(gate) . up (ops.ts:102)"""
+    return elementwise(graph, "swiglu", gate, up, n, dtype=dtype)
+
+
+def sigmoid_gate(graph: Graph, a, gate, n: int, dtype: str = "f32") -> Buffer:
+    """a . sigmoid(gate) (ops.ts:104)"""
+    return elementwise(graph, "sigmoid_gate", a, gate, n, dtype=dtype)
+
+
+def gated_add(graph: Graph, x, h, g, n: int, d: int, dtype: str = "f32") -> Buffer:
+    """x + g[column] . h, g of length d (ops.ts:106-107)"""
+    return elementwise(graph, "gated_add", x, h, n, g=g, d=d, dtype=dtype)
+
+
+def add(graph: Graph, x, h, n: int, dtype: str = "f32") -> Buffer:
+    """x + h (ops.ts:109)"""
+    return elementwise(graph, "add", x, h, n, dtype=dtype)
+
+
+def gelu(graph: Graph, x, n: int, dtype: str = "f32") -> Buffer:
+    """GELU, tanh form (ops.ts:111)"""
+    return elementwise(graph, "gelu_tanh", x, None, n, dtype=dtype)
+
+
+def silu(graph: Graph, x, n: int, dtype: str = "f32") -> Buffer:
+    """x . sigmoid(x) (ops.ts:113)"""
+    return elementwise(graph, "silu", x, None, n, dtype=dtype)
