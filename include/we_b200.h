@@ -260,6 +260,15 @@ int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weig
                   const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
                   uint8_t* lo, float* row_scale);
 
+/* ---------------- latent <-> tokens: patchify / unpatchify (src/model/transformer.ts:53-82) ----------------
+   tokens [ceil(H/2) * ceil(W/2), 4 channels] <- latent [channels, H, W]: 2x2 patches, features in (channel, patch
+   row, patch column) order; an odd H or W wraps to row / column 0 (patchify, transformer.ts:59-69). unpatchify is
+   the inverse and crops the padding off (transformer.ts:72-82). f32 or bf16 on either side; bit-exact moves. */
+int we_patchify(we_ctx* ctx, const void* latent, int32_t latent_dtype, int64_t channels, int64_t height, int64_t width,
+                void* tokens, int32_t tokens_dtype);
+int we_unpatchify(we_ctx* ctx, const void* tokens, int32_t tokens_dtype, int64_t channels, int64_t height,
+                  int64_t width, void* latent, int32_t latent_dtype);
+
 /* ---------------- attention: attention() (src/kernels/attention.ts:20-51) ----------------
    softmax(q k^T / sqrt(dim)) v per head with grouped-query heads (query head h uses kv head
    h / (heads / kv_heads)); q [tokens, heads, dim], k, v [tokens, kv_heads, dim] -> out [tokens, heads, dim].

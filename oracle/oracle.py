@@ -296,40 +296,65 @@ def block_reference(x, w: dict, cfg: dict, temb, cos, sin) -> np.ndarray:
     formulas: fp8 linears with a scalar or per-channel scale, zero-centred norms (offset 1), GQA attention
     with an optional sigmoid gate, and a SwiGLU or tanh-GELU MLP. w holds host arrays: linears as dicts
     {"bytes", "n", "k", "scale" | "chan_scale"}, norms f32, table f32 [6 hidden]."""
+    return joint_block_reference(x, [(0, x.shape[0], w)], cfg, temb, cos, sin)
+
+
+def _mm(a, lin):
+    """a . W^T with W decoded from e4m3 (or given as float), times the scalar or per-channel scale, plus bias."""
+    if "bytes" in lin:
+        wv = e4m3_table()[lin["bytes"]].reshape(lin["n"], lin["k"])
+    else:
+        wv = np.asarray(lin["w"], np.float64).reshape(lin["n"], lin["k"])
+    y = np.asarray(a, np.float64).reshape(-1, lin["k"]) @ wv.T
+    y = y * (lin["chan_scale"].astype(np.float64) if lin.get("chan_scale") is not None else lin.get("scale", 1.0))
+    if lin.get("bias") is not None:
+        y = y + lin["bias"].astype(np.float64)
+    return y
+
+
+def _rms(a, wt, rows, d, sc=None, sh=None, eps=1e-5, offset=1.0):
+    """RMSNorm with modulation (src/kernels/rmsnorm.ts:42-46) in float64."""
+    a = np.asarray(a, np.float64).reshape(rows, d)
+    inv = 1.0 / np.sqrt((a * a).sum(1) / d + eps)
+    y = a * inv[:, None] * (offset + np.asarray(wt, np.float64))
+    if sc is not None:
+        y = y * (1.0 + sc) + sh
+    return y
+
+
+def _gelu(u):
+    return 0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))
+
+
+def joint_block_reference(x, parts: list, cfg: dict, temb, cos, sin) -> np.ndarray:
+    """float64 block over a token sequence split into parts (row0, rows, w): each part has its own weights and
+    modulation, attention runs over all rows. One part = the single-stream block of tests/gpu/block.test.ts:26-100;
+    two parts (text rows, image rows) = the double-stream block built from the same ops."""
     t, hid, heads, kvh, hd = x.shape[0], cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
     eps = cfg.get("eps", 1e-5)
-    e4 = e4m3_table()
+    pairs = hd // 2
 
-    def mm(a, lin):
-        wv = e4[lin["bytes"]].reshape(lin["n"], lin["k"])
-        y = a @ wv.T
-        return y * (lin["chan_scale"].astype(np.float64) if lin.get("chan_scale") is not None else lin["scale"])
-
-    def rms(a, wt, rows, d, sc=None, sh=None):
-        a = a.reshape(rows, d)
-        inv = 1.0 / np.sqrt((a * a).sum(1) / d + eps)
-        y = a * inv[:, None] * (1.0 + wt.astype(np.float64))
-        if sc is not None:
-            y = y * (1.0 + sc) + sh
-        return y
-
-    def rope_np(a, tokens, nh):
-        pairs = hd // 2
+    def rope_np(a, r0, tokens, nh):
         a = a.reshape(tokens, nh, pairs, 2)
-        c = cos.reshape(tokens, 1, pairs).astype(np.float64)
-        s = sin.reshape(tokens, 1, pairs).astype(np.float64)
+        c = cos.reshape(-1, pairs)[r0:r0 + tokens].reshape(tokens, 1, pairs).astype(np.float64)
+        s = sin.reshape(-1, pairs)[r0:r0 + tokens].reshape(tokens, 1, pairs).astype(np.float64)
         out = np.empty_like(a)
         out[..., 0] = a[..., 0] * c - a[..., 1] * s
         out[..., 1] = a[..., 1] * c + a[..., 0] * s
         return out.reshape(tokens, nh * hd)
 
-    x = x.astype(np.float64)
-    mod = [(temb[i * hid:(i + 1) * hid].astype(np.float64) + w["table"][i * hid:(i + 1) * hid]) for i in range(6)]
-    prescale, preshift, pregate, postscale, postshift, postgate = mod
-    h = rms(x, w["norm1"], t, hid, prescale, preshift)
-    q = rope_np(rms(mm(h, w["wq"]), w["norm_q"], t * heads, hd), t, heads).reshape(t, heads, hd)
-    k = rope_np(rms(mm(h, w["wk"]), w["norm_k"], t * kvh, hd), t, kvh).reshape(t, kvh, hd)
-    v = mm(h, w["wv"]).reshape(t, kvh, hd)
+    x = np.asarray(x, np.float64)
+    q, k, v = np.empty((t, heads, hd)), np.empty((t, kvh, hd)), np.empty((t, kvh, hd))
+    hs, mods = [], []
+    for r0, n, w in parts:
+        mod = [(np.asarray(temb[i * hid:(i + 1) * hid], np.float64) + w["table"][i * hid:(i + 1) * hid])
+               for i in range(6)]
+        h = _rms(x[r0:r0 + n], w["norm1"], n, hid, mod[0], mod[1], eps)
+        q[r0:r0 + n] = rope_np(_rms(_mm(h, w["wq"]), w["norm_q"], n * heads, hd, eps=eps), r0, n, heads).reshape(n, heads, hd)
+        k[r0:r0 + n] = rope_np(_rms(_mm(h, w["wk"]), w["norm_k"], n * kvh, hd, eps=eps), r0, n, kvh).reshape(n, kvh, hd)
+        v[r0:r0 + n] = _mm(h, w["wv"]).reshape(n, kvh, hd)
+        hs.append(h)
+        mods.append(mod)
     o = np.empty((t, heads, hd))
     for hh in range(heads):
         g = hh // (heads // kvh)
@@ -337,14 +362,109 @@ def block_reference(x, w: dict, cfg: dict, temb, cos, sin) -> np.ndarray:
         p = np.exp(s - s.max(1, keepdims=True))
         o[:, hh] = (p / p.sum(1, keepdims=True)) @ v[:, g]
     o = o.reshape(t, hid)
-    if cfg.get("attn_gate", True):
-        o = o / (1.0 + np.exp(-mm(h, w["gate"])))
-    x1 = x + pregate * mm(o, w["wo"])
-    h2 = rms(x1, w["norm2"], t, hid, postscale, postshift)
-    if cfg.get("mlp_act", "swiglu") == "swiglu":
-        gg = mm(h2, w["mlp_gate"])
-        m = gg / (1.0 + np.exp(-gg)) * mm(h2, w["mlp_up"])
-    else:
-        u = mm(h2, w["mlp_up"])
-        m = 0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))
-    return x1 + postgate * mm(m, w["mlp_down"])
+    out = np.empty_like(x)
+    for (r0, n, w), h, mod in zip(parts, hs, mods):
+        prescale, preshift, pregate, postscale, postshift, postgate = mod
+        op = o[r0:r0 + n]
+        if cfg.get("attn_gate", True):
+            op = op / (1.0 + np.exp(-_mm(h, w["gate"])))
+        x1 = x[r0:r0 + n] + pregate * _mm(op, w["wo"])
+        h2 = _rms(x1, w["norm2"], n, hid, postscale, postshift, eps)
+        if cfg.get("mlp_act", "swiglu") == "swiglu":
+            gg = _mm(h2, w["mlp_gate"])
+            m = gg / (1.0 + np.exp(-gg)) * _mm(h2, w["mlp_up"])
+        else:
+            m = _gelu(_mm(h2, w["mlp_up"]))
+        out[r0:r0 + n] = x1 + postgate * _mm(m, w["mlp_down"])
+    return out
+
+
+# ---------------- the step driver's host parts (src/model/transformer.ts, src/model/sampler.ts) ----------------
+def timestep_embedding(timestep: float, dim: int = 256) -> np.ndarray:
+    """[cos(1000 t f_i), sin(1000 t f_i)], f_i = 10000^(-i / (dim/2)), cos first (transformer.ts:41-51)."""
+    half = dim // 2
+    arg = 1000.0 * timestep * np.exp(-np.log(10000.0) * np.arange(half) / half)
+    return np.concatenate([np.cos(arg), np.sin(arg)]).astype(np.float32)
+
+
+def patch_grid(height: int, width: int):
+    return (height + 1) // 2, (width + 1) // 2
+
+
+def patchify(latent, height: int, width: int, channels: int = 16) -> np.ndarray:
+    """Latent [C, H, W] -> tokens [rows*cols, 4C], feature (channel, patch row, patch col); odd sizes wrap
+    (transformer.ts:59-69). A loop restatement of the reference's index formula."""
+    lat = np.asarray(latent).reshape(channels, height, width)
+    rows, cols = patch_grid(height, width)
+    out = np.empty((rows * cols, channels * 4), dtype=lat.dtype)
+    for r in range(rows):
+        for c in range(cols):
+            for pr in range(2):
+                for pc in range(2):
+                    out[r * cols + c, np.arange(channels) * 4 + pr * 2 + pc] = \
+                        lat[:, (r * 2 + pr) % height, (c * 2 + pc) % width]
+    return out.reshape(-1)
+
+
+def unpatchify(tokens, height: int, width: int, channels: int = 16) -> np.ndarray:
+    """The inverse of patchify; the padding is cropped off (transformer.ts:72-82)."""
+    rows, cols = patch_grid(height, width)
+    tok = np.asarray(tokens).reshape(rows * cols, channels * 4)
+    out = np.empty((channels, height, width), dtype=tok.dtype)
+    for y in range(height):
+        for x in range(width):
+            out[:, y, x] = tok[(y // 2) * cols + x // 2, np.arange(channels) * 4 + (y % 2) * 2 + (x % 2)]
+    return out.reshape(-1)
+
+
+def sigmas(steps: int = 8, mu: float = 1.15) -> list:
+    """linspace(1, 1/steps, steps) under the exponential time shift, then 0 (src/model/sampler.ts:9-19)."""
+    raw = [1 - i * (1 - 1 / steps) / ((steps - 1) or 1) for i in range(steps)]
+    return [float(np.exp(mu) / (np.exp(mu) + (1 / s - 1))) for s in raw] + [0.0]
+
+
+def euler_step(x, velocity, sigma: float, nxt: float) -> np.ndarray:
+    """x + (sigma_next - sigma) v, in f32 like the reference's Float32Array (sampler.ts:22-24)."""
+    return (np.asarray(x, np.float32) + np.float32(nxt - sigma) * np.asarray(velocity, np.float32)).astype(np.float32)
+
+
+def gaussian(n: int, seed: int) -> np.ndarray:
+    """Seeded Box-Muller normals from a 32-bit LCG (sampler.ts:27-38): u = (s + 0.5) / 2^32 per draw."""
+    s = (seed & 0xFFFFFFFF) or 1
+    out = np.empty(n, dtype=np.float32)
+    for i in range(0, n, 2):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        u1 = (s + 0.5) / 2 ** 32
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        u2 = (s + 0.5) / 2 ** 32
+        r, a = np.sqrt(-2 * np.log(u1)), 2 * np.pi * u2
+        out[i] = r * np.cos(a)
+        if i + 1 < n:
+            out[i + 1] = r * np.sin(a)
+    return out
+
+
+def step_reference(latent, height: int, width: int, timestep: float, ctx, w: dict, cfg: dict) -> np.ndarray:
+    """float64 denoising step (transformer.ts:134-176) of a Flux-style layout: time MLP, text projection,
+    patchify + first linear, `double` two-part blocks over [text, image] rows, `single` one-part blocks, the
+    modulated last norm and linear, unpatchify. w: {"first", "tmlp0", "tmlp2", "tproj", "txt_in", "last_linear":
+    linear dicts; "double": [(txt, img)], "single": [block dicts]; "last_norm", "last_scale", "last_shift"}."""
+    hid, ch = cfg["hidden"], cfg.get("channels", 16)
+    rows, cols = patch_grid(height, width)
+    ctx = np.asarray(ctx, np.float64).reshape(-1, w["txt_in"]["k"])
+    L = ctx.shape[0]
+    T = L + rows * cols
+    emb = timestep_embedding(timestep, cfg.get("time_dim", 256)).astype(np.float64)
+    t = _mm(_gelu(_mm(emb, w["tmlp0"])), w["tmlp2"]).reshape(-1)
+    tvec = _mm(_gelu(t), w["tproj"]).reshape(-1)
+    img = _mm(patchify(np.asarray(latent, np.float32), height, width, ch), w["first"])
+    x = np.concatenate([_mm(ctx, w["txt_in"]), img])
+    cos, sin, pairs = rope_tables(positions(L, rows, cols), cfg["axes"], cfg["theta"])
+    for txt_w, img_w in w["double"]:
+        x = joint_block_reference(x, [(0, L, txt_w), (L, T - L, img_w)], cfg, tvec, cos, sin)
+    for bw in w["single"]:
+        x = joint_block_reference(x, [(0, T, bw)], cfg, tvec, cos, sin)
+    scale = t + w["last_scale"].astype(np.float64)
+    shift = t + w["last_shift"].astype(np.float64)
+    last = _mm(_rms(x, w["last_norm"], T, hid, scale, shift, cfg.get("eps", 1e-5)), w["last_linear"])
+    return unpatchify(last[L:], height, width, ch)

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from util import bf16, bf16_round, fast_fp8, lcg_floats, randn
+from util import bf16, bf16_round, fast_fp8, lcg_floats, make_block, randn
 
 pytestmark = pytest.mark.gpu
 
@@ -121,33 +121,6 @@ def test_gemm_epilogue_fusions(we, graph, path):
     got = graph.read(yb, m * n * 4, np.float32).reshape(m, n)
     assert O.rel_error(got, start.reshape(m, n) + gate.astype(np.float64) * base) < 1e-5
     graph.release(mark)
-
-
-def make_block(we, graph, cfg, seed, per_channel=False):
-    """Random fp8 block weights on the device plus their host copies for the float64 reference."""
-    hid, mlp, heads, kvh, hd = cfg.hidden, cfg.mlp, cfg.heads, cfg.kv_heads, cfg.head_dim
-    shapes = {"wq": (heads * hd, hid), "wk": (kvh * hd, hid), "wv": (kvh * hd, hid), "wo": (hid, hid),
-              "mlp_up": (mlp, hid), "mlp_down": (hid, mlp)}
-    if cfg.attn_gate:
-        shapes["gate"] = (hid, hid)
-    if cfg.mlp_act == "swiglu":
-        shapes["mlp_gate"] = (mlp, hid)
-    host, dev = {}, {}
-    for i, (name, (n, k)) in enumerate(sorted(shapes.items())):
-        if per_channel:
-            q, s = O.quant_fp8_channel(randn(n * k, seed + i, 0.02), n, k)
-            host[name] = {"bytes": q, "n": n, "k": k, "chan_scale": s}
-            dev[name] = we.Linear(graph.buffer(q), "fp8", 1.0, n, k, chan_scale=graph.buffer(s))
-        else:
-            q = fast_fp8(n * k, seed + i)
-            sc = 0.002 if k <= 512 else 0.002 * (512 / k) ** 0.5
-            host[name] = {"bytes": q, "n": n, "k": k, "scale": sc}
-            dev[name] = we.Linear(graph.buffer(q), "fp8", sc, n, k)
-    vec = {"norm1": randn(hid, seed + 50, 0.5), "norm2": randn(hid, seed + 51, 0.5), "norm_q": randn(hd, seed + 52, 0.5),
-           "norm_k": randn(hd, seed + 53, 0.5), "table": randn(6 * hid, seed + 54, 0.3)}
-    host.update(vec)
-    bw = we.blocks.BlockWeights(**dev, **{k: graph.buffer(v) for k, v in vec.items()})
-    return host, bw
 
 
 def test_block_f32_matches_the_float64_block(we, graph):  # tests/gpu/block.test.ts:102-136

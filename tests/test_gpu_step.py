@@ -1,0 +1,140 @@
+"""GPU parity of the step driver (src/model/transformer.ts:41-176, src/model/sampler.ts).
+
+- patchify / unpatchify on the device: bit-exact against the oracle on the reference test's shapes (even, odd
+  and the 128x128 latent of a 1024x1024 image), f32 and bf16.
+- the double-stream block (two parts, one attention) against the float64 joint-block restatement: f32 with the
+  reference block test's tolerance (cosine > 0.99999, relErr < 1e-4), bf16 with the bf16 block test's
+  (update cosine >= 0.9999, max-abs-rel < 1e-2).
+- whole steps against oracle.step_reference: f32 on a tiny model (cosine > 0.99999, relErr < 1e-4); bf16 on a
+  small model with 128-wide heads (velocity cosine >= 0.9999, max-abs-rel < 2e-2: bf16 activations at every GEMM
+  input across 4 blocks, against float64).
+- the text cache gives the same velocity bit for bit; the device Euler step equals the f32 formula.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from util import bf16, bf16_round, make_block, make_step, randn
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("h,w", [(4, 6), (3, 5), (5, 7), (8, 8), (128, 128)])
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_patchify_unpatchify_bit_exact(we, graph, h, w, dt):
+    T = we.transformer
+    lat = np.sin(np.arange(16 * h * w) * 0.37).astype(np.float32) * 3
+    if dt == "bf16":
+        lat = bf16_round(lat)
+    rows, cols = T.patch_grid(h, w)
+    es = 2 if dt == "bf16" else 4
+    mark = graph.mark()
+    src = graph.buffer(bf16(lat) if dt == "bf16" else lat)
+    tok = graph.buffer(rows * cols * 64 * es)
+    back = graph.buffer(16 * h * w * 4)
+    T.patchify(graph, src, h, w, tok, 16, dt, dt)
+    T.unpatchify(graph, tok, h, w, back, 16, dt, "f32")
+    raw = graph.read(tok, rows * cols * 64 * es)
+    got = O.bf16_to_f32(raw.view(np.uint16)) if dt == "bf16" else raw.view(np.float32)
+    again = graph.read(back, 16 * h * w * 4, np.float32).copy()
+    graph.release(mark)
+    assert np.array_equal(got, O.patchify(lat, h, w))
+    assert np.array_equal(again, lat)
+
+
+def test_patchify_rejects_bad_shapes(we, graph):
+    b = graph.buffer(64)
+    with pytest.raises(we._lib.WeError, match="positive"):
+        we.transformer.patchify(graph, b, 0, 4, b)
+
+
+def _double_case(we, graph, cfg, text, side, seed, dtype, per_channel=False):
+    tokens = text + side * side
+    axes = (8, 12, 12) if cfg.head_dim == 32 else (16, 56, 56)
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(text, side, side), axes, 1e4)
+    ht, dt_ = make_block(we, graph, cfg, seed, per_channel)
+    hi, di = make_block(we, graph, cfg, seed + 77, per_channel)
+    x, temb = randn(tokens * cfg.hidden, seed + 1, 1.0), randn(6 * cfg.hidden, seed + 2, 0.3)
+    want = O.joint_block_reference(x.reshape(tokens, -1), [(0, text, ht), (text, tokens - text, hi)], vars(cfg), temb,
+                                   cos, sin)
+    mark = graph.mark()
+    rope = we.Rope(graph.buffer(cos), graph.buffer(sin), pairs, tokens)
+    out = we.blocks.double_block(graph, dt_, di, cfg, graph.buffer(x), text, graph.buffer(temb), rope, dtype=dtype)
+    got = graph.read(out, tokens * cfg.hidden * 4, np.float32).reshape(tokens, -1).copy()
+    assert graph.device_error() == 0
+    graph.release(mark)
+    return x.reshape(tokens, -1), got, want
+
+
+def test_double_block_f32(we, graph):
+    cfg = we.blocks.BlockConfig(hidden=64, mlp=96, heads=2, kv_heads=1, head_dim=32, mlp_act="gelu", attn_gate=False)
+    _, got, want = _double_case(we, graph, cfg, 5, 4, 300, "f32")
+    c = O.compare(got.ravel(), want.ravel())
+    assert c["cosine"] > 0.99999 and c["relativeError"] < 1e-4, c
+
+
+@pytest.mark.parametrize("mlp_act,gate", [("gelu", False), ("swiglu", True)])
+def test_double_block_bf16(we, graph, mlp_act, gate):
+    cfg = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=4, head_dim=128, mlp_act=mlp_act,
+                                attn_gate=gate)
+    x, got, want = _double_case(we, graph, cfg, 24, 18, 400, "bf16", per_channel=True)
+    delta, wdelta = got - x, want - x
+    c = O.compare(delta.ravel(), wdelta.ravel())
+    rel = float(np.max(np.abs(delta - wdelta)) / np.max(np.abs(wdelta)))
+    assert c["cosine"] >= 0.9999 and rel < 1e-2, (c, rel)
+
+
+def _step_case(we, graph, scfg, h, w, text, seed, dtype, per_channel=False):
+    T = we.transformer
+    host, wts = make_step(we, graph, scfg, seed, per_channel)
+    lat = randn(scfg.channels * h * w, seed + 5)
+    ctx = randn(text * scfg.ctx_dim, seed + 6)
+    if dtype == "bf16":
+        lat, ctx = bf16_round(lat), bf16_round(ctx)
+    want = O.step_reference(lat, h, w, 0.63, ctx, host, {**vars(scfg.block), "axes": scfg.axes, "theta": scfg.theta,
+                                                          "channels": scfg.channels, "time_dim": scfg.time_dim})
+    conv = bf16 if dtype == "bf16" else (lambda a: a)
+    mark = graph.mark()
+    inp = T.StepInputs(graph.buffer(conv(lat)), h, w, 0.63, graph.buffer(conv(ctx)), text)
+    vel, txt = T.transformer(graph, wts, scfg, inp, dtype=dtype)
+    got = graph.read(vel, scfg.channels * h * w * 4, np.float32).copy()
+    inp.text_cache = txt
+    vel2, _ = T.transformer(graph, wts, scfg, inp, dtype=dtype)
+    again = graph.read(vel2, scfg.channels * h * w * 4, np.float32).copy()
+    assert graph.device_error() == 0
+    graph.release(mark)
+    return got, again, want
+
+
+def test_step_f32_matches_the_float64_step(we, graph):
+    T = we.transformer
+    bc = we.blocks.BlockConfig(hidden=64, mlp=128, heads=2, kv_heads=2, head_dim=32, mlp_act="gelu", attn_gate=False)
+    scfg = T.StepConfig(block=bc, double=1, single=2, ctx_dim=48, axes=(8, 12, 12))
+    got, again, want = _step_case(we, graph, scfg, 6, 10, 5, 500, "f32")
+    c = O.compare(got, want)
+    assert c["cosine"] > 0.99999 and c["relativeError"] < 1e-4, c
+    assert np.array_equal(got, again)
+
+
+def test_step_bf16_matches_the_float64_step(we, graph):
+    T = we.transformer
+    bc = we.blocks.BlockConfig(hidden=256, mlp=1024, heads=2, kv_heads=2, head_dim=128, mlp_act="gelu",
+                               attn_gate=False)
+    scfg = T.StepConfig(block=bc, double=2, single=2, ctx_dim=256)
+    got, again, want = _step_case(we, graph, scfg, 16, 18, 8, 600, "bf16", per_channel=True)
+    c = O.compare(got, want)
+    rel = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    assert c["cosine"] >= 0.9999 and rel < 2e-2, (c, rel)
+    assert np.array_equal(got, again)
+
+
+def test_euler_step_on_device(we, graph):
+    T = we.transformer
+    x, v = randn(1000, 1), randn(1000, 2)
+    s = T.sigmas(4)
+    mark = graph.mark()
+    out = T.euler_step(graph, graph.buffer(x), graph.buffer(v), s[1], s[2], 1000)
+    got = graph.read(out, 4000, np.float32).copy()
+    graph.release(mark)
+    want = O.euler_step(x, v, s[1], s[2])
+    assert np.max(np.abs(got - want)) <= 2 * np.spacing(np.abs(want).max())

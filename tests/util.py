@@ -45,3 +45,62 @@ def bf16_round(x):
 
 def max_err(a, b):
     return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64)))) if np.size(a) else 0.0
+
+
+def make_linear(we, graph, n, k, seed, per_channel=True, std=0.02):
+    """A random fp8 linear on the device and its host dict for the float64 oracle. per_channel: N(0, std)
+    weights quantised with per-output-channel absmax scales; else random e4m3 bytes with a scalar scale."""
+    if per_channel:
+        q, s = O.quant_fp8_channel(randn(n * k, seed, std), n, k)
+        return {"bytes": q, "n": n, "k": k, "chan_scale": s}, we.Linear(graph.buffer(q), "fp8", 1.0, n, k,
+                                                                         chan_scale=graph.buffer(s))
+    q = fast_fp8(n * k, seed)
+    sc = 0.002 if k <= 512 else 0.002 * (512 / k) ** 0.5
+    return {"bytes": q, "n": n, "k": k, "scale": sc}, we.Linear(graph.buffer(q), "fp8", sc, n, k)
+
+
+def make_block(we, graph, cfg, seed, per_channel=False):
+    """Random fp8 block weights on the device plus their host copies for the float64 reference."""
+    hid, mlp, heads, kvh, hd = cfg.hidden, cfg.mlp, cfg.heads, cfg.kv_heads, cfg.head_dim
+    shapes = {"wq": (heads * hd, hid), "wk": (kvh * hd, hid), "wv": (kvh * hd, hid), "wo": (hid, hid),
+              "mlp_up": (mlp, hid), "mlp_down": (hid, mlp)}
+    if cfg.attn_gate:
+        shapes["gate"] = (hid, hid)
+    if cfg.mlp_act == "swiglu":
+        shapes["mlp_gate"] = (mlp, hid)
+    host, dev = {}, {}
+    for i, (name, (n, k)) in enumerate(sorted(shapes.items())):
+        host[name], dev[name] = make_linear(we, graph, n, k, seed + i, per_channel)
+    vec = {"norm1": randn(hid, seed + 50, 0.5), "norm2": randn(hid, seed + 51, 0.5), "norm_q": randn(hd, seed + 52, 0.5),
+           "norm_k": randn(hd, seed + 53, 0.5), "table": randn(6 * hid, seed + 54, 0.3)}
+    host.update(vec)
+    bw = we.blocks.BlockWeights(**dev, **{k: graph.buffer(v) for k, v in vec.items()})
+    return host, bw
+
+
+def make_step(we, graph, scfg, seed, per_channel=False):
+    """Random weights of a whole step model (Flux-style layout) on the device plus host copies for
+    oracle.step_reference. The edge linears (time MLP, text, first, last) are per-channel N(0, 0.02)."""
+    bc, T = scfg.block, we.transformer
+    hid, ch = bc.hidden, scfg.channels
+    host, dev = {}, {}
+    for i, (name, (n, k)) in enumerate([("first", (hid, 4 * ch)), ("tmlp0", (hid, scfg.time_dim)),
+                                        ("tmlp2", (hid, hid)), ("tproj", (6 * hid, hid)),
+                                        ("txt_in", (hid, scfg.ctx_dim)), ("last_linear", (4 * ch, hid))]):
+        host[name], dev[name] = make_linear(we, graph, n, k, seed + i, True)
+    host["double"], dev["double"] = [], []
+    for i in range(scfg.double):
+        ht, dt = make_block(we, graph, bc, seed + 1000 + 200 * i, per_channel)
+        hi, di = make_block(we, graph, bc, seed + 1100 + 200 * i, per_channel)
+        host["double"].append((ht, hi))
+        dev["double"].append((dt, di))
+    host["single"], dev["single"] = [], []
+    for i in range(scfg.single):
+        hb, db = make_block(we, graph, bc, seed + 9000 + 100 * i, per_channel)
+        host["single"].append(hb)
+        dev["single"].append(db)
+    for i, name in enumerate(("last_norm", "last_scale", "last_shift")):
+        host[name] = randn(hid, seed + 60 + i, 0.3)
+        dev[name] = graph.buffer(host[name])
+    return host, T.TransformerWeights(**dev)
+

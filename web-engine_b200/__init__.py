@@ -9,9 +9,10 @@ from .ops import Linear, Mod, Rope, attention, k_split_for, linear, no_mod, norm
 from . import kernels, parallel
 from .stream import Streamer
 from . import block as blocks
+from . import transformer
 
 __all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "norm", "no_mod", "rotate",
-           "qk_norm_rotate", "k_split_for", "kernels", "build"]
+           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "build"]
 
 
 def build(verbose: bool = False) -> str:

@@ -1,12 +1,18 @@
-"""One transformer block on the hot-path kernels: the caller of linear / norm / rotate (src/model/block.ts).
+"""Transformer blocks on the hot-path kernels: the callers of linear / norm / rotate (src/model/block.ts).
+
+A single-stream block (block.ts:83-105):
 
     h  = (1 + prescale) norm1(x) + preshift
     x1 = x + pregate  wo(attention(rope(norm_q(wq h)), rope(norm_k(wk h)), wv h) [ * sigmoid(gate h)])
     h2 = (1 + postscale) norm2(x1) + postshift
-    y  = x1 + postgate down(mlp(h2)),  mlp = silu(mlp_gate h2) up h2 (Krea 2)  or  gelu(up h2)
+    y  = x1 + postgate down(mlp(h2)),  mlp = silu(mlp_gate h2) up h2 (Krea 2)  or  gelu(up h2) (GELU MLP)
 
-`block(..., dtype="f32")` mirrors block.ts op by op (linear, norm, rotate, attention, sigmoidGate, gatedAdd,
-swiglu: the reference's f32 semantics, src/model/block.ts:91-105). `dtype="bf16"` is the B200 path:
+A double-stream block runs the same formulas on two row ranges of one token sequence (text rows first, then
+image rows), each with its own weights and modulation table, and one attention over all rows (the Flux-style
+MMDiT block; every op it uses is the single block's). Both are `joint_block` over a list of `Part`s.
+
+`dtype="f32"` mirrors block.ts op by op (linear, norm, rotate, attention, sigmoidGate, gatedAdd, swiglu: the
+reference's f32 semantics, src/model/block.ts:91-105). `dtype="bf16"` is the B200 path:
 - each RMSNorm writes the e4m3 split of its bf16 output directly (we_norm_split) for the fp8 GEMMs;
 - q/k get the fused norm + RoPE;
 - attention runs on the tcgen05 flash kernel;
@@ -19,7 +25,7 @@ from dataclasses import dataclass
 
 from . import kernels as K
 from . import ops
-from .graph import Buffer, Graph
+from .graph import Buffer, Graph, addr
 
 
 @dataclass
@@ -32,14 +38,14 @@ class BlockConfig:
     kv_heads: int
     head_dim: int
     eps: float = 1e-5
-    mlp_act: str = "swiglu"   # "swiglu" (Krea 2) | "gelu"
+    mlp_act: str = "swiglu"   # "swiglu" (Krea 2) | "gelu" (tanh GELU, 4x MLP)
     attn_gate: bool = True
 
 
 @dataclass
 class BlockWeights:
-    """Device weights of one block. Linears are ops.Linear (fp8 with per-tensor or per-channel scales);
-    norm weights and the modulation table are f32."""
+    """Device weights of one block (or one stream of a double block). Linears are ops.Linear (fp8 with
+    per-tensor or per-channel scales); norm weights and the modulation table are f32."""
 
     wq: ops.Linear
     wk: ops.Linear
@@ -56,64 +62,106 @@ class BlockWeights:
     mlp_gate: ops.Linear | None = None
 
 
+@dataclass
+class Part:
+    """Rows [row0, row0 + rows) of the token sequence, with their own block weights."""
+
+    row0: int
+    rows: int
+    w: BlockWeights
+
+
 MOD = ("prescale", "preshift", "pregate", "postscale", "postshift", "postgate")
 
 
 def modulation(graph: Graph, tvec, table, hidden: int) -> dict:
     """tvec + the block's table, split into the 6 modulation vectors (src/model/block.ts:33-37)."""
     mod = ops.add(graph, tvec, table, 6 * hidden)
-    return {name: Graph.slice(mod, i * hidden * 4, hidden * 4) if (i * hidden * 4) % 256 == 0
-            else _Offset(mod, i * hidden * 4) for i, name in enumerate(MOD)}
+    return {name: mod.ptr + i * hidden * 4 for i, name in enumerate(MOD)}
 
 
-class _Offset:
-    """A device address inside a buffer, for slices not on a 256-byte boundary."""
+def rows_at(buf, row0: int, row_bytes: int) -> int:
+    """Device address of row `row0` of a row-major buffer."""
+    return addr(buf).value + row0 * row_bytes
 
-    def __init__(self, buf: Buffer, offset: int):
-        self.ptr = buf.ptr + offset
 
-    @property
-    def c(self):
-        import ctypes
-
-        return ctypes.c_void_p(self.ptr)
+def part_rope(rope: ops.Rope, p: Part) -> ops.Rope:
+    """The cos/sin rows of one part."""
+    return ops.Rope(rows_at(rope.cos, p.row0, rope.pairs * 4), rows_at(rope.sin, p.row0, rope.pairs * 4), rope.pairs,
+                    p.rows)
 
 
 def block(graph: Graph, w: BlockWeights, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32") -> Buffer:
-    """x [tokens, hidden] f32 -> a new [tokens, hidden] f32 buffer."""
+    """A single-stream block: x [tokens, hidden] f32 -> a new [tokens, hidden] f32 buffer."""
+    return joint_block(graph, [Part(0, rope.tokens, w)], cfg, x, tvec, rope, dtype)
+
+
+def double_block(graph: Graph, txt: BlockWeights, img: BlockWeights, cfg: BlockConfig, x, txt_rows: int, tvec,
+                 rope: ops.Rope, dtype: str = "f32") -> Buffer:
+    """A double-stream block: rows [0, txt_rows) use `txt`, the rest `img`; attention spans all rows."""
+    return joint_block(graph, [Part(0, txt_rows, txt), Part(txt_rows, rope.tokens - txt_rows, img)], cfg, x, tvec, rope,
+                       dtype)
+
+
+def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32") -> Buffer:
+    parts = [p for p in parts if p.rows > 0]
+    if sum(p.rows for p in parts) != rope.tokens:
+        raise ValueError("the parts must cover the rope's tokens")
     if dtype == "f32":
-        return _block_f32(graph, w, cfg, x, tvec, rope)
+        return _joint_f32(graph, parts, cfg, x, tvec, rope)
     if dtype == "bf16":
-        return _block_bf16(graph, w, cfg, x, tvec, rope)
+        return _joint_bf16(graph, parts, cfg, x, tvec, rope)
     raise ValueError(f"unknown block dtype {dtype}")
 
 
-def _block_f32(graph, w, cfg, x, tvec, rope):
-    t, hd = rope.tokens, cfg.hidden
+def _joint_f32(graph, parts, cfg, x, tvec, rope):
+    t, hd, hdim = rope.tokens, cfg.hidden, cfg.head_dim
+    qw, kw = cfg.heads * hdim, cfg.kv_heads * hdim
     mark = graph.mark()
-    mod = modulation(graph, tvec, w.table, hd)
-    h = ops.norm(graph, x, w.norm1, t, hd, ops.Mod(mod["prescale"], mod["preshift"]), cfg.eps)
-    none = ops.no_mod(graph, cfg.head_dim)
-    q = ops.linear(graph, h, w.wq, t)
-    q = ops.norm(graph, q, w.norm_q, t * cfg.heads, cfg.head_dim, none, cfg.eps)
-    q = ops.rotate(graph, q, cfg.heads, rope)
-    k = ops.linear(graph, h, w.wk, t)
-    k = ops.norm(graph, k, w.norm_k, t * cfg.kv_heads, cfg.head_dim, none, cfg.eps)
-    k = ops.rotate(graph, k, cfg.kv_heads, rope)
-    v = ops.linear(graph, h, w.wv, t)
-    o = ops.attention(graph, q, k, v, t, cfg.heads, cfg.kv_heads, cfg.head_dim)
-    if cfg.attn_gate:
-        g = ops.linear(graph, h, w.gate, t)
-        o = ops.sigmoid_gate(graph, o, g, t * hd)
-    a = ops.linear(graph, o, w.wo, t)
-    x1 = ops.gated_add(graph, x, a, mod["pregate"], t * hd, hd)
-    h2 = ops.norm(graph, x1, w.norm2, t, hd, ops.Mod(mod["postscale"], mod["postshift"]), cfg.eps)
-    if cfg.mlp_act == "swiglu":
-        m = ops.swiglu(graph, ops.linear(graph, h2, w.mlp_gate, t), ops.linear(graph, h2, w.mlp_up, t), t * cfg.mlp)
-    else:
-        m = ops.gelu(graph, ops.linear(graph, h2, w.mlp_up, t), t * cfg.mlp)
-    d = ops.linear(graph, m, w.mlp_down, t)
-    out = ops.gated_add(graph, x1, d, mod["postgate"], t * hd, hd)
+    none = ops.no_mod(graph, hdim)
+    one = len(parts) == 1
+    if not one:
+        q, k, v = graph.buffer(t * qw * 4), graph.buffer(t * kw * 4), graph.buffer(t * kw * 4)
+    hs, mods = [], []
+    for p in parts:
+        mod = modulation(graph, tvec, p.w.table, hd)
+        h = ops.norm(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd,
+                     ops.Mod(mod["prescale"], mod["preshift"]), cfg.eps)
+        pr = part_rope(rope, p)
+        qp = ops.linear(graph, h, p.w.wq, p.rows)
+        qp = ops.rotate(graph, ops.norm(graph, qp, p.w.norm_q, p.rows * cfg.heads, hdim, none, cfg.eps), cfg.heads, pr)
+        kp = ops.linear(graph, h, p.w.wk, p.rows)
+        kp = ops.rotate(graph, ops.norm(graph, kp, p.w.norm_k, p.rows * cfg.kv_heads, hdim, none, cfg.eps),
+                        cfg.kv_heads, pr)
+        vp = ops.linear(graph, h, p.w.wv, p.rows)
+        if one:
+            q, k, v = qp, kp, vp
+        else:
+            graph.copy(qp, 0, q, p.row0 * qw * 4, p.rows * qw * 4)
+            graph.copy(kp, 0, k, p.row0 * kw * 4, p.rows * kw * 4)
+            graph.copy(vp, 0, v, p.row0 * kw * 4, p.rows * kw * 4)
+        hs.append(h)
+        mods.append(mod)
+    o = ops.attention(graph, q, k, v, t, cfg.heads, cfg.kv_heads, hdim)
+    out = None if one else graph.buffer(t * hd * 4)
+    for p, h, mod in zip(parts, hs, mods):
+        op = rows_at(o, p.row0, hd * 4)
+        if cfg.attn_gate:
+            op = ops.sigmoid_gate(graph, op, ops.linear(graph, h, p.w.gate, p.rows), p.rows * hd)
+        a = ops.linear(graph, op, p.w.wo, p.rows)
+        x1 = ops.gated_add(graph, rows_at(x, p.row0, hd * 4), a, mod["pregate"], p.rows * hd, hd)
+        h2 = ops.norm(graph, x1, p.w.norm2, p.rows, hd, ops.Mod(mod["postscale"], mod["postshift"]), cfg.eps)
+        if cfg.mlp_act == "swiglu":
+            m = ops.swiglu(graph, ops.linear(graph, h2, p.w.mlp_gate, p.rows), ops.linear(graph, h2, p.w.mlp_up, p.rows),
+                           p.rows * cfg.mlp)
+        else:
+            m = ops.gelu(graph, ops.linear(graph, h2, p.w.mlp_up, p.rows), p.rows * cfg.mlp)
+        d = ops.linear(graph, m, p.w.mlp_down, p.rows)
+        op_out = ops.gated_add(graph, x1, d, mod["postgate"], p.rows * hd, hd)
+        if one:
+            out = op_out
+        else:
+            graph.copy(op_out, 0, out, p.row0 * hd * 4, p.rows * hd * 4)
     graph.release(mark, [out])
     return out
 
@@ -124,51 +172,72 @@ def _gemm(graph, split, lin: ops.Linear, y, t, y_dtype, **epi):
                bias=lin.bias, y_dtype=y_dtype, **epi)
 
 
-def _block_bf16(graph, w, cfg, x, tvec, rope):
+def _split_rows(split, p: Part, width: int):
+    """The e4m3 planes (1 byte per value) and row scales of one part."""
+    return (rows_at(split[0], p.row0, width), rows_at(split[1], p.row0, width), rows_at(split[2], p.row0, 4))
+
+
+def _joint_bf16(graph, parts, cfg, x, tvec, rope):
     t, hd, hdim = rope.tokens, cfg.hidden, cfg.head_dim
+    qw, kw = cfg.heads * hdim, cfg.kv_heads * hdim
     mark = graph.mark()
-    mod = modulation(graph, tvec, w.table, hd)
+    mods = [modulation(graph, tvec, p.w.table, hd) for p in parts]
     split = (graph.buffer(t * hd), graph.buffer(t * hd), graph.buffer(t * 4))
-    K.norm_split(graph, x, w.norm1, t, hd, *split, scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
-    q = graph.buffer(t * cfg.heads * hdim * 2)
-    k = graph.buffer(t * cfg.kv_heads * hdim * 2)
-    v = graph.buffer(t * cfg.kv_heads * hdim * 2)
-    _gemm(graph, split, w.wq, q, t, "bf16")
-    _gemm(graph, split, w.wk, k, t, "bf16")
-    _gemm(graph, split, w.wv, v, t, "bf16")
-    K.qknorm_rope(graph, q, w.norm_q, rope.cos, rope.sin, t, cfg.heads, rope.pairs, q, eps=cfg.eps,
-                  x_dtype="bf16", out_dtype="bf16")
-    K.qknorm_rope(graph, k, w.norm_k, rope.cos, rope.sin, t, cfg.kv_heads, rope.pairs, k, eps=cfg.eps,
-                  x_dtype="bf16", out_dtype="bf16")
+    q, k, v = graph.buffer(t * qw * 2), graph.buffer(t * kw * 2), graph.buffer(t * kw * 2)
+    for p, mod in zip(parts, mods):
+        sp = _split_rows(split, p, hd)
+        K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *sp, scale=mod["prescale"],
+                     shift=mod["preshift"], eps=cfg.eps)
+        qp, kp = rows_at(q, p.row0, qw * 2), rows_at(k, p.row0, kw * 2)
+        _gemm(graph, sp, p.w.wq, qp, p.rows, "bf16")
+        _gemm(graph, sp, p.w.wk, kp, p.rows, "bf16")
+        _gemm(graph, sp, p.w.wv, rows_at(v, p.row0, kw * 2), p.rows, "bf16")
+        pr = part_rope(rope, p)
+        K.qknorm_rope(graph, qp, p.w.norm_q, pr.cos, pr.sin, p.rows, cfg.heads, rope.pairs, qp, eps=cfg.eps,
+                      x_dtype="bf16", out_dtype="bf16")
+        K.qknorm_rope(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, cfg.kv_heads, rope.pairs, kp, eps=cfg.eps,
+                      x_dtype="bf16", out_dtype="bf16")
     o = graph.buffer(t * hd * 2)
     K.attention(graph, q, k, v, t, cfg.heads, cfg.kv_heads, hdim, o, dtype="bf16", out_dtype="bf16")
     if cfg.attn_gate:  # og = o * sigmoid(gate h), in the gate GEMM's epilogue
         og = graph.buffer(t * hd * 2)
-        _gemm(graph, split, w.gate, og, t, "bf16", aux_op="sigmoid_gate", aux=o, aux_dtype="bf16")
+        for p in parts:
+            _gemm(graph, _split_rows(split, p, hd), p.w.gate, rows_at(og, p.row0, hd * 2), p.rows, "bf16",
+                  aux_op="sigmoid_gate", aux=rows_at(o, p.row0, hd * 2), aux_dtype="bf16")
         o = og
     K.quantize_act(graph, o, t, hd, *split, terms=2)
     x1 = graph.buffer(t * hd * 4)
     graph.copy(x, 0, x1, 0, t * hd * 4)
-    _gemm(graph, split, w.wo, x1, t, "f32", accumulate=True, gate=mod["pregate"])  # x1 = x + pregate wo(o)
-    K.norm_split(graph, x1, w.norm2, t, hd, *split, scale=mod["postscale"], shift=mod["postshift"], eps=cfg.eps)
+    for p, mod in zip(parts, mods):  # x1 = x + pregate wo(o)
+        _gemm(graph, _split_rows(split, p, hd), p.w.wo, rows_at(x1, p.row0, hd * 4), p.rows, "f32", accumulate=True,
+              gate=mod["pregate"])
     u = graph.buffer(t * cfg.mlp * 2)
-    if cfg.mlp_act == "swiglu":
-        g = graph.buffer(t * cfg.mlp * 2)
-        _gemm(graph, split, w.mlp_gate, g, t, "bf16")
-        _gemm(graph, split, w.mlp_up, u, t, "bf16", aux_op="swiglu", aux=g, aux_dtype="bf16")
-    else:
-        _gemm(graph, split, w.mlp_up, u, t, "bf16", act="gelu_tanh")
+    g = graph.buffer(t * cfg.mlp * 2) if cfg.mlp_act == "swiglu" else None
+    for p, mod in zip(parts, mods):
+        sp = _split_rows(split, p, hd)
+        K.norm_split(graph, rows_at(x1, p.row0, hd * 4), p.w.norm2, p.rows, hd, *sp, scale=mod["postscale"],
+                     shift=mod["postshift"], eps=cfg.eps)
+        up = rows_at(u, p.row0, cfg.mlp * 2)
+        if cfg.mlp_act == "swiglu":
+            gp = rows_at(g, p.row0, cfg.mlp * 2)
+            _gemm(graph, sp, p.w.mlp_gate, gp, p.rows, "bf16")
+            _gemm(graph, sp, p.w.mlp_up, up, p.rows, "bf16", aux_op="swiglu", aux=gp, aux_dtype="bf16")
+        else:
+            _gemm(graph, sp, p.w.mlp_up, up, p.rows, "bf16", act="gelu_tanh")
     msplit = (graph.buffer(t * cfg.mlp), graph.buffer(t * cfg.mlp), split[2])
     K.quantize_act(graph, u, t, cfg.mlp, *msplit, terms=2)
     out = graph.buffer(t * hd * 4)
     graph.copy(x1, 0, out, 0, t * hd * 4)
-    _gemm(graph, msplit, w.mlp_down, out, t, "f32", accumulate=True, gate=mod["postgate"])  # out = x1 + postgate d
+    for p, mod in zip(parts, mods):  # out = x1 + postgate down(m)
+        _gemm(graph, _split_rows(msplit, p, cfg.mlp), p.w.mlp_down, rows_at(out, p.row0, hd * 4), p.rows, "f32",
+              accumulate=True, gate=mod["postgate"])
     graph.release(mark, [out])
     return out
 
 
 def block_flops(cfg: BlockConfig, tokens: int) -> dict:
-    """Multiply-add work of one block (2 FLOP per MAC): linears and attention (4 T^2 H D)."""
+    """Multiply-add work of one block (2 FLOP per MAC): linears and attention (4 T^2 H D). A double block over the
+    same tokens does the same work (each row goes through one stream's linears)."""
     hd, kvd = cfg.hidden, cfg.kv_heads * cfg.head_dim
     lin = 2 * tokens * (hd * hd * (2 + (1 if cfg.attn_gate else 0)) + 2 * hd * kvd
                         + hd * cfg.mlp * (3 if cfg.mlp_act == "swiglu" else 2))

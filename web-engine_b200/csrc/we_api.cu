@@ -658,6 +658,35 @@ int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weig
   return WE_OK;
 }
 
+// ---------------- latent <-> tokens ----------------
+static int layout_check(we_ctx* ctx, const void* a, const void* b, int32_t adt, int32_t bdt, int64_t c, int64_t h,
+                        int64_t w) {
+  if (!a || !b) return fail(ctx, WE_EINVAL, "patchify: missing buffer");
+  if (!act_dtype_ok(adt) || !act_dtype_ok(bdt)) return fail(ctx, WE_EINVAL, "patchify: f32 or bf16 only");
+  if (c <= 0 || h <= 0 || w <= 0) return fail(ctx, WE_EINVAL, "patchify: channels, height and width must be positive");
+  return WE_OK;
+}
+
+int we_patchify(we_ctx* ctx, const void* latent, int32_t latent_dtype, int64_t channels, int64_t height, int64_t width,
+                void* tokens, int32_t tokens_dtype) {
+  if (!ctx) return WE_EINVAL;
+  int rc = layout_check(ctx, latent, tokens, latent_dtype, tokens_dtype, channels, height, width);
+  if (rc != WE_OK) return rc;
+  LK(we::launch_patchify(latent, latent_dtype, channels, height, width, tokens, tokens_dtype, ctx->sms, ctx->stream),
+     "patchify");
+  return WE_OK;
+}
+
+int we_unpatchify(we_ctx* ctx, const void* tokens, int32_t tokens_dtype, int64_t channels, int64_t height,
+                  int64_t width, void* latent, int32_t latent_dtype) {
+  if (!ctx) return WE_EINVAL;
+  int rc = layout_check(ctx, tokens, latent, tokens_dtype, latent_dtype, channels, height, width);
+  if (rc != WE_OK) return rc;
+  LK(we::launch_unpatchify(tokens, tokens_dtype, channels, height, width, latent, latent_dtype, ctx->sms, ctx->stream),
+     "unpatchify");
+  return WE_OK;
+}
+
 // ---------------- attention ----------------
 int we_attention(we_ctx* ctx, const void* q, const void* k, const void* v, int32_t dtype, int64_t tokens, int64_t heads,
                  int64_t kv_heads, int64_t dim, int32_t causal, void* out, int32_t out_dtype) {

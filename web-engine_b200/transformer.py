@@ -1,0 +1,223 @@
+"""The denoising step around the blocks (src/model/transformer.ts:41-176) and the sampler (src/model/sampler.ts).
+
+One step, as transformer.ts:134-176 lays it out:
+
+    t, tvec = time(timestep)                 tmlp2(gelu(tmlp0(sincos(1000 t))))  and  tproj(gelu(t)) -> 6 x hidden
+    txt     = txt_in(context)                [L, hidden], cached per image (it does not depend on the timestep)
+    img     = first(patchify(latent))        [rows * cols, hidden]
+    x       = [txt; img]                     [T, hidden] f32 residual stream, T = L + rows * cols
+    x       = double blocks (text rows / image rows with their own weights, one attention), then single blocks
+    v       = unpatchify(last((1 + t + last_scale) norm(x) + t + last_shift)[L:])
+
+The reference's model is Krea 2 (single-stream blocks only, a text encoder in front); the layout here is the
+Flux-style MMDiT of the benchmark configs (`double` two-stream blocks, then `single` blocks, a linear text
+projection). Every op is the reference's: linear, norm, rotate, attention, the elementwise steps.
+
+`dtype="f32"` runs the reference's f32 op semantics. `dtype="bf16"` is the B200 path: bf16 latent and context,
+fp8 tcgen05 GEMMs on the exact e4m3 split, fused norm + split, q/k norm + RoPE, flash attention, fused epilogues;
+the residual stream stays f32.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _lib as L
+from . import kernels as K
+from . import ops
+from .block import BlockConfig, BlockWeights, block_flops, double_block, joint_block, Part
+from .graph import Buffer, Graph, addr
+
+LATENT_CHANNELS = 16
+TIME_DIM = 256
+
+# Config 3/4 block: 3072 hidden, 24 x 128 heads, 4x GELU MLP, no attention gate; RoPE axes 16/56/56, theta 1e4
+FLUX_BLOCK = BlockConfig(hidden=3072, mlp=12288, heads=24, kv_heads=24, head_dim=128, eps=1e-5, mlp_act="gelu",
+                         attn_gate=False)
+
+
+@dataclass
+class StepConfig:
+    block: BlockConfig = field(default_factory=lambda: FLUX_BLOCK)
+    double: int = 19
+    single: int = 38
+    channels: int = LATENT_CHANNELS
+    ctx_dim: int = 3072
+    time_dim: int = TIME_DIM
+    axes: tuple = (16, 56, 56)
+    theta: float = 1e4
+
+
+@dataclass
+class TransformerWeights:
+    """Device weights of the whole model (TransformerWeights, transformer.ts:20-37, Flux-style layout)."""
+
+    first: ops.Linear            # [hidden, 4 channels]
+    tmlp0: ops.Linear            # [hidden, time_dim]
+    tmlp2: ops.Linear            # [hidden, hidden]
+    tproj: ops.Linear            # [6 hidden, hidden]
+    txt_in: ops.Linear           # [hidden, ctx_dim]
+    double: list                 # [(txt BlockWeights, img BlockWeights)]
+    single: list                 # [BlockWeights]
+    last_norm: object            # [hidden]
+    last_scale: object           # [hidden]
+    last_shift: object           # [hidden]
+    last_linear: ops.Linear      # [4 channels, hidden]
+
+
+def timestep_embedding(timestep: float, dim: int = TIME_DIM) -> np.ndarray:
+    """[cos(1000 t f_i), sin(1000 t f_i)], f_i = 10000^(-i / (dim / 2)) (transformer.ts:41-51)."""
+    half = dim // 2
+    arg = 1000.0 * timestep * np.exp(-math.log(10000.0) * np.arange(half) / half)
+    return np.concatenate([np.cos(arg), np.sin(arg)]).astype(np.float32)
+
+
+def patch_grid(height: int, width: int) -> tuple:
+    """Token grid of a latent: 2x2 patches, odd sizes padded up (transformer.ts:53)."""
+    return (height + 1) // 2, (width + 1) // 2
+
+
+def patchify(graph: Graph, latent, height: int, width: int, tokens, channels: int = LATENT_CHANNELS,
+             latent_dtype: str = "f32", tokens_dtype: str = "f32") -> None:
+    """latent [C, H, W] -> tokens [rows * cols, 4C] on the device (transformer.ts:59-69)."""
+    L.check(graph.ctx, L.lib().we_patchify(graph.ctx, addr(latent), L.DTYPES[latent_dtype], channels, height, width,
+                                           addr(tokens), L.DTYPES[tokens_dtype]))
+
+
+def unpatchify(graph: Graph, tokens, height: int, width: int, latent, channels: int = LATENT_CHANNELS,
+               tokens_dtype: str = "f32", latent_dtype: str = "f32") -> None:
+    """tokens [rows * cols, 4C] -> latent [C, H, W], padding cropped (transformer.ts:72-82)."""
+    L.check(graph.ctx, L.lib().we_unpatchify(graph.ctx, addr(tokens), L.DTYPES[tokens_dtype], channels, height, width,
+                                             addr(latent), L.DTYPES[latent_dtype]))
+
+
+def time(graph: Graph, w: TransformerWeights, timestep: float, time_dim: int = TIME_DIM):
+    """t [hidden] and tvec [6 hidden] for one timestep (transformer.ts:85-90); M = 1 linears."""
+    emb = graph.buffer(timestep_embedding(timestep, time_dim))
+    t = ops.linear(graph, ops.gelu(graph, ops.linear(graph, emb, w.tmlp0, 1), w.tmlp0.n), w.tmlp2, 1)
+    tvec = ops.linear(graph, ops.gelu(graph, t, w.tmlp2.n), w.tproj, 1)
+    return t, tvec
+
+
+def text(graph: Graph, w: TransformerWeights, context, tokens: int, dtype: str = "f32") -> Buffer:
+    """The text rows of the sequence: txt_in(context) [tokens, hidden] f32 (the Flux-style text projection; the
+    reference's Krea 2 text stack, transformer.ts:93-117, is a different model's front end)."""
+    return ops.linear(graph, context, w.txt_in, tokens, x_dtype=dtype, y_dtype="f32")
+
+
+@dataclass
+class StepInputs:
+    """One image's step inputs (Inputs, transformer.ts:124-132). latent [C, H, W] and context [L, ctx_dim] are
+    device buffers of `dtype` elements; text_cache: txt rows from an earlier step of the same image."""
+
+    latent: object
+    height: int
+    width: int
+    timestep: float
+    context: object
+    text_tokens: int
+    text_cache: object = None
+
+
+def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp: StepInputs, dtype: str = "f32",
+                velocity=None, on_block=None) -> tuple:
+    """One denoising step: the predicted velocity [C, H, W] f32 (a new buffer, or written into `velocity`), and
+    the txt rows for the next step's text_cache (transformer.ts:134-176)."""
+    bc = cfg.block
+    hid, ch = bc.hidden, cfg.channels
+    rows, cols = patch_grid(inp.height, inp.width)
+    image, Lt = rows * cols, inp.text_tokens
+    T = Lt + image
+    tables = K.rope_tables(K.positions(Lt, rows, cols), cfg.axes, cfg.theta)
+    mark = graph.mark()
+    t, tvec = time(graph, w, inp.timestep, cfg.time_dim)
+    txt = inp.text_cache if inp.text_cache is not None else text(graph, w, inp.context, Lt, dtype)
+    tok = graph.buffer(image * 4 * ch * (2 if dtype == "bf16" else 4))
+    patchify(graph, inp.latent, inp.height, inp.width, tok, ch, dtype, dtype)
+    img = ops.linear(graph, tok, w.first, image, x_dtype=dtype, y_dtype="f32")
+    x = graph.buffer(T * hid * 4)
+    graph.copy(txt, 0, x, 0, Lt * hid * 4)
+    graph.copy(img, 0, x, Lt * hid * 4, image * hid * 4)
+    rope = ops.Rope(graph.buffer(tables[0]), graph.buffer(tables[1]), tables[2], T)
+    i = 0
+    for txt_w, img_w in w.double:
+        bm = graph.mark()
+        nxt = double_block(graph, txt_w, img_w, bc, x, Lt, tvec, rope, dtype)
+        graph.release(bm, [nxt])
+        graph.free(x)
+        x = nxt
+        if on_block:
+            on_block(i)
+        i += 1
+    for bw in w.single:
+        bm = graph.mark()
+        nxt = joint_block(graph, [Part(0, T, bw)], bc, x, tvec, rope, dtype)
+        graph.release(bm, [nxt])
+        graph.free(x)
+        x = nxt
+        if on_block:
+            on_block(i)
+        i += 1
+    scale = ops.add(graph, t, w.last_scale, hid)
+    shift = ops.add(graph, t, w.last_shift, hid)
+    if dtype == "bf16":
+        split = (graph.buffer(T * hid), graph.buffer(T * hid), graph.buffer(T * 4))
+        K.norm_split(graph, x, w.last_norm, T, hid, *split, scale=scale, shift=shift, eps=bc.eps)
+        last = graph.buffer(T * 4 * ch * 4)
+        K.gemm_fp8(graph, *split, w.last_linear.buffer, last, T, w.last_linear.n, w.last_linear.k,
+                   w.last_linear.scale, chan_scale=w.last_linear.chan_scale, bias=w.last_linear.bias, y_dtype="f32")
+    else:
+        h = ops.norm(graph, x, w.last_norm, T, hid, ops.Mod(scale, shift), bc.eps)
+        last = ops.linear(graph, h, w.last_linear, T)
+    out = velocity if velocity is not None else graph.buffer(ch * inp.height * inp.width * 4)
+    unpatchify(graph, addr(last).value + Lt * 4 * ch * 4, inp.height, inp.width, out, ch, "f32", "f32")
+    keep = [b for b in (out, txt) if isinstance(b, Buffer)]
+    graph.release(mark, keep)
+    return out, txt
+
+
+def step_flops(cfg: StepConfig, text_tokens: int, image_tokens: int) -> dict:
+    """FLOPs of one step: the blocks (linears + attention) plus the first, text and last linears."""
+    T = text_tokens + image_tokens
+    b = block_flops(cfg.block, T)
+    n = cfg.double + cfg.single
+    hid = cfg.block.hidden
+    edge = 2 * (image_tokens * 4 * cfg.channels * hid + text_tokens * cfg.ctx_dim * hid + T * hid * 4 * cfg.channels)
+    return {"linear": n * b["linear"] + edge, "attention": n * b["attention"], "total": n * b["total"] + edge}
+
+
+# ---------------- sampler (src/model/sampler.ts) ----------------
+TURBO = {"steps": 8, "mu": 1.15}
+
+
+def sigmas(steps: int = TURBO["steps"], mu: float = TURBO["mu"]) -> list:
+    """linspace(1, 1/steps, steps) under the time shift e^mu / (e^mu + 1/s - 1), then 0 (sampler.ts:9-19)."""
+    raw = [1 - i * (1 - 1 / steps) / ((steps - 1) or 1) for i in range(steps)]
+    return [math.exp(mu) / (math.exp(mu) + (1 / s - 1)) for s in raw] + [0.0]
+
+
+def euler_step(graph: Graph, x, velocity, sigma: float, nxt: float, n: int, out=None) -> Buffer:
+    """x + (sigma_next - sigma) v on the device (eulerStep, sampler.ts:22-24), f32."""
+    g = graph.buffer(np.array([nxt - sigma], np.float32))
+    if out is None:
+        return ops.gated_add(graph, x, velocity, g, n, 1)
+    L.check(graph.ctx, L.lib().we_elementwise(graph.ctx, L.EW["gated_add"], addr(x), addr(velocity), addr(g), n, 1,
+                                              L.DTYPES["f32"], addr(out), L.DTYPES["f32"]))
+    return out
+
+
+def gaussian(n: int, seed: int) -> np.ndarray:
+    """Seeded standard normals: Box-Muller on a 32-bit LCG, u = (s + 0.5) / 2^32 (gaussian, sampler.ts:27-38)."""
+    s = (seed & 0xFFFFFFFF) or 1
+    m = (n + 1) // 2
+    draws = np.empty(2 * m, dtype=np.uint64)
+    for i in range(2 * m):  # the LCG is sequential; the transcendental part below is vectorised
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        draws[i] = s
+    u = (draws.astype(np.float64) + 0.5) / 2.0 ** 32
+    r, a = np.sqrt(-2.0 * np.log(u[0::2])), 2.0 * np.pi * u[1::2]
+    out = np.empty(2 * m, dtype=np.float32)
+    out[0::2], out[1::2] = r * np.cos(a), r * np.sin(a)
+    return out[:n]
