@@ -143,6 +143,115 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def random_linear(we, g, torch, dev, gen, n: int, k: int):
+    """fp8 e4m3 weights ~N(0, 0.02) with per-output-channel absmax scales (config 1's weight recipe)."""
+    w32 = torch.randn(n, k, generator=gen, device=dev) * 0.02
+    q = torch.empty(n, k, dtype=torch.uint8, device=dev)
+    s = torch.empty(n, dtype=torch.float32, device=dev)
+    we.kernels.quantize_fp8(g, w32, n, k, q, s, per_channel=True, w_dtype="f32")
+    return we.Linear(q, "fp8", 1.0, n, k, chan_scale=s)
+
+
+def random_block(we, g, torch, dev, gen, bc):
+    """One block's random weights: fp8 linears, norm weights ~N(0, 0.5), modulation table ~N(0, 0.3)."""
+    hid, hd = bc.hidden, bc.head_dim
+    lin = {"wq": (bc.heads * hd, hid), "wk": (bc.kv_heads * hd, hid), "wv": (bc.kv_heads * hd, hid),
+           "wo": (hid, hid), "mlp_up": (bc.mlp, hid), "mlp_down": (hid, bc.mlp)}
+    if bc.attn_gate:
+        lin["gate"] = (hid, hid)
+    if bc.mlp_act == "swiglu":
+        lin["mlp_gate"] = (bc.mlp, hid)
+    w = {name: random_linear(we, g, torch, dev, gen, n, k) for name, (n, k) in lin.items()}
+    for name, d, std in (("norm1", hid, 0.5), ("norm2", hid, 0.5), ("norm_q", hd, 0.5), ("norm_k", hd, 0.5),
+                         ("table", 6 * hid, 0.3)):
+        w[name] = torch.randn(d, generator=gen, device=dev) * std
+    return we.blocks.BlockWeights(**w)
+
+
+def random_model(we, g, torch, dev, gen, scfg):
+    """Config 4's model: `double` two-stream and `single` one-stream blocks plus the edge linears."""
+    bc, hid, ch = scfg.block, scfg.block.hidden, scfg.channels
+    edge = {name: random_linear(we, g, torch, dev, gen, n, k) for name, (n, k) in
+            (("first", (hid, 4 * ch)), ("tmlp0", (hid, scfg.time_dim)), ("tmlp2", (hid, hid)),
+             ("tproj", (6 * hid, hid)), ("txt_in", (hid, scfg.ctx_dim)), ("last_linear", (4 * ch, hid)))}
+    double = [(random_block(we, g, torch, dev, gen, bc), random_block(we, g, torch, dev, gen, bc))
+              for _ in range(scfg.double)]
+    single = [random_block(we, g, torch, dev, gen, bc) for _ in range(scfg.single)]
+    vec = {name: torch.randn(hid, generator=gen, device=dev) * 0.3 for name in ("last_norm", "last_scale", "last_shift")}
+    return we.transformer.TransformerWeights(double=double, single=single, **edge, **vec)
+
+
+def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float) -> dict:
+    """Config 3 (one single-stream block, 4608 tokens) and config 4 (one denoising step of the 19 + 38 block
+    model at 1024x1024: 512 text + 4096 image tokens), bf16 path, weights resident, inputs ~N(0, 1)."""
+    T = we.transformer
+    scfg = T.StepConfig()
+    bc, text_tokens, side = scfg.block, 512, 128
+    rows, cols = T.patch_grid(side, side)
+    tokens = text_tokens + rows * cols
+    out = {}
+    # config 3: one block
+    bw = random_block(we, g, torch, dev, gen, bc)
+    xb = torch.randn(tokens, bc.hidden, generator=gen, device=dev)
+    tvec = torch.randn(6 * bc.hidden, generator=gen, device=dev) * 0.3
+    cos_h, sin_h, pairs = we.kernels.rope_tables(we.kernels.positions(text_tokens, rows, cols), scfg.axes, scfg.theta)
+    rope = we.Rope(torch.from_numpy(cos_h).to(dev), torch.from_numpy(sin_h).to(dev), pairs, tokens)
+
+    def step_block():
+        mark = g.mark()
+        we.blocks.block(g, bw, bc, xb, tvec, rope, dtype="bf16")
+        g.release(mark)
+
+    l0 = g.stats["launches"]
+    blk_ms = timed(step_block, steps, 3) / steps
+    blk_launches = (g.stats["launches"] - l0) // (steps + 3)
+    bf = we.blocks.block_flops(bc, tokens)
+    out["block_config3"] = {"ms": blk_ms, "tflops": bf["total"] / (blk_ms * 1e-3) / 1e12,
+                            "frac_bf16_peak": bf["total"] / (blk_ms * 1e-3) / 1e12 / bf16_peak,
+                            "flop": bf["total"], "launches_per_block": blk_launches,
+                            "note": "one single-stream block, 4608 tokens, hidden 3072, 24x128 heads, 4x GELU MLP, "
+                                    "fp8 per-channel linears, bf16 activations, f32 residual"}
+    del bw, xb
+    # config 4: one whole denoising step
+    model = random_model(we, g, torch, dev, gen, scfg)
+    lat = torch.randn(scfg.channels, side, side, generator=gen, device=dev).to(torch.bfloat16)
+    ctx = torch.randn(text_tokens, scfg.ctx_dim, generator=gen, device=dev).to(torch.bfloat16)
+    vel = torch.empty(scfg.channels, side, side, dtype=torch.float32, device=dev)
+    inp = T.StepInputs(lat, side, side, 0.7, ctx, text_tokens)
+
+    def step_model():
+        T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel)
+
+    ksteps = max(3, steps // 4)
+    l0 = g.stats["launches"]
+    st_ms = timed(step_model, ksteps, 3) / ksteps
+    st_launches = (g.stats["launches"] - l0) // (ksteps + 3)
+    sf = T.step_flops(scfg, text_tokens, rows * cols)
+    assert torch.isfinite(vel).all().item(), "non-finite velocity"
+    # end to end: latent + context from pinned host memory, velocity back to pinned host memory
+    lat_h, ctx_h = lat.cpu().pin_memory(), ctx.cpu().pin_memory()
+    vel_h = torch.empty(scfg.channels, side, side, dtype=torch.float32).pin_memory()
+    lat_d, ctx_d = torch.empty_like(lat), torch.empty_like(ctx)
+    inp_e = T.StepInputs(lat_d, side, side, 0.7, ctx_d, text_tokens)
+
+    def step_e2e():
+        lat_d.copy_(lat_h, non_blocking=True)
+        ctx_d.copy_(ctx_h, non_blocking=True)
+        T.transformer(g, model, scfg, inp_e, dtype="bf16", velocity=vel)
+        g.read_into(vel, vel_h.data_ptr(), vel.numel() * 4)
+
+    e2e_ms = timed(step_e2e, ksteps, 1) / ksteps
+    out["step_config4"] = {"ms": st_ms, "tflops": sf["total"] / (st_ms * 1e-3) / 1e12,
+                           "frac_bf16_peak": sf["total"] / (st_ms * 1e-3) / 1e12 / bf16_peak, "flop": sf["total"],
+                           "launches_per_step": st_launches, "e2e_ms": e2e_ms,
+                           "e2e_h2d_bytes": lat.numel() * 2 + ctx.numel() * 2, "e2e_d2h_bytes": vel.numel() * 4,
+                           "note": "19 double + 38 single blocks of config 3 shape, 512 text + 4096 image tokens "
+                                   "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def config_dict(args) -> dict:
     return {"workload": "config 2: dequant-GEMM M=4608 K=3072 N=12288, bf16 activations ~N(0,1), fp8 e4m3 weights "
                         "~N(0,0.02) with per-output-channel absmax scales, exact two-term e4m3 activation split",
@@ -157,6 +266,9 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-variants", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the config 3 block and config 4 step variants")
+    ap.add_argument("--profile-block", action="store_true",
+                    help="run config 3's block (bf16 path) three times, untimed, for an ncu launch list")
     ap.add_argument("--profile-case", action="store_true",
                     help="run each hot-path kernel of config 2 twice, untimed, for an ncu capture")
     args = ap.parse_args()
@@ -232,6 +344,26 @@ def main() -> None:
         wall_ms[0] = (time.perf_counter() - t0) * 1e3
         total = sum(a.elapsed_time(b) for a, b in ev)
         return we.parallel.max_over_ranks(total, device=dev)
+
+    if args.profile_block:
+        T = we.transformer
+        bc = T.FLUX_BLOCK
+        bw = random_block(we, g, torch, dev, gen, bc)
+        rows, cols = T.patch_grid(128, 128)
+        tokens = 512 + rows * cols
+        xb = torch.randn(tokens, bc.hidden, generator=gen, device=dev)
+        tvec = torch.randn(6 * bc.hidden, generator=gen, device=dev) * 0.3
+        cos_h, sin_h, pairs = we.kernels.rope_tables(we.kernels.positions(512, rows, cols), (16, 56, 56), 1e4)
+        rope = we.Rope(torch.from_numpy(cos_h).to(dev), torch.from_numpy(sin_h).to(dev), pairs, tokens)
+        for _ in range(3):
+            mark = g.mark()
+            we.blocks.block(g, bw, bc, xb, tvec, rope, dtype="bf16")
+            g.release(mark)
+        torch.cuda.synchronize()
+        assert g.device_error() == 0
+        g.destroy()
+        print("profile block done", flush=True)
+        return
 
     if args.profile_case:
         # the activation split, the two-term and one-term GEMMs, the int4 decode + kind::f16 GEMM,
@@ -350,6 +482,10 @@ def main() -> None:
                                                "frac_bf16_peak": at_flops / (at_ms * 1e-3) / 1e12 / bf16_peak,
                                                "note": "4 T^2 H D FLOP, T=4608, 24 heads x 128, incl. the V transpose"}
         del qa, ka, va, oa
+
+    # ---- config 3 (one block) and config 4 (one whole denoising step) on the bf16 fused path ----
+    if not args.no_variants and not args.no_model:
+        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak))
 
     # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
     if not args.no_variants:

@@ -128,6 +128,15 @@ __device__ __forceinline__ float aux_apply(int op, float aux, float v) {
   return op == WE_AUX_SIGMOID_GATE ? aux * sigmoid_ref(v) : (op == WE_AUX_SWIGLU ? aux * sigmoid_ref(aux) * v : v);
 }
 
+// The GEMM epilogue's forms of the same functions, on the hardware exp2 / reciprocal approximations
+// (__expf, __fdividef: a few ulp): tanh-GELU through the identity 0.5 (1 + tanh u) = 1 / (1 + e^(-2u)), so
+// gelu(v) = v / (1 + e^(-2u)). Both limits are exact: e^(-2u) -> inf gives -0, -> 0 gives v.
+__device__ __forceinline__ float sigmoid_fast(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
+__device__ __forceinline__ float gelu_tanh_fast(float v) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * v, v * v, v);
+  return __fdividef(v, 1.f + __expf(-2.f * u));
+}
+
 // ---- warp reductions ----
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

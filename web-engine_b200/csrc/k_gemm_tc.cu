@@ -72,19 +72,103 @@ __host__ __device__ constexpr uint32_t make_idesc() {
          ((uint32_t)(BM >> 4) << 24);
 }
 
-// Epilogue of one 32-token chunk of a warp's 32 channels: scale by the row scale (one coalesced load,
-// broadcast by shuffle), channel scale and bias, transpose through shared memory (row stride EPI_LD,
-// conflict-free), then 8 consecutive channels of one token per lane: one 16-byte bf16 store (or two
-// f32), scalar stores on ragged edges.
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], float* stage, int lane, int64_t tok0,
-                                               int64_t ch_base, float cs, float bias, const Params& p) {
-  const int cg = (lane & 3) * 8;
-  // the 32 row scales of this chunk: one coalesced load, then broadcast by shuffle
-  const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
+// Epilogue of one 32-token chunk of a warp's 32 channels, in two layouts:
+// - as read from TMEM (lane = channel, 32 tokens per thread): row scale (one coalesced load, broadcast by
+//   shuffle), channel scale, bias and the activation, 32 independent values per thread;
+// - after a transpose through shared memory (row stride EPI_LD, conflict-free): 8 consecutive channels of one
+//   token per lane, where the aux operand, the channel gate and the accumulate read-modify-write run on
+//   16-byte words, then one 16-byte bf16 store (or two f32); scalar accesses on ragged edges.
+// The old y (accumulate) and the aux rows do not depend on the accumulator: EpiFetch holds them as raw
+// 16-byte words, loaded one chunk ahead (each slot is refilled for the next chunk as soon as it is used), so
+// their HBM latency hides behind the work of the chunk before.
+struct EpiFetch {
+  uint4 y[4][2];
+  uint4 a[4][2];
+};
+
+// whether iteration `it` of the chunk at tok0 takes the 16-byte path (and so was fetched ahead)
+__device__ __forceinline__ bool epi_fast(const Params& p, int64_t tok, int64_t c0) {
+  return tok < p.m && c0 + 8 <= p.n && p.vec_ok && (!p.epi.aux_op || p.epi_vec_ok);
+}
+
+__device__ __forceinline__ void epi_fetch_iter(EpiFetch& f, int it, int lane, int64_t tok0, int64_t c0,
+                                               const Params& p) {
+  const int64_t tok = tok0 + it * 8 + (lane >> 2);
+  if (!epi_fast(p, tok, c0)) return;
+  const int64_t o = tok * p.y_stride + c0;
+  if (p.accumulate) {
+    if (p.y_dtype == WE_BF16) {
+      f.y[it][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.y) + o);
+    } else {
+      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const float*>(p.y) + o);
+      f.y[it][0] = q[0];
+      f.y[it][1] = q[1];
+    }
+  }
+  if (p.epi.aux_op) {
+    if (p.epi.aux_dtype == WE_BF16) {
+      f.a[it][0] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.epi.aux) + o));
+    } else {
+      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const float*>(p.epi.aux) + o);
+      f.a[it][0] = __ldg(q);
+      f.a[it][1] = __ldg(q + 1);
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack8(const uint4 (&w)[2], bool bf16, float (&v)[8]) {
+  if (bf16) {
+    const uint32_t u[4] = {w[0].x, w[0].y, w[0].z, w[0].w};
 #pragma unroll
-  for (int j = 0; j < 32; j++)
-    stage[j * EPI_LD + lane] = __uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j) * cs + bias;
+    for (int e = 0; e < 4; e++) {
+      v[2 * e] = __uint_as_float(u[e] << 16);
+      v[2 * e + 1] = __uint_as_float(u[e] & 0xffff0000u);
+    }
+  } else {
+    v[0] = __uint_as_float(w[0].x); v[1] = __uint_as_float(w[0].y);
+    v[2] = __uint_as_float(w[0].z); v[3] = __uint_as_float(w[0].w);
+    v[4] = __uint_as_float(w[1].x); v[5] = __uint_as_float(w[1].y);
+    v[6] = __uint_as_float(w[1].z); v[7] = __uint_as_float(w[1].w);
+  }
+}
+
+// the per-tile channel gate of this lane's 8 post-transpose channels (zeros past n)
+__device__ __forceinline__ void epi_gate(float (&gt)[8], int lane, int64_t ch_base, const Params& p) {
+  const int64_t c0 = ch_base + (lane & 3) * 8;
+  if (!p.epi.gate) return;
+  if (p.epi_vec_ok && c0 + 8 <= p.n) {
+    load8f(p.epi.gate, c0, gt);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; e++) gt[e] = (c0 + e < p.n) ? p.epi.gate[c0 + e] : 0.f;
+  }
+}
+
+// `more`: the warp goes on to the chunk at tok0 + 32, whose operands are fetched into f as slots free up
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch& f, const float (&gt)[8],
+                                               bool more, float* stage, int lane, int64_t tok0, int64_t ch_base,
+                                               float cs, float bias, const Params& p) {
+  const int cg = (lane & 3) * 8;
+  const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
+  if (p.epi.act == WE_ACT_GELU_TANH) {
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      stage[j * EPI_LD + lane] =
+          gelu_tanh_fast(fmaf(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j), cs, bias));
+  } else if (p.epi.act == WE_ACT_SILU) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      const float v = fmaf(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j), cs, bias);
+      stage[j * EPI_LD + lane] = v * sigmoid_fast(v);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      stage[j * EPI_LD + lane] = fmaf(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j), cs, bias);
+  }
   __syncwarp();
+  const int64_t c0 = ch_base + cg;
+  const bool ybf = p.y_dtype == WE_BF16, abf = p.epi.aux_dtype == WE_BF16;
 #pragma unroll
   for (int it = 0; it < 4; it++) {
     const int tr = it * 8 + (lane >> 2);
@@ -92,76 +176,70 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], float* s
     const float4 a = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg);
     const float4 b = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg + 4);
     float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const int64_t c0 = ch_base + cg;
-    if (tok >= p.m || c0 >= p.n) continue;
-    const int64_t o = tok * p.y_stride + c0;
-    const bool full8 = c0 + 8 <= p.n;
-    if (p.epi.act | p.epi.aux_op | (p.epi.gate != nullptr)) {
-      // fused per-value steps: activation, aux gate / swiglu, residual gate
-      float ax[8], gt[8];
+    if (epi_fast(p, tok, c0)) {
+      const int64_t o = tok * p.y_stride + c0;
       if (p.epi.aux_op) {
-        if (p.epi_vec_ok && full8) {
-          if (p.epi.aux_dtype == WE_BF16) load8<WE_BF16>(p.epi.aux, o, ax);
-          else load8<WE_F32>(p.epi.aux, o, ax);
-        } else
+        float ax[8];
+        unpack8(f.a[it], abf, ax);
+        if (p.epi.aux_op == WE_AUX_SIGMOID_GATE) {
 #pragma unroll
-          for (int e = 0; e < 8; e++)
-            ax[e] = (c0 + e < p.n) ? (p.epi.aux_dtype == WE_BF16 ? load_act<WE_BF16>(p.epi.aux, o + e)
-                                                                 : load_act<WE_F32>(p.epi.aux, o + e))
-                                   : 0.f;
+          for (int e = 0; e < 8; e++) v[e] = ax[e] * sigmoid_fast(v[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; e++) v[e] = ax[e] * sigmoid_fast(ax[e]) * v[e];
+        }
       }
       if (p.epi.gate) {
-        if (p.epi_vec_ok && full8) load8f(p.epi.gate, c0, gt);
-        else
 #pragma unroll
-          for (int e = 0; e < 8; e++) gt[e] = (c0 + e < p.n) ? p.epi.gate[c0 + e] : 0.f;
+        for (int e = 0; e < 8; e++) v[e] *= gt[e];
       }
+      if (p.accumulate) {
+        float yo[8];
+        unpack8(f.y[it], ybf, yo);
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        v[e] = act_apply(p.epi.act, v[e]);
-        if (p.epi.aux_op) v[e] = aux_apply(p.epi.aux_op, ax[e], v[e]);
-        if (p.epi.gate) v[e] *= gt[e];
+        for (int e = 0; e < 8; e++) v[e] += yo[e];
       }
-    }
-    if (p.vec_ok && c0 + 8 <= p.n) {
-      if (p.y_dtype == WE_BF16) {
-        uint4* y = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o);
-        if (p.accumulate) {
-          const uint4 old = *y;
-          const uint32_t w[4] = {old.x, old.y, old.z, old.w};
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            v[2 * e] += __uint_as_float(w[e] << 16);
-            v[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
-          }
-        }
-        *y = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                        pack_bf16x2(v[6], v[7]));
+      if (ybf) {
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o) =
+            make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                       pack_bf16x2(v[6], v[7]));
       } else {
         float4* y = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
-        if (p.accumulate) {
-          const float4 o0 = y[0], o1 = y[1];
-          v[0] += o0.x; v[1] += o0.y; v[2] += o0.z; v[3] += o0.w;
-          v[4] += o1.x; v[5] += o1.y; v[6] += o1.z; v[7] += o1.w;
-        }
         y[0] = make_float4(v[0], v[1], v[2], v[3]);
         y[1] = make_float4(v[4], v[5], v[6], v[7]);
       }
-    } else {
+    } else if (tok < p.m && c0 < p.n) {
+      // ragged or unaligned: per value, loads at use
 #pragma unroll
       for (int e = 0; e < 8; e++) {
         if (c0 + e >= p.n) break;
-        if (p.y_dtype == WE_BF16) {
+        const int64_t o = tok * p.y_stride + c0 + e;
+        float val = v[e];
+        if (p.epi.aux_op) {
+          const float ax = abf ? load_act<WE_BF16>(p.epi.aux, o) : load_act<WE_F32>(p.epi.aux, o);
+          val = aux_apply(p.epi.aux_op, ax, val);
+        }
+        if (p.epi.gate) val *= gt[e];
+        if (ybf) {
           uint16_t* y = static_cast<uint16_t*>(p.y);
-          float val = v[e] + (p.accumulate ? bf16_bits_to_f32(y[o + e]) : 0.f);
-          y[o + e] = f32_to_bf16_bits(val);
+          y[o] = f32_to_bf16_bits(val + (p.accumulate ? bf16_bits_to_f32(y[o]) : 0.f));
         } else {
           float* y = static_cast<float*>(p.y);
-          y[o + e] = v[e] + (p.accumulate ? y[o + e] : 0.f);
+          y[o] = val + (p.accumulate ? y[o] : 0.f);
         }
       }
     }
+    if (more && (p.accumulate || p.epi.aux_op)) epi_fetch_iter(f, it, lane, tok0 + 32, c0, p);
   }
+}
+
+// Operands of a tile's first chunk, issued before the wait for its accumulator
+__device__ __forceinline__ void epi_fetch_first(EpiFetch& f, int lane, int64_t tok0, int64_t ch_base,
+                                                const Params& p) {
+  if (!(p.accumulate || p.epi.aux_op)) return;
+  const int64_t c0 = ch_base + (lane & 3) * 8;
+#pragma unroll
+  for (int it = 0; it < 4; it++) epi_fetch_iter(f, it, lane, tok0, c0, p);
 }
 
 // ---------------- the kernel ----------------
@@ -298,28 +376,34 @@ __global__ void __launch_bounds__(THREADS, 1)
     int ab = 0;
     uint32_t aph = 0;
     for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
+      // everything that does not need the accumulator is loaded before waiting for it
       const int64_t ch_base = (t % tiles_n) * BM + q * 32;  // first output channel of this warp
       const int64_t ch = ch_base + lane;
       const int64_t tok_base = (t / tiles_n) * BT;
       const bool ch_ok = ch < p.n;
       const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
       const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+      EpiFetch f;
+      float gt[8];
+      epi_fetch_first(f, lane, tok_base, ch_base, p);
+      epi_gate(gt, lane, ch_base, p);
+      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < BT / 32; c++) {
         const int64_t tok0 = tok_base + c * 32;
         if (tok0 >= p.m) break;  // warp-uniform: the rest of the tile is padding
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BT + c * 32), r);
-        if (c == BT / 32 - 1 || tok0 + 32 >= p.m) {
+        const bool last = c == BT / 32 - 1 || tok0 + 32 >= p.m;
+        if (last) {
           // last TMEM read of this tile: hand the accumulator back to the MMA warp before the stores
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(TEMPTY(ab));
         }
-        epilogue_chunk(r, stage, lane, tok0, ch_base, cs, bias, p);
+        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, p);
         __syncwarp();
       }
       if (++ab == 2) {
@@ -574,27 +658,32 @@ __global__ void __launch_bounds__(THREADS, 1)
     int ab = 0;
     uint32_t aph = 0;
     for (int64_t t = cid; t < tiles; t += ncl) {
-      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
       const int64_t ch_base = (t % tiles_n) * 2 * BM + rank * BM + q * 32;
       const int64_t ch = ch_base + lane;
       const int64_t tok_base = (t / tiles_n) * BT;
       const bool ch_ok = ch < p.n;
       const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
       const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+      EpiFetch f;
+      float gt[8];
+      epi_fetch_first(f, lane, tok_base, ch_base, p);
+      epi_gate(gt, lane, ch_base, p);
+      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < BT / 32; c++) {
         const int64_t tok0 = tok_base + c * 32;
         if (tok0 >= p.m) break;
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BT + c * 32), r);
-        if (c == BT / 32 - 1 || tok0 + 32 >= p.m) {
+        const bool last = c == BT / 32 - 1 || tok0 + 32 >= p.m;
+        if (last) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(map_rank(TEMPTY(ab), 0));
         }
-        epilogue_chunk(r, stage, lane, tok0, ch_base, cs, bias, p);
+        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, p);
         __syncwarp();
       }
       if (++ab == 2) {

@@ -4,6 +4,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cstring>
+#include <deque>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -24,6 +26,17 @@ struct we_ctx {
   we_stats stats{0, 0, 0, 0, 0, 0};
   uint32_t* dev_err = nullptr;  // device error word written by bounded waits
   unsigned int* amax_word = nullptr;
+  // Pinned staging ring for host -> device uploads. Like WebGPU's queue.writeBuffer, an upload copies the
+  // caller's data before returning and the DMA then runs in stream order: a copy straight from pageable
+  // memory would first wait for the whole stream, and the GPU would idle while the host catches up.
+  struct Staged {
+    size_t begin, end;
+    cudaEvent_t done;
+  };
+  char* stage = nullptr;
+  size_t stage_head = 0;
+  std::deque<Staged> staged;
+  std::vector<cudaEvent_t> spare_events;
 };
 
 namespace {
@@ -49,6 +62,53 @@ int cuda_fail(we_ctx* c, cudaError_t e, const char* what) {
   } while (0)
 
 size_t round4(size_t b) { return std::max<size_t>(4, (b + 3) / 4 * 4); }
+
+constexpr size_t kStageBytes = 16u << 20;  // uploads up to half of this go through the staging ring
+
+// Host -> device copy of `bytes` at `host` into `dst`, in stream order, without waiting for the stream: small
+// uploads are copied into the pinned ring first (waiting only for earlier copies still reading the region to
+// be overwritten), large ones go straight from the caller's memory.
+int upload(we_ctx* ctx, void* dst, const void* host, size_t bytes, const char* what) {
+  if (bytes == 0) return WE_OK;
+  if (bytes > kStageBytes / 2) {
+    CK(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream), what);
+    return WE_OK;
+  }
+  if (!ctx->stage) CK(cudaHostAlloc(reinterpret_cast<void**>(&ctx->stage), kStageBytes, cudaHostAllocDefault),
+                      "staging ring");
+  const size_t len = (bytes + 255) & ~size_t(255);
+  const size_t off = ctx->stage_head + len <= kStageBytes ? ctx->stage_head : 0;
+  for (auto it = ctx->staged.begin(); it != ctx->staged.end();) {
+    if (it->begin < off + len && off < it->end) {
+      CK(cudaEventSynchronize(it->done), "staging wait");
+      ctx->spare_events.push_back(it->done);
+      it = ctx->staged.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  while (!ctx->staged.empty() && cudaEventQuery(ctx->staged.front().done) == cudaSuccess) {
+    ctx->spare_events.push_back(ctx->staged.front().done);
+    ctx->staged.pop_front();
+  }
+  std::memcpy(ctx->stage + off, host, bytes);
+  CK(cudaMemcpyAsync(dst, ctx->stage + off, bytes, cudaMemcpyHostToDevice, ctx->stream), what);
+  cudaEvent_t ev;
+  if (ctx->spare_events.empty()) {
+    CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "staging event");
+  } else {
+    ev = ctx->spare_events.back();
+    ctx->spare_events.pop_back();
+  }
+  const cudaError_t e = cudaEventRecord(ev, ctx->stream);
+  if (e != cudaSuccess) {
+    ctx->spare_events.push_back(ev);
+    return cuda_fail(ctx, e, "staging event");
+  }
+  ctx->staged.push_back({off, off + len, ev});
+  ctx->stage_head = off + len;
+  return WE_OK;
+}
 
 // Takes a pooled buffer of exactly `size` bytes or allocates one (graph.ts:41-45).
 int pool_take(we_ctx* ctx, size_t size, void** out, bool* reused) {
@@ -152,6 +212,9 @@ int we_destroy(we_ctx* ctx) {
   if (!ctx) return WE_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  for (auto& st : ctx->staged) cudaEventDestroy(st.done);
+  for (cudaEvent_t ev : ctx->spare_events) cudaEventDestroy(ev);
+  if (ctx->stage) cudaFreeHost(ctx->stage);
   for (auto& kv : ctx->sizes) cudaFree(kv.first);
   cudaFree(ctx->dev_err);
   cudaStreamDestroy(ctx->own);
@@ -192,7 +255,8 @@ int we_buffer(we_ctx* ctx, size_t bytes, const void* host, void** out) {
   if (rc != WE_OK) return rc;
   size_t size = ctx->sizes[*out];
   if (host) {
-    CK(cudaMemcpyAsync(*out, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "upload");
+    rc = upload(ctx, *out, host, bytes, "upload");
+    if (rc != WE_OK) return rc;
     if (size > bytes) CK(cudaMemsetAsync(static_cast<char*>(*out) + bytes, 0, size - bytes, ctx->stream), "pad");
   } else {
     CK(cudaMemsetAsync(*out, 0, size, ctx->stream), "zero buffer");
@@ -202,8 +266,7 @@ int we_buffer(we_ctx* ctx, size_t bytes, const void* host, void** out) {
 
 int we_write(we_ctx* ctx, void* dst, const void* host, size_t bytes) {
   if (!ctx) return WE_EINVAL;
-  CK(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "we_write");
-  return WE_OK;
+  return upload(ctx, dst, host, bytes, "we_write");
 }
 
 int we_read(we_ctx* ctx, const void* src, void* host, size_t bytes) {

@@ -19,6 +19,7 @@ the residual stream stays f32.
 """
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass, field
 
@@ -93,6 +94,16 @@ def unpatchify(graph: Graph, tokens, height: int, width: int, latent, channels: 
                                              addr(latent), L.DTYPES[latent_dtype]))
 
 
+@functools.lru_cache(maxsize=16)
+def _tables(text_tokens: int, rows: int, cols: int, axes: tuple, theta: float):
+    """RoPE cos/sin of a sequence geometry (ropeTables(positions(...)), transformer.ts:158); computed once per
+    geometry on the host, uploaded each step through the library's staging ring."""
+    cos, sin, pairs = K.rope_tables(K.positions(text_tokens, rows, cols), axes, theta)
+    cos.setflags(write=False)
+    sin.setflags(write=False)
+    return cos, sin, pairs
+
+
 def time(graph: Graph, w: TransformerWeights, timestep: float, time_dim: int = TIME_DIM):
     """t [hidden] and tvec [6 hidden] for one timestep (transformer.ts:85-90); M = 1 linears."""
     emb = graph.buffer(timestep_embedding(timestep, time_dim))
@@ -130,7 +141,7 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp: StepI
     rows, cols = patch_grid(inp.height, inp.width)
     image, Lt = rows * cols, inp.text_tokens
     T = Lt + image
-    tables = K.rope_tables(K.positions(Lt, rows, cols), cfg.axes, cfg.theta)
+    tables = _tables(Lt, rows, cols, tuple(cfg.axes), float(cfg.theta))
     mark = graph.mark()
     t, tvec = time(graph, w, inp.timestep, cfg.time_dim)
     txt = inp.text_cache if inp.text_cache is not None else text(graph, w, inp.context, Lt, dtype)
