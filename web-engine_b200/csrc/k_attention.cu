@@ -92,6 +92,31 @@ __global__ void transpose_v_kernel(const uint16_t* __restrict__ v, int64_t token
 }
 
 // ---------------- tcgen05 flash attention ----------------
+// Blackwell packed-pair and 3-input forms (PTX ISA 8.6+ for sm_100a): one instruction per two values
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// the hardware 2^x (MUFU.EX2, results below 2^-126 flush to 0: negligible weights)
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 namespace fa {
 constexpr int BQ = 128, BK = 128, D = 128;
 constexpr int ATOM = 128 * 128;          // one 128-row x 128-byte swizzle-128B atom (64 bf16 per row)
@@ -101,12 +126,12 @@ constexpr int V_BYTES = 2 * ATOM;        // 128 dims x 128 keys (V^T)
 constexpr int P_BYTES = 2 * ATOM;        // 128 queries x 128 keys
 constexpr int STAGES = 2;
 constexpr int Q_OFF = 0;
-constexpr int KV_OFF = Q_OFF + Q_BYTES;
-constexpr int KV_STAGE = K_BYTES + V_BYTES;
-constexpr int P_OFF = KV_OFF + STAGES * KV_STAGE;
+constexpr int K_OFF = Q_OFF + Q_BYTES;          // K stages: released as soon as S_j = Q K_j^T completes
+constexpr int V_OFF = K_OFF + STAGES * K_BYTES;  // V^T stages: released when PV_j completes
+constexpr int P_OFF = V_OFF + STAGES * V_BYTES;
 constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
-// barriers: q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain
-constexpr int NUM_BARS = 1 + 2 * 6 + 1;
+// barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain
+constexpr int NUM_BARS = 1 + 2 * 8 + 1;
 constexpr int TOTAL = BAR_OFF + NUM_BARS * 8 + 16;
 constexpr int ALLOC = TOTAL + 1024;
 constexpr int THREADS = 192;
@@ -137,13 +162,15 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + BAR_OFF + NUM_BARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const uint32_t Q_FULL = bars;
-#define KV_FULL(s) (bars + 8u * (1 + (s)))
-#define KV_EMPTY(s) (bars + 8u * (3 + (s)))
-#define S_FULL(b) (bars + 8u * (5 + (b)))
-#define S_FREE(b) (bars + 8u * (7 + (b)))
-#define P_FULL(b) (bars + 8u * (9 + (b)))
-#define PV_DONE(b) (bars + 8u * (11 + (b)))
-#define DRAIN (bars + 8u * 13)
+#define K_FULL(s) (bars + 8u * (1 + (s)))
+#define K_EMPTY(s) (bars + 8u * (3 + (s)))
+#define V_FULL(s) (bars + 8u * (5 + (s)))
+#define V_EMPTY(s) (bars + 8u * (7 + (s)))
+#define S_FULL(b) (bars + 8u * (9 + (b)))
+#define S_FREE(b) (bars + 8u * (11 + (b)))
+#define P_FULL(b) (bars + 8u * (13 + (b)))
+#define PV_DONE(b) (bars + 8u * (15 + (b)))
+#define DRAIN (bars + 8u * 17)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t q0 = (int64_t)blockIdx.x * BQ;
@@ -154,8 +181,10 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(Q_FULL, 1);
     for (int i = 0; i < 2; i++) {
-      mbar_init(KV_FULL(i), 1);
-      mbar_init(KV_EMPTY(i), 1);
+      mbar_init(K_FULL(i), 1);
+      mbar_init(K_EMPTY(i), 1);
+      mbar_init(V_FULL(i), 1);
+      mbar_init(V_EMPTY(i), 1);
       mbar_init(S_FULL(i), 1);
       mbar_init(S_FREE(i), 4);
       mbar_init(P_FULL(i), 4);
@@ -178,27 +207,49 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
       mbar_expect_tx(Q_FULL, Q_BYTES);
       tma_load_2d(sbase + Q_OFF, &tm_q, Q_FULL, (int32_t)(h * D), (int32_t)q0);
       tma_load_2d(sbase + Q_OFF + ATOM, &tm_q, Q_FULL, (int32_t)(h * D + 64), (int32_t)q0);
-      int issued = 0;
+      // K runs two tiles ahead of V: V_j, then K_{j+2} (its stage was freed by S_j, long before S_{j+2})
+      auto load_k = [&](int t) -> bool {
+        const int st = t & 1;
+        if (!wait_bounded(K_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
+                          WAIT_LIMIT_NS, true))
+          return false;
+        const uint32_t dst = sbase + K_OFF + st * K_BYTES;
+        mbar_expect_tx(K_FULL(st), K_BYTES);
+        tma_load_2d(dst, &tm_k, K_FULL(st), (int32_t)(g * D), t * BK);
+        tma_load_2d(dst + ATOM, &tm_k, K_FULL(st), (int32_t)(g * D + 64), t * BK);
+        return true;
+      };
+      auto load_v = [&](int t) -> bool {
+        const int st = t & 1;
+        if (!wait_bounded(V_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
+                          WAIT_LIMIT_NS, true))
+          return false;
+        const uint32_t dst = sbase + V_OFF + st * V_BYTES;
+        mbar_expect_tx(V_FULL(st), V_BYTES);
+        tma_load_2d(dst, &tm_vt, V_FULL(st), t * BK, (int32_t)(g * D));
+        tma_load_2d(dst + ATOM, &tm_vt, V_FULL(st), t * BK + 64, (int32_t)(g * D));
+        return true;
+      };
+      int k_issued = 0, v_issued = 0;
+      for (int t = 0; t < 2 && t < nt && ok; t++) {
+        ok = load_k(t);
+        if (ok) k_issued = t + 1;
+      }
       for (int j = 0; j < nt && ok; j++) {
-        const int s = j & 1;
-        if (!wait_bounded(KV_EMPTY(s), ((j >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
-                          WAIT_LIMIT_NS, true)) {
-          ok = false;
-          break;
+        ok = load_v(j);
+        if (!ok) break;
+        v_issued = j + 1;
+        if (j + 2 < nt) {
+          ok = load_k(j + 2);
+          if (ok) k_issued = j + 3;
         }
-        const uint32_t st = sbase + KV_OFF + s * KV_STAGE;
-        mbar_expect_tx(KV_FULL(s), KV_STAGE);
-        const int32_t j0 = j * BK;
-        tma_load_2d(st, &tm_k, KV_FULL(s), (int32_t)(g * D), j0);
-        tma_load_2d(st + ATOM, &tm_k, KV_FULL(s), (int32_t)(g * D + 64), j0);
-        tma_load_2d(st + K_BYTES, &tm_vt, KV_FULL(s), j0, (int32_t)(g * D));
-        tma_load_2d(st + K_BYTES + ATOM, &tm_vt, KV_FULL(s), j0 + 64, (int32_t)(g * D));
-        issued = j + 1;
       }
       if (!ok) {  // the copies already issued land before the CTA exits
         wait_bounded(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
-        for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; j++)
-          wait_bounded(KV_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+        for (int t = k_issued - 2 < 0 ? 0 : k_issued - 2; t < k_issued; t++)
+          wait_bounded(K_FULL(t & 1), (t >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+        for (int t = v_issued - 2 < 0 ? 0 : v_issued - 2; t < v_issued; t++)
+          wait_bounded(V_FULL(t & 1), (t >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
       }
     }
     __syncwarp();
@@ -210,34 +261,36 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
       // O += P_j V_j^T for tile j (P in buffer j & 1, V^T in KV stage j & 1)
       auto pv = [&](int j) -> bool {
         const int b = j & 1;
-        if (!wait_bounded(P_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
+        if (!wait_bounded(P_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
+            !wait_bounded(V_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
           return false;
         tc_fence_after();
         const uint64_t pdesc = sw128_desc(sbase + P_OFF + b * P_BYTES);
-        const uint64_t vdesc = sw128_desc(sbase + KV_OFF + (j & 1) * KV_STAGE + K_BYTES);
+        const uint64_t vdesc = sw128_desc(sbase + V_OFF + b * V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) {  // K = 128 keys: two 64-key atoms, 4 MMAs of 16 each
           const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
           umma<true>(tmem + O_COL, pdesc + off, vdesc + off, IDESC, (j | kk) != 0);
         }
-        umma_commit(KV_EMPTY(j & 1));
+        umma_commit(V_EMPTY(b));
         umma_commit(PV_DONE(b));
         return true;
       };
       for (int j = 0; j < nt && ok; j++) {
         const int s = j & 1, b = j & 1;
-        if (!wait_bounded(KV_FULL(s), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
+        if (!wait_bounded(K_FULL(s), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
             !wait_bounded(S_FREE(b), ((j >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t kdesc = sw128_desc(sbase + KV_OFF + s * KV_STAGE);
+        const uint64_t kdesc = sw128_desc(sbase + K_OFF + s * K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) {  // K = 128 dims
           const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
           umma<true>(tmem + (uint32_t)(b * 128), qdesc + off, kdesc + off, IDESC, kk != 0);
         }
+        umma_commit(K_EMPTY(s));
         umma_commit(S_FULL(b));
         if (j > 0 && !pv(j - 1)) {
           ok = false;
@@ -251,11 +304,15 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
     }
     __syncwarp();
   } else {
-    // softmax: thread = query row r of this CTA, TMEM lane r
+    // softmax: thread = query row r of this CTA, TMEM lane r. Per key tile: the raw scores (one TMEM read of
+    // 128 columns), the row maximum (3-input max), then p = 2^(s * scale_log2 - m) with the scale folded into
+    // one packed f32x2 FMA per pair, the hardware exp2, packed f32x2 sums, and bf16 pairs stored into the
+    // swizzled P tile.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    float m_used = -INFINITY, l = 0.f;
+    const int rx = r & 7;
+    float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and denominator
     bool ok = true;
     for (int j = 0; j < nt; j++) {
       const int b = j & 1;
@@ -265,32 +322,34 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         break;
       }
       tc_fence_after();
-      float t[BK];
+      uint32_t sc[BK];
 #pragma unroll
-      for (int c = 0; c < BK / 32; c++) {
-        uint32_t u[32];
-        tmem_ld32(tmem + lane_addr + (uint32_t)(b * 128 + c * 32), u);
-#pragma unroll
-        for (int e = 0; e < 32; e++) t[c * 32 + e] = __uint_as_float(u[e]) * p.scale_log2;
-      }
+      for (int c = 0; c < BK / 32; c++)
+        tmem_ld32(tmem + lane_addr + (uint32_t)(b * 128 + c * 32), *reinterpret_cast<uint32_t(*)[32]>(sc + c * 32));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(S_FREE(b));
-      const int64_t valid = p.tokens - (int64_t)j * BK;  // keys of this tile that exist
-      float mt = -INFINITY;
+      const int64_t valid = p.tokens - (int64_t)j * BK;  // keys of this tile that exist (warp-uniform)
+      if (valid < BK) {
 #pragma unroll
-      for (int c = 0; c < BK; c++) {
-        if (c >= valid) t[c] = -INFINITY;
-        mt = fmaxf(mt, t[c]);
+        for (int c = 0; c < BK; c++)
+          if (c >= valid) sc[c] = __float_as_uint(-INFINITY);
       }
+      float mx[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) mx[i] = __uint_as_float(sc[i]);
+#pragma unroll
+      for (int c = 4; c < BK; c += 8)
+#pragma unroll
+        for (int i = 0; i < 4; i++) mx[i] = max3f(mx[i], __uint_as_float(sc[c + 2 * i]), __uint_as_float(sc[c + 2 * i + 1]));
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
       float corr = 1.f;
       const bool grow = mt > m_used + RESCALE_LOG2;
       if (grow) {
-        corr = exp2f(m_used - mt);  // 0 on the first tile
+        corr = exp2_approx(m_used - mt);  // 0 on the first tile
         l *= corr;
         m_used = mt;
       }
-      float sum = 0.f;
       // P buffer b was last read by PV_{j-2}
       if (j >= 2) {
         ok = wait_bounded(PV_DONE(b), ((j - 2) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS,
@@ -301,19 +360,23 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         }
       }
       uint8_t* prow = smem + P_OFF + b * P_BYTES + r * 128;
+      const float nm = -m_used;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 4 packed pairs of running sums
 #pragma unroll
       for (int ch = 0; ch < 16; ch++) {  // 16 chunks of 8 keys; chunk ch lives in atom ch / 8
-        float e8[8];
+        uint32_t pk[4];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-          e8[e] = exp2f(t[ch * 8 + e] - m_used);
-          sum += e8[e];
+        for (int e = 0; e < 4; e++) {
+          float x0, x1;
+          ffma2(x0, x1, __uint_as_float(sc[ch * 8 + 2 * e]), __uint_as_float(sc[ch * 8 + 2 * e + 1]), p.scale_log2,
+                p.scale_log2, nm, nm);
+          const float e0 = exp2_approx(x0), e1 = exp2_approx(x1);
+          fadd2(acc[2 * e], acc[2 * e + 1], acc[2 * e], acc[2 * e + 1], e0, e1);
+          pk[e] = pack_bf16x2(e0, e1);
         }
-        const uint4 packed = make_uint4(pack_bf16x2(e8[0], e8[1]), pack_bf16x2(e8[2], e8[3]),
-                                        pack_bf16x2(e8[4], e8[5]), pack_bf16x2(e8[6], e8[7]));
-        *reinterpret_cast<uint4*>(prow + (ch >> 3) * ATOM + (((ch & 7) ^ (r & 7)) << 4)) = packed;
+        *reinterpret_cast<uint4*>(prow + (ch >> 3) * ATOM + (((ch & 7) ^ rx) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      l += sum;
+      l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
       // O was scaled for the old maximum: bring it to the new one before PV_j adds to it
       if (__any_sync(0xffffffffu, grow && j > 0)) {
         ok = wait_bounded(PV_DONE((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE,
@@ -378,8 +441,10 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
-#undef KV_FULL
-#undef KV_EMPTY
+#undef K_FULL
+#undef K_EMPTY
+#undef V_FULL
+#undef V_EMPTY
 #undef S_FULL
 #undef S_FREE
 #undef P_FULL
