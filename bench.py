@@ -181,7 +181,7 @@ def random_model(we, g, torch, dev, gen, scfg):
     return we.transformer.TransformerWeights(double=double, single=single, **edge, **vec)
 
 
-def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float) -> dict:
+def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, world: int = 1) -> dict:
     """Config 3 (one single-stream block, 4608 tokens) and config 4 (one denoising step of the 19 + 38 block
     model at 1024x1024: 512 text + 4096 image tokens), bf16 path, weights resident, inputs ~N(0, 1)."""
     T = we.transformer
@@ -247,7 +247,24 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float) -> 
                            "e2e_h2d_bytes": lat.numel() * 2 + ctx.numel() * 2, "e2e_d2h_bytes": vel.numel() * 4,
                            "note": "19 double + 38 single blocks of config 3 shape, 512 text + 4096 image tokens "
                                    "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
-    del model
+    # config 5's batch: 8 images per step in total, split data-parallel across the ranks (no collective); each
+    # rank runs its share as one token stream (every linear one GEMM over all its images' rows)
+    per = max(1, 8 // world)
+    lats = [torch.randn(scfg.channels, side, side, generator=gen, device=dev).to(torch.bfloat16) for _ in range(per)]
+    ctxs = [torch.randn(text_tokens, scfg.ctx_dim, generator=gen, device=dev).to(torch.bfloat16) for _ in range(per)]
+    vels = [torch.empty(scfg.channels, side, side, dtype=torch.float32, device=dev) for _ in range(per)]
+    binp = [T.StepInputs(l_, side, side, 0.7, c_, text_tokens) for l_, c_ in zip(lats, ctxs)]
+
+    def step_batch():
+        T.transformer(g, model, scfg, binp, dtype="bf16", velocity=vels)
+
+    b_ms = timed(step_batch, 2, 1) / 2
+    out["batch8_config5"] = {"ms_per_step": b_ms, "images_per_s": world * per / (b_ms * 1e-3),
+                             "images_per_rank": per, "tflops": world * per * sf["total"] / (b_ms * 1e-3) / 1e12,
+                             "scaling": "strong: 8 images per step in total, 8 / n_gpus per rank",
+                             "note": "one denoising step of config 4's model on a batch of 1024x1024 images, "
+                                     "data-parallel over images, weights resident"}
+    del model, lats, ctxs, vels
     torch.cuda.empty_cache()
     return out
 
@@ -485,7 +502,7 @@ def main() -> None:
 
     # ---- config 3 (one block) and config 4 (one whole denoising step) on the bf16 fused path ----
     if not args.no_variants and not args.no_model:
-        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak))
+        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak, world))
 
     # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
     if not args.no_variants:

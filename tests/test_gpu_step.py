@@ -138,3 +138,57 @@ def test_euler_step_on_device(we, graph):
     graph.release(mark)
     want = O.euler_step(x, v, s[1], s[2])
     assert np.max(np.abs(got - want)) <= 2 * np.spacing(np.abs(want).max())
+
+
+def test_batch_of_images_equals_one_at_a_time(we, graph):
+    """A batch runs as one token stream (one GEMM per linear over all images' rows, attention per image): each
+    image's velocity matches the single-image step and the float64 step."""
+    T = we.transformer
+    bc = we.blocks.BlockConfig(hidden=256, mlp=1024, heads=2, kv_heads=2, head_dim=128, mlp_act="gelu",
+                               attn_gate=False)
+    scfg = T.StepConfig(block=bc, double=1, single=2, ctx_dim=256)
+    h, w, text = 12, 14, 8
+    host, wts = make_step(we, graph, scfg, 700, per_channel=True)
+    cfgd = {**vars(bc), "axes": scfg.axes, "theta": scfg.theta, "channels": scfg.channels, "time_dim": scfg.time_dim}
+    lats = [bf16_round(randn(16 * h * w, 710 + i)) for i in range(3)]
+    ctxs = [bf16_round(randn(text * 256, 720 + i)) for i in range(3)]
+    mark = graph.mark()
+    inputs = [T.StepInputs(graph.buffer(bf16(l)), h, w, 0.41, graph.buffer(bf16(c)), text) for l, c in zip(lats, ctxs)]
+    vel, txts = T.transformer(graph, wts, scfg, inputs, dtype="bf16")
+    got = [graph.read(v, 16 * h * w * 4, np.float32).copy() for v in vel]
+    single = []
+    for ib in inputs:
+        v1, _ = T.transformer(graph, wts, scfg, ib, dtype="bf16")
+        single.append(graph.read(v1, 16 * h * w * 4, np.float32).copy())
+    assert graph.device_error() == 0
+    graph.release(mark)
+    for i in range(3):
+        assert np.allclose(got[i], single[i], rtol=1e-5, atol=1e-6 * np.abs(single[i]).max())
+        want = O.step_reference(lats[i], h, w, 0.41, ctxs[i], host, cfgd)
+        c = O.compare(got[i], want)
+        assert c["cosine"] >= 0.9999, c
+
+
+def test_sampling_loop_matches_the_float64_loop(we, graph):
+    """Two Euler steps (src/pipeline/generate.ts:94-105) of a tiny f32 model against the float64 step + eulerStep."""
+    T = we.transformer
+    bc = we.blocks.BlockConfig(hidden=64, mlp=128, heads=2, kv_heads=2, head_dim=32, mlp_act="gelu", attn_gate=False)
+    scfg = T.StepConfig(block=bc, double=1, single=1, ctx_dim=32, axes=(8, 12, 12))
+    h, w, text = 6, 8, 4
+    host, wts = make_step(we, graph, scfg, 800)
+    cfgd = {**vars(bc), "axes": scfg.axes, "theta": scfg.theta, "channels": scfg.channels, "time_dim": scfg.time_dim}
+    noise = [O.gaussian(16 * h * w, 5 + i) for i in range(2)]
+    ctxs = [randn(text * 32, 810 + i) for i in range(2)]
+    mark = graph.mark()
+    out = T.sample(graph, wts, scfg, [graph.buffer(z) for z in noise], [graph.buffer(c) for c in ctxs], h, w, text,
+                   steps=2, dtype="f32")
+    got = [graph.read(o, 16 * h * w * 4, np.float32).copy() for o in out]
+    graph.release(mark)
+    sig = O.sigmas(2)
+    for i in range(2):
+        x = noise[i]
+        for s in range(2):
+            v = O.step_reference(x, h, w, sig[s], ctxs[i], host, cfgd)
+            x = O.euler_step(x, v, sig[s], sig[s + 1])
+        c = O.compare(got[i], x)
+        assert c["cosine"] > 0.99999 and c["relativeError"] < 1e-4, c

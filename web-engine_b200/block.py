@@ -103,18 +103,33 @@ def double_block(graph: Graph, txt: BlockWeights, img: BlockWeights, cfg: BlockC
                        dtype)
 
 
-def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32") -> Buffer:
+def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32",
+                images: int = 1) -> Buffer:
+    """Rows of `images` sequences of rope.tokens / images tokens each, stacked; each part covers a row range with its
+    own weights, attention runs within each image. rope: cos/sin for all stacked rows (per image, tiled)."""
     parts = [p for p in parts if p.rows > 0]
     if sum(p.rows for p in parts) != rope.tokens:
         raise ValueError("the parts must cover the rope's tokens")
+    if images < 1 or rope.tokens % images:
+        raise ValueError("the rows must split evenly into images")
     if dtype == "f32":
-        return _joint_f32(graph, parts, cfg, x, tvec, rope)
+        return _joint_f32(graph, parts, cfg, x, tvec, rope, images)
     if dtype == "bf16":
-        return _joint_bf16(graph, parts, cfg, x, tvec, rope)
+        return _joint_bf16(graph, parts, cfg, x, tvec, rope, images)
     raise ValueError(f"unknown block dtype {dtype}")
 
 
-def _joint_f32(graph, parts, cfg, x, tvec, rope):
+def _attend_images(graph, q, k, v, o, rows: int, cfg: BlockConfig, images: int, dtype: str) -> None:
+    """Attention of each image's rows into o (one launch per image)."""
+    t = rows // images
+    qw, kw = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    es = 2 if dtype == "bf16" else 4
+    for i in range(images):
+        K.attention(graph, rows_at(q, i * t, qw * es), rows_at(k, i * t, kw * es), rows_at(v, i * t, kw * es), t,
+                    cfg.heads, cfg.kv_heads, cfg.head_dim, rows_at(o, i * t, qw * es), dtype=dtype, out_dtype=dtype)
+
+
+def _joint_f32(graph, parts, cfg, x, tvec, rope, images=1):
     t, hd, hdim = rope.tokens, cfg.hidden, cfg.head_dim
     qw, kw = cfg.heads * hdim, cfg.kv_heads * hdim
     mark = graph.mark()
@@ -142,7 +157,11 @@ def _joint_f32(graph, parts, cfg, x, tvec, rope):
             graph.copy(vp, 0, v, p.row0 * kw * 4, p.rows * kw * 4)
         hs.append(h)
         mods.append(mod)
-    o = ops.attention(graph, q, k, v, t, cfg.heads, cfg.kv_heads, hdim)
+    if images == 1:
+        o = ops.attention(graph, q, k, v, t, cfg.heads, cfg.kv_heads, hdim)
+    else:
+        o = graph.buffer(t * qw * 4)
+        _attend_images(graph, q, k, v, o, t, cfg, images, "f32")
     out = None if one else graph.buffer(t * hd * 4)
     for p, h, mod in zip(parts, hs, mods):
         op = rows_at(o, p.row0, hd * 4)
@@ -177,11 +196,16 @@ def _split_rows(split, p: Part, width: int):
     return (rows_at(split[0], p.row0, width), rows_at(split[1], p.row0, width), rows_at(split[2], p.row0, 4))
 
 
-def _joint_bf16(graph, parts, cfg, x, tvec, rope):
+def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1):
     t, hd, hdim = rope.tokens, cfg.hidden, cfg.head_dim
     qw, kw = cfg.heads * hdim, cfg.kv_heads * hdim
     mark = graph.mark()
-    mods = [modulation(graph, tvec, p.w.table, hd) for p in parts]
+    shared: dict = {}  # parts with the same weights (the images of a batch) share one modulation
+    mods = []
+    for p in parts:
+        if id(p.w) not in shared:
+            shared[id(p.w)] = modulation(graph, tvec, p.w.table, hd)
+        mods.append(shared[id(p.w)])
     split = (graph.buffer(t * hd), graph.buffer(t * hd), graph.buffer(t * 4))
     q, k, v = graph.buffer(t * qw * 2), graph.buffer(t * kw * 2), graph.buffer(t * kw * 2)
     for p, mod in zip(parts, mods):
@@ -198,7 +222,7 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope):
         K.qknorm_rope(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, cfg.kv_heads, rope.pairs, kp, eps=cfg.eps,
                       x_dtype="bf16", out_dtype="bf16")
     o = graph.buffer(t * hd * 2)
-    K.attention(graph, q, k, v, t, cfg.heads, cfg.kv_heads, hdim, o, dtype="bf16", out_dtype="bf16")
+    _attend_images(graph, q, k, v, o, t, cfg, images, "bf16")
     if cfg.attn_gate:  # og = o * sigmoid(gate h), in the gate GEMM's epilogue
         og = graph.buffer(t * hd * 2)
         for p in parts:

@@ -28,7 +28,7 @@ import numpy as np
 from . import _lib as L
 from . import kernels as K
 from . import ops
-from .block import BlockConfig, BlockWeights, block_flops, double_block, joint_block, Part
+from .block import BlockConfig, BlockWeights, Part, block_flops, joint_block
 from .graph import Buffer, Graph, addr
 
 LATENT_CHANNELS = 16
@@ -130,63 +130,78 @@ class StepInputs:
     context: object
     text_tokens: int
     text_cache: object = None
+    latent_dtype: str | None = None  # the latent's element type when it differs from the step's (f32 sampler state)
 
 
-def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp: StepInputs, dtype: str = "f32",
-                velocity=None, on_block=None) -> tuple:
-    """One denoising step: the predicted velocity [C, H, W] f32 (a new buffer, or written into `velocity`), and
-    the txt rows for the next step's text_cache (transformer.ts:134-176)."""
+def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype: str = "f32", velocity=None,
+                on_block=None) -> tuple:
+    """One denoising step (transformer.ts:134-176) of one image (`inp` a StepInputs) or of a batch of images (a list
+    of StepInputs with the same geometry and timestep). The batch runs as one token stream: every linear is one
+    GEMM over all images' rows, attention runs per image.
+
+    Returns the predicted velocity [C, H, W] f32 (a new buffer, or written into `velocity`) and the txt rows for
+    the next step's text_cache; for a batch, lists of both."""
+    batch = list(inp) if isinstance(inp, (list, tuple)) else [inp]
+    b0 = batch[0]
+    if any((b.height, b.width, b.text_tokens, b.timestep) != (b0.height, b0.width, b0.text_tokens, b0.timestep)
+           for b in batch):
+        raise ValueError("the images of a batch need the same size, text length and timestep")
     bc = cfg.block
-    hid, ch = bc.hidden, cfg.channels
-    rows, cols = patch_grid(inp.height, inp.width)
-    image, Lt = rows * cols, inp.text_tokens
+    hid, ch, B = bc.hidden, cfg.channels, len(batch)
+    rows, cols = patch_grid(b0.height, b0.width)
+    image, Lt = rows * cols, b0.text_tokens
     T = Lt + image
-    tables = _tables(Lt, rows, cols, tuple(cfg.axes), float(cfg.theta))
+    R = B * T
+    cos, sin, pairs = _tables(Lt, rows, cols, tuple(cfg.axes), float(cfg.theta))
+    outs = velocity if isinstance(velocity, (list, tuple)) else [velocity] * B if velocity is not None else [None] * B
     mark = graph.mark()
-    t, tvec = time(graph, w, inp.timestep, cfg.time_dim)
-    txt = inp.text_cache if inp.text_cache is not None else text(graph, w, inp.context, Lt, dtype)
-    tok = graph.buffer(image * 4 * ch * (2 if dtype == "bf16" else 4))
-    patchify(graph, inp.latent, inp.height, inp.width, tok, ch, dtype, dtype)
-    img = ops.linear(graph, tok, w.first, image, x_dtype=dtype, y_dtype="f32")
-    x = graph.buffer(T * hid * 4)
-    graph.copy(txt, 0, x, 0, Lt * hid * 4)
-    graph.copy(img, 0, x, Lt * hid * 4, image * hid * 4)
-    rope = ops.Rope(graph.buffer(tables[0]), graph.buffer(tables[1]), tables[2], T)
-    i = 0
-    for txt_w, img_w in w.double:
+    t, tvec = time(graph, w, b0.timestep, cfg.time_dim)
+    x = graph.buffer(R * hid * 4)
+    es = 2 if dtype == "bf16" else 4
+    tok = graph.buffer(B * image * 4 * ch * es)
+    txts = []
+    for i, ib in enumerate(batch):
+        txt = ib.text_cache if ib.text_cache is not None else text(graph, w, ib.context, Lt, dtype)
+        txts.append(txt)
+        graph.copy(txt, 0, x, i * T * hid * 4, Lt * hid * 4)
+        patchify(graph, ib.latent, ib.height, ib.width, addr(tok).value + i * image * 4 * ch * es, ch,
+                 ib.latent_dtype or dtype, dtype)
+    img = ops.linear(graph, tok, w.first, B * image, x_dtype=dtype, y_dtype="f32")
+    for i in range(B):
+        graph.copy(img, i * image * hid * 4, x, (i * T + Lt) * hid * 4, image * hid * 4)
+    rope = ops.Rope(graph.buffer(np.tile(cos, B)), graph.buffer(np.tile(sin, B)), pairs, R)
+    # double blocks: each image's text rows and image rows; single blocks: all rows of the batch at once
+    layers = [[p for i in range(B) for p in (Part(i * T, Lt, tw), Part(i * T + Lt, image, iw))] for tw, iw in w.double]
+    layers += [[Part(0, R, bw)] for bw in w.single]
+    for i, parts in enumerate(layers):
         bm = graph.mark()
-        nxt = double_block(graph, txt_w, img_w, bc, x, Lt, tvec, rope, dtype)
+        nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B)
         graph.release(bm, [nxt])
         graph.free(x)
         x = nxt
         if on_block:
             on_block(i)
-        i += 1
-    for bw in w.single:
-        bm = graph.mark()
-        nxt = joint_block(graph, [Part(0, T, bw)], bc, x, tvec, rope, dtype)
-        graph.release(bm, [nxt])
-        graph.free(x)
-        x = nxt
-        if on_block:
-            on_block(i)
-        i += 1
     scale = ops.add(graph, t, w.last_scale, hid)
     shift = ops.add(graph, t, w.last_shift, hid)
     if dtype == "bf16":
-        split = (graph.buffer(T * hid), graph.buffer(T * hid), graph.buffer(T * 4))
-        K.norm_split(graph, x, w.last_norm, T, hid, *split, scale=scale, shift=shift, eps=bc.eps)
-        last = graph.buffer(T * 4 * ch * 4)
-        K.gemm_fp8(graph, *split, w.last_linear.buffer, last, T, w.last_linear.n, w.last_linear.k,
+        split = (graph.buffer(R * hid), graph.buffer(R * hid), graph.buffer(R * 4))
+        K.norm_split(graph, x, w.last_norm, R, hid, *split, scale=scale, shift=shift, eps=bc.eps)
+        last = graph.buffer(R * 4 * ch * 4)
+        K.gemm_fp8(graph, *split, w.last_linear.buffer, last, R, w.last_linear.n, w.last_linear.k,
                    w.last_linear.scale, chan_scale=w.last_linear.chan_scale, bias=w.last_linear.bias, y_dtype="f32")
     else:
-        h = ops.norm(graph, x, w.last_norm, T, hid, ops.Mod(scale, shift), bc.eps)
-        last = ops.linear(graph, h, w.last_linear, T)
-    out = velocity if velocity is not None else graph.buffer(ch * inp.height * inp.width * 4)
-    unpatchify(graph, addr(last).value + Lt * 4 * ch * 4, inp.height, inp.width, out, ch, "f32", "f32")
-    keep = [b for b in (out, txt) if isinstance(b, Buffer)]
+        h = ops.norm(graph, x, w.last_norm, R, hid, ops.Mod(scale, shift), bc.eps)
+        last = ops.linear(graph, h, w.last_linear, R)
+    vel = []
+    for i in range(B):
+        out = outs[i] if outs[i] is not None else graph.buffer(ch * b0.height * b0.width * 4)
+        unpatchify(graph, addr(last).value + (i * T + Lt) * 4 * ch * 4, b0.height, b0.width, out, ch, "f32", "f32")
+        vel.append(out)
+    keep = [b for b in vel + txts if isinstance(b, Buffer)]
     graph.release(mark, keep)
-    return out, txt
+    if isinstance(inp, (list, tuple)):
+        return vel, txts
+    return vel[0], txts[0]
 
 
 def step_flops(cfg: StepConfig, text_tokens: int, image_tokens: int) -> dict:
@@ -213,9 +228,11 @@ def euler_step(graph: Graph, x, velocity, sigma: float, nxt: float, n: int, out=
     """x + (sigma_next - sigma) v on the device (eulerStep, sampler.ts:22-24), f32."""
     g = graph.buffer(np.array([nxt - sigma], np.float32))
     if out is None:
-        return ops.gated_add(graph, x, velocity, g, n, 1)
-    L.check(graph.ctx, L.lib().we_elementwise(graph.ctx, L.EW["gated_add"], addr(x), addr(velocity), addr(g), n, 1,
-                                              L.DTYPES["f32"], addr(out), L.DTYPES["f32"]))
+        out = ops.gated_add(graph, x, velocity, g, n, 1)
+    else:
+        L.check(graph.ctx, L.lib().we_elementwise(graph.ctx, L.EW["gated_add"], addr(x), addr(velocity), addr(g), n, 1,
+                                                  L.DTYPES["f32"], addr(out), L.DTYPES["f32"]))
+    graph.free(g)  # back to the pool: a later user of it is queued after this step
     return out
 
 
@@ -232,3 +249,29 @@ def gaussian(n: int, seed: int) -> np.ndarray:
     out = np.empty(2 * m, dtype=np.float32)
     out[0::2], out[1::2] = r * np.cos(a), r * np.sin(a)
     return out[:n]
+
+
+def sample(graph: Graph, w: TransformerWeights, cfg: StepConfig, noise: list, contexts: list, height: int, width: int,
+           text_tokens: int, steps: int = TURBO["steps"], mu: float = TURBO["mu"], dtype: str = "bf16",
+           on_step=None) -> list:
+    """Flow-matching Euler sampling of a batch of images (the loop of src/pipeline/generate.ts:94-105): the text
+    rows are computed once per image, each step feeds timestep = sigma_i, then x += (sigma_{i+1} - sigma_i) v.
+    noise: f32 latents [C, H, W] on the device (one per image); contexts: [text_tokens, ctx_dim] of `dtype`.
+    Returns new f32 latent buffers."""
+    sig = sigmas(steps, mu)
+    n = cfg.channels * height * width
+    xs, caches = list(noise), [None] * len(noise)
+    for i in range(steps):
+        inputs = [StepInputs(xs[b], height, width, sig[i], contexts[b], text_tokens, caches[b], latent_dtype="f32")
+                  for b in range(len(xs))]
+        vel, caches = transformer(graph, w, cfg, inputs, dtype)
+        nxt = [euler_step(graph, xs[b], vel[b], sig[i], sig[i + 1], n) for b in range(len(xs))]
+        for v in vel:
+            graph.free(v)
+        if i > 0:
+            for x in xs:
+                graph.free(x)
+        xs = nxt
+        if on_step:
+            on_step(i)
+    return xs
