@@ -181,7 +181,7 @@ def random_model(we, g, torch, dev, gen, scfg):
     return we.transformer.TransformerWeights(double=double, single=single, **edge, **vec)
 
 
-def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, world: int = 1) -> dict:
+def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, world: int = 1, gpu: int = 0) -> dict:
     """Config 3 (one single-stream block, 4608 tokens) and config 4 (one denoising step of the 19 + 38 block
     model at 1024x1024: 512 text + 4096 image tokens), bf16 path, weights resident, inputs ~N(0, 1)."""
     T = we.transformer
@@ -203,12 +203,13 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
         g.release(mark)
 
     l0 = g.stats["launches"]
-    blk_ms = timed(step_block, steps, 3) / steps
+    with ClockSampler(gpu) as blk_clocks:
+        blk_ms = timed(step_block, steps, 3) / steps
     blk_launches = (g.stats["launches"] - l0) // (steps + 3)
     bf = we.blocks.block_flops(bc, tokens)
     out["block_config3"] = {"ms": blk_ms, "tflops": bf["total"] / (blk_ms * 1e-3) / 1e12,
                             "frac_bf16_peak": bf["total"] / (blk_ms * 1e-3) / 1e12 / bf16_peak,
-                            "flop": bf["total"], "launches_per_block": blk_launches,
+                            "flop": bf["total"], "launches_per_block": blk_launches, "clocks": blk_clocks.summary(),
                             "note": "one single-stream block, 4608 tokens, hidden 3072, 24x128 heads, 4x GELU MLP, "
                                     "fp8 per-channel linears, bf16 activations, f32 residual"}
     del bw, xb
@@ -224,7 +225,8 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
 
     ksteps = max(3, steps // 4)
     l0 = g.stats["launches"]
-    st_ms = timed(step_model, ksteps, 3) / ksteps
+    with ClockSampler(gpu) as st_clocks:
+        st_ms = timed(step_model, ksteps, 3) / ksteps
     st_launches = (g.stats["launches"] - l0) // (ksteps + 3)
     sf = T.step_flops(scfg, text_tokens, rows * cols)
     assert torch.isfinite(vel).all().item(), "non-finite velocity"
@@ -240,10 +242,12 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
         T.transformer(g, model, scfg, inp_e, dtype="bf16", velocity=vel)
         g.read_into(vel, vel_h.data_ptr(), vel.numel() * 4)
 
-    e2e_ms = timed(step_e2e, ksteps, 1) / ksteps
+    with ClockSampler(gpu) as e2e_clocks:
+        e2e_ms = timed(step_e2e, ksteps, 1) / ksteps
     out["step_config4"] = {"ms": st_ms, "tflops": sf["total"] / (st_ms * 1e-3) / 1e12,
                            "frac_bf16_peak": sf["total"] / (st_ms * 1e-3) / 1e12 / bf16_peak, "flop": sf["total"],
-                           "launches_per_step": st_launches, "e2e_ms": e2e_ms,
+                           "launches_per_step": st_launches, "e2e_ms": e2e_ms, "clocks": st_clocks.summary(),
+                           "e2e_clocks": e2e_clocks.summary(),
                            "e2e_h2d_bytes": lat.numel() * 2 + ctx.numel() * 2, "e2e_d2h_bytes": vel.numel() * 4,
                            "note": "19 double + 38 single blocks of config 3 shape, 512 text + 4096 image tokens "
                                    "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
@@ -258,9 +262,11 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
     def step_batch():
         T.transformer(g, model, scfg, binp, dtype="bf16", velocity=vels)
 
-    b_ms = timed(step_batch, 2, 1) / 2
+    with ClockSampler(gpu) as b_clocks:
+        b_ms = timed(step_batch, 2, 1) / 2
     out["batch8_config5"] = {"ms_per_step": b_ms, "images_per_s": world * per / (b_ms * 1e-3),
                              "images_per_rank": per, "tflops": world * per * sf["total"] / (b_ms * 1e-3) / 1e12,
+                             "clocks": b_clocks.summary(),
                              "scaling": "strong: 8 images per step in total, 8 / n_gpus per rank",
                              "note": "one denoising step of config 4's model on a batch of 1024x1024 images, "
                                      "data-parallel over images, weights resident"}
@@ -502,7 +508,7 @@ def main() -> None:
 
     # ---- config 3 (one block) and config 4 (one whole denoising step) on the bf16 fused path ----
     if not args.no_variants and not args.no_model:
-        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak, world))
+        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak, world, local))
 
     # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
     if not args.no_variants:

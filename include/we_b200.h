@@ -34,7 +34,8 @@ enum {
   WE_ECUDA = 3,       /* a CUDA runtime/driver call failed */
   WE_ENCCL = 4,       /* a collective failed */
   WE_ETIMEOUT = 5,    /* a bounded device-side wait gave up (see we_device_error) */
-  WE_EUNSUPPORTED = 6 /* valid request that this build does not implement */
+  WE_EUNSUPPORTED = 6, /* valid request that this build does not implement */
+  WE_EIO = 7           /* a file could not be opened, read or mapped */
 };
 
 /* ---------------- element types ---------------- */
@@ -318,6 +319,39 @@ enum { WE_NOALLOC_SYNC = 1u << 3 };
 int we_matmul_fp8_noalloc(void* stream, const void* x, int64_t m, int64_t k, int64_t x_stride, const uint8_t* w,
                           int64_t n, float scale, const float* chan_scale, const float* bias, void* y,
                           int64_t y_stride, int32_t y_dtype, uint32_t flags, char* errbuf, size_t errlen);
+
+/* ---------------- weights: .safetensors files (src/weights/safetensors.ts:1-70) ----------------
+   The file is untrusted: we_st_open checks every offset and size before use, with the reference's checks and
+   messages (readHeader, safetensors.ts:27-64): "File is too small to be a .safetensors file", "Bad header size: N"
+   (over 100 MB or past the end), "Header is not valid JSON", "Header is not an object", "<name>: unknown dtype D",
+   "<name>: bad shape", "<name>: bad data_offsets", "<name>: has N bytes, its shape needs M bytes", "<name>: data
+   goes past the end of the file", "<a> and <b> overlap". Those return WE_EINVAL, OS failures WE_EIO, with the
+   message in err. The data region is mapped read-only; nothing is read until a tensor is asked for. */
+typedef struct we_st we_st;
+typedef struct {
+  const char* name;  /* owned by the we_st */
+  const char* dtype; /* "F32", "BF16", "F16", "F8_E4M3", "F8_E5M2", "I64", ... "BOOL" */
+  int32_t ndim;
+  int64_t shape[8]; /* the first min(ndim, 8) dimensions */
+  int64_t offset;   /* absolute byte offset of the data in the file */
+  int64_t size;     /* bytes */
+} we_st_tensor;
+
+int we_st_open(const char* path, we_st** out, char* err, size_t err_len);
+int64_t we_st_count(const we_st* st);
+/* the i-th tensor in header order */
+int we_st_tensor_at(const we_st* st, int64_t i, we_st_tensor* out);
+/* WE_EINVAL when the file has no tensor of that name */
+int we_st_find(const we_st* st, const char* name, we_st_tensor* out);
+int64_t we_st_metadata_count(const we_st* st);
+int we_st_metadata_at(const we_st* st, int64_t i, const char** key, const char** value);
+/* readTensor (safetensors.ts:67-70): the first min(limit, size) bytes of a tensor (limit < 0: all) into host memory */
+int we_st_read(const we_st* st, const char* name, void* dst, int64_t limit);
+/* The tensor's bytes into device memory on the context's stream: the mapped file is copied through two pinned
+   32 MB staging chunks, each chunk's DMA overlapping the host copy of the next. The loader's device upload of a
+   linear layer (loadLinear's graph.buffer, src/model/weights.ts:26-50). */
+int we_st_upload(we_ctx* ctx, we_st* st, const char* name, void* device_dst);
+void we_st_close(we_st* st);
 
 #ifdef __cplusplus
 }

@@ -10,9 +10,10 @@ from . import kernels, parallel
 from .stream import Streamer
 from . import block as blocks
 from . import transformer
+from . import weights
 
 __all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "norm", "no_mod", "rotate",
-           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "build"]
+           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "weights", "build"]
 
 
 def build(verbose: bool = False) -> str:

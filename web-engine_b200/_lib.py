@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libwe_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "we_b200.h")
 
-WE_OK, WE_EINVAL, WE_ENOMEM, WE_ECUDA, WE_ENCCL, WE_ETIMEOUT, WE_EUNSUPPORTED = range(7)
+WE_OK, WE_EINVAL, WE_ENOMEM, WE_ECUDA, WE_ENCCL, WE_ETIMEOUT, WE_EUNSUPPORTED, WE_EIO = range(8)
 F32, BF16, FP8, INT4G64, F16 = 0, 1, 2, 3, 4
 MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT, NOALLOC_SYNC = 1, 2, 4, 8
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
@@ -66,6 +66,11 @@ class LinearDesc(C.Structure):
 LinearDesc._fields_ = [("weight", C.c_void_p), ("dtype", C.c_int32), ("scale", C.c_float), ("chan_scale", C.c_void_p),
                        ("group_scale", C.c_void_p), ("n", C.c_int64), ("k", C.c_int64), ("bias", C.c_void_p),
                        ("lora_down", C.POINTER(LinearDesc)), ("lora_up", C.POINTER(LinearDesc))]
+
+
+class StTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_char_p), ("ndim", C.c_int32), ("shape", C.c_int64 * 8),
+                ("offset", C.c_int64), ("size", C.c_int64)]
 
 
 class ModDesc(C.Structure):
@@ -133,6 +138,15 @@ _SIGS = {
     "we_streamer_release": (C.c_int, [_P, C.c_int32]),
     "we_streamer_stats": (C.c_int, [_P, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "we_streamer_destroy": (C.c_int, [_P]),
+    "we_st_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
+    "we_st_count": (_I64, [_P]),
+    "we_st_tensor_at": (C.c_int, [_P, _I64, C.POINTER(StTensor)]),
+    "we_st_find": (C.c_int, [_P, C.c_char_p, C.POINTER(StTensor)]),
+    "we_st_metadata_count": (_I64, [_P]),
+    "we_st_metadata_at": (C.c_int, [_P, _I64, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p)]),
+    "we_st_read": (C.c_int, [_P, C.c_char_p, _P, _I64]),
+    "we_st_upload": (C.c_int, [_P, _P, C.c_char_p, _P]),
+    "we_st_close": (None, [_P]),
     "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
                                         C.c_uint32, C.c_char_p, C.c_size_t]),
 }
