@@ -181,7 +181,8 @@ def random_model(we, g, torch, dev, gen, scfg):
     return we.transformer.TransformerWeights(double=double, single=single, **edge, **vec)
 
 
-def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, world: int = 1, gpu: int = 0) -> dict:
+def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, world: int = 1, gpu: int = 0,
+                step_ms=None) -> dict:
     """Config 3 (one single-stream block, 4608 tokens) and config 4 (one denoising step of the 19 + 38 block
     model at 1024x1024: 512 text + 4096 image tokens), bf16 path, weights resident, inputs ~N(0, 1)."""
     T = we.transformer
@@ -251,6 +252,24 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
                            "e2e_h2d_bytes": lat.numel() * 2 + ctx.numel() * 2, "e2e_d2h_bytes": vel.numel() * 4,
                            "note": "19 double + 38 single blocks of config 3 shape, 512 text + 4096 image tokens "
                                    "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
+    # config 4's one image split over all ranks: sequence parallelism (rows sharded, heads exchanged by all-to-all)
+    if world > 1:
+        sp = we.sequence.SequenceParallel(device=dev)
+
+        def step_sp():
+            T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, sp=sp)
+
+        sp_steps = max(6, steps // 2)
+        with ClockSampler(gpu) as sp_clocks:
+            sp_ms = timed(step_sp, sp_steps, 3) / sp_steps
+        per = sorted(step_ms or [sp_ms])
+        out["step_config4_sequence_parallel"] = {
+            "ms": sp_ms, "median_ms_this_rank": per[len(per) // 2], "steps": sp_steps, "n_gpus": world,
+            "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12,
+            "clocks": sp_clocks.summary(),
+            "note": "one 1024x1024 image's step over all GPUs: every rank runs the blocks on 4608 / n_gpus rows, "
+                    "q/k/v/o exchanged by NCCL all-to-all (heads / n_gpus heads per rank in attention)"}
+
     # config 5's batch: 8 images per step in total, split data-parallel across the ranks (no collective); each
     # rank runs its share as one token stream (every linear one GEMM over all its images' rows)
     per = max(1, 8 // world)
@@ -347,6 +366,7 @@ def main() -> None:
     torch.cuda.synchronize()
 
     wall_ms = [0.0]
+    step_ms: list = []  # per-step event times of the last timed() call, this rank
 
     def timed(step, steps, warmup, sampler=None):
         """Sum of per-step CUDA-event times (ms) with an L2 flush before each step, outside the events."""
@@ -365,7 +385,8 @@ def main() -> None:
             b.record(stream)
         torch.cuda.synchronize()
         wall_ms[0] = (time.perf_counter() - t0) * 1e3
-        total = sum(a.elapsed_time(b) for a, b in ev)
+        step_ms[:] = [a.elapsed_time(b) for a, b in ev]
+        total = sum(step_ms)
         return we.parallel.max_over_ranks(total, device=dev)
 
     if args.profile_block:
@@ -508,7 +529,7 @@ def main() -> None:
 
     # ---- config 3 (one block) and config 4 (one whole denoising step) on the bf16 fused path ----
     if not args.no_variants and not args.no_model:
-        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak, world, local))
+        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak, world, local, step_ms))
 
     # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
     if not args.no_variants:

@@ -270,6 +270,13 @@ int we_patchify(we_ctx* ctx, const void* latent, int32_t latent_dtype, int64_t c
 int we_unpatchify(we_ctx* ctx, const void* tokens, int32_t tokens_dtype, int64_t channels, int64_t height,
                   int64_t width, void* latent, int32_t latent_dtype);
 
+/* Sequence-parallel exchange layout (no reference counterpart: the reference runs on one GPU). rows holds
+   [tokens, groups, group_bytes] (a token shard with every head), groups holds [groups, tokens, group_bytes]
+   (chunk g = the heads of rank g, what an all-to-all sends to rank g). to_groups = 1 moves rows -> groups, 0 the
+   reverse. group_bytes must be a multiple of 16 and both buffers 16-byte aligned. */
+int we_head_groups(we_ctx* ctx, const void* rows, void* groups, int64_t tokens, int64_t n_groups, int64_t group_bytes,
+                   int32_t to_groups);
+
 /* ---------------- attention: attention() (src/kernels/attention.ts:20-51) ----------------
    softmax(q k^T / sqrt(dim)) v per head with grouped-query heads (query head h uses kv head
    h / (heads / kv_heads)); q [tokens, heads, dim], k, v [tokens, kv_heads, dim] -> out [tokens, heads, dim].

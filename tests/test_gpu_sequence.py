@@ -1,0 +1,80 @@
+"""Sequence parallelism of one image's step on 2 GPUs (one process each, NCCL): every rank runs the blocks on half
+of the rows, attention exchanges heads by all-to-all; the velocity must equal the one-GPU step's. 80 tokens (8
+text + 72 image), so rank 0's shard holds text and image rows and rank 1's image rows only. Needs two B200s;
+skipped otherwise. NVLS is off (NCCL_NVLS_ENABLE=0)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from test_gpu_multi import _free_port
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _rank_main(rank, world, port, errq):
+    try:
+        sys.path.insert(0, ROOT)
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        from conftest import load_package
+        from util import bf16, bf16_round, make_step, randn
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        we = load_package()
+        g = we.Graph(rank)
+        st = torch.cuda.Stream(device=dev)
+        torch.cuda.set_stream(st)
+        g.set_stream(st.cuda_stream)
+        T = we.transformer
+        bc = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=2, head_dim=128, mlp_act="gelu",
+                                   attn_gate=False)
+        scfg = T.StepConfig(block=bc, double=1, single=2, ctx_dim=256)
+        h, w, text = 16, 18, 8
+        _, wts = make_step(we, g, scfg, 1200, per_channel=True)  # same seeds on every rank: the same model
+        lat, ctx = bf16_round(randn(16 * h * w, 1201)), bf16_round(randn(text * 256, 1202))
+        inp = T.StepInputs(g.buffer(bf16(lat)), h, w, 0.37, g.buffer(bf16(ctx)), text)
+        v1, _ = T.transformer(g, wts, scfg, inp, dtype="bf16")
+        one = g.read(v1, 16 * h * w * 4, np.float32).copy()
+        sp = we.sequence.SequenceParallel()
+        v2, _ = T.transformer(g, wts, scfg, inp, dtype="bf16", sp=sp)
+        got = g.read(v2, 16 * h * w * 4, np.float32).copy()
+        err = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
+        assert err < 1e-6, ("sequence-parallel step differs from the one-GPU step", err)
+        assert g.device_error() == 0
+        g.destroy()
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:  # noqa: BLE001
+        errq.put(f"rank {rank}: {type(exc).__name__}: {exc}")
+        raise
+
+
+def test_sequence_parallel_step_on_two_gpus():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp = torch.multiprocessing.get_context("spawn")
+    errq = mp.SimpleQueue()
+    world, port = 2, _free_port()
+    procs = [mp.Process(target=_rank_main, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not alive and not errors and all(p.exitcode == 0 for p in procs), errors

@@ -4,6 +4,7 @@ timestepEmbedding / patchify / unpatchify (tests/transformer.test.ts), sigmas / 
 import math
 
 import numpy as np
+import pytest
 
 from oracle import oracle as O
 
@@ -68,3 +69,12 @@ def test_step_flops_match_the_benchmark_arithmetic(we):
     blk = we.blocks.block_flops(T.FLUX_BLOCK, 4608)
     assert blk["linear"] == 2 * 4608 * (4 * 3072 ** 2 + 2 * 3072 * 12288)
     assert abs(57 * blk["linear"] / 1e12 - 59.5) < 0.05 and abs(f["attention"] / 1e12 - 14.87) < 0.05
+
+
+def test_block_config_checks_its_shapes(we):
+    B = we.blocks.BlockConfig
+    B(hidden=256, mlp=1024, heads=2, kv_heads=1, head_dim=128)
+    with pytest.raises(ValueError, match="must equal hidden"):
+        B(hidden=256, mlp=1024, heads=4, kv_heads=2, head_dim=128)
+    with pytest.raises(ValueError, match="multiple of kvHeads"):
+        B(hidden=384, mlp=1024, heads=3, kv_heads=2, head_dim=128)

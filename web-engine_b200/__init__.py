@@ -11,9 +11,10 @@ from .stream import Streamer
 from . import block as blocks
 from . import transformer
 from . import weights
+from . import sequence
 
 __all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "norm", "no_mod", "rotate",
-           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "weights", "build"]
+           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "weights", "sequence", "build"]
 
 
 def build(verbose: bool = False) -> str:

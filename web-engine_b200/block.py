@@ -41,6 +41,15 @@ class BlockConfig:
     mlp_act: str = "swiglu"   # "swiglu" (Krea 2) | "gelu" (tanh GELU, 4x MLP)
     attn_gate: bool = True
 
+    def __post_init__(self):
+        # attention's output is rows x hidden (sigmoidGate over rows * hidden, wo [hidden, hidden]: block.ts:61-64)
+        if self.heads * self.head_dim != self.hidden:
+            raise ValueError(f"heads x head_dim ({self.heads} x {self.head_dim}) must equal hidden ({self.hidden})")
+        if self.kv_heads <= 0 or self.heads % self.kv_heads:
+            raise ValueError("heads must be a multiple of kvHeads")
+        if self.mlp_act not in ("swiglu", "gelu"):
+            raise ValueError(f"unknown MLP activation {self.mlp_act}")
+
 
 @dataclass
 class BlockWeights:
@@ -104,19 +113,35 @@ def double_block(graph: Graph, txt: BlockWeights, img: BlockWeights, cfg: BlockC
 
 
 def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32",
-                images: int = 1) -> Buffer:
+                images: int = 1, sp=None) -> Buffer:
     """Rows of `images` sequences of rope.tokens / images tokens each, stacked; each part covers a row range with its
-    own weights, attention runs within each image. rope: cos/sin for all stacked rows (per image, tiled)."""
+    own weights, attention runs within each image. rope: cos/sin for all stacked rows (per image, tiled).
+    sp: a sequence.SequenceParallel when the rows are this rank's shard of one image (bf16 path)."""
     parts = [p for p in parts if p.rows > 0]
     if sum(p.rows for p in parts) != rope.tokens:
         raise ValueError("the parts must cover the rope's tokens")
     if images < 1 or rope.tokens % images:
         raise ValueError("the rows must split evenly into images")
+    if sp is not None and (dtype != "bf16" or images != 1):
+        raise ValueError("a sequence-parallel block runs one image on the bf16 path")
     if dtype == "f32":
         return _joint_f32(graph, parts, cfg, x, tvec, rope, images)
     if dtype == "bf16":
-        return _joint_bf16(graph, parts, cfg, x, tvec, rope, images)
+        return _joint_bf16(graph, parts, cfg, x, tvec, rope, images, sp)
     raise ValueError(f"unknown block dtype {dtype}")
+
+
+def _attend_sp(graph, sp, q, k, v, o, t: int, cfg: BlockConfig) -> None:
+    """Attention of one image whose rows are sharded over sp's ranks: q/k/v go token shard -> head shard by
+    all-to-all, this rank attends heads / world heads over every token, the output comes back the same way."""
+    hb, T = cfg.head_dim * 2, t * sp.world
+    qh = sp.scatter_heads(graph, q, t, cfg.heads, hb, "q")
+    kh = sp.scatter_heads(graph, k, t, cfg.kv_heads, hb, "k")
+    vh = sp.scatter_heads(graph, v, t, cfg.kv_heads, hb, "v")
+    oh = sp.buffer("o_heads", T * (cfg.heads // sp.world) * hb)
+    K.attention(graph, qh, kh, vh, T, cfg.heads // sp.world, cfg.kv_heads // sp.world, cfg.head_dim, oh, dtype="bf16",
+                out_dtype="bf16")
+    sp.gather_heads(graph, oh, t, cfg.heads, hb, o)
 
 
 def _attend_images(graph, q, k, v, o, rows: int, cfg: BlockConfig, images: int, dtype: str) -> None:
@@ -196,7 +221,7 @@ def _split_rows(split, p: Part, width: int):
     return (rows_at(split[0], p.row0, width), rows_at(split[1], p.row0, width), rows_at(split[2], p.row0, 4))
 
 
-def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1):
+def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
     t, hd, hdim = rope.tokens, cfg.hidden, cfg.head_dim
     qw, kw = cfg.heads * hdim, cfg.kv_heads * hdim
     mark = graph.mark()
@@ -209,20 +234,23 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1):
     split = (graph.buffer(t * hd), graph.buffer(t * hd), graph.buffer(t * 4))
     q, k, v = graph.buffer(t * qw * 2), graph.buffer(t * kw * 2), graph.buffer(t * kw * 2)
     for p, mod in zip(parts, mods):
-        sp = _split_rows(split, p, hd)
-        K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *sp, scale=mod["prescale"],
+        sr = _split_rows(split, p, hd)
+        K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *sr, scale=mod["prescale"],
                      shift=mod["preshift"], eps=cfg.eps)
         qp, kp = rows_at(q, p.row0, qw * 2), rows_at(k, p.row0, kw * 2)
-        _gemm(graph, sp, p.w.wq, qp, p.rows, "bf16")
-        _gemm(graph, sp, p.w.wk, kp, p.rows, "bf16")
-        _gemm(graph, sp, p.w.wv, rows_at(v, p.row0, kw * 2), p.rows, "bf16")
+        _gemm(graph, sr, p.w.wq, qp, p.rows, "bf16")
+        _gemm(graph, sr, p.w.wk, kp, p.rows, "bf16")
+        _gemm(graph, sr, p.w.wv, rows_at(v, p.row0, kw * 2), p.rows, "bf16")
         pr = part_rope(rope, p)
         K.qknorm_rope(graph, qp, p.w.norm_q, pr.cos, pr.sin, p.rows, cfg.heads, rope.pairs, qp, eps=cfg.eps,
                       x_dtype="bf16", out_dtype="bf16")
         K.qknorm_rope(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, cfg.kv_heads, rope.pairs, kp, eps=cfg.eps,
                       x_dtype="bf16", out_dtype="bf16")
     o = graph.buffer(t * hd * 2)
-    _attend_images(graph, q, k, v, o, t, cfg, images, "bf16")
+    if sp is None:
+        _attend_images(graph, q, k, v, o, t, cfg, images, "bf16")
+    else:
+        _attend_sp(graph, sp, q, k, v, o, t, cfg)
     if cfg.attn_gate:  # og = o * sigmoid(gate h), in the gate GEMM's epilogue
         og = graph.buffer(t * hd * 2)
         for p in parts:
@@ -238,16 +266,16 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1):
     u = graph.buffer(t * cfg.mlp * 2)
     g = graph.buffer(t * cfg.mlp * 2) if cfg.mlp_act == "swiglu" else None
     for p, mod in zip(parts, mods):
-        sp = _split_rows(split, p, hd)
-        K.norm_split(graph, rows_at(x1, p.row0, hd * 4), p.w.norm2, p.rows, hd, *sp, scale=mod["postscale"],
+        sr = _split_rows(split, p, hd)
+        K.norm_split(graph, rows_at(x1, p.row0, hd * 4), p.w.norm2, p.rows, hd, *sr, scale=mod["postscale"],
                      shift=mod["postshift"], eps=cfg.eps)
         up = rows_at(u, p.row0, cfg.mlp * 2)
         if cfg.mlp_act == "swiglu":
             gp = rows_at(g, p.row0, cfg.mlp * 2)
-            _gemm(graph, sp, p.w.mlp_gate, gp, p.rows, "bf16")
-            _gemm(graph, sp, p.w.mlp_up, up, p.rows, "bf16", aux_op="swiglu", aux=gp, aux_dtype="bf16")
+            _gemm(graph, sr, p.w.mlp_gate, gp, p.rows, "bf16")
+            _gemm(graph, sr, p.w.mlp_up, up, p.rows, "bf16", aux_op="swiglu", aux=gp, aux_dtype="bf16")
         else:
-            _gemm(graph, sp, p.w.mlp_up, up, p.rows, "bf16", act="gelu_tanh")
+            _gemm(graph, sr, p.w.mlp_up, up, p.rows, "bf16", act="gelu_tanh")
     msplit = (graph.buffer(t * cfg.mlp), graph.buffer(t * cfg.mlp), split[2])
     K.quantize_act(graph, u, t, cfg.mlp, *msplit, terms=2)
     out = graph.buffer(t * hd * 4)

@@ -71,3 +71,32 @@ cudaError_t launch_unpatchify(const void* tokens, int tdt, int64_t C, int64_t H,
 }
 
 }  // namespace we
+
+namespace we {
+
+// Head-group exchange layout of sequence parallelism: rows [tokens, groups * hg, row_bytes] (token-major, a
+// rank's token shard with every head) <-> [groups, tokens, hg, row_bytes] (head-group-major: chunk g is what
+// rank g receives). `to_groups` picks the direction. One thread moves 16 bytes; row_bytes % 16 == 0.
+__global__ void head_groups_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t tokens,
+                                   int64_t groups, int64_t hg_vec, int to_groups, int64_t total) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    // i indexes the token-major layout: (t, g, v) with v < hg_vec 16-byte words per (token, group)
+    const int64_t v = i % hg_vec, tg = i / hg_vec;
+    const int64_t g = tg % groups, t = tg / groups;
+    const int64_t j = (g * tokens + t) * hg_vec + v;  // the same word in the group-major layout
+    if (to_groups) dst[j] = src[i];
+    else dst[i] = src[j];
+  }
+}
+
+cudaError_t launch_head_groups(const void* src, void* dst, int64_t tokens, int64_t groups, int64_t group_bytes,
+                               int to_groups, int sms, cudaStream_t st) {
+  const int64_t hg_vec = group_bytes / 16, total = tokens * groups * hg_vec;
+  if (total <= 0) return cudaSuccess;
+  const unsigned g = layout_grid(total, sms);
+  head_groups_kernel<<<g, 256, 0, st>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst), tokens, groups,
+                                        hg_vec, to_groups, total);
+  return cudaGetLastError();
+}
+
+}  // namespace we

@@ -86,6 +86,8 @@ cudaError_t launch_patchify(const void* latent, int ldt, int64_t C, int64_t H, i
                             int sms, cudaStream_t st);
 cudaError_t launch_unpatchify(const void* tokens, int tdt, int64_t C, int64_t H, int64_t W, void* latent, int ldt,
                               int sms, cudaStream_t st);
+cudaError_t launch_head_groups(const void* src, void* dst, int64_t tokens, int64_t groups, int64_t group_bytes,
+                               int to_groups, int sms, cudaStream_t st);
 
 // attention(q [T, H, D], k, v [T, Hkv, D]) -> out [T, H, D]
 struct AttnArgs {

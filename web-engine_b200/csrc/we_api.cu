@@ -750,6 +750,20 @@ int we_unpatchify(we_ctx* ctx, const void* tokens, int32_t tokens_dtype, int64_t
   return WE_OK;
 }
 
+int we_head_groups(we_ctx* ctx, const void* rows, void* groups, int64_t tokens, int64_t n_groups, int64_t group_bytes,
+                   int32_t to_groups) {
+  if (!ctx) return WE_EINVAL;
+  if (!rows || !groups) return fail(ctx, WE_EINVAL, "head groups: missing buffer");
+  if (group_bytes <= 0 || group_bytes % 16 || ((uintptr_t)rows | (uintptr_t)groups) % 16)
+    return fail(ctx, WE_EINVAL, "head groups need 16-byte groups and 16-byte aligned buffers");
+  if (tokens < 0 || n_groups <= 0) return fail(ctx, WE_EINVAL, "head groups: bad sizes");
+  // to_groups reads rows and writes groups; the reverse reads groups and writes rows
+  LK(we::launch_head_groups(to_groups ? rows : groups, to_groups ? groups : const_cast<void*>(rows), tokens, n_groups,
+                            group_bytes, to_groups ? 1 : 0, ctx->sms, ctx->stream),
+     "head groups");
+  return WE_OK;
+}
+
 // ---------------- attention ----------------
 int we_attention(we_ctx* ctx, const void* q, const void* k, const void* v, int32_t dtype, int64_t tokens, int64_t heads,
                  int64_t kv_heads, int64_t dim, int32_t causal, void* out, int32_t out_dtype) {

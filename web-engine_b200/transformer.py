@@ -134,13 +134,17 @@ class StepInputs:
 
 
 def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype: str = "f32", velocity=None,
-                on_block=None) -> tuple:
+                on_block=None, sp=None) -> tuple:
     """One denoising step (transformer.ts:134-176) of one image (`inp` a StepInputs) or of a batch of images (a list
     of StepInputs with the same geometry and timestep). The batch runs as one token stream: every linear is one
     GEMM over all images' rows, attention runs per image.
 
     Returns the predicted velocity [C, H, W] f32 (a new buffer, or written into `velocity`) and the txt rows for
-    the next step's text_cache; for a batch, lists of both."""
+    the next step's text_cache; for a batch, lists of both.
+
+    sp: a sequence.SequenceParallel to split one image's rows over the ranks of its group (bf16 path): each rank
+    runs the blocks on T / world consecutive rows, attention exchanges heads by all-to-all, and every rank gets the
+    whole velocity."""
     batch = list(inp) if isinstance(inp, (list, tuple)) else [inp]
     b0 = batch[0]
     if any((b.height, b.width, b.text_tokens, b.timestep) != (b0.height, b0.width, b0.text_tokens, b0.timestep)
@@ -153,6 +157,9 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     T = Lt + image
     R = B * T
     cos, sin, pairs = _tables(Lt, rows, cols, tuple(cfg.axes), float(cfg.theta))
+    if sp is not None and (B != 1 or dtype != "bf16"):
+        raise ValueError("sequence parallelism runs one image on the bf16 path")
+    r0, n = sp.shard(T) if sp is not None else (0, R)  # this rank's rows
     outs = velocity if isinstance(velocity, (list, tuple)) else [velocity] * B if velocity is not None else [None] * B
     mark = graph.mark()
     t, tvec = time(graph, w, b0.timestep, cfg.time_dim)
@@ -169,13 +176,27 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     img = ops.linear(graph, tok, w.first, B * image, x_dtype=dtype, y_dtype="f32")
     for i in range(B):
         graph.copy(img, i * image * hid * 4, x, (i * T + Lt) * hid * 4, image * hid * 4)
-    rope = ops.Rope(graph.buffer(np.tile(cos, B)), graph.buffer(np.tile(sin, B)), pairs, R)
+    if sp is not None:  # keep this rank's rows
+        xs = graph.buffer(n * hid * 4)
+        graph.copy(x, r0 * hid * 4, xs, 0, n * hid * 4)
+        graph.free(x)
+        x = xs
+        rope = ops.Rope(graph.buffer(cos[r0 * pairs:(r0 + n) * pairs]), graph.buffer(sin[r0 * pairs:(r0 + n) * pairs]),
+                        pairs, n)
+    else:
+        rope = ops.Rope(graph.buffer(np.tile(cos, B)), graph.buffer(np.tile(sin, B)), pairs, R)
+
+    def clip(lo, hi, wt):  # rows [lo, hi) of the stacked sequence, as local rows of this rank
+        a, b = max(lo, r0), min(hi, r0 + n)
+        return [Part(a - r0, b - a, wt)] if b > a else []
+
     # double blocks: each image's text rows and image rows; single blocks: all rows of the batch at once
-    layers = [[p for i in range(B) for p in (Part(i * T, Lt, tw), Part(i * T + Lt, image, iw))] for tw, iw in w.double]
-    layers += [[Part(0, R, bw)] for bw in w.single]
+    layers = [[p for i in range(B) for p in clip(i * T, i * T + Lt, tw) + clip(i * T + Lt, (i + 1) * T, iw)]
+              for tw, iw in w.double]
+    layers += [clip(0, R, bw) for bw in w.single]
     for i, parts in enumerate(layers):
         bm = graph.mark()
-        nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B)
+        nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp)
         graph.release(bm, [nxt])
         graph.free(x)
         x = nxt
@@ -184,11 +205,13 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     scale = ops.add(graph, t, w.last_scale, hid)
     shift = ops.add(graph, t, w.last_shift, hid)
     if dtype == "bf16":
-        split = (graph.buffer(R * hid), graph.buffer(R * hid), graph.buffer(R * 4))
-        K.norm_split(graph, x, w.last_norm, R, hid, *split, scale=scale, shift=shift, eps=bc.eps)
-        last = graph.buffer(R * 4 * ch * 4)
-        K.gemm_fp8(graph, *split, w.last_linear.buffer, last, R, w.last_linear.n, w.last_linear.k,
+        split = (graph.buffer(n * hid), graph.buffer(n * hid), graph.buffer(n * 4))
+        K.norm_split(graph, x, w.last_norm, n, hid, *split, scale=scale, shift=shift, eps=bc.eps)
+        last = graph.buffer(n * 4 * ch * 4)
+        K.gemm_fp8(graph, *split, w.last_linear.buffer, last, n, w.last_linear.n, w.last_linear.k,
                    w.last_linear.scale, chan_scale=w.last_linear.chan_scale, bias=w.last_linear.bias, y_dtype="f32")
+        if sp is not None:  # every rank's rows of the last linear, in order
+            last = sp.all_gather_rows(graph, last, n * 4 * ch * 4)
     else:
         h = ops.norm(graph, x, w.last_norm, R, hid, ops.Mod(scale, shift), bc.eps)
         last = ops.linear(graph, h, w.last_linear, R)
