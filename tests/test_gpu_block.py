@@ -56,7 +56,8 @@ def test_elementwise_ops_match_the_reference_formulas(we, graph):  # tests/gpu/e
     assert np.max(np.abs(ew(we, graph, "swiglu", x, y, dtype="bf16") - x * sigmoid(x) * y)) < 1e-4
 
 
-@pytest.mark.parametrize("rows,d,xdt", [(300, 3072, "bf16"), (64, 512, "f32"), (17, 136, "f32")])
+@pytest.mark.parametrize("rows,d,xdt", [(300, 3072, "bf16"), (300, 3072, "f32"), (64, 512, "f32"), (17, 136, "f32"),
+                                        (5, 8192, "f32")])
 def test_norm_split_equals_norm_then_split(we, graph, rows, d, xdt):
     x = randn(rows * d, 11, 2.0)
     if xdt == "bf16":
@@ -76,13 +77,13 @@ def test_norm_split_equals_norm_then_split(we, graph, rows, d, xdt):
     e4 = O.e4m3_table()
     recon = [(e4[hi] + e4[lo]).reshape(rows, d) * rs.view(np.float32)[:, None]
              for hi, lo, rs in (planes[:3], planes[3:])]
-    if xdt == "bf16":  # same row reduction as the bf16 RMSNorm kernel: identical bits
-        for u, v in zip(planes[:3], planes[3:]):
-            assert np.array_equal(u, v)
-    else:  # f32 rows: the two kernels sum the squares in different orders; a rare 1-ulp bf16 difference
-        diff = np.abs(recon[0] - recon[1])
-        assert np.all(diff <= np.abs(recon[0]) * 2.0 ** -7 + 1e-30)
-        assert np.mean(diff == 0) > 0.999
+    # the two paths sum the row's squares in different orders: a rare 1-ulp bf16 difference, and when that moves
+    # the row maximum across a power of two the scale differs and the smallest values round in e4m3's subnormal
+    # range (absolute step 2^-9 of the scale, about 2^-17 of the row maximum)
+    diff = np.abs(recon[0] - recon[1])
+    rowmax = np.abs(recon[0]).max(axis=1, keepdims=True)
+    assert np.all(diff <= np.abs(recon[0]) * 2.0 ** -7 + rowmax * 2.0 ** -16)
+    assert np.mean(diff == 0) > 0.999
 
 
 @pytest.mark.parametrize("path", ["tc", "simt"])

@@ -149,10 +149,113 @@ __global__ void __launch_bounds__(128) norm_split_kernel(const void* __restrict_
   }
 }
 
+// The same, one 256-thread CTA per row for rows of 2048+ values: thread t keeps the row's 4-value chunks t,
+// t + 256, ... in registers (3 chunks at d = 3072: few registers, many rows in flight per SM, where the warp per
+// row form holds a whole row per warp and is latency-bound); the sum of squares and the maximum go through a
+// shared-memory reduction over the 8 warps in a fixed order.
+template <int DT>
+__device__ __forceinline__ void load4(const void* p, int64_t i, float v[4]) {
+  if constexpr (DT == WE_F32) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  } else {
+    const uint2 a = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
+    v[0] = __uint_as_float(a.x << 16); v[1] = __uint_as_float(a.x & 0xffff0000u);
+    v[2] = __uint_as_float(a.y << 16); v[3] = __uint_as_float(a.y & 0xffff0000u);
+  }
+}
+
+template <int DT, int TERMS, int CH>
+__global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                             const float* __restrict__ sc, const float* __restrict__ sh,
+                                                             int64_t rows, int64_t d, float eps, float offset,
+                                                             uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
+                                                             float* __restrict__ row_scale) {
+  __shared__ float red[2][8];
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[CH][4];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i < d) {
+        load4<DT>(x, row * d + i, v[c]);
+        ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
+        ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[0][wp] = ss;
+    __syncthreads();
+    const float tot = ((red[0][0] + red[0][1]) + (red[0][2] + red[0][3])) + ((red[0][4] + red[0][5]) + (red[0][6] + red[0][7]));
+    const float inv = rsqrtf(tot / (float)d + eps);
+    float amax = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i >= d) continue;
+      const float4 ww = *reinterpret_cast<const float4*>(w + i);
+      const float4 s4 = sc ? *reinterpret_cast<const float4*>(sc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 h4 = sh ? *reinterpret_cast<const float4*>(sh + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float wv[4] = {ww.x, ww.y, ww.z, ww.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float y = v[c][j] * inv * (offset + wv[j]) * (1.f + sv[j]) + hv[j];
+        v[c][j] = bf16_bits_to_f32(f32_to_bf16_bits(y));
+        amax = fmaxf(amax, fabsf(v[c][j]));
+      }
+    }
+    amax = warp_max(amax);
+    if (lane == 0) red[1][wp] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3])),
+                 fmaxf(fmaxf(red[1][4], red[1][5]), fmaxf(red[1][6], red[1][7])));
+    int e = 0;
+    if (amax > 0.f) {
+      int E;
+      const float f = frexpf(amax, &E);
+      e = (2.f * f <= 1.75f) ? E - 9 : E - 8;
+    }
+    if (tid == 0) row_scale[row] = ldexpf(1.0f, e);
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i >= d) continue;
+      float s[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) s[j] = ldexpf(v[c][j], -e);
+      const uint16_t h0 = f32x2_to_e4m3x2(s[0], s[1]), h1 = f32x2_to_e4m3x2(s[2], s[3]);
+      *reinterpret_cast<uint32_t*>(hi + row * d + i) = (uint32_t)h0 | ((uint32_t)h1 << 16);
+      if (TERMS > 1) {
+        const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+        const uint16_t l0 = f32x2_to_e4m3x2(s[0] - d0.x, s[1] - d0.y), l1 = f32x2_to_e4m3x2(s[2] - d1.x, s[3] - d1.y);
+        *reinterpret_cast<uint32_t*>(lo + row * d + i) = (uint32_t)l0 | ((uint32_t)l1 << 16);
+      }
+    }
+    // red[0] was read before the second barrier and red[1] is next written after the next row's first one
+  }
+}
+
+template <int DT, int TERMS>
+static bool norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
+                           float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs, int sms, cudaStream_t st) {
+  const unsigned g = (unsigned)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
+  const int64_t ch = (d / 4 + 255) / 256;
+  if (ch <= 2) norm_split_row_kernel<DT, TERMS, 2><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (ch <= 3) norm_split_row_kernel<DT, TERMS, 3><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (ch <= 4) norm_split_row_kernel<DT, TERMS, 4><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (ch <= 6) norm_split_row_kernel<DT, TERMS, 6><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else if (ch <= 8) norm_split_row_kernel<DT, TERMS, 8><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+  else return false;
+  return true;
+}
+
 template <int DT, int TERMS>
 static bool norm_split_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
                                 int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs, int sms,
                                 cudaStream_t st) {
+  if (d >= 2048 && norm_split_row<DT, TERMS>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st)) return true;
   int64_t g = (rows + 3) / 4;
   if (g > (int64_t)sms * 16) g = (int64_t)sms * 16;
   if (d <= 256 * 4) norm_split_kernel<DT, TERMS, 4><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);

@@ -316,6 +316,82 @@ __global__ void __launch_bounds__(128, 6) quant_act_warp_kernel(const uint16_t* 
   }
 }
 
+// CTA-per-row split for long bf16 rows (k % 8 == 0, k <= 2048 CH, 16-byte aligned rows): 256 threads, thread t
+// keeps the row's 16-byte chunks t, t + 256, ... in registers (few registers: many rows in flight per SM); the
+// row max is a warp shuffle then a shared-memory reduction over the 8 warps.
+template <int TERMS, int CH>
+__global__ void __launch_bounds__(256) quant_act_row_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
+                                                            int64_t stride, uint8_t* __restrict__ hi,
+                                                            uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
+  __shared__ float red[8];
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
+    const uint16_t* xr = x + row * stride;
+    uint4 v[CH];
+    uint32_t mx = 0;
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t t = (int64_t)(c * 256 + tid) * 8;
+      if (t < k) {
+        v[c] = *reinterpret_cast<const uint4*>(xr + t);
+        // |bf16| max on the bit patterns: clear the sign bits, compare as integers
+        mx = __vmaxu2(mx, __vmaxu2(__vmaxu2(v[c].x & 0x7fff7fffu, v[c].y & 0x7fff7fffu),
+                                   __vmaxu2(v[c].z & 0x7fff7fffu, v[c].w & 0x7fff7fffu)));
+      }
+    }
+    float amax = warp_max(fmaxf(__uint_as_float(mx << 16), __uint_as_float(mx & 0xffff0000u)));
+    if (lane == 0) red[wp] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])), fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+    __syncthreads();  // red is rewritten by the next row
+    const int e = act_exponent(amax);
+    if (tid == 0) row_scale[row] = ldexpf(1.0f, e);
+    const float mul = pow2_neg(e);  // exact: scaling by a power of two
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t t = (int64_t)(c * 256 + tid) * 8;
+      if (t >= k) continue;
+      const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+      float s[8];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+        s[2 * j] = mul != 0.f ? a * mul : ldexpf(a, -e);
+        s[2 * j + 1] = mul != 0.f ? b * mul : ldexpf(b, -e);
+      }
+      uint32_t h[2], l[2];
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const uint16_t h0 = f32x2_to_e4m3x2(s[4 * j], s[4 * j + 1]);
+        const uint16_t h1 = f32x2_to_e4m3x2(s[4 * j + 2], s[4 * j + 3]);
+        h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        if (TERMS > 1) {
+          const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+          const uint16_t l0 = f32x2_to_e4m3x2(s[4 * j] - d0.x, s[4 * j + 1] - d0.y);
+          const uint16_t l1 = f32x2_to_e4m3x2(s[4 * j + 2] - d1.x, s[4 * j + 3] - d1.y);
+          l[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        }
+      }
+      *reinterpret_cast<uint2*>(hi + row * k + t) = make_uint2(h[0], h[1]);
+      if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * k + t) = make_uint2(l[0], l[1]);
+    }
+  }
+}
+
+template <int TERMS>
+static bool quant_act_row(const uint16_t* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo, float* rs,
+                          int sms, cudaStream_t st) {
+  const int g = (int)std::min<int64_t>(m, (int64_t)sms * 8);
+  const int64_t ch = (k / 8 + 255) / 256;
+  if (ch <= 2) quant_act_row_kernel<TERMS, 2><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (ch <= 3) quant_act_row_kernel<TERMS, 3><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (ch <= 4) quant_act_row_kernel<TERMS, 4><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (ch <= 6) quant_act_row_kernel<TERMS, 6><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else if (ch <= 8) quant_act_row_kernel<TERMS, 8><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  else return false;
+  return true;
+}
+
 template <int TERMS>
 static bool quant_act_warp(const uint16_t* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo, float* rs,
                            int sms, cudaStream_t st) {
@@ -409,6 +485,10 @@ cudaError_t launch_quant_act(const void* x, int dt, int64_t m, int64_t k, int64_
   if (vec_ok && (uintptr_t)x % 16 == 0 && (stride * esz) % 16 == 0) {
     if (dt == WE_BF16) {
       const uint16_t* xb = static_cast<const uint16_t*>(x);
+      // rows of 2048+ values: a CTA per row; shorter rows: a warp per row
+      if (k >= 2048 && (terms > 1 ? quant_act_row<2>(xb, m, k, stride, hi, lo, row_scale, sms, st)
+                                  : quant_act_row<1>(xb, m, k, stride, hi, lo, row_scale, sms, st)))
+        return cudaGetLastError();
       if (terms > 1 ? quant_act_warp<2>(xb, m, k, stride, hi, lo, row_scale, sms, st)
                     : quant_act_warp<1>(xb, m, k, stride, hi, lo, row_scale, sms, st))
         return cudaGetLastError();

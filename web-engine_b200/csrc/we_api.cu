@@ -715,7 +715,7 @@ int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weig
   cudaError_t e = we::launch_norm_split(x, x_dtype, weight, scale, shift, rows, d, eps, offset, terms, hi, lo,
                                         row_scale, ctx->sms, ctx->stream);
   if (e == cudaErrorNotSupported)
-    return fail(ctx, WE_EINVAL, "norm + split needs d % 8 == 0, d <= 6144 and 16-byte aligned rows");
+    return fail(ctx, WE_EINVAL, "norm + split needs d % 8 == 0, d <= 8192 and 16-byte aligned rows");
   CK(e, "norm + split");
   ctx->stats.launches++;
   return WE_OK;
