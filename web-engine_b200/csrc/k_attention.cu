@@ -6,13 +6,14 @@
 //  * attention_simt_kernel: CUDA cores, fp32, one warp per (query, head) with an online softmax over
 //    the keys. The exact path for the reference's f32 buffers (its tests hold 1e-5) and for head
 //    sizes / masks the tensor-core kernel does not take.
-//  * flash_attn_kernel: tcgen05 flash attention for bf16 q/k/v with 128-wide heads, no mask (the DiT
-//    blocks). One CTA = one head x 128 queries. Warp 0 TMA-loads Q once and K / V^T key tiles of 128
-//    into a 2-stage ring; warp 1 issues S = Q K^T into one of two TMEM score buffers and O += P V^T into
-//    a TMEM accumulator; warps 2-5 (one thread per query row) run the online softmax on the scores
-//    (tcgen05.ld), write P as bf16 into shared memory in the UMMA 128-byte-swizzled layout, and rescale
-//    O in TMEM only when a row's running maximum grows by more than 2^8 (the probabilities stay <= 256
-//    in between, which fp32 accumulation and bf16 P hold without loss of relative precision).
+//  * flash_attn2_kernel: tcgen05 flash attention for bf16 q/k/v with 128-wide heads, no mask (the DiT
+//    blocks). One CTA = one head x 256 queries (two 128-row tiles). Warp 0 TMA-loads both Q tiles once
+//    and K / V^T key tiles of 128 into separate 2-stage rings (K runs two tiles ahead); warp 1 issues
+//    S_i = Q_i K^T into TMEM and O_i += P_i V^T with P read from TMEM, interleaving the two tiles; warps
+//    2-9 (two groups of four, thread = query row) run the online softmax (tcgen05.ld, packed f32x2 math,
+//    ex2.approx), write P as bf16 over the first half of S_i (tcgen05.st), and rescale O_i in TMEM only
+//    when a row's running maximum grows by more than 2^8 (the probabilities stay <= 256 in between,
+//    which fp32 accumulation and bf16 P hold without loss of relative precision).
 //    V is transposed once per call into [kv_heads, dim, tokens] so both MMAs take K-major operands.
 #include <cudaTypedefs.h>
 
@@ -118,29 +119,6 @@ __device__ __forceinline__ float exp2_approx(float x) {
 }
 
 namespace fa {
-constexpr int BQ = 128, BK = 128, D = 128;
-constexpr int ATOM = 128 * 128;          // one 128-row x 128-byte swizzle-128B atom (64 bf16 per row)
-constexpr int Q_BYTES = 2 * ATOM;        // 128 queries x 128 dims
-constexpr int K_BYTES = 2 * ATOM;        // 128 keys x 128 dims
-constexpr int V_BYTES = 2 * ATOM;        // 128 dims x 128 keys (V^T)
-constexpr int P_BYTES = 2 * ATOM;        // 128 queries x 128 keys
-constexpr int STAGES = 2;
-constexpr int Q_OFF = 0;
-constexpr int K_OFF = Q_OFF + Q_BYTES;          // K stages: released as soon as S_j = Q K_j^T completes
-constexpr int V_OFF = K_OFF + STAGES * K_BYTES;  // V^T stages: released when PV_j completes
-constexpr int P_OFF = V_OFF + STAGES * V_BYTES;
-constexpr int BAR_OFF = P_OFF + 2 * P_BYTES;
-// barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain
-constexpr int NUM_BARS = 1 + 2 * 8 + 1;
-constexpr int TOTAL = BAR_OFF + NUM_BARS * 8 + 16;
-constexpr int ALLOC = TOTAL + 1024;
-constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128), S1 [128,256), O [256,384)
-constexpr uint32_t O_COL = 256;
-// kind::f16, bf16 x bf16 -> f32, K-major A and B, N = 128, M = 128
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-constexpr float RESCALE_LOG2 = 8.f;  // rescale O only when a row maximum grows by more than 2^8
-
 struct Params {
   int64_t tokens, heads, kv_heads;
   float scale_log2;  // log2(e) / sqrt(dim)
@@ -150,11 +128,39 @@ struct Params {
 };
 }  // namespace fa
 
-__global__ void __launch_bounds__(fa::THREADS, 1)
-    flash_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_vt, const fa::Params p) {
+// ---------------- two query tiles per CTA, P in TMEM ----------------
+// One CTA = 256 queries (two 128-row tiles) of one head; K and V tiles of 128 keys are loaded once for both.
+// TMEM (512 columns): S_i at 128 i, O_i at 256 + 128 i. Each softmax group (4 warps, thread = query row) turns
+// S_i into bf16 P written back over the first 64 columns of S_i, and O_i += P_i V_j reads P straight from TMEM
+// (no shared-memory round trip for P). The MMA warp interleaves the two tiles:
+//     S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) PV1(1) S1(2) | ...
+// so each softmax group works while the tensor core runs the other group's PV and S. The commit that signals
+// S_i(j) also covers PV_i(j - 1) (issued before it), so the softmax may overwrite P_i and rescale O_i then.
+namespace fa2 {
+constexpr int BQ = 128, BK = 128, D = 128, QT = 2;
+constexpr int ATOM = 128 * 128;  // one 128-row x 128-byte swizzle-128B box (64 bf16 per row)
+constexpr int TILE = 2 * ATOM;   // 128 rows x 128 dims (or dims x keys for V^T)
+constexpr int STAGES = 2;
+constexpr int Q_OFF = 0;
+constexpr int K_OFF = Q_OFF + QT * TILE;
+constexpr int V_OFF = K_OFF + STAGES * TILE;
+constexpr int BAR_OFF = V_OFF + STAGES * TILE;
+// barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[QT], p_full[QT], pv_done[QT], drain
+constexpr int NUM_BARS = 1 + 8 + 3 * QT + 1;
+constexpr int TOTAL = BAR_OFF + NUM_BARS * 8 + 16;
+constexpr int ALLOC = TOTAL + 1024;
+constexpr int THREADS = 64 + QT * 128;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t O_COL = 256;
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr float RESCALE_LOG2 = 8.f;
+}  // namespace fa2
+
+__global__ void __launch_bounds__(fa2::THREADS, 1)
+    flash_attn2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_vt, const fa::Params p) {
   using namespace tc;
-  using namespace fa;
+  using namespace fa2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -166,14 +172,13 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
 #define K_EMPTY(s) (bars + 8u * (3 + (s)))
 #define V_FULL(s) (bars + 8u * (5 + (s)))
 #define V_EMPTY(s) (bars + 8u * (7 + (s)))
-#define S_FULL(b) (bars + 8u * (9 + (b)))
-#define S_FREE(b) (bars + 8u * (11 + (b)))
-#define P_FULL(b) (bars + 8u * (13 + (b)))
-#define PV_DONE(b) (bars + 8u * (15 + (b)))
-#define DRAIN (bars + 8u * 17)
+#define S_FULL(i) (bars + 8u * (9 + (i)))
+#define P_FULL(i) (bars + 8u * (9 + QT + (i)))
+#define PV_DONE(i) (bars + 8u * (9 + 2 * QT + (i)))
+#define DRAIN (bars + 8u * (9 + 3 * QT))
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t q0 = (int64_t)blockIdx.x * BQ;
+  const int64_t q0 = (int64_t)blockIdx.x * (QT * BQ);
   const int64_t h = blockIdx.y;
   const int64_t g = h / (p.heads / p.kv_heads);
   const int nt = (int)((p.tokens + BK - 1) / BK);
@@ -185,8 +190,9 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
       mbar_init(K_EMPTY(i), 1);
       mbar_init(V_FULL(i), 1);
       mbar_init(V_EMPTY(i), 1);
+    }
+    for (int i = 0; i < QT; i++) {
       mbar_init(S_FULL(i), 1);
-      mbar_init(S_FREE(i), 4);
       mbar_init(P_FULL(i), 4);
       mbar_init(PV_DONE(i), 1);
     }
@@ -204,17 +210,19 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      mbar_expect_tx(Q_FULL, Q_BYTES);
-      tma_load_2d(sbase + Q_OFF, &tm_q, Q_FULL, (int32_t)(h * D), (int32_t)q0);
-      tma_load_2d(sbase + Q_OFF + ATOM, &tm_q, Q_FULL, (int32_t)(h * D + 64), (int32_t)q0);
-      // K runs two tiles ahead of V: V_j, then K_{j+2} (its stage was freed by S_j, long before S_{j+2})
+      mbar_expect_tx(Q_FULL, QT * TILE);
+      for (int i = 0; i < QT; i++) {
+        tma_load_2d(sbase + Q_OFF + i * TILE, &tm_q, Q_FULL, (int32_t)(h * D), (int32_t)(q0 + i * BQ));
+        tma_load_2d(sbase + Q_OFF + i * TILE + ATOM, &tm_q, Q_FULL, (int32_t)(h * D + 64), (int32_t)(q0 + i * BQ));
+      }
+      // K runs two tiles ahead of V: V_j, then K_{j+2} (its stage is freed once S0(j) and S1(j) are done)
       auto load_k = [&](int t) -> bool {
         const int st = t & 1;
         if (!wait_bounded(K_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
                           WAIT_LIMIT_NS, true))
           return false;
-        const uint32_t dst = sbase + K_OFF + st * K_BYTES;
-        mbar_expect_tx(K_FULL(st), K_BYTES);
+        const uint32_t dst = sbase + K_OFF + st * TILE;
+        mbar_expect_tx(K_FULL(st), TILE);
         tma_load_2d(dst, &tm_k, K_FULL(st), (int32_t)(g * D), t * BK);
         tma_load_2d(dst + ATOM, &tm_k, K_FULL(st), (int32_t)(g * D + 64), t * BK);
         return true;
@@ -224,8 +232,8 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         if (!wait_bounded(V_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
                           WAIT_LIMIT_NS, true))
           return false;
-        const uint32_t dst = sbase + V_OFF + st * V_BYTES;
-        mbar_expect_tx(V_FULL(st), V_BYTES);
+        const uint32_t dst = sbase + V_OFF + st * TILE;
+        mbar_expect_tx(V_FULL(st), TILE);
         tma_load_2d(dst, &tm_vt, V_FULL(st), t * BK, (int32_t)(g * D));
         tma_load_2d(dst + ATOM, &tm_vt, V_FULL(st), t * BK + 64, (int32_t)(g * D));
         return true;
@@ -257,66 +265,67 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
     if (lane == 0) {
       bool ok = wait_bounded(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true);
       tc_fence_after();
-      const uint64_t qdesc = sw128_desc(sbase + Q_OFF);
-      // O += P_j V_j^T for tile j (P in buffer j & 1, V^T in KV stage j & 1)
-      auto pv = [&](int j) -> bool {
-        const int b = j & 1;
-        if (!wait_bounded(P_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
-            !wait_bounded(V_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
+      // S_i(j) = Q_i K_j^T into TMEM columns [128 i, 128 i + 128)
+      auto s_mma = [&](int i, int j) -> bool {
+        if (!wait_bounded(K_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
           return false;
         tc_fence_after();
-        const uint64_t pdesc = sw128_desc(sbase + P_OFF + b * P_BYTES);
-        const uint64_t vdesc = sw128_desc(sbase + V_OFF + b * V_BYTES);
+        const uint64_t qdesc = sw128_desc(sbase + Q_OFF + i * TILE);
+        const uint64_t kdesc = sw128_desc(sbase + K_OFF + (j & 1) * TILE);
 #pragma unroll
-        for (int kk = 0; kk < 8; kk++) {  // K = 128 keys: two 64-key atoms, 4 MMAs of 16 each
+        for (int kk = 0; kk < 8; kk++) {  // K = 128 dims: two 64-dim boxes, 4 MMAs of 16 each
           const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
-          umma<true>(tmem + O_COL, pdesc + off, vdesc + off, IDESC, (j | kk) != 0);
+          umma<true>(tmem + (uint32_t)(i * 128), qdesc + off, kdesc + off, IDESC, kk != 0);
         }
-        umma_commit(V_EMPTY(b));
-        umma_commit(PV_DONE(b));
+        umma_commit(S_FULL(i));
         return true;
       };
-      for (int j = 0; j < nt && ok; j++) {
-        const int s = j & 1, b = j & 1;
-        if (!wait_bounded(K_FULL(s), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
-            !wait_bounded(S_FREE(b), ((j >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
-          ok = false;
-          break;
-        }
+      // O_i += P_i(j) V_j: A = P_i from TMEM columns [128 i, 128 i + 64), B = V_j^T from shared memory
+      auto pv_mma = [&](int i, int j) -> bool {
+        if (!wait_bounded(P_FULL(i), j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
+            !wait_bounded(V_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
+          return false;
         tc_fence_after();
-        const uint64_t kdesc = sw128_desc(sbase + K_OFF + s * K_BYTES);
+        const uint64_t vdesc = sw128_desc(sbase + V_OFF + (j & 1) * TILE);
 #pragma unroll
-        for (int kk = 0; kk < 8; kk++) {  // K = 128 dims
+        for (int kk = 0; kk < 8; kk++) {  // K = 128 keys: 8 MMAs of 16 keys = 8 TMEM columns of packed P each
           const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
-          umma<true>(tmem + (uint32_t)(b * 128), qdesc + off, kdesc + off, IDESC, kk != 0);
+          umma_tmem_a(tmem + O_COL + (uint32_t)(i * 128), tmem + (uint32_t)(i * 128 + kk * 8), vdesc + off, IDESC,
+                      (j | kk) != 0);
         }
-        umma_commit(K_EMPTY(s));
-        umma_commit(S_FULL(b));
-        if (j > 0 && !pv(j - 1)) {
-          ok = false;
-          break;
+        umma_commit(PV_DONE(i));
+        return true;
+      };
+      if (ok && nt > 0) {
+        ok = s_mma(0, 0) && s_mma(1, 0);
+        if (ok) umma_commit(K_EMPTY(0));
+      }
+      for (int j = 0; j < nt && ok; j++) {
+        const bool more = j + 1 < nt;
+        ok = pv_mma(0, j) && (!more || s_mma(0, j + 1)) && pv_mma(1, j);
+        if (!ok) break;
+        umma_commit(V_EMPTY(j & 1));
+        if (more) {
+          ok = s_mma(1, j + 1);
+          if (ok) umma_commit(K_EMPTY((j + 1) & 1));
         }
       }
-      if (ok && nt > 0) pv(nt - 1);
       // every MMA this thread issued completes before TMEM is freed
       umma_commit(DRAIN);
       wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
     }
     __syncwarp();
   } else {
-    // softmax: thread = query row r of this CTA, TMEM lane r. Per key tile: the raw scores (one TMEM read of
-    // 128 columns), the row maximum (3-input max), then p = 2^(s * scale_log2 - m) with the scale folded into
-    // one packed f32x2 FMA per pair, the hardware exp2, packed f32x2 sums, and bf16 pairs stored into the
-    // swizzled P tile.
+    // softmax group grp (query tile), thread = query row r, TMEM lane r
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const int rx = r & 7;
-    float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and denominator
+    const uint32_t s_col = (uint32_t)(grp * 128), o_col = O_COL + (uint32_t)(grp * 128);
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; j++) {
-      const int b = j & 1;
-      ok = wait_bounded(S_FULL(b), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      ok = wait_bounded(S_FULL(grp), j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
@@ -324,11 +333,11 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
       tc_fence_after();
       uint32_t sc[BK];
 #pragma unroll
-      for (int c = 0; c < BK / 32; c++)
-        tmem_ld32(tmem + lane_addr + (uint32_t)(b * 128 + c * 32), *reinterpret_cast<uint32_t(*)[32]>(sc + c * 32));
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(S_FREE(b));
+      for (int c = 0; c < BK / 32; c++)  // four loads in flight, one wait
+        tmem_ld32_async(tmem + lane_addr + s_col + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(sc + c * 32));
+      tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(sc));
+#pragma unroll
+      for (int c = 1; c < BK / 32; c++) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(sc + c * 32));
       const int64_t valid = p.tokens - (int64_t)j * BK;  // keys of this tile that exist (warp-uniform)
       if (valid < BK) {
 #pragma unroll
@@ -350,69 +359,50 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
         l *= corr;
         m_used = mt;
       }
-      // P buffer b was last read by PV_{j-2}
-      if (j >= 2) {
-        ok = wait_bounded(PV_DONE(b), ((j - 2) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS,
-                          true);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-      }
-      uint8_t* prow = smem + P_OFF + b * P_BYTES + r * 128;
       const float nm = -m_used;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 4 packed pairs of running sums
 #pragma unroll
-      for (int ch = 0; ch < 16; ch++) {  // 16 chunks of 8 keys; chunk ch lives in atom ch / 8
-        uint32_t pk[4];
+      for (int half = 0; half < 2; half++) {  // P as 64 packed bf16 pairs over S's first 64 columns, 32 at a time
+        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
+        for (int e = 0; e < 32; e++) {
+          const int c = half * 64 + 2 * e;
           float x0, x1;
-          ffma2(x0, x1, __uint_as_float(sc[ch * 8 + 2 * e]), __uint_as_float(sc[ch * 8 + 2 * e + 1]), p.scale_log2,
-                p.scale_log2, nm, nm);
+          ffma2(x0, x1, __uint_as_float(sc[c]), __uint_as_float(sc[c + 1]), p.scale_log2, p.scale_log2, nm, nm);
           const float e0 = exp2_approx(x0), e1 = exp2_approx(x1);
-          fadd2(acc[2 * e], acc[2 * e + 1], acc[2 * e], acc[2 * e + 1], e0, e1);
+          fadd2(acc[2 * (e & 3)], acc[2 * (e & 3) + 1], acc[2 * (e & 3)], acc[2 * (e & 3) + 1], e0, e1);
           pk[e] = pack_bf16x2(e0, e1);
         }
-        *reinterpret_cast<uint4*>(prow + (ch >> 3) * ATOM + (((ch & 7) ^ rx) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        tmem_st32(tmem + lane_addr + s_col + (uint32_t)(half * 32), pk);
       }
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-      // O was scaled for the old maximum: bring it to the new one before PV_j adds to it
+      // O_i was scaled for the old maximum: bring it to the new one before PV_i(j) adds to it (PV_i(j-1) is done)
       if (__any_sync(0xffffffffu, grow && j > 0)) {
-        ok = wait_bounded(PV_DONE((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE,
-                          WAIT_LIMIT_NS, true);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const float f = (grow && j > 0) ? corr : 1.f;
 #pragma unroll
         for (int c = 0; c < D / 32; c++) {
           uint32_t u[32];
-          tmem_ld32(tmem + lane_addr + O_COL + (uint32_t)(c * 32), u);
+          tmem_ld32(tmem + lane_addr + o_col + (uint32_t)(c * 32), u);
 #pragma unroll
           for (int e = 0; e < 32; e++) u[e] = __float_as_uint(__uint_as_float(u[e]) * f);
-          tmem_st32(tmem + lane_addr + O_COL + (uint32_t)(c * 32), u);
+          tmem_st32(tmem + lane_addr + o_col + (uint32_t)(c * 32), u);
         }
-        tmem_st_wait();
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P stores -> visible to the tensor core
+      tmem_st_wait();  // P (and O) stores land before the MMA reads them
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(P_FULL(b));
+      if (lane == 0) mbar_arrive(P_FULL(grp));
     }
     if (ok && nt > 0) {
-      ok = wait_bounded(PV_DONE((nt - 1) & 1), ((nt - 1) >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE,
-                        WAIT_LIMIT_NS, true);
+      ok = wait_bounded(PV_DONE(grp), (nt - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (__all_sync(0xffffffffu, ok)) {
         tc_fence_after();
-        const int64_t qi = q0 + r;
+        const int64_t qi = q0 + grp * BQ + r;
         const float inv = 1.f / l;
 #pragma unroll
         for (int c = 0; c < D / 32; c++) {
           uint32_t u[32];
-          tmem_ld32(tmem + lane_addr + O_COL + (uint32_t)(c * 32), u);
+          tmem_ld32(tmem + lane_addr + o_col + (uint32_t)(c * 32), u);
           if (qi < p.tokens) {
             const int64_t o = (qi * p.heads + h) * D + c * 32;
             if (p.out_dtype == WE_BF16) {
@@ -446,7 +436,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1)
 #undef V_FULL
 #undef V_EMPTY
 #undef S_FULL
-#undef S_FREE
 #undef P_FULL
 #undef PV_DONE
 #undef DRAIN
@@ -509,10 +498,10 @@ cudaError_t launch_flash_attention(const AttnArgs& a, void* vt_scratch, uint32_t
   p.out = a.out;
   p.out_dtype = a.out_dtype;
   p.err = err;
-  cudaError_t e = cudaFuncSetAttribute(flash_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::ALLOC);
+  cudaError_t e = cudaFuncSetAttribute(flash_attn2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa2::ALLOC);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((a.tokens + fa::BQ - 1) / fa::BQ), (unsigned)a.heads);
-  flash_attn_kernel<<<grid, fa::THREADS, fa::ALLOC, st>>>(mq, mk, mv, p);
+  dim3 grid((unsigned)((a.tokens + fa2::QT * fa2::BQ - 1) / (fa2::QT * fa2::BQ)), (unsigned)a.heads);
+  flash_attn2_kernel<<<grid, fa2::THREADS, fa2::ALLOC, st>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
