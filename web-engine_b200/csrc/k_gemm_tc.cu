@@ -434,10 +434,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 // epilogue drains its own 128-lane accumulator, releasing it on the leader's barrier (remote arrive).
 // Per SM this halves the token bytes per FLOP of the 1-SM kernel, so the same shared memory holds
 // twice the stages.
-template <int BT, int TERMS>
+// ATOMS: 128-byte K atoms per stage and operand. bf16 (kind::f16) takes 2, so a stage holds 8 MMAs like a
+// two-term e4m3 stage and the ring needs half the barrier round trips per FLOP.
+template <int BT, int TERMS, int ATOMS = 1>
 struct Layout2 {
-  static constexpr int W_BYTES = BM * KB_BYTES;
-  static constexpr int X_BYTES = (BT / 2) * KB_BYTES;
+  static constexpr int W_ATOM = BM * KB_BYTES;
+  static constexpr int X_ATOM = (BT / 2) * KB_BYTES;
+  static constexpr int W_BYTES = ATOMS * W_ATOM;
+  static constexpr int X_BYTES = ATOMS * X_ATOM;
   static constexpr int STAGE_BYTES = W_BYTES + TERMS * X_BYTES;
   static constexpr int STAGES = (SMEM_BUDGET / STAGE_BYTES) > 8 ? 8 : (SMEM_BUDGET / STAGE_BYTES);
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
@@ -524,12 +528,14 @@ template <int BT, int TERMS, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x0,
                     const __grid_constant__ CUtensorMap tm_x1, const Params p) {
-  using L = Layout2<BT, TERMS>;
+  constexpr int ATOMS = F16 ? 2 : 1;
+  using L = Layout2<BT, TERMS, ATOMS>;
   constexpr int STAGES = L::STAGES;
-  constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;
+  constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;  // K elements per atom
   constexpr uint32_t TMEM_COLS = 2 * BT;
   constexpr uint32_t IDESC = make_idesc_pair<BT, F16>();
   constexpr int MMAS_PER_KB = KB_BYTES / 32;
+  const int num_stages = (p.num_kb + ATOMS - 1) / ATOMS;  // a K atom past the end loads as zeros
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -584,7 +590,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int64_t t = cid; t < tiles && ok; t += ncl) {
         const int32_t row_w = (int32_t)((t % tiles_n) * 2 * BM + rank * BM);
         const int32_t row_x = (int32_t)((t / tiles_n) * BT + rank * (BT / 2));
-        for (int kb = 0; kb < p.num_kb; kb++) {
+        for (int kb = 0; kb < num_stages; kb++) {
           if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
             ok = false;
             break;
@@ -592,10 +598,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
           if (leader) mbar_expect_tx(FULL(s), 2 * L::STAGE_BYTES);
           const uint32_t bar = map_rank(FULL(s), 0);
-          const int32_t kc = kb * KB_ELEMS;
-          tma_load_2d_pair(st, &tm_w, bar, kc, row_w);
-          tma_load_2d_pair(st + L::W_BYTES, &tm_x0, bar, kc, row_x);
-          if (TERMS > 1) tma_load_2d_pair(st + L::W_BYTES + L::X_BYTES, &tm_x1, bar, kc, row_x);
+#pragma unroll
+          for (int a = 0; a < ATOMS; a++) {
+            const int32_t kc = (kb * ATOMS + a) * KB_ELEMS;
+            tma_load_2d_pair(st + a * L::W_ATOM, &tm_w, bar, kc, row_w);
+            tma_load_2d_pair(st + L::W_BYTES + a * L::X_ATOM, &tm_x0, bar, kc, row_x);
+            if (TERMS > 1) tma_load_2d_pair(st + L::W_BYTES + L::X_BYTES + a * L::X_ATOM, &tm_x1, bar, kc, row_x);
+          }
           issued_ph[s] = ph;
           issued++;
           if (++s == STAGES) {
@@ -620,20 +629,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!wait_bounded(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BT);
-        for (int kb = 0; kb < p.num_kb; kb++) {
+        for (int kb = 0; kb < num_stages; kb++) {
           if (!wait_bounded(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
-          const uint64_t adesc = sw128_desc(st);
 #pragma unroll
-          for (int term = 0; term < TERMS; term++) {
-            const uint64_t bdesc = sw128_desc(st + L::W_BYTES + term * L::X_BYTES);
+          for (int a = 0; a < ATOMS; a++) {
+            const uint64_t adesc = sw128_desc(st + a * L::W_ATOM);
 #pragma unroll
-            for (int kk = 0; kk < MMAS_PER_KB; kk++)
-              umma_pair<F16>(d, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | term | kk) != 0);
+            for (int term = 0; term < TERMS; term++) {
+              const uint64_t bdesc = sw128_desc(st + L::W_BYTES + term * L::X_BYTES + a * L::X_ATOM);
+#pragma unroll
+              for (int kk = 0; kk < MMAS_PER_KB; kk++)
+                umma_pair<F16>(d, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | a | term | kk) != 0);
+            }
           }
           umma_commit_pair_both(EMPTY(s));
           if (++s == STAGES) {
@@ -783,7 +795,7 @@ static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
 
 template <int BT, int TERMS, bool F16>
 static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
-  using L = Layout2<BT, TERMS>;
+  using L = Layout2<BT, TERMS, F16 ? 2 : 1>;  // as the kernel lays out its stages
   CUtensorMap mw, mx0, mx1;
   if (!make_map(&mw, a.w, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
   if (!make_map(&mx0, a.x[0], F16, a.k, a.m, a.x_stride_bytes, BT / 2)) return cudaErrorNotSupported;
