@@ -245,9 +245,32 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
 
     with ClockSampler(gpu) as e2e_clocks:
         e2e_ms = timed(step_e2e, ksteps, 1) / ksteps
+    # the same step with its 57 blocks replayed from a CUDA graph (one launch from the host instead of ~1000)
+    sgr = T.StepGraph(g, model, scfg, side, side, text_tokens, dtype="bf16")
+
+    def step_graph():
+        T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, captured=sgr)
+
+    def step_graph_e2e():
+        lat_d.copy_(lat_h, non_blocking=True)
+        ctx_d.copy_(ctx_h, non_blocking=True)
+        T.transformer(g, model, scfg, inp_e, dtype="bf16", velocity=vel, captured=sgr)
+        g.read_into(vel, vel_h.data_ptr(), vel.numel() * 4)
+
+    gr_ms = timed(step_graph, ksteps, 3) / ksteps
+    gr_e2e_ms = timed(step_graph_e2e, ksteps, 1) / ksteps
+    issue = {}
+    for name, fn in (("eager", step_model), ("graph", step_graph)):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fn()
+        issue[name] = (time.perf_counter() - t0) * 1e3
+        torch.cuda.synchronize()
+    sgr.destroy()
     out["step_config4"] = {"ms": st_ms, "tflops": sf["total"] / (st_ms * 1e-3) / 1e12,
                            "frac_bf16_peak": sf["total"] / (st_ms * 1e-3) / 1e12 / bf16_peak, "flop": sf["total"],
                            "launches_per_step": st_launches, "e2e_ms": e2e_ms, "clocks": st_clocks.summary(),
+                           "graph_ms": gr_ms, "graph_e2e_ms": gr_e2e_ms, "host_issue_ms": issue,
                            "e2e_clocks": e2e_clocks.summary(),
                            "e2e_h2d_bytes": lat.numel() * 2 + ctx.numel() * 2, "e2e_d2h_bytes": vel.numel() * 4,
                            "note": "19 double + 38 single blocks of config 3 shape, 512 text + 4096 image tokens "

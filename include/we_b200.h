@@ -262,6 +262,19 @@ int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weig
                   const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
                   uint8_t* lo, float* row_scale);
 
+/* ---------------- CUDA graphs (no reference counterpart: WebGPU records its command buffers each time) ----------------
+   we_capture_begin starts capturing the context's stream (a stream set with we_set_stream, not the legacy default
+   stream); every op of this library issued until we_capture_end is recorded, not run. Buffers the ops take while
+   capturing come from a pool of the capture's own and belong to the graph afterwards (a replay writes them; they
+   stay valid, with their addresses, until we_graph_destroy); host data uploaded while capturing is copied into
+   pinned memory the graph owns. Buffers made before the capture and used by it must outlive the graph.
+   we_read and we_sync refuse while capturing. we_graph_launch replays on the context's stream. */
+typedef struct we_graph we_graph;
+int we_capture_begin(we_ctx* ctx);
+int we_capture_end(we_ctx* ctx, we_graph** out);
+int we_graph_launch(we_ctx* ctx, we_graph* graph);
+int we_graph_destroy(we_ctx* ctx, we_graph* graph);
+
 /* ---------------- latent <-> tokens: patchify / unpatchify (src/model/transformer.ts:53-82) ----------------
    tokens [ceil(H/2) * ceil(W/2), 4 channels] <- latent [channels, H, W]: 2x2 patches, features in (channel, patch
    row, patch column) order; an odd H or W wraps to row / column 0 (patchify, transformer.ts:59-69). unpatchify is

@@ -37,6 +37,22 @@ struct we_ctx {
   size_t stage_head = 0;
   std::deque<Staged> staged;
   std::vector<cudaEvent_t> spare_events;
+  // Stream capture (we_capture_begin / we_capture_end). Buffers taken while capturing come from, and go back to,
+  // a pool of the capture's own and belong to the graph afterwards: a replay writes them, so nothing else may
+  // be handed them. Uploads made while capturing read from pinned copies the graph owns.
+  bool capturing = false;
+  std::unordered_map<size_t, std::vector<void*>> cap_pool;
+  std::vector<void*> cap_bufs;
+  std::vector<void*> cap_host;
+  uint64_t cap_launches0 = 0;
+  std::vector<we_graph*> graphs;  // live graphs, destroyed with the context
+};
+
+struct we_graph {
+  cudaGraphExec_t exec = nullptr;
+  std::vector<void*> bufs;  // device buffers the graph reads and writes
+  std::vector<void*> host;  // pinned sources of its uploads
+  uint64_t launches = 0;    // kernels of this library in one replay
 };
 
 namespace {
@@ -70,6 +86,14 @@ constexpr size_t kStageBytes = 16u << 20;  // uploads up to half of this go thro
 // be overwritten), large ones go straight from the caller's memory.
 int upload(we_ctx* ctx, void* dst, const void* host, size_t bytes, const char* what) {
   if (bytes == 0) return WE_OK;
+  if (ctx->capturing) {  // the graph replays the copy from a pinned copy of its own
+    void* pin = nullptr;
+    CK(cudaHostAlloc(&pin, bytes, cudaHostAllocDefault), "capture upload copy");
+    ctx->cap_host.push_back(pin);
+    std::memcpy(pin, host, bytes);
+    CK(cudaMemcpyAsync(dst, pin, bytes, cudaMemcpyHostToDevice, ctx->stream), what);
+    return WE_OK;
+  }
   if (bytes > kStageBytes / 2) {
     CK(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream), what);
     return WE_OK;
@@ -112,8 +136,9 @@ int upload(we_ctx* ctx, void* dst, const void* host, size_t bytes, const char* w
 
 // Takes a pooled buffer of exactly `size` bytes or allocates one (graph.ts:41-45).
 int pool_take(we_ctx* ctx, size_t size, void** out, bool* reused) {
-  auto it = ctx->pool.find(size);
-  if (it != ctx->pool.end() && !it->second.empty()) {
+  auto& pool = ctx->capturing ? ctx->cap_pool : ctx->pool;
+  auto it = pool.find(size);
+  if (it != pool.end() && !it->second.empty()) {
     *out = it->second.back();
     it->second.pop_back();
     *reused = true;
@@ -126,11 +151,22 @@ int pool_take(we_ctx* ctx, size_t size, void** out, bool* reused) {
     return fail(ctx, WE_ENOMEM, "cudaMalloc of " + std::to_string(size) + " bytes failed: " + cudaGetErrorString(e));
   }
   ctx->sizes[p] = size;
+  if (ctx->capturing) ctx->cap_bufs.push_back(p);
   *out = p;
   *reused = false;
   return WE_OK;
 }
-void pool_put(we_ctx* ctx, void* p) { ctx->pool[ctx->sizes[p]].push_back(p); }
+void pool_put(we_ctx* ctx, void* p) {
+  const bool mine = ctx->capturing && std::find(ctx->cap_bufs.begin(), ctx->cap_bufs.end(), p) != ctx->cap_bufs.end();
+  (mine ? ctx->cap_pool : ctx->pool)[ctx->sizes[p]].push_back(p);
+}
+
+void graph_free(we_graph* g) {
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  for (void* b : g->bufs) cudaFree(b);
+  for (void* h : g->host) cudaFreeHost(h);
+  delete g;
+}
 
 // A temporary of the library (activation split, decoded int4 weights): from the pool, not owned by
 // the caller, returned to the pool right after the work using it is queued (stream order keeps it safe).
@@ -212,6 +248,7 @@ int we_destroy(we_ctx* ctx) {
   if (!ctx) return WE_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  for (we_graph* g : ctx->graphs) graph_free(g);
   for (auto& st : ctx->staged) cudaEventDestroy(st.done);
   for (cudaEvent_t ev : ctx->spare_events) cudaEventDestroy(ev);
   if (ctx->stage) cudaFreeHost(ctx->stage);
@@ -234,6 +271,7 @@ void* we_get_stream(const we_ctx* ctx) { return ctx ? ctx->stream : nullptr; }
 
 int we_sync(we_ctx* ctx) {
   if (!ctx) return WE_EINVAL;
+  if (ctx->capturing) return fail(ctx, WE_EINVAL, "cannot synchronize while capturing a graph");
   CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
   return WE_OK;
 }
@@ -271,6 +309,7 @@ int we_write(we_ctx* ctx, void* dst, const void* host, size_t bytes) {
 
 int we_read(we_ctx* ctx, const void* src, void* host, size_t bytes) {
   if (!ctx) return WE_EINVAL;
+  if (ctx->capturing) return fail(ctx, WE_EINVAL, "cannot read back while capturing a graph");
   CK(cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "we_read");
   CK(cudaStreamSynchronize(ctx->stream), "we_read sync");
   return WE_OK;
@@ -718,6 +757,65 @@ int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weig
     return fail(ctx, WE_EINVAL, "norm + split needs d % 8 == 0, d <= 8192 and 16-byte aligned rows");
   CK(e, "norm + split");
   ctx->stats.launches++;
+  return WE_OK;
+}
+
+// ---------------- CUDA graphs: capture a sequence of this library's ops once, replay it ----------------
+int we_capture_begin(we_ctx* ctx) {
+  if (!ctx) return WE_EINVAL;
+  if (ctx->capturing) return fail(ctx, WE_EINVAL, "a capture is already open");
+  if (ctx->stream == nullptr) return fail(ctx, WE_EINVAL, "cannot capture the legacy default stream");
+  CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeRelaxed), "begin capture");
+  ctx->capturing = true;
+  ctx->cap_launches0 = ctx->stats.launches;
+  return WE_OK;
+}
+
+int we_capture_end(we_ctx* ctx, we_graph** out) {
+  if (!ctx || !out) return WE_EINVAL;
+  if (!ctx->capturing) return fail(ctx, WE_EINVAL, "no capture is open");
+  *out = nullptr;
+  ctx->capturing = false;
+  we_graph* g = new we_graph();
+  g->bufs.swap(ctx->cap_bufs);
+  g->host.swap(ctx->cap_host);
+  g->launches = ctx->stats.launches - ctx->cap_launches0;
+  ctx->cap_pool.clear();
+  // the graph's buffers leave the context: no release or free may hand them to anything else
+  for (void* b : g->bufs) {
+    ctx->sizes.erase(b);
+    auto it = std::find(ctx->owned.begin(), ctx->owned.end(), b);
+    if (it != ctx->owned.end()) ctx->owned.erase(it);
+  }
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&g->exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    graph_free(g);
+    return cuda_fail(ctx, e, "end capture");
+  }
+  ctx->graphs.push_back(g);
+  *out = g;
+  return WE_OK;
+}
+
+int we_graph_launch(we_ctx* ctx, we_graph* g) {
+  if (!ctx || !g) return WE_EINVAL;
+  if (ctx->capturing) return fail(ctx, WE_EINVAL, "cannot replay a graph while capturing");
+  CK(cudaGraphLaunch(g->exec, ctx->stream), "graph launch");
+  ctx->stats.launches += g->launches;
+  return WE_OK;
+}
+
+int we_graph_destroy(we_ctx* ctx, we_graph* g) {
+  if (!ctx || !g) return WE_EINVAL;
+  auto it = std::find(ctx->graphs.begin(), ctx->graphs.end(), g);
+  if (it == ctx->graphs.end()) return fail(ctx, WE_EINVAL, "graph is not owned by this context");
+  CK(cudaStreamSynchronize(ctx->stream), "graph destroy");  // no replay of it is still running
+  ctx->graphs.erase(it);
+  graph_free(g);
   return WE_OK;
 }
 

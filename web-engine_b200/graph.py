@@ -9,6 +9,7 @@ step's temporaries, ``free`` one buffer, ``destroy`` everything.
 from __future__ import annotations
 
 import ctypes as C
+from contextlib import contextmanager
 from dataclasses import dataclass
 
 import numpy as np
@@ -54,6 +55,23 @@ def addr(b) -> C.c_void_p:
     if hasattr(b, "data_ptr"):  # a torch tensor on the device
         return C.c_void_p(b.data_ptr())
     return b.c
+
+
+class Captured:
+    """A CUDA graph of a sequence of ops recorded by Graph.capture(): launch() replays it on the graph's stream.
+    The buffers the recorded ops created belong to it and keep their addresses until destroy()."""
+
+    def __init__(self, graph: "Graph"):
+        self.graph = graph
+        self.handle = None
+
+    def launch(self) -> None:
+        L.check(self.graph.ctx, L.lib().we_graph_launch(self.graph.ctx, self.handle))
+
+    def destroy(self) -> None:
+        if self.handle is not None and self.graph._live:
+            L.check(self.graph.ctx, L.lib().we_graph_destroy(self.graph.ctx, self.handle))
+        self.handle = None
 
 
 class Graph:
@@ -126,6 +144,22 @@ class Graph:
 
     def sync(self) -> None:
         L.check(self.ctx, L.lib().we_sync(self.ctx))
+
+    @contextmanager
+    def capture(self):
+        """Records the ops issued inside the block as a CUDA graph (we_capture_begin / we_capture_end) instead of
+        running them; yields the Captured, which is ready to launch() when the block exits."""
+        L.check(self.ctx, L.lib().we_capture_begin(self.ctx))
+        cap = Captured(self)
+        h = C.c_void_p()
+        try:
+            yield cap
+        except BaseException:
+            if L.lib().we_capture_end(self.ctx, C.byref(h)) == L.WE_OK and h.value:
+                L.lib().we_graph_destroy(self.ctx, h)
+            raise
+        L.check(self.ctx, L.lib().we_capture_end(self.ctx, C.byref(h)))
+        cap.handle = h
 
     def set_stream(self, stream: int | None) -> None:
         L.check(self.ctx, L.lib().we_set_stream(self.ctx, C.c_void_p(stream)))

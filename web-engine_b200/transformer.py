@@ -133,8 +133,63 @@ class StepInputs:
     latent_dtype: str | None = None  # the latent's element type when it differs from the step's (f32 sampler state)
 
 
+def _layers(w: TransformerWeights, images: int, T: int, Lt: int, image: int, r0: int, n: int) -> list:
+    """The parts of every block: double blocks split each image's text and image rows, single blocks take all rows;
+    clipped to this rank's rows [r0, r0 + n) of the stacked sequence."""
+    R = images * T
+
+    def clip(lo, hi, wt):
+        a, b = max(lo, r0), min(hi, r0 + n)
+        return [Part(a - r0, b - a, wt)] if b > a else []
+
+    layers = [[p for i in range(images) for p in clip(i * T, i * T + Lt, tw) + clip(i * T + Lt, (i + 1) * T, iw)]
+              for tw, iw in w.double]
+    return layers + [clip(0, R, bw) for bw in w.single]
+
+
+class StepGraph:
+    """The blocks of a step (all 57 for config 4), recorded once as a CUDA graph for one geometry and replayed
+    each step: the host issues one launch instead of about 1000, so a step no longer depends on how fast Python
+    issues its ops. It owns the blocks' input rows and timestep vector; a step copies its own into them."""
+
+    def __init__(self, graph: Graph, w: TransformerWeights, cfg: StepConfig, height: int, width: int,
+                 text_tokens: int, images: int = 1, dtype: str = "bf16"):
+        bc = cfg.block
+        rows, cols = patch_grid(height, width)
+        image = rows * cols
+        T = text_tokens + image
+        R = images * T
+        self.key = (height, width, text_tokens, images, dtype)
+        self.rows, self.hidden = R, bc.hidden
+        cos, sin, pairs = _tables(text_tokens, rows, cols, tuple(cfg.axes), float(cfg.theta))
+        self.x_in = graph.buffer(R * bc.hidden * 4)
+        self.tvec = graph.buffer(6 * bc.hidden * 4)
+        self.cos, self.sin = graph.buffer(np.tile(cos, images)), graph.buffer(np.tile(sin, images))
+        rope = ops.Rope(self.cos, self.sin, pairs, R)
+        with graph.capture() as cap:
+            x = self.x_in
+            for parts in _layers(w, images, T, text_tokens, image, 0, R):
+                bm = graph.mark()
+                nxt = joint_block(graph, parts, bc, x, self.tvec, rope, dtype, images=images)
+                graph.release(bm, [nxt])
+                if x is not self.x_in:
+                    graph.free(x)
+                x = nxt
+        self.captured, self.out = cap, x
+
+    def run(self, graph: Graph, x, tvec) -> Buffer:
+        """The blocks on x [rows, hidden] f32 with tvec [6 hidden]: a new result in self.out (graph-owned)."""
+        graph.copy(x, 0, self.x_in, 0, self.rows * self.hidden * 4)
+        graph.copy(tvec, 0, self.tvec, 0, 6 * self.hidden * 4)
+        self.captured.launch()
+        return self.out
+
+    def destroy(self) -> None:
+        self.captured.destroy()
+
+
 def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype: str = "f32", velocity=None,
-                on_block=None, sp=None) -> tuple:
+                on_block=None, sp=None, captured: StepGraph | None = None) -> tuple:
     """One denoising step (transformer.ts:134-176) of one image (`inp` a StepInputs) or of a batch of images (a list
     of StepInputs with the same geometry and timestep). The batch runs as one token stream: every linear is one
     GEMM over all images' rows, attention runs per image.
@@ -144,7 +199,9 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
 
     sp: a sequence.SequenceParallel to split one image's rows over the ranks of its group (bf16 path): each rank
     runs the blocks on T / world consecutive rows, attention exchanges heads by all-to-all, and every rank gets the
-    whole velocity."""
+    whole velocity.
+
+    captured: a StepGraph of this geometry; the blocks then run as its replay (on_block is not called)."""
     batch = list(inp) if isinstance(inp, (list, tuple)) else [inp]
     b0 = batch[0]
     if any((b.height, b.width, b.text_tokens, b.timestep) != (b0.height, b0.width, b0.text_tokens, b0.timestep)
@@ -183,25 +240,22 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
         x = xs
         rope = ops.Rope(graph.buffer(cos[r0 * pairs:(r0 + n) * pairs]), graph.buffer(sin[r0 * pairs:(r0 + n) * pairs]),
                         pairs, n)
-    else:
+    elif captured is None:  # (a captured step holds its own tables)
         rope = ops.Rope(graph.buffer(np.tile(cos, B)), graph.buffer(np.tile(sin, B)), pairs, R)
 
-    def clip(lo, hi, wt):  # rows [lo, hi) of the stacked sequence, as local rows of this rank
-        a, b = max(lo, r0), min(hi, r0 + n)
-        return [Part(a - r0, b - a, wt)] if b > a else []
-
-    # double blocks: each image's text rows and image rows; single blocks: all rows of the batch at once
-    layers = [[p for i in range(B) for p in clip(i * T, i * T + Lt, tw) + clip(i * T + Lt, (i + 1) * T, iw)]
-              for tw, iw in w.double]
-    layers += [clip(0, R, bw) for bw in w.single]
-    for i, parts in enumerate(layers):
-        bm = graph.mark()
-        nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp)
-        graph.release(bm, [nxt])
-        graph.free(x)
-        x = nxt
-        if on_block:
-            on_block(i)
+    if captured is not None:
+        if captured.key != (b0.height, b0.width, Lt, B, dtype) or sp is not None:
+            raise ValueError("the captured step is for another geometry, batch or dtype")
+        x = captured.run(graph, x, tvec)  # graph-owned; the last layer reads it
+    else:
+        for i, parts in enumerate(_layers(w, B, T, Lt, image, r0, n)):
+            bm = graph.mark()
+            nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp)
+            graph.release(bm, [nxt])
+            graph.free(x)
+            x = nxt
+            if on_block:
+                on_block(i)
     scale = ops.add(graph, t, w.last_scale, hid)
     shift = ops.add(graph, t, w.last_shift, hid)
     if dtype == "bf16":
