@@ -173,6 +173,22 @@ __global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restr
                                                              float* __restrict__ row_scale) {
   __shared__ float red[2][8];
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  float wo[CH][4], g1[CH][4], sf[CH][4];  // offset + w, 1 + scale, shift of this thread's columns, once per CTA
+#pragma unroll
+  for (int c = 0; c < CH; c++) {
+    const int64_t i = (int64_t)(c * 256 + tid) * 4;
+    const bool live = i < d;
+    const float4 ww = live ? *reinterpret_cast<const float4*>(w + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 s4 = live && sc ? *reinterpret_cast<const float4*>(sc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 h4 = live && sh ? *reinterpret_cast<const float4*>(sh + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float wv[4] = {ww.x, ww.y, ww.z, ww.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      wo[c][j] = offset + wv[j];
+      g1[c][j] = 1.f + sv[j];
+      sf[c][j] = hv[j];
+    }
+  }
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     float v[CH][4];
     float ss = 0.f;
@@ -195,13 +211,9 @@ __global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restr
     for (int c = 0; c < CH; c++) {
       const int64_t i = (int64_t)(c * 256 + tid) * 4;
       if (i >= d) continue;
-      const float4 ww = *reinterpret_cast<const float4*>(w + i);
-      const float4 s4 = sc ? *reinterpret_cast<const float4*>(sc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 h4 = sh ? *reinterpret_cast<const float4*>(sh + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float wv[4] = {ww.x, ww.y, ww.z, ww.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const float y = v[c][j] * inv * (offset + wv[j]) * (1.f + sv[j]) + hv[j];
+        const float y = v[c][j] * inv * wo[c][j] * g1[c][j] + sf[c][j];
         v[c][j] = bf16_bits_to_f32(f32_to_bf16_bits(y));
         amax = fmaxf(amax, fabsf(v[c][j]));
       }

@@ -160,6 +160,75 @@ __global__ void __launch_bounds__(128) rmsnorm_warp_kernel(const uint16_t* __res
   }
 }
 
+// CTA-per-row RMSNorm for rows of 2048..8192 values (16-byte aligned, d % 4 == 0): 256 threads, thread t owns
+// the 4-value chunks t, t + 256, ... of every row. Its weight / scale / shift values are loaded once per CTA and
+// kept in registers across the rows the CTA strides over (a warp-per-row form reloads those three f32 vectors,
+// six times the row's own bytes, for every row). Sum of squares: warp shuffle, then the 8 warps in a fixed order.
+template <int DT, int OT, int CH>
+__global__ void __launch_bounds__(256) rmsnorm_row_kernel(const void* __restrict__ x, const float* __restrict__ w,
+                                                          const float* __restrict__ sc, const float* __restrict__ sh,
+                                                          int64_t rows, int64_t d, float eps, float offset,
+                                                          void* __restrict__ out) {
+  __shared__ float red[8];
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  float wo[CH][4], g1[CH][4], sf[CH][4];  // offset + w, 1 + scale, shift of this thread's columns
+#pragma unroll
+  for (int c = 0; c < CH; c++) {
+    const int64_t i = (int64_t)(c * 256 + tid) * 4;
+    const bool live = i < d;
+    const float4 ww = live ? *reinterpret_cast<const float4*>(w + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 s4 = live && sc ? *reinterpret_cast<const float4*>(sc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 h4 = live && sh ? *reinterpret_cast<const float4*>(sh + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float wv[4] = {ww.x, ww.y, ww.z, ww.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      wo[c][j] = offset + wv[j];
+      g1[c][j] = 1.f + sv[j];
+      sf[c][j] = hv[j];
+    }
+  }
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[CH][4];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i < d) {
+        if constexpr (DT == WE_F32) {
+          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + row * d + i);
+          v[c][0] = a.x; v[c][1] = a.y; v[c][2] = a.z; v[c][3] = a.w;
+        } else {
+          const uint2 a = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + row * d + i);
+          v[c][0] = __uint_as_float(a.x << 16); v[c][1] = __uint_as_float(a.x & 0xffff0000u);
+          v[c][2] = __uint_as_float(a.y << 16); v[c][3] = __uint_as_float(a.y & 0xffff0000u);
+        }
+        ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
+        ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[wp] = ss;
+    __syncthreads();
+    const float inv = rsqrtf((((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]))) /
+                                 (float)d + eps);
+    __syncthreads();  // red is rewritten by the next row
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i >= d) continue;
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) y[j] = v[c][j] * inv * wo[c][j] * g1[c][j] + sf[c][j];  // rmsnorm.ts:42-46 order
+      if constexpr (OT == WE_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(out) + row * d + i) = make_float4(y[0], y[1], y[2], y[3]);
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + row * d + i) =
+            make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+      }
+    }
+  }
+}
+
 // q/k norm + RoPE for 128-wide heads: 16 lanes per head row, 8 values (16 bytes of bf16) per lane,
 // two rows per warp. Interleaved pairs stay in a lane; half pairing exchanges with lane ^ 8.
 template <int DT, int OT, int PAIRING>
@@ -327,6 +396,16 @@ static int capped(int64_t want, int sms, int per_sm) {
 template <int DT, int OT>
 static void rmsnorm_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
                              float eps, float offset, void* out, bool vec, int sms, cudaStream_t st) {
+  if (vec && d >= 2048 && d % 4 == 0 && d <= 8192) {  // CTA per row, weights held across rows
+    const unsigned g = (unsigned)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
+    const int64_t ch = (d / 4 + 255) / 256;
+    if (ch <= 2) rmsnorm_row_kernel<DT, OT, 2><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+    else if (ch <= 3) rmsnorm_row_kernel<DT, OT, 3><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+    else if (ch <= 4) rmsnorm_row_kernel<DT, OT, 4><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+    else if (ch <= 6) rmsnorm_row_kernel<DT, OT, 6><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+    else rmsnorm_row_kernel<DT, OT, 8><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+    return;
+  }
   if constexpr (DT == WE_BF16) {
     if (vec && d <= 256 * 24) {
       const int g = capped((rows + 3) / 4, sms, 16);
