@@ -450,6 +450,7 @@ def main() -> None:
             g.release(mark)
             we.kernels.rmsnorm(g, x, wn, M, K, xn, x_dtype="bf16", out_dtype="bf16")
             we.kernels.qknorm_rope(g, x, qn, cs_d, sn_d, M, K // 128, pairs, xn, x_dtype="bf16", out_dtype="bf16")
+            we.kernels.rope_apply(g, x, cs_d, sn_d, M, K // 128, pairs, xn, x_dtype="bf16", out_dtype="bf16")
         torch.cuda.synchronize()
         assert g.device_error() == 0
         g.destroy()

@@ -229,63 +229,78 @@ __global__ void __launch_bounds__(256) rmsnorm_row_kernel(const void* __restrict
   }
 }
 
-// q/k norm + RoPE for 128-wide heads: 16 lanes per head row, 8 values (16 bytes of bf16) per lane,
-// two rows per warp. Interleaved pairs stay in a lane; half pairing exchanges with lane ^ 8.
-template <int DT, int OT, int PAIRING>
-__global__ void __launch_bounds__(256) qknorm_rope128_kernel(const void* __restrict__ x, const float* __restrict__ w,
+// q/k norm + RoPE for 128-wide heads (NORM false: RoPE alone): 16 lanes per head row, 8 values (16 bytes of
+// bf16) per lane; a warp takes 2 R rows per step (R per half-warp) and issues all their loads (rows and cos/sin)
+// before any arithmetic, so each warp keeps R x 48 bytes per lane in flight. Interleaved pairs stay in a lane;
+// half pairing exchanges with lane ^ 8.
+template <int DT, int OT, int PAIRING, bool NORM>
+__global__ void __launch_bounds__(256, 3) qknorm_rope128_kernel(const void* __restrict__ x, const float* __restrict__ w,
                                                              float eps, float offset, const float* __restrict__ cs,
                                                              const float* __restrict__ sn, int64_t tokens,
                                                              int64_t heads, void* __restrict__ out) {
-  constexpr int D = 128, P = 64;
-  const int lane = threadIdx.x & 31, sub = lane & 15;
+  constexpr int D = 128, P = 64, R = 4;
+  const int lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4;
   const int64_t rows = tokens * heads;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   float ww[8];
-  load8f(w, sub * 8, ww);
+  if (NORM) {
+    load8f(w, sub * 8, ww);
 #pragma unroll
-  for (int e = 0; e < 8; e++) ww[e] += offset;
-  // warp-uniform loop over row pairs: half-warp (lane >> 4) takes row 2 pr + (lane >> 4); a row beyond
-  // the end (odd row count) is computed on row rows - 1 and not stored, so the shuffles stay full-warp
-  for (int64_t pr = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); 2 * pr < rows; pr += warps) {
-    const int64_t row0 = 2 * pr + (lane >> 4);
-    const bool live = row0 < rows;
-    const int64_t row = live ? row0 : rows - 1;
-    const int64_t t = row / heads;
-    const int64_t base = row * D + sub * 8;
-    float v[8];
-    load8<DT>(x, base, v);
-    float ss = 0.f;
+    for (int e = 0; e < 8; e++) ww[e] += offset;
+  }
+  // warp-uniform loop over groups of 2 R rows; a row past the end is computed on row rows - 1 and not stored,
+  // so the shuffles stay full-warp
+  for (int64_t gi = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); gi * 2 * R < rows; gi += warps) {
+    float v[R][8], c[R][8], sv[R][8];
+    int64_t base[R];
+    bool live[R];
 #pragma unroll
-    for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-    for (int e = 0; e < 8; e++) v[e] *= inv * ww[e];
-    float o8[8];
-    if (PAIRING == WE_ROPE_INTERLEAVED) {
-      float c4[4], s4[4];
-      const float4 cc = *reinterpret_cast<const float4*>(cs + t * P + sub * 4);
-      const float4 sv = *reinterpret_cast<const float4*>(sn + t * P + sub * 4);
-      c4[0] = cc.x; c4[1] = cc.y; c4[2] = cc.z; c4[3] = cc.w;
-      s4[0] = sv.x; s4[1] = sv.y; s4[2] = sv.z; s4[3] = sv.w;
-#pragma unroll
-      for (int g = 0; g < 4; g++) {
-        o8[2 * g] = v[2 * g] * c4[g] - v[2 * g + 1] * s4[g];
-        o8[2 * g + 1] = v[2 * g + 1] * c4[g] + v[2 * g] * s4[g];
-      }
-    } else {
-      const bool first = sub < 8;
-      float c8[8], s8[8];
-      load8f(cs, t * P + (sub & 7) * 8, c8);
-      load8f(sn, t * P + (sub & 7) * 8, s8);
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 8);
-        o8[e] = first ? v[e] * c8[e] - partner * s8[e] : v[e] * c8[e] + partner * s8[e];
+    for (int r = 0; r < R; r++) {
+      const int64_t row0 = gi * 2 * R + 2 * r + half;
+      live[r] = row0 < rows;
+      const int64_t row = live[r] ? row0 : rows - 1;
+      const int64_t t = row / heads;
+      base[r] = row * D + sub * 8;
+      load8<DT>(x, base[r], v[r]);
+      if (PAIRING == WE_ROPE_INTERLEAVED) {
+        const float4 cc = *reinterpret_cast<const float4*>(cs + t * P + sub * 4);
+        const float4 ss4 = *reinterpret_cast<const float4*>(sn + t * P + sub * 4);
+        c[r][0] = cc.x; c[r][1] = cc.y; c[r][2] = cc.z; c[r][3] = cc.w;
+        sv[r][0] = ss4.x; sv[r][1] = ss4.y; sv[r][2] = ss4.z; sv[r][3] = ss4.w;
+      } else {
+        load8f(cs, t * P + (sub & 7) * 8, c[r]);
+        load8f(sn, t * P + (sub & 7) * 8, sv[r]);
       }
     }
-    if (live) store8<OT>(out, base, o8);
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      if (NORM) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss = fmaf(v[r][e], v[r][e], ss);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[r][e] *= inv * ww[e];
+      }
+      float o8[8];
+      if (PAIRING == WE_ROPE_INTERLEAVED) {
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+          o8[2 * g] = v[r][2 * g] * c[r][g] - v[r][2 * g + 1] * sv[r][g];
+          o8[2 * g + 1] = v[r][2 * g + 1] * c[r][g] + v[r][2 * g] * sv[r][g];
+        }
+      } else {
+        const bool first = sub < 8;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float partner = __shfl_xor_sync(0xffffffffu, v[r][e], 8);
+          o8[e] = first ? v[r][e] * c[r][e] - partner * sv[r][e] : v[r][e] * c[r][e] + partner * sv[r][e];
+        }
+      }
+      if (live[r]) store8<OT>(out, base[r], o8);
+    }
   }
 }
 
@@ -446,6 +461,14 @@ cudaError_t launch_rmsnorm(const void* x, int xdt, const float* w, const float* 
 template <int DT, int OT>
 static void rope_dispatch(const void* x, const float* cs, const float* sn, int64_t tokens, int64_t heads, int64_t pairs,
                           int pairing, void* out, bool vec, int sms, cudaStream_t st) {
+  if (pairs == 64 && vec && ((uintptr_t)cs & 15) == 0 && ((uintptr_t)sn & 15) == 0) {  // 128-wide heads: row layout
+    const int g = capped((tokens * heads + 63) / 64, sms, 8);
+    if (pairing == WE_ROPE_INTERLEAVED)
+      qknorm_rope128_kernel<DT, OT, WE_ROPE_INTERLEAVED, false><<<g, 256, 0, st>>>(x, nullptr, 0.f, 0.f, cs, sn, tokens, heads, out);
+    else
+      qknorm_rope128_kernel<DT, OT, WE_ROPE_HALF, false><<<g, 256, 0, st>>>(x, nullptr, 0.f, 0.f, cs, sn, tokens, heads, out);
+    return;
+  }
   int threads = 128;
   if (pairing == WE_ROPE_INTERLEAVED) {
     if (vec) {
@@ -489,11 +512,11 @@ static bool qk_dispatch(const void* x, const float* w, float eps, float offset, 
   if (pairs * 2 == 128 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0 && ((uintptr_t)cs & 15) == 0 &&
       ((uintptr_t)sn & 15) == 0) {
     const int64_t rows = tokens * heads;
-    const int g = capped((rows + 15) / 16, sms, 8);
+    const int g = capped((rows + 63) / 64, sms, 8);
     if (pairing == WE_ROPE_INTERLEAVED)
-      qknorm_rope128_kernel<DT, OT, WE_ROPE_INTERLEAVED><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+      qknorm_rope128_kernel<DT, OT, WE_ROPE_INTERLEAVED, true><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
     else
-      qknorm_rope128_kernel<DT, OT, WE_ROPE_HALF><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+      qknorm_rope128_kernel<DT, OT, WE_ROPE_HALF, true><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
     return true;
   }
   switch (pairs * 2) {

@@ -319,10 +319,11 @@ __global__ void __launch_bounds__(128, 6) quant_act_warp_kernel(const uint16_t* 
 // CTA-per-row split for long bf16 rows (k % 8 == 0, k <= 2048 CH, 16-byte aligned rows): 256 threads, thread t
 // keeps the row's 16-byte chunks t, t + 256, ... in registers (few registers: many rows in flight per SM); the
 // row max is a warp shuffle then a shared-memory reduction over the 8 warps.
-template <int TERMS, int CH>
-__global__ void __launch_bounds__(256) quant_act_row_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
-                                                            int64_t stride, uint8_t* __restrict__ hi,
-                                                            uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
+template <int TERMS, int CH, int NT = 256>
+__global__ void __launch_bounds__(NT) quant_act_row_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
+                                                           int64_t stride, uint8_t* __restrict__ hi,
+                                                           uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
+  constexpr int NW = NT / 32;
   __shared__ float red[8];
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
   for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(256) quant_act_row_kernel(const uint16_t* __re
     uint32_t mx = 0;
 #pragma unroll
     for (int c = 0; c < CH; c++) {
-      const int64_t t = (int64_t)(c * 256 + tid) * 8;
+      const int64_t t = (int64_t)(c * NT + tid) * 8;
       if (t < k) {
         v[c] = *reinterpret_cast<const uint4*>(xr + t);
         // |bf16| max on the bit patterns: clear the sign bits, compare as integers
@@ -342,14 +343,16 @@ __global__ void __launch_bounds__(256) quant_act_row_kernel(const uint16_t* __re
     float amax = warp_max(fmaxf(__uint_as_float(mx << 16), __uint_as_float(mx & 0xffff0000u)));
     if (lane == 0) red[wp] = amax;
     __syncthreads();
-    amax = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])), fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+    amax = red[0];
+#pragma unroll
+    for (int i = 1; i < NW; i++) amax = fmaxf(amax, red[i]);
     __syncthreads();  // red is rewritten by the next row
     const int e = act_exponent(amax);
     if (tid == 0) row_scale[row] = ldexpf(1.0f, e);
     const float mul = pow2_neg(e);  // exact: scaling by a power of two
 #pragma unroll
     for (int c = 0; c < CH; c++) {
-      const int64_t t = (int64_t)(c * 256 + tid) * 8;
+      const int64_t t = (int64_t)(c * NT + tid) * 8;
       if (t >= k) continue;
       const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
       float s[8];
@@ -381,6 +384,14 @@ __global__ void __launch_bounds__(256) quant_act_row_kernel(const uint16_t* __re
 template <int TERMS>
 static bool quant_act_row(const uint16_t* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo, float* rs,
                           int sms, cudaStream_t st) {
+  if (k <= 128 * 8 * 4) {  // up to 4096 values: 128 threads, every thread busy at k = 3072
+    const int g = (int)std::min<int64_t>(m, (int64_t)sms * 16);
+    const int64_t ch = (k / 8 + 127) / 128;
+    if (ch <= 2) quant_act_row_kernel<TERMS, 2, 128><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+    else if (ch <= 3) quant_act_row_kernel<TERMS, 3, 128><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+    else quant_act_row_kernel<TERMS, 4, 128><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+    return true;
+  }
   const int g = (int)std::min<int64_t>(m, (int64_t)sms * 8);
   const int64_t ch = (k / 8 + 255) / 256;
   if (ch <= 2) quant_act_row_kernel<TERMS, 2><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
