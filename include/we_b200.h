@@ -275,6 +275,13 @@ int we_capture_end(we_ctx* ctx, we_graph** out);
 int we_graph_launch(we_ctx* ctx, we_graph* graph);
 int we_graph_destroy(we_ctx* ctx, we_graph* graph);
 
+/* The residual add of a block fused with the next norm + split: xo = x + r (f32 rows), then the planes and row
+   scales of norm(xo) exactly as we_norm_split computes them from xo. f32 only; d <= 8192, d % 8 == 0,
+   16-byte aligned rows. */
+int we_add_norm_split(we_ctx* ctx, const float* x, const float* r, float* xo, const float* weight, const float* scale,
+                      const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
+                      uint8_t* lo, float* row_scale);
+
 /* ---------------- latent <-> tokens: patchify / unpatchify (src/model/transformer.ts:53-82) ----------------
    tokens [ceil(H/2) * ceil(W/2), 4 channels] <- latent [channels, H, W]: 2x2 patches, features in (channel, patch
    row, patch column) order; an odd H or W wraps to row / column 0 (patchify, transformer.ts:59-69). unpatchify is

@@ -160,3 +160,31 @@ def test_block_bf16_fused_path(we, graph, mlp_act, kv_heads, per_channel):
     c = O.compare(delta.ravel(), wdelta.ravel())
     rel = float(np.max(np.abs(delta - wdelta)) / np.max(np.abs(wdelta)))
     assert c["cosine"] >= 0.9999 and rel < 1e-2, (c, rel)
+
+
+@pytest.mark.parametrize("rows,d", [(300, 3072), (33, 512), (7, 64)])
+def test_add_norm_split_equals_add_then_norm_split(we, graph, rows, d):
+    """we_add_norm_split: xo = x + r exactly, and the planes of norm(xo) exactly as we_norm_split makes them."""
+    x, r = randn(rows * d, 41, 2.0), randn(rows * d, 42, 0.5)
+    w, sc, sh = randn(d, 43, 0.1), randn(d, 44, 0.3), randn(d, 45, 0.3)
+    mark = graph.mark()
+    xb, rb, wb, scb, shb = (graph.buffer(a) for a in (x, r, w, sc, sh))
+    xo = graph.buffer(rows * d * 4)
+    a = [graph.buffer(rows * d), graph.buffer(rows * d), graph.buffer(rows * 4)]
+    we.kernels.add_norm_split(graph, xb, rb, xo, wb, rows, d, *a, scale=scb, shift=shb)
+    xs = graph.buffer((x + r).astype(np.float32))
+    b = [graph.buffer(rows * d), graph.buffer(rows * d), graph.buffer(rows * 4)]
+    we.kernels.norm_split(graph, xs, wb, rows, d, *b, scale=scb, shift=shb, x_dtype="f32")
+    got_x = graph.read(xo, rows * d * 4, np.float32).copy()
+    planes = [graph.read(buf, nb).copy() for buf, nb in zip(a + b, (rows * d, rows * d, rows * 4) * 2)]
+    graph.release(mark)
+    assert np.array_equal(got_x, (x + r).astype(np.float32))
+    if d >= 2048:  # both run the CTA-per-row reduction: identical bits
+        for u, v in zip(planes[:3], planes[3:]):
+            assert np.array_equal(u, v)
+    else:  # norm + split alone takes the warp-per-row reduction below 2048 values: a rare 1-ulp bf16 difference
+        e4 = O.e4m3_table()
+        ra, rb = [(e4[h] + e4[l]).reshape(rows, d) * s.view(np.float32)[:, None]
+                  for h, l, s in (planes[:3], planes[3:])]
+        diff = np.abs(ra - rb)
+        assert np.all(diff <= np.abs(ra) * 2.0 ** -7 + np.abs(ra).max(axis=1, keepdims=True) * 2.0 ** -16)

@@ -131,6 +131,8 @@ _SIGS = {
     "we_capture_end": (C.c_int, [_P, C.POINTER(C.c_void_p)]),
     "we_graph_launch": (C.c_int, [_P, _P]),
     "we_graph_destroy": (C.c_int, [_P, _P]),
+    "we_add_norm_split": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, C.c_float, C.c_float, C.c_int32, _P, _P,
+                                    _P]),
     "we_head_groups": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, C.c_int32]),
     "we_patchify": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, _P, C.c_int32]),
     "we_unpatchify": (C.c_int, [_P, _P, C.c_int32, _I64, _I64, _I64, _P, C.c_int32]),

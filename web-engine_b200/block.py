@@ -16,7 +16,8 @@ reference's f32 semantics, src/model/block.ts:91-105). `dtype="bf16"` is the B20
 - each RMSNorm writes the e4m3 split of its bf16 output directly (we_norm_split) for the fp8 GEMMs;
 - q/k get the fused norm + RoPE;
 - attention runs on the tcgen05 flash kernel;
-- the sigmoid gate, the MLP activation and the gated residual adds run inside the GEMM epilogues.
+- the sigmoid gate, the MLP activation and the residual gates run inside the GEMM epilogues; the first residual
+  add is fused with the second RMSNorm + split (we_add_norm_split), the second is one f32 add.
 The residual stream stays f32.
 """
 from __future__ import annotations
@@ -258,17 +259,16 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
                   aux_op="sigmoid_gate", aux=rows_at(o, p.row0, hd * 2), aux_dtype="bf16")
         o = og
     K.quantize_act(graph, o, t, hd, *split, terms=2)
+    a = graph.buffer(t * hd * 4)
+    for p, mod in zip(parts, mods):  # a = pregate wo(o), the gate in the epilogue
+        _gemm(graph, _split_rows(split, p, hd), p.w.wo, rows_at(a, p.row0, hd * 4), p.rows, "f32", gate=mod["pregate"])
     x1 = graph.buffer(t * hd * 4)
-    graph.copy(x, 0, x1, 0, t * hd * 4)
-    for p, mod in zip(parts, mods):  # x1 = x + pregate wo(o)
-        _gemm(graph, _split_rows(split, p, hd), p.w.wo, rows_at(x1, p.row0, hd * 4), p.rows, "f32", accumulate=True,
-              gate=mod["pregate"])
     u = graph.buffer(t * cfg.mlp * 2)
     g = graph.buffer(t * cfg.mlp * 2) if cfg.mlp_act == "swiglu" else None
-    for p, mod in zip(parts, mods):
+    for p, mod in zip(parts, mods):  # x1 = x + a, and the norm + split of x1, in one pass
         sr = _split_rows(split, p, hd)
-        K.norm_split(graph, rows_at(x1, p.row0, hd * 4), p.w.norm2, p.rows, hd, *sr, scale=mod["postscale"],
-                     shift=mod["postshift"], eps=cfg.eps)
+        K.add_norm_split(graph, rows_at(x, p.row0, hd * 4), rows_at(a, p.row0, hd * 4), rows_at(x1, p.row0, hd * 4),
+                         p.w.norm2, p.rows, hd, *sr, scale=mod["postscale"], shift=mod["postshift"], eps=cfg.eps)
         up = rows_at(u, p.row0, cfg.mlp * 2)
         if cfg.mlp_act == "swiglu":
             gp = rows_at(g, p.row0, cfg.mlp * 2)
@@ -278,11 +278,11 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
             _gemm(graph, sr, p.w.mlp_up, up, p.rows, "bf16", act="gelu_tanh")
     msplit = (graph.buffer(t * cfg.mlp), graph.buffer(t * cfg.mlp), split[2])
     K.quantize_act(graph, u, t, cfg.mlp, *msplit, terms=2)
-    out = graph.buffer(t * hd * 4)
-    graph.copy(x1, 0, out, 0, t * hd * 4)
-    for p, mod in zip(parts, mods):  # out = x1 + postgate down(m)
-        _gemm(graph, _split_rows(msplit, p, cfg.mlp), p.w.mlp_down, rows_at(out, p.row0, hd * 4), p.rows, "f32",
-              accumulate=True, gate=mod["postgate"])
+    dn = graph.buffer(t * hd * 4)
+    for p, mod in zip(parts, mods):  # dn = postgate down(m)
+        _gemm(graph, _split_rows(msplit, p, cfg.mlp), p.w.mlp_down, rows_at(dn, p.row0, hd * 4), p.rows, "f32",
+              gate=mod["postgate"])
+    out = ops.add(graph, x1, dn, t * hd)  # x1 + postgate down(m): the block's output
     graph.release(mark, [out])
     return out
 

@@ -165,12 +165,16 @@ __device__ __forceinline__ void load4(const void* p, int64_t i, float v[4]) {
   }
 }
 
-template <int DT, int TERMS, int CH>
+// RES: the row is x + r (f32 residual plus f32 update), written to xo before it is normalised (the residual add
+// of a block, fused with the next RMSNorm and split)
+template <int DT, int TERMS, int CH, bool RES = false>
 __global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restrict__ x, const float* __restrict__ w,
                                                              const float* __restrict__ sc, const float* __restrict__ sh,
                                                              int64_t rows, int64_t d, float eps, float offset,
                                                              uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
-                                                             float* __restrict__ row_scale) {
+                                                             float* __restrict__ row_scale,
+                                                             const float* __restrict__ r = nullptr,
+                                                             float* __restrict__ xo = nullptr) {
   __shared__ float red[2][8];
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
   float wo[CH][4], g1[CH][4], sf[CH][4];  // offset + w, 1 + scale, shift of this thread's columns, once per CTA
@@ -197,6 +201,11 @@ __global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restr
       const int64_t i = (int64_t)(c * 256 + tid) * 4;
       if (i < d) {
         load4<DT>(x, row * d + i, v[c]);
+        if (RES) {
+          const float4 u = *reinterpret_cast<const float4*>(r + row * d + i);
+          v[c][0] += u.x; v[c][1] += u.y; v[c][2] += u.z; v[c][3] += u.w;
+          *reinterpret_cast<float4*>(xo + row * d + i) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
+        }
         ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
         ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
       }
@@ -277,6 +286,31 @@ static bool norm_split_dispatch(const void* x, const float* w, const float* sc, 
   else if (d <= 256 * 24) norm_split_kernel<DT, TERMS, 24><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
   else return false;
   return true;
+}
+
+cudaError_t launch_add_norm_split(const float* x, const float* r, float* xo, const float* w, const float* sc,
+                                  const float* sh, int64_t rows, int64_t d, float eps, float offset, int terms,
+                                  uint8_t* hi, uint8_t* lo, float* rs, int sms, cudaStream_t st) {
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (d % 8 || d > 8192 || !al(x) || !al(r) || !al(xo) || !al(w) || (sc && !al(sc)) || (sh && !al(sh)) ||
+      ((uintptr_t)hi & 7) || (lo && ((uintptr_t)lo & 7)))
+    return cudaErrorNotSupported;
+  const unsigned g = (unsigned)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
+  const int64_t ch = (d / 4 + 255) / 256;
+#define WE_ANS(CH)                                                                                                  \
+  {                                                                                                                 \
+    if (terms > 1)                                                                                                  \
+      norm_split_row_kernel<WE_F32, 2, CH, true><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo); \
+    else                                                                                                            \
+      norm_split_row_kernel<WE_F32, 1, CH, true><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo); \
+  }
+  if (ch <= 2) WE_ANS(2)
+  else if (ch <= 3) WE_ANS(3)
+  else if (ch <= 4) WE_ANS(4)
+  else if (ch <= 6) WE_ANS(6)
+  else WE_ANS(8)
+#undef WE_ANS
+  return cudaGetLastError();
 }
 
 cudaError_t launch_norm_split(const void* x, int xdt, const float* w, const float* sc, const float* sh, int64_t rows,

@@ -81,6 +81,10 @@ cudaError_t launch_norm_split(const void* x, int xdt, const float* w, const floa
                               int64_t d, float eps, float offset, int terms, uint8_t* hi, uint8_t* lo, float* rs,
                               int sms, cudaStream_t st);
 
+cudaError_t launch_add_norm_split(const float* x, const float* r, float* xo, const float* w, const float* sc,
+                                  const float* sh, int64_t rows, int64_t d, float eps, float offset, int terms,
+                                  uint8_t* hi, uint8_t* lo, float* rs, int sms, cudaStream_t st);
+
 // k_layout.cu: latent <-> tokens (2x2 patches, odd sizes wrap / crop)
 cudaError_t launch_patchify(const void* latent, int ldt, int64_t C, int64_t H, int64_t W, void* tokens, int tdt,
                             int sms, cudaStream_t st);

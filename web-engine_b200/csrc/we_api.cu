@@ -760,6 +760,23 @@ int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weig
   return WE_OK;
 }
 
+int we_add_norm_split(we_ctx* ctx, const float* x, const float* r, float* xo, const float* weight, const float* scale,
+                      const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
+                      uint8_t* lo, float* row_scale) {
+  if (!ctx) return WE_EINVAL;
+  if (!x || !r || !xo || !weight || !hi || !row_scale) return fail(ctx, WE_EINVAL, "add + norm + split: missing buffer");
+  if (terms != 1 && terms != 2) return fail(ctx, WE_EINVAL, "terms must be 1 or 2");
+  if (terms == 2 && !lo) return fail(ctx, WE_EINVAL, "two terms need a lo buffer");
+  if (rows <= 0) return WE_OK;
+  cudaError_t e = we::launch_add_norm_split(x, r, xo, weight, scale, shift, rows, d, eps, offset, terms, hi, lo,
+                                            row_scale, ctx->sms, ctx->stream);
+  if (e == cudaErrorNotSupported)
+    return fail(ctx, WE_EINVAL, "add + norm + split needs d <= 8192, d % 8 == 0 and 16-byte aligned rows");
+  CK(e, "add + norm + split");
+  ctx->stats.launches++;
+  return WE_OK;
+}
+
 // ---------------- CUDA graphs: capture a sequence of this library's ops once, replay it ----------------
 int we_capture_begin(we_ctx* ctx) {
   if (!ctx) return WE_EINVAL;

@@ -246,3 +246,12 @@ def norm_split(graph: Graph, x, weight, rows: int, d: int, hi, lo, row_scale, sc
     L.check(graph.ctx, L.lib().we_norm_split(graph.ctx, addr(x), L.DTYPES[x_dtype], addr(weight), addr(scale),
                                              addr(shift), rows, d, eps, offset, terms, addr(hi), addr(lo),
                                              addr(row_scale)))
+
+
+def add_norm_split(graph: Graph, x, r, xo, weight, rows: int, d: int, hi, lo, row_scale, scale=None, shift=None,
+                   eps=1e-5, offset=1.0, terms: int = 2) -> None:
+    """xo = x + r (f32), then norm + split of xo (we_add_norm_split): a block's residual add fused with the next
+    RMSNorm and activation split."""
+    L.check(graph.ctx, L.lib().we_add_norm_split(graph.ctx, addr(x), addr(r), addr(xo), addr(weight), addr(scale),
+                                                 addr(shift), rows, d, eps, offset, terms, addr(hi), addr(lo),
+                                                 addr(row_scale)))
