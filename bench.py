@@ -181,8 +181,8 @@ def random_model(we, g, torch, dev, gen, scfg):
     return we.transformer.TransformerWeights(double=double, single=single, **edge, **vec)
 
 
-def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, world: int = 1, gpu: int = 0,
-                step_ms=None) -> dict:
+def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_peak: float, world: int = 1,
+                gpu: int = 0, step_ms=None) -> dict:
     """Config 3 (one single-stream block, 4608 tokens) and config 4 (one denoising step of the 19 + 38 block
     model at 1024x1024: 512 text + 4096 image tokens), bf16 path, weights resident, inputs ~N(0, 1)."""
     T = we.transformer
@@ -243,8 +243,6 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
         T.transformer(g, model, scfg, inp_e, dtype="bf16", velocity=vel)
         g.read_into(vel, vel_h.data_ptr(), vel.numel() * 4)
 
-    with ClockSampler(gpu) as e2e_clocks:
-        e2e_ms = timed(step_e2e, ksteps, 1) / ksteps
     # the same step with its 57 blocks replayed from a CUDA graph (one launch from the host instead of ~1000)
     sgr = T.StepGraph(g, model, scfg, side, side, text_tokens, dtype="bf16")
 
@@ -257,8 +255,11 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
         T.transformer(g, model, scfg, inp_e, dtype="bf16", velocity=vel, captured=sgr)
         g.read_into(vel, vel_h.data_ptr(), vel.numel() * 4)
 
-    gr_ms = timed(step_graph, ksteps, 3) / ksteps
-    gr_e2e_ms = timed(step_graph_e2e, ksteps, 2) / ksteps
+    # the four ways of running the step take turns, so that the power cap's clock drift falls on all of them
+    with ClockSampler(gpu) as e2e_clocks:
+        med = interleaved({"eager": step_model, "eager_e2e": step_e2e, "graph": step_graph,
+                           "graph_e2e": step_graph_e2e}, ksteps, 2)
+    e2e_ms, gr_ms, gr_e2e_ms = med["eager_e2e"], med["graph"], med["graph_e2e"]
     issue = {}
     for name, fn in (("eager", step_model), ("graph", step_graph)):
         torch.cuda.synchronize()
@@ -271,7 +272,7 @@ def bench_model(we, g, torch, dev, gen, timed, steps: int, bf16_peak: float, wor
                            "frac_bf16_peak": sf["total"] / (st_ms * 1e-3) / 1e12 / bf16_peak, "flop": sf["total"],
                            "launches_per_step": st_launches, "e2e_ms": e2e_ms, "clocks": st_clocks.summary(),
                            "graph_ms": gr_ms, "graph_e2e_ms": gr_e2e_ms, "host_issue_ms": issue,
-                           "e2e_clocks": e2e_clocks.summary(),
+                           "interleaved_median_ms": med, "e2e_clocks": e2e_clocks.summary(),
                            "e2e_h2d_bytes": lat.numel() * 2 + ctx.numel() * 2, "e2e_d2h_bytes": vel.numel() * 4,
                            "note": "19 double + 38 single blocks of config 3 shape, 512 text + 4096 image tokens "
                                    "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
@@ -411,6 +412,33 @@ def main() -> None:
         step_ms[:] = [a.elapsed_time(b) for a, b in ev]
         total = sum(step_ms)
         return we.parallel.max_over_ranks(total, device=dev)
+
+    def interleaved(fns: dict, rounds: int, warmup: int) -> dict:
+        """Median CUDA-event ms per step of each function, the functions taking turns (one step each per round,
+        an L2 flush before every step) so that clock and power drift over the run falls on all of them alike;
+        max over ranks."""
+        for _ in range(warmup):
+            for fn in fns.values():
+                flush_l2()
+                fn()
+        ev = {name: [] for name in fns}
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for _ in range(rounds):
+            for name, fn in fns.items():
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                flush_l2()
+                a.record(stream)
+                fn()
+                b.record(stream)
+                ev[name].append((a, b))
+        torch.cuda.synchronize()
+        out = {}
+        for name, pairs in ev.items():
+            t = sorted(a.elapsed_time(b) for a, b in pairs)
+            out[name] = we.parallel.max_over_ranks(t[len(t) // 2], device=dev)
+        return out
 
     if args.profile_block:
         T = we.transformer
@@ -561,7 +589,8 @@ def main() -> None:
 
     # ---- config 3 (one block) and config 4 (one whole denoising step) on the bf16 fused path ----
     if not args.no_variants and not args.no_model:
-        variants.update(bench_model(we, g, torch, dev, gen, timed, args.steps, bf16_peak, world, local, step_ms))
+        variants.update(bench_model(we, g, torch, dev, gen, timed, interleaved, args.steps, bf16_peak, world, local,
+                                     step_ms))
 
     # ---- fp8 dense peak of this GPU, measured like the bf16 one (cuBLAS through torch, 8192^3) ----
     if not args.no_variants:
@@ -617,21 +646,33 @@ def main() -> None:
                         "through 2 slots on a side stream"}
         del xs, ysb, host_w
 
-    # ---- end to end through the public API with host buffers ----
+    # ---- end to end through the public API with host buffers: we_linear_host takes x from pinned host memory and
+    #      returns y in pinned host memory, its row chunks' copies overlapping the GEMMs ----
     xh = x.cpu().pin_memory()
     yh = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(x)
 
     def step_e2e():
+        we.linear_host(g, xh, lin, M, yh, x_dtype="bf16", y_dtype="bf16")
+
+    l0 = g.stats["launches"]
+    e2e_ms = timed(step_e2e, args.steps, 2) / args.steps
+    e2e_launches = (g.stats["launches"] - l0) // (args.steps + 2)
+    e2e = {"value": world * FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": M * K * 2,
+           "d2h_bytes_per_step": M * N * 2, "ms_per_step": e2e_ms, "call": "we_linear_host (8 row chunks)",
+           "gpu_launches_per_step": e2e_launches}
+    # the same without the overlap: one upload, the linear, one read-back, in stream order
+    xd = torch.empty_like(x)
+
+    def step_serial():
         xd.copy_(xh, non_blocking=True)  # pinned host -> HBM on the library's stream
         mark = g.mark()
         y = we.linear(g, xd, lin, M, x_dtype="bf16", y_dtype="bf16")
         g.read_into(y, yh.data_ptr(), M * N * 2)  # HBM -> pinned host, then wait for the stream
         g.release(mark)
 
-    e2e_ms = timed(step_e2e, args.steps, 2) / args.steps
-    e2e = {"value": world * FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "h2d_bytes_per_step": M * K * 2,
-           "d2h_bytes_per_step": M * N * 2, "ms_per_step": e2e_ms}
+    serial_ms = timed(step_serial, max(3, args.steps // 2), 2) / max(3, args.steps // 2)
+    e2e["serial_ms_per_step"] = serial_ms
+    e2e["pcie_gbs_estimate"] = (M * K * 2 + M * N * 2) / (serial_ms - ms) / 1e6 if serial_ms > ms else None
 
     line = None
     if rank == 0:

@@ -174,6 +174,16 @@ typedef struct we_linear {
    [m, n] of y_dtype. LoRA shape errors: "LoRA shapes do not fit the linear layer". */
 int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m,
                       int32_t y_dtype, uint32_t flags, void** y);
+/* linear from host memory to host memory: y_host [m, n] = linear(x_host [m, k]). One call does the upload of x,
+   the linear and the read-back of y. A caller of ops.ts:61-73 does the same with queue.writeBuffer before the
+   dispatch and a mapped read after it (graph.ts:37-47, graph.ts:108-119). Rows go in chunks of chunk_rows
+   (0: about m / 8, a multiple of 128) through three streams, so the host -> device copy of chunk c + 1, the GEMM
+   of chunk c and the device -> host copy of chunk c - 1 overlap. Returns when y_host holds the result. Copies
+   overlap only when both host buffers are page-locked (cudaHostAlloc / cudaHostRegister); pageable buffers give
+   the same result. Each chunk is the linear of its rows, as we_linear_forward computes it for that many rows.
+   Refused while capturing. */
+int we_linear_host(we_ctx* ctx, const void* x_host, int32_t x_dtype, const we_linear* w, int64_t m,
+                   int32_t y_dtype, uint32_t flags, void* y_host, int64_t chunk_rows);
 /* Mod (ops.ts:75): scale/shift device vectors of length d (NULL = zeros). */
 typedef struct {
   const float* scale;

@@ -5,7 +5,7 @@ mirror of the reference's operator API (src/model/ops.ts over src/gpu/graph.ts) 
 """
 from . import _lib
 from .graph import Binding, Buffer, Graph
-from .ops import Linear, Mod, Rope, attention, k_split_for, linear, no_mod, norm, qk_norm_rotate, rotate
+from .ops import Linear, Mod, Rope, attention, k_split_for, linear, linear_host, no_mod, norm, qk_norm_rotate, rotate
 from . import kernels, parallel
 from .stream import Streamer
 from . import block as blocks
@@ -13,7 +13,7 @@ from . import transformer
 from . import weights
 from . import sequence
 
-__all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "norm", "no_mod", "rotate",
+__all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "linear_host", "norm", "no_mod", "rotate",
            "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "weights", "sequence", "build"]
 
 

@@ -106,6 +106,7 @@ _SIGS = {
     "we_ksplit_for": (_I64, [_I64, _I64, _I64]),
     "we_linear_forward": (C.c_int, [_P, _P, C.c_int32, C.POINTER(LinearDesc), _I64, C.c_int32, C.c_uint32,
                                     C.POINTER(C.c_void_p)]),
+    "we_linear_host": (C.c_int, [_P, _P, C.c_int32, C.POINTER(LinearDesc), _I64, C.c_int32, C.c_uint32, _P, _I64]),
     "we_no_mod": (C.c_int, [_P, _I64, C.POINTER(ModDesc)]),
     "we_norm": (C.c_int, [_P, _P, C.c_int32, _P, _I64, _I64, C.POINTER(ModDesc), C.c_float, C.c_float, C.c_int32,
                           C.POINTER(C.c_void_p)]),

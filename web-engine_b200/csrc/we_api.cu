@@ -46,6 +46,10 @@ struct we_ctx {
   std::vector<void*> cap_host;
   uint64_t cap_launches0 = 0;
   std::vector<we_graph*> graphs;  // live graphs, destroyed with the context
+  // we_linear_host's copy engines: host -> device and device -> host streams beside the compute stream, and
+  // the events that order one call's row chunks between the three (created on first use)
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  std::vector<cudaEvent_t> io_events;
 };
 
 struct we_graph {
@@ -252,6 +256,9 @@ int we_destroy(we_ctx* ctx) {
   for (auto& st : ctx->staged) cudaEventDestroy(st.done);
   for (cudaEvent_t ev : ctx->spare_events) cudaEventDestroy(ev);
   if (ctx->stage) cudaFreeHost(ctx->stage);
+  for (cudaEvent_t ev : ctx->io_events) cudaEventDestroy(ev);
+  if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
+  if (ctx->d2h) cudaStreamDestroy(ctx->d2h);
   for (auto& kv : ctx->sizes) cudaFree(kv.first);
   cudaFree(ctx->dev_err);
   cudaStreamDestroy(ctx->own);
@@ -544,16 +551,13 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
 // ---------------- ops ----------------
 static int sum_partials(we_ctx* ctx, const float* partials, int64_t split, int64_t count, float* out);
 
-int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m, int32_t y_dtype,
-                      uint32_t flags, void** y) {
-  if (!ctx || !w || !y) return WE_EINVAL;
+// The linear's GEMM descriptor for m rows, and its shape checks (LoRA included), before anything is enqueued.
+static int linear_check(we_ctx* ctx, int32_t x_dtype, const we_linear* w, int64_t m, int32_t y_dtype, uint32_t flags) {
   if (w->lora_down || w->lora_up) {
     const we_linear *down = w->lora_down, *up = w->lora_up;
     if (!down || !up || down->k != w->k || up->n != w->n || up->k != down->n || down->n % 4)
       return fail(ctx, WE_EINVAL, "LoRA shapes do not fit the linear layer");
   }
-  int rc = op_output(ctx, (size_t)(m * w->n) * dsize(y_dtype), y);
-  if (rc != WE_OK) return rc;
   we_matmul_desc d{};
   d.m = m;
   d.n = w->n;
@@ -566,7 +570,39 @@ int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_line
   d.w_dtype = w->dtype;
   d.y_dtype = y_dtype;
   d.flags = flags & (WE_MM_FP8_FAST | WE_MM_FORCE_SIMT);
-  if ((rc = matmul_impl(ctx, &d, x, w->weight, *y)) != WE_OK) return rc;
+  return we_matmul_check(ctx, &d);
+}
+
+static int linear_into(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m, int32_t y_dtype,
+                       uint32_t flags, void* y);
+
+int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m, int32_t y_dtype,
+                      uint32_t flags, void** y) {
+  if (!ctx || !w || !y) return WE_EINVAL;
+  int rc = linear_check(ctx, x_dtype, w, m, y_dtype, flags);
+  if (rc != WE_OK) return rc;
+  if ((rc = op_output(ctx, (size_t)(m * w->n) * dsize(y_dtype), y)) != WE_OK) return rc;
+  return linear_into(ctx, x, x_dtype, w, m, y_dtype, flags, *y);
+}
+
+// y[m, n] = linear(x) into an existing buffer: the body of we_linear_forward, also run per row chunk by
+// we_linear_host.
+static int linear_into(we_ctx* ctx, const void* x, int32_t x_dtype, const we_linear* w, int64_t m, int32_t y_dtype,
+                       uint32_t flags, void* y) {
+  int rc;
+  we_matmul_desc d{};
+  d.m = m;
+  d.n = w->n;
+  d.k = w->k;
+  d.scale = w->scale;
+  d.chan_scale = w->chan_scale;
+  d.group_scale = w->group_scale;
+  d.bias = w->bias;
+  d.x_dtype = x_dtype;
+  d.w_dtype = w->dtype;
+  d.y_dtype = y_dtype;
+  d.flags = flags & (WE_MM_FP8_FAST | WE_MM_FORCE_SIMT);
+  if ((rc = matmul_impl(ctx, &d, x, w->weight, y)) != WE_OK) return rc;
   if (!w->lora_down) return WE_OK;
   // narrowLinear (ops.ts:48-58): t = x . down^T, split over K when narrow, then y += up.scale t . up^T
   const we_linear *down = w->lora_down, *up = w->lora_up;
@@ -604,7 +640,68 @@ int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_line
   du.w_dtype = up->dtype;
   du.y_dtype = y_dtype;
   du.flags = WE_MM_ACCUMULATE;
-  return matmul_impl(ctx, &du, t, up->weight, *y);
+  return matmul_impl(ctx, &du, t, up->weight, y);
+}
+
+int we_linear_host(we_ctx* ctx, const void* x_host, int32_t x_dtype, const we_linear* w, int64_t m,
+                   int32_t y_dtype, uint32_t flags, void* y_host, int64_t chunk_rows) {
+  if (!ctx || !w || m < 0 || chunk_rows < 0 || (m > 0 && (!x_host || !y_host))) return WE_EINVAL;
+  if (ctx->capturing) return fail(ctx, WE_EINVAL, "cannot read back while capturing a graph");
+  int rc = linear_check(ctx, x_dtype, w, m, y_dtype, flags);
+  if (rc != WE_OK || m == 0) return rc;
+  if (chunk_rows == 0) chunk_rows = std::max<int64_t>(128, ((m + 7) / 8 + 127) / 128 * 128);
+  const int64_t chunks = (m + chunk_rows - 1) / chunk_rows;
+  const size_t xrow = (size_t)w->k * dsize(x_dtype), yrow = (size_t)w->n * dsize(y_dtype);
+  if (!ctx->h2d) CK(cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking), "copy stream");
+  if (!ctx->d2h) CK(cudaStreamCreateWithFlags(&ctx->d2h, cudaStreamNonBlocking), "copy stream");
+  while (ctx->io_events.size() < (size_t)(2 * chunks + 2)) {
+    cudaEvent_t ev;
+    CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+    ctx->io_events.push_back(ev);
+  }
+  cudaEvent_t* ev = ctx->io_events.data();  // [0] start, [1] end, [2 + 2c] x chunk c in, [3 + 2c] y chunk c out
+  Scratch scratch(ctx);
+  void *xd, *yd;
+  if ((rc = scratch.take((size_t)m * xrow, &xd)) != WE_OK) return rc;
+  if ((rc = scratch.take((size_t)m * yrow, &yd)) != WE_OK) return rc;
+  // Before the scratch goes back to the pool (a stream-ordered reuse on the compute stream), the compute stream
+  // waits for the last device -> host copy; on an error part-way, the copies already enqueued finish first.
+  struct Drain {
+    we_ctx* c;
+    bool ok = false;
+    ~Drain() {
+      if (ok) return;
+      cudaStreamSynchronize(c->h2d);
+      cudaStreamSynchronize(c->d2h);
+    }
+  } drain{ctx};
+  // the pooled buffers may still be read by earlier work of the compute stream
+  CK(cudaEventRecord(ev[0], ctx->stream), "cudaEventRecord");
+  CK(cudaStreamWaitEvent(ctx->h2d, ev[0], 0), "cudaStreamWaitEvent");
+  for (int64_t c = 0; c < chunks; c++) {  // every input chunk goes first: the link runs ahead of the GEMMs
+    const int64_t r0 = c * chunk_rows, rows = std::min(chunk_rows, m - r0);
+    CK(cudaMemcpyAsync(static_cast<char*>(xd) + r0 * xrow, static_cast<const char*>(x_host) + r0 * xrow,
+                       rows * xrow, cudaMemcpyHostToDevice, ctx->h2d),
+       "host -> device chunk");
+    CK(cudaEventRecord(ev[2 + 2 * c], ctx->h2d), "cudaEventRecord");
+  }
+  for (int64_t c = 0; c < chunks; c++) {
+    const int64_t r0 = c * chunk_rows, rows = std::min(chunk_rows, m - r0);
+    CK(cudaStreamWaitEvent(ctx->stream, ev[2 + 2 * c], 0), "cudaStreamWaitEvent");
+    if ((rc = linear_into(ctx, static_cast<const char*>(xd) + r0 * xrow, x_dtype, w, rows, y_dtype, flags,
+                          static_cast<char*>(yd) + r0 * yrow)) != WE_OK)
+      return rc;
+    CK(cudaEventRecord(ev[3 + 2 * c], ctx->stream), "cudaEventRecord");
+    CK(cudaStreamWaitEvent(ctx->d2h, ev[3 + 2 * c], 0), "cudaStreamWaitEvent");
+    CK(cudaMemcpyAsync(static_cast<char*>(y_host) + r0 * yrow, static_cast<char*>(yd) + r0 * yrow, rows * yrow,
+                       cudaMemcpyDeviceToHost, ctx->d2h),
+       "device -> host chunk");
+  }
+  CK(cudaEventRecord(ev[1], ctx->d2h), "cudaEventRecord");
+  CK(cudaStreamWaitEvent(ctx->stream, ev[1], 0), "cudaStreamWaitEvent");
+  drain.ok = true;
+  CK(cudaStreamSynchronize(ctx->stream), "we_linear_host sync");
+  return WE_OK;
 }
 
 int we_no_mod(we_ctx* ctx, int64_t d, we_mod* out) {

@@ -47,13 +47,15 @@ class Binding:
 
 
 def addr(b) -> C.c_void_p:
-    """Device address of a Buffer, Binding, raw int pointer, or None."""
+    """Address of a Buffer, Binding, torch tensor, numpy array, raw int pointer, or None."""
     if b is None:
         return C.c_void_p(None)
     if isinstance(b, int):
         return C.c_void_p(b)
-    if hasattr(b, "data_ptr"):  # a torch tensor on the device
+    if hasattr(b, "data_ptr"):  # a torch tensor (device, or host for the host-memory entry points)
         return C.c_void_p(b.data_ptr())
+    if hasattr(b, "ctypes"):  # a numpy array (host)
+        return C.c_void_p(b.ctypes.data)
     return b.c
 
 

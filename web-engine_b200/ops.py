@@ -73,6 +73,19 @@ def linear(graph: Graph, x, w: Linear, m: int, x_dtype: str = "f32", y_dtype: st
     return Buffer(out.value, m * w.n * L.DTYPE_BYTES[L.DTYPES[y_dtype]])
 
 
+def linear_host(graph: Graph, x_host, w: Linear, m: int, y_host, x_dtype: str = "bf16", y_dtype: str = "bf16",
+                fast: bool = False, chunk_rows: int = 0) -> None:
+    """y_host[m, n] = linear(x_host[m, k]) from host memory to host memory in one call: the upload, the linear
+    (ops.ts:61-73) and the read-back (graph.ts:108-119), row chunk by row chunk on three streams so that both
+    copies overlap the GEMMs. x_host / y_host are CPU tensors (page-locked for the overlap) or host addresses.
+    Returns when y_host holds the result."""
+    keep: list = []
+    d = w.desc(keep)
+    flags = L.MM_FP8_FAST if fast else 0
+    L.check(graph.ctx, L.lib().we_linear_host(graph.ctx, addr(x_host), L.DTYPES[x_dtype], C.byref(d), m,
+                                              L.DTYPES[y_dtype], flags, addr(y_host), chunk_rows))
+
+
 @dataclass
 class Mod:
     """Modulation vectors of length d (ops.ts:75); None = zeros."""
