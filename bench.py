@@ -584,7 +584,7 @@ def main() -> None:
         at_flops = 4.0 * M * M * heads * 128
         variants["flash_attention_config3"] = {"tflops": at_flops / (at_ms * 1e-3) / 1e12, "ms": at_ms,
                                                "frac_bf16_peak": at_flops / (at_ms * 1e-3) / 1e12 / bf16_peak,
-                                               "note": "4 T^2 H D FLOP, T=4608, 24 heads x 128, incl. the V transpose"}
+                                               "note": "4 T^2 H D FLOP, T=4608, 24 heads x 128"}
         del qa, ka, va, oa
 
     # ---- config 3 (one block) and config 4 (one whole denoising step) on the bf16 fused path ----

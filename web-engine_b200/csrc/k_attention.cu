@@ -8,13 +8,15 @@
 //    sizes / masks the tensor-core kernel does not take.
 //  * flash_attn2_kernel: tcgen05 flash attention for bf16 q/k/v with 128-wide heads, no mask (the DiT
 //    blocks). One CTA = one head x 256 queries (two 128-row tiles). Warp 0 TMA-loads both Q tiles once
-//    and K / V^T key tiles of 128 into separate 2-stage rings (K runs two tiles ahead); warp 1 issues
-//    S_i = Q_i K^T into TMEM and O_i += P_i V^T with P read from TMEM, interleaving the two tiles; warps
-//    2-9 (two groups of four, thread = query row) run the online softmax (tcgen05.ld, packed f32x2 math,
-//    ex2.approx), write P as bf16 over the first half of S_i (tcgen05.st), and rescale O_i in TMEM only
-//    when a row's running maximum grows by more than 2^8 (the probabilities stay <= 256 in between,
-//    which fp32 accumulation and bf16 P hold without loss of relative precision).
-//    V is transposed once per call into [kv_heads, dim, tokens] so both MMAs take K-major operands.
+//    and K / V key tiles of 128 into separate 2-stage rings (K runs two tiles ahead); warp 1 issues
+//    S_i = Q_i K^T into TMEM and O_i += P_i V with P read from TMEM and V an MN-major operand straight from
+//    its [tokens, kv_heads, dim] layout, interleaving the two tiles; warps 2-17 (two groups of eight, a
+//    thread = one query row and one half of the keys, so two warps per scheduler work on each group) run the
+//    online softmax (tcgen05.ld, packed f32x2 math, three quarters of the exponentials on the transcendental
+//    unit and one quarter as a cubic on the FMA pipe), write P as bf16 over the first half of S_i
+//    (tcgen05.st), and rescale O_i in TMEM only when a row's running maximum grows by more than 2^8 (the
+//    probabilities stay <= 256 in between, which fp32 accumulation and bf16 P hold without loss of relative
+//    precision).
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -72,26 +74,6 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const void* __restr
   }
 }
 
-// ---------------- V transpose: [tokens, kv_heads, dim] -> [kv_heads, dim, tokens_padded] (bf16) ----------------
-__global__ void transpose_v_kernel(const uint16_t* __restrict__ v, int64_t tokens, int64_t kv_heads, int64_t dim,
-                                   int64_t tp, uint16_t* __restrict__ vt) {
-  __shared__ uint16_t tile[32][33];
-  const int64_t rows = kv_heads * dim;  // output rows
-  const int64_t tx = (int64_t)blockIdx.x * 32, ry = (int64_t)blockIdx.y * 32;
-  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
-    // read: token tx + threadIdx.x... as the fast index of the input is dim, read input rows = tokens
-    const int64_t t = tx + yy, r = ry + threadIdx.x;  // input element (token t, (g, d) = r)
-    uint16_t val = 0;
-    if (t < tokens && r < rows) val = v[t * rows + r];
-    tile[yy][threadIdx.x] = val;
-  }
-  __syncthreads();
-  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
-    const int64_t r = ry + yy, t = tx + threadIdx.x;
-    if (r < rows && t < tp) vt[r * tp + t] = tile[threadIdx.x][yy];
-  }
-}
-
 // ---------------- tcgen05 flash attention ----------------
 // Blackwell packed-pair and 3-input forms (PTX ISA 8.6+ for sm_100a): one instruction per two values
 __device__ __forceinline__ float max3f(float a, float b, float c) {
@@ -100,16 +82,14 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+  const float2 d = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(c0, c1));
+  d0 = d.x;
+  d1 = d.y;
 }
 __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  const float2 d = __fadd2_rn(make_float2(a0, a1), make_float2(b0, b1));
+  d0 = d.x;
+  d1 = d.y;
 }
 // the hardware 2^x (MUFU.EX2, results below 2^-126 flush to 0: negligible weights)
 __device__ __forceinline__ float exp2_approx(float x) {
@@ -117,6 +97,42 @@ __device__ __forceinline__ float exp2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for two x <= 2^22 on the FMA pipe, leaving the transcendental unit to the other exponentials of the row:
+// x = n + f with n = floor(x) (an add rounding toward -inf against 1.5 * 2^23 leaves n in the low mantissa bits),
+// 2^f on [0, 1) by a cubic 1 + f (c1 + f (c2 + f c3)), and n added to the result's exponent field. The cubic is a
+// relative-error minimax fit of 2^f on [0, 1) (Lawson's iteratively reweighted least squares): max relative
+// error 9.5e-5, below bf16's 2^-9. x is clamped to -126 first, so a masked key (x = -inf) weighs 2^-126 ~ 1e-38.
+__device__ __forceinline__ void exp2_poly2(float& y0, float& y1, float x0, float x1) {
+  constexpr float C1 = 0.69507056f, C2 = 0.22765099f, C3 = 0.07714326f, MAGIC = 12582912.f;
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float n0, n1, f0, f1, p0, p1;
+  const float2 t = __fadd2_rd(make_float2(x0, x1), make_float2(MAGIC, MAGIC));
+  const float t0 = t.x, t1 = t.y;
+  fadd2(n0, n1, t0, t1, -MAGIC, -MAGIC);  // floor(x), exact
+  fadd2(f0, f1, x0, x1, -n0, -n1);        // f in [0, 1)
+  ffma2(p0, p1, f0, f1, C3, C3, C2, C2);
+  ffma2(p0, p1, p0, p1, f0, f1, C1, C1);
+  ffma2(p0, p1, p0, p1, f0, f1, 1.f, 1.f);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+// two non-negative f32 as bf16x2 (lo in the low half) with integer ops instead of the conversion unit: round to
+// nearest by adding half a bf16 ulp to the bits (ties away from zero), then keep the high halves
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+
+// which pair slots (e mod 8) of a row take the FMA-pipe exponential instead of MUFU.EX2. 0: none. Measured on
+// config 3's attention (4608 tokens, 24 heads): none 258 us, a quarter 274 us, three eighths 280 us, a half
+// 279 us. The softmax warps are bound by instruction issue, not by the transcendental unit.
+#ifndef FA_POLY_MASK
+#define FA_POLY_MASK 0x00
+#endif
+// 1: pack P to bf16 with cvt.rn.bf16x2.f32 (one instruction per pair); 0: with integer rounding (three)
+#ifndef FA_PACK_CVT
+#define FA_PACK_CVT 0
+#endif
 
 namespace fa {
 struct Params {
@@ -130,7 +146,7 @@ struct Params {
 
 // ---------------- two query tiles per CTA, P in TMEM ----------------
 // One CTA = 256 queries (two 128-row tiles) of one head; K and V tiles of 128 keys are loaded once for both.
-// TMEM (512 columns): S_i at 128 i, O_i at 256 + 128 i. Each softmax group (4 warps, thread = query row) turns
+// TMEM (512 columns): S_i at 128 i, O_i at 256 + 128 i. Each softmax group (8 warps, thread = query row x half) turns
 // S_i into bf16 P written back over the first 64 columns of S_i, and O_i += P_i V_j reads P straight from TMEM
 // (no shared-memory round trip for P). The MMA warp interleaves the two tiles:
 //     S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) PV1(1) S1(2) | ...
@@ -147,18 +163,21 @@ constexpr int V_OFF = K_OFF + STAGES * TILE;
 constexpr int BAR_OFF = V_OFF + STAGES * TILE;
 // barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[QT], p_full[QT], pv_done[QT], drain
 constexpr int NUM_BARS = 1 + 8 + 3 * QT + 1;
-constexpr int TOTAL = BAR_OFF + NUM_BARS * 8 + 16;
+constexpr int RED_OFF = BAR_OFF + NUM_BARS * 8 + 16;              // row maxima (two tile parities) and row sums
+constexpr int TOTAL = RED_OFF + (2 * QT * 2 * BQ + QT * 2 * BQ) * 4;
 constexpr int ALLOC = TOTAL + 1024;
-constexpr int THREADS = 64 + QT * 128;
+constexpr int SOFTMAX_WARPS = 8;                                   // per query tile: 4 row quarters x 2 key halves
+constexpr int THREADS = 64 + QT * SOFTMAX_WARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t O_COL = 256;
 constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t IDESC_V = IDESC | (1u << 16);  // B (V) MN-major
 constexpr float RESCALE_LOG2 = 8.f;
 }  // namespace fa2
 
 __global__ void __launch_bounds__(fa2::THREADS, 1)
     flash_attn2_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_vt, const fa::Params p) {
+                       const __grid_constant__ CUtensorMap tm_v, const fa::Params p) {
   using namespace tc;
   using namespace fa2;
   extern __shared__ uint8_t smem_raw[];
@@ -193,7 +212,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
     }
     for (int i = 0; i < QT; i++) {
       mbar_init(S_FULL(i), 1);
-      mbar_init(P_FULL(i), 4);
+      mbar_init(P_FULL(i), SOFTMAX_WARPS);
       mbar_init(PV_DONE(i), 1);
     }
     mbar_init(DRAIN, 1);
@@ -218,7 +237,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
       // K runs two tiles ahead of V: V_j, then K_{j+2} (its stage is freed once S0(j) and S1(j) are done)
       auto load_k = [&](int t) -> bool {
         const int st = t & 1;
-        if (!wait_bounded(K_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
+        if (!wait_fast(K_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
                           WAIT_LIMIT_NS, true))
           return false;
         const uint32_t dst = sbase + K_OFF + st * TILE;
@@ -229,13 +248,13 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
       };
       auto load_v = [&](int t) -> bool {
         const int st = t & 1;
-        if (!wait_bounded(V_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
+        if (!wait_fast(V_EMPTY(st), ((t >> 1) & 1) ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER,
                           WAIT_LIMIT_NS, true))
           return false;
         const uint32_t dst = sbase + V_OFF + st * TILE;
         mbar_expect_tx(V_FULL(st), TILE);
-        tma_load_2d(dst, &tm_vt, V_FULL(st), t * BK, (int32_t)(g * D));
-        tma_load_2d(dst + ATOM, &tm_vt, V_FULL(st), t * BK + 64, (int32_t)(g * D));
+        tma_load_2d(dst, &tm_v, V_FULL(st), (int32_t)(g * D), t * BK);  // V as stored: keys x 64 dims per box
+        tma_load_2d(dst + ATOM, &tm_v, V_FULL(st), (int32_t)(g * D + 64), t * BK);
         return true;
       };
       int k_issued = 0, v_issued = 0;
@@ -253,21 +272,21 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
         }
       }
       if (!ok) {  // the copies already issued land before the CTA exits
-        wait_bounded(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+        wait_fast(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
         for (int t = k_issued - 2 < 0 ? 0 : k_issued - 2; t < k_issued; t++)
-          wait_bounded(K_FULL(t & 1), (t >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+          wait_fast(K_FULL(t & 1), (t >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
         for (int t = v_issued - 2 < 0 ? 0 : v_issued - 2; t < v_issued; t++)
-          wait_bounded(V_FULL(t & 1), (t >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+          wait_fast(V_FULL(t & 1), (t >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      bool ok = wait_bounded(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true);
+      bool ok = wait_fast(Q_FULL, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true);
       tc_fence_after();
       // S_i(j) = Q_i K_j^T into TMEM columns [128 i, 128 i + 128)
       auto s_mma = [&](int i, int j) -> bool {
-        if (!wait_bounded(K_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
+        if (!wait_fast(K_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
           return false;
         tc_fence_after();
         const uint64_t qdesc = sw128_desc(sbase + Q_OFF + i * TILE);
@@ -280,18 +299,18 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
         umma_commit(S_FULL(i));
         return true;
       };
-      // O_i += P_i(j) V_j: A = P_i from TMEM columns [128 i, 128 i + 64), B = V_j^T from shared memory
+      // O_i += P_i(j) V_j: A = P_i from TMEM columns [128 i, 128 i + 64), B = V_j from shared memory, MN-major (dims
+      // contiguous, as V is stored): two 64-dim boxes of 128 keys, the second one ATOM bytes after the first
       auto pv_mma = [&](int i, int j) -> bool {
-        if (!wait_bounded(P_FULL(i), j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
-            !wait_bounded(V_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
+        if (!wait_spin(P_FULL(i), j & 1, 4096, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true) ||
+            !wait_fast(V_FULL(j & 1), (j >> 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true))
           return false;
         tc_fence_after();
-        const uint64_t vdesc = sw128_desc(sbase + V_OFF + (j & 1) * TILE);
+        const uint64_t vdesc = mn_sw128_desc(sbase + V_OFF + (j & 1) * TILE, ATOM);
 #pragma unroll
-        for (int kk = 0; kk < 8; kk++) {  // K = 128 keys: 8 MMAs of 16 keys = 8 TMEM columns of packed P each
-          const uint64_t off = (uint64_t)((kk >> 2) * (ATOM >> 4) + (kk & 3) * 2);
-          umma_tmem_a(tmem + O_COL + (uint32_t)(i * 128), tmem + (uint32_t)(i * 128 + kk * 8), vdesc + off, IDESC,
-                      (j | kk) != 0);
+        for (int kk = 0; kk < 8; kk++) {  // K = 128 keys: 8 MMAs of 16 keys (16 rows of 128 bytes) = 8 TMEM columns of P
+          umma_tmem_a(tmem + O_COL + (uint32_t)(i * 128), tmem + (uint32_t)(i * 128 + kk * 8),
+                      vdesc + (uint64_t)(kk * (16 * 128 >> 4)), IDESC_V, (j | kk) != 0);
         }
         umma_commit(PV_DONE(i));
         return true;
@@ -312,46 +331,55 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
       }
       // every MMA this thread issued completes before TMEM is freed
       umma_commit(DRAIN);
-      wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      wait_fast(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
     }
     __syncwarp();
   } else {
-    // softmax group grp (query tile), thread = query row r, TMEM lane r
-    const int grp = (warp - 2) >> 2;
+    // softmax: group grp (query tile i = grp) of 8 warps; a thread holds query row r (TMEM lane r) and one half of
+    // the 128 keys of a tile (and of the 128 output dims). The two warps of a row quarter exchange their halves'
+    // maxima through shared memory behind a 64-thread named barrier, so both take the same rescaling decisions.
+    const int sw = warp - 2;
+    const int grp = sw >> 3;
+    const int half = (sw >> 2) & 1;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_col = (uint32_t)(grp * 128), o_col = O_COL + (uint32_t)(grp * 128);
+    const uint32_t s_col = (uint32_t)(grp * 128), o_col = O_COL + (uint32_t)(grp * 128 + half * 64);
+    const uint32_t pair_bar = 1u + (uint32_t)(grp * 4 + quarter);
+    float* red_max = reinterpret_cast<float*>(smem + RED_OFF);         // [2 parities][QT][2 halves][128 rows]
+    float* red_sum = red_max + 2 * QT * 2 * BQ;                       // [QT][2 halves][128 rows]
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; j++) {
-      ok = wait_bounded(S_FULL(grp), j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
+      ok = wait_fast(S_FULL(grp), j & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
-      uint32_t sc[BK];
-#pragma unroll
-      for (int c = 0; c < BK / 32; c++)  // four loads in flight, one wait
-        tmem_ld32_async(tmem + lane_addr + s_col + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(sc + c * 32));
+      uint32_t sc[64];
+      tmem_ld32_async(tmem + lane_addr + s_col + (uint32_t)(half * 64), *reinterpret_cast<uint32_t(*)[32]>(sc));
+      tmem_ld32_async(tmem + lane_addr + s_col + (uint32_t)(half * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(sc + 32));
       tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(sc));
+      reg_fence(*reinterpret_cast<uint32_t(*)[32]>(sc + 32));
+      const int64_t valid = p.tokens - (int64_t)j * BK - half * 64;  // keys of this half that exist (warp-uniform)
+      if (valid < 64) {
 #pragma unroll
-      for (int c = 1; c < BK / 32; c++) reg_fence(*reinterpret_cast<uint32_t(*)[32]>(sc + c * 32));
-      const int64_t valid = p.tokens - (int64_t)j * BK;  // keys of this tile that exist (warp-uniform)
-      if (valid < BK) {
-#pragma unroll
-        for (int c = 0; c < BK; c++)
+        for (int c = 0; c < 64; c++)
           if (c >= valid) sc[c] = __float_as_uint(-INFINITY);
       }
       float mx[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++) mx[i] = __uint_as_float(sc[i]);
+      for (int i = 0; i < 4; i++) mx[i] = fmaxf(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]));
 #pragma unroll
-      for (int c = 4; c < BK; c += 8)
+      for (int c = 8; c < 64; c += 8)
 #pragma unroll
         for (int i = 0; i < 4; i++) mx[i] = max3f(mx[i], __uint_as_float(sc[c + 2 * i]), __uint_as_float(sc[c + 2 * i + 1]));
-      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
+      float* rm = red_max + ((j & 1) * QT + grp) * 2 * BQ;
+      rm[half * BQ + r] = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      // the exchange barrier also ANDs the two warps' wait results, so a pair always leaves the loop together
+      if (!named_bar_and(pair_bar, 64, ok)) {
+        ok = false;
+        break;
+      }
+      const float mt = fmaxf(rm[r], rm[BQ + r]) * p.scale_log2;
       float corr = 1.f;
       const bool grow = mt > m_used + RESCALE_LOG2;
       if (grow) {
@@ -361,26 +389,29 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
       }
       const float nm = -m_used;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 4 packed pairs of running sums
+      uint32_t pk[32];  // this half's 64 keys as 32 packed bf16 pairs: P columns [32 half, 32 half + 32) of S_i
 #pragma unroll
-      for (int half = 0; half < 2; half++) {  // P as 64 packed bf16 pairs over S's first 64 columns, 32 at a time
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 32; e++) {
-          const int c = half * 64 + 2 * e;
-          float x0, x1;
-          ffma2(x0, x1, __uint_as_float(sc[c]), __uint_as_float(sc[c + 1]), p.scale_log2, p.scale_log2, nm, nm);
-          const float e0 = exp2_approx(x0), e1 = exp2_approx(x1);
-          fadd2(acc[2 * (e & 3)], acc[2 * (e & 3) + 1], acc[2 * (e & 3)], acc[2 * (e & 3) + 1], e0, e1);
-          pk[e] = pack_bf16x2(e0, e1);
+      for (int e = 0; e < 32; e++) {
+        const int c = 2 * e;
+        float x0, x1, e0, e1;
+        ffma2(x0, x1, __uint_as_float(sc[c]), __uint_as_float(sc[c + 1]), p.scale_log2, p.scale_log2, nm, nm);
+        if ((FA_POLY_MASK >> (e & 7)) & 1) {  // a share of the row on the FMA pipe, the rest on the MUFU
+          exp2_poly2(e0, e1, x0, x1);
+        } else {
+          e0 = exp2_approx(x0);
+          e1 = exp2_approx(x1);
         }
-        tmem_st32(tmem + lane_addr + s_col + (uint32_t)(half * 32), pk);
+        fadd2(acc[2 * (e & 3)], acc[2 * (e & 3) + 1], acc[2 * (e & 3)], acc[2 * (e & 3) + 1], e0, e1);
+        pk[e] = FA_PACK_CVT ? pack_bf16x2(e0, e1) : pack_bf16x2_int(e0, e1);
       }
+      tmem_st32(tmem + lane_addr + s_col + (uint32_t)(half * 32), pk);
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
-      // O_i was scaled for the old maximum: bring it to the new one before PV_i(j) adds to it (PV_i(j-1) is done)
+      // O_i was scaled for the old maximum: bring this half of it to the new one before PV_i(j) adds to it
+      // (PV_i(j-1) is done: its commit preceded S_i(j)'s)
       if (__any_sync(0xffffffffu, grow && j > 0)) {
         const float f = (grow && j > 0) ? corr : 1.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; c++) {
+        for (int c = 0; c < 2; c++) {
           uint32_t u[32];
           tmem_ld32(tmem + lane_addr + o_col + (uint32_t)(c * 32), u);
 #pragma unroll
@@ -394,17 +425,21 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
       if (lane == 0) mbar_arrive(P_FULL(grp));
     }
     if (ok && nt > 0) {
-      ok = wait_bounded(PV_DONE(grp), (nt - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      // the row's sum over both halves of the keys
+      red_sum[(grp * 2 + half) * BQ + r] = l;
+      named_bar_sync(pair_bar, 64);
+      l += red_sum[(grp * 2 + (half ^ 1)) * BQ + r];
+      ok = wait_fast(PV_DONE(grp), (nt - 1) & 1, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (__all_sync(0xffffffffu, ok)) {
         tc_fence_after();
         const int64_t qi = q0 + grp * BQ + r;
         const float inv = 1.f / l;
 #pragma unroll
-        for (int c = 0; c < D / 32; c++) {
+        for (int c = 0; c < 2; c++) {  // this half's 64 output dims
           uint32_t u[32];
           tmem_ld32(tmem + lane_addr + o_col + (uint32_t)(c * 32), u);
           if (qi < p.tokens) {
-            const int64_t o = (qi * p.heads + h) * D + c * 32;
+            const int64_t o = (qi * p.heads + h) * D + half * 64 + c * 32;
             if (p.out_dtype == WE_BF16) {
               uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + o);
 #pragma unroll
@@ -473,22 +508,11 @@ bool flash_attention_supported(const AttnArgs& a) {
          al(a.out) && a.heads % a.kv_heads == 0 && a.tokens <= 0x7fffffffLL;
 }
 
-int64_t flash_attention_scratch_bytes(const AttnArgs& a) {
-  const int64_t tp = (a.tokens + 7) / 8 * 8;
-  return a.kv_heads * a.dim * tp * 2;
-}
-
-cudaError_t launch_flash_attention(const AttnArgs& a, void* vt_scratch, uint32_t* err, cudaStream_t st) {
-  const int64_t tp = (a.tokens + 7) / 8 * 8;
-  {
-    dim3 blk(32, 8), grd((unsigned)((tp + 31) / 32), (unsigned)((a.kv_heads * a.dim + 31) / 32));
-    transpose_v_kernel<<<grd, blk, 0, st>>>(static_cast<const uint16_t*>(a.v), a.tokens, a.kv_heads, a.dim, tp,
-                                            static_cast<uint16_t*>(vt_scratch));
-  }
+cudaError_t launch_flash_attention(const AttnArgs& a, uint32_t* err, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   if (!bf16_map(&mq, a.q, a.heads * a.dim, a.tokens, a.heads * a.dim * 2) ||
       !bf16_map(&mk, a.k, a.kv_heads * a.dim, a.tokens, a.kv_heads * a.dim * 2) ||
-      !bf16_map(&mv, vt_scratch, tp, a.kv_heads * a.dim, tp * 2))
+      !bf16_map(&mv, a.v, a.kv_heads * a.dim, a.tokens, a.kv_heads * a.dim * 2))
     return cudaErrorNotSupported;
   fa::Params p;
   p.tokens = a.tokens;

@@ -104,8 +104,7 @@ struct AttnArgs {
   int dtype, out_dtype;
 };
 bool flash_attention_supported(const AttnArgs& a);
-int64_t flash_attention_scratch_bytes(const AttnArgs& a);
-cudaError_t launch_flash_attention(const AttnArgs& a, void* vt_scratch, uint32_t* err, cudaStream_t st);
+cudaError_t launch_flash_attention(const AttnArgs& a, uint32_t* err, cudaStream_t st);
 cudaError_t launch_attention_simt(const AttnArgs& a, int sms, cudaStream_t st);
 
 }  // namespace we

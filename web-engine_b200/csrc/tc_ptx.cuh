@@ -53,6 +53,49 @@ static __device__ __noinline__ bool wait_bounded(uint32_t bar, uint32_t parity, 
   }
 }
 
+// Non-blocking test of a phase (mbarrier.test_wait): the fast path of a wait that has usually completed already.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// wait_bounded with an inline test first: a completed phase costs one instruction, not a call.
+__device__ __forceinline__ bool wait_fast(uint32_t bar, uint32_t parity, volatile int* abort_flag, uint32_t* err,
+                                          uint32_t code, uint64_t limit_ns, bool watch_abort) {
+  return mbar_test_wait(bar, parity) || wait_bounded(bar, parity, abort_flag, err, code, limit_ns, watch_abort);
+}
+
+// Polls the phase without suspending for up to `spins` tests, then falls back to the suspending bounded wait: for a
+// waiter whose wake-up latency is on the critical path (a suspended try_wait resumes some 100 ns late).
+__device__ __forceinline__ bool wait_spin(uint32_t bar, uint32_t parity, int spins, volatile int* abort_flag,
+                                          uint32_t* err, uint32_t code, uint64_t limit_ns, bool watch_abort) {
+  for (int i = 0; i < spins; i++)
+    if (mbar_test_wait(bar, parity)) return true;
+  return wait_bounded(bar, parity, abort_flag, err, code, limit_ns, watch_abort);
+}
+// Named barrier over `threads` threads (a multiple of 32) of the CTA; orders their shared-memory accesses.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Named barrier that also ANDs a predicate over its `threads` threads: every participant gets the same answer.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t threads, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return out != 0;
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t c0, int32_t c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
@@ -76,6 +119,17 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
   d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// MN-major operand written by TMA with SWIZZLE_128B: each K row holds 64 bf16 of MN in 128 bytes, K rows 128
+// bytes apart, 8-row K groups 1024 bytes apart (SBO), 64-element MN chunks `mn_chunk_bytes` apart (LBO).
+__device__ __forceinline__ uint64_t mn_sw128_desc(uint32_t saddr, uint32_t mn_chunk_bytes) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((mn_chunk_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)(1024 >> 4) << 32;
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;

@@ -986,13 +986,9 @@ int we_attention(we_ctx* ctx, const void* q, const void* k, const void* v, int32
   if (tokens <= 0 || heads <= 0) return WE_OK;
   we::AttnArgs a{q, k, v, out, tokens, heads, kv_heads, dim, causal ? 1 : 0, dtype, out_dtype};
   if (we::flash_attention_supported(a)) {
-    Scratch scratch(ctx);
-    void* vt;
-    int rc = scratch.take((size_t)we::flash_attention_scratch_bytes(a), &vt);
-    if (rc != WE_OK) return rc;
-    cudaError_t e = we::launch_flash_attention(a, vt, ctx->dev_err, ctx->stream);
+    cudaError_t e = we::launch_flash_attention(a, ctx->dev_err, ctx->stream);
     if (e == cudaSuccess) {
-      ctx->stats.launches += 2;
+      ctx->stats.launches++;
       return WE_OK;
     }
     if (e != cudaErrorNotSupported) return cuda_fail(ctx, e, "flash attention");
