@@ -278,21 +278,32 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
                                    "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
     # config 4's one image split over all ranks: sequence parallelism (rows sharded, heads exchanged by all-to-all)
     if world > 1:
-        sp = we.sequence.SequenceParallel(device=dev)
+        sp = we.sequence.SequenceParallel(device=dev)  # the peer-memory exchange kernel
+        sp_nccl = we.sequence.SequenceParallel(device=dev, peer=False)
 
         def step_sp():
             T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, sp=sp)
+
+        def step_sp_nccl():
+            T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, sp=sp_nccl)
 
         sp_steps = max(6, steps // 2)
         with ClockSampler(gpu) as sp_clocks:
             sp_ms = timed(step_sp, sp_steps, 3) / sp_steps
         per = sorted(step_ms or [sp_ms])
+        l0 = g.stats["launches"]
+        step_sp()
+        sp_launches = g.stats["launches"] - l0
+        nccl_ms = timed(step_sp_nccl, sp_steps, 2) / sp_steps
+        sp.destroy()
         out["step_config4_sequence_parallel"] = {
             "ms": sp_ms, "median_ms_this_rank": per[len(per) // 2], "steps": sp_steps, "n_gpus": world,
-            "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12,
-            "clocks": sp_clocks.summary(),
-            "note": "one 1024x1024 image's step over all GPUs: every rank runs the blocks on 4608 / n_gpus rows, "
-                    "q/k/v/o exchanged by NCCL all-to-all (heads / n_gpus heads per rank in attention)"}
+            "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12, "launches_per_step": sp_launches,
+            "nccl_all_to_all_ms": nccl_ms, "clocks": sp_clocks.summary(),
+            "note": "one 1024x1024 image's step over all GPUs: every rank runs the blocks on 4608 / n_gpus rows; "
+                    "q/k/v go to the ranks attending their heads and o comes back through the peer-memory exchange "
+                    "kernel (IPC-mapped HBM of every GPU, one kernel per exchange with a flag barrier); "
+                    "nccl_all_to_all_ms: the same step with NCCL all_to_all_single"}
 
     # config 5's batch: 8 images per step in total, split data-parallel across the ranks (no collective); each
     # rank runs its share as one token stream (every linear one GEMM over all its images' rows)

@@ -338,6 +338,37 @@ int we_streamer_release(we_streamer* s, int32_t layer);
 int we_streamer_stats(const we_streamer* s, uint64_t* copies, uint64_t* bytes_copied);
 int we_streamer_destroy(we_streamer* s);
 
+/* ---------------- peer memory for sequence parallelism (no counterpart in the reference) ----------------
+   The reference runs on one GPU. With one image's rows split over the GPUs of a node, its attention needs an
+   all-to-all of q, k, v and o per block. Each rank creates an exchange region of `bytes` in its own HBM
+   (we_peer_create), exports it (we_peer_export: an opaque blob of WE_PEER_HANDLE_BYTES), gathers every rank's
+   blob by any host channel, and opens them (we_peer_open, blobs in rank order; a blob equal to this rank's own
+   export maps to its own memory). we_peer_exchange then runs ONE kernel on the context's stream: for each copy,
+   peer p and row i it copies chunk_bytes from
+       src + p * src_peer_stride + i * src_row_stride                      (this rank's memory)
+   to  region_p + dst_offset + rank * dst_rank_stride + i * dst_row_stride  (rank p's region, over NVLink),
+   and then meets every rank at a flag barrier in the same memory, so kernels after it on the stream see every
+   rank's chunks. Every rank must issue the same exchanges in the same order. The barrier's wait is bounded by
+   timeout_ns (0: 2 s); on timeout the kernel sets the context's device error word (we_device_error) and returns.
+   Sources, chunks and strides must be multiples of 16 bytes; a copy may not run past the region. The kernel
+   can be captured in a CUDA graph (its epoch lives on the device). */
+#define WE_PEER_MAX 8
+#define WE_PEER_HANDLE_BYTES 128
+typedef struct we_peer we_peer;
+typedef struct {
+  const void* src;
+  int64_t rows;             /* rows per peer */
+  int64_t chunk_bytes;      /* bytes per (peer, row) */
+  int64_t src_row_stride, src_peer_stride;
+  int64_t dst_offset, dst_row_stride, dst_rank_stride;
+} we_peer_copy;
+int we_peer_create(we_ctx* ctx, int32_t rank, int32_t world, size_t bytes, we_peer** out);
+int we_peer_export(const we_peer* peer, void* handle);
+int we_peer_open(we_peer* peer, const void* handles);
+void* we_peer_region(const we_peer* peer);
+int we_peer_exchange(we_ctx* ctx, we_peer* peer, const we_peer_copy* copies, int32_t ncopies, uint64_t timeout_ns);
+int we_peer_destroy(we_peer* peer);
+
 /* ---------------- allocation-free linear (no counterpart in the reference) ----------------
    For callers that cannot allocate device memory: code inside someone else's CUDA-graph capture, a
    serving loop with a fixed memory budget, or a runtime whose allocator owns all device memory.

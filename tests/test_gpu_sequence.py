@@ -1,7 +1,10 @@
-"""Sequence parallelism of one image's step on 2 GPUs (one process each, NCCL): every rank runs the blocks on half
-of the rows, attention exchanges heads by all-to-all; the velocity must equal the one-GPU step's. 80 tokens (8
-text + 72 image), so rank 0's shard holds text and image rows and rank 1's image rows only. Needs two B200s;
-skipped otherwise. NVLS is off (NCCL_NVLS_ENABLE=0)."""
+"""Sequence parallelism of one image's step on 2 GPUs (one process each): every rank runs the blocks on half of the
+rows, attention exchanges heads all-to-all, through the peer-memory exchange kernel (we_peer_exchange) or NCCL;
+the velocity must equal the one-GPU step's. 80 tokens (8 text + 72 image), so rank 0's shard holds text and image
+rows and rank 1's image rows only. The peer case also checks the exchange itself bit for bit: scattering each
+rank's q rows and gathering them back through an identity "attention" returns them unchanged, and every rank
+receives exactly its heads of every rank's rows. Needs two B200s; skipped otherwise. NVLS is off
+(NCCL_NVLS_ENABLE=0)."""
 import os
 import sys
 
@@ -14,7 +17,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _rank_main(rank, world, port, errq):
+def _rank_main(rank, world, port, peer, errq):
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -45,12 +48,34 @@ def _rank_main(rank, world, port, errq):
         inp = T.StepInputs(g.buffer(bf16(lat)), h, w, 0.37, g.buffer(bf16(ctx)), text)
         v1, _ = T.transformer(g, wts, scfg, inp, dtype="bf16")
         one = g.read(v1, 16 * h * w * 4, np.float32).copy()
-        sp = we.sequence.SequenceParallel()
+        sp = we.sequence.SequenceParallel(peer=peer)
         v2, _ = T.transformer(g, wts, scfg, inp, dtype="bf16", sp=sp)
         got = g.read(v2, 16 * h * w * 4, np.float32).copy()
         err = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
         assert err < 1e-6, ("sequence-parallel step differs from the one-GPU step", err)
+        if peer:  # the exchange alone, bit for bit
+            t, heads, kvh, hb = 40, 4, 2, 256
+            rows = [np.random.default_rng(70 + r).integers(0, 65536, t * heads * 128, dtype=np.uint16)
+                    for r in range(world)]
+            kv = [np.random.default_rng(80 + r).integers(0, 65536, t * kvh * 128, dtype=np.uint16)
+                  for r in range(world)]
+            qb, kb = g.buffer(rows[rank]), g.buffer(kv[rank])
+            seen = {}
+
+            def identity(qh, kh, vh, oh):  # copies the received q block into the output
+                seen["q"] = g.read(qh, world * t * heads // world * hb, np.uint16).copy()
+                seen["k"] = g.read(kh, world * t * kvh // world * hb, np.uint16).copy()
+                g.copy(qh, 0, oh.data_ptr(), 0, world * t * heads // world * hb)
+
+            o = sp.exchange_heads(g, qb, kb, kb, t, heads, kvh, hb, identity)
+            back = g.read(o, t * heads * hb, np.uint16)
+            assert np.array_equal(back, rows[rank]), "scatter + gather did not return the rows"
+            hl, kl = heads // world, kvh // world
+            want_q = np.concatenate([x.reshape(t, heads, 128)[:, rank * hl:(rank + 1) * hl] for x in rows]).ravel()
+            want_k = np.concatenate([x.reshape(t, kvh, 128)[:, rank * kl:(rank + 1) * kl] for x in kv]).ravel()
+            assert np.array_equal(seen["q"], want_q) and np.array_equal(seen["k"], want_k)
         assert g.device_error() == 0
+        sp.destroy()
         g.destroy()
         dist.barrier()
         dist.destroy_process_group()
@@ -59,14 +84,15 @@ def _rank_main(rank, world, port, errq):
         raise
 
 
-def test_sequence_parallel_step_on_two_gpus():
+@pytest.mark.parametrize("peer", [True, False], ids=["peer", "nccl"])
+def test_sequence_parallel_step_on_two_gpus(peer):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     mp = torch.multiprocessing.get_context("spawn")
     errq = mp.SimpleQueue()
     world, port = 2, _free_port()
-    procs = [mp.Process(target=_rank_main, args=(r, world, port, errq)) for r in range(world)]
+    procs = [mp.Process(target=_rank_main, args=(r, world, port, peer, errq)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

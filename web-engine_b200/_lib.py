@@ -73,6 +73,16 @@ class StTensor(C.Structure):
                 ("offset", C.c_int64), ("size", C.c_int64)]
 
 
+class PeerCopy(C.Structure):
+    _fields_ = [("src", C.c_void_p), ("rows", C.c_int64), ("chunk_bytes", C.c_int64), ("src_row_stride", C.c_int64),
+                ("src_peer_stride", C.c_int64), ("dst_offset", C.c_int64), ("dst_row_stride", C.c_int64),
+                ("dst_rank_stride", C.c_int64)]
+
+
+PEER_MAX = 8
+PEER_HANDLE_BYTES = 128
+
+
 class ModDesc(C.Structure):
     _fields_ = [("scale", C.c_void_p), ("shift", C.c_void_p)]
 
@@ -155,6 +165,12 @@ _SIGS = {
     "we_st_read": (C.c_int, [_P, C.c_char_p, _P, _I64]),
     "we_st_upload": (C.c_int, [_P, _P, C.c_char_p, _P]),
     "we_st_close": (None, [_P]),
+    "we_peer_create": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_size_t, C.POINTER(C.c_void_p)]),
+    "we_peer_export": (C.c_int, [_P, _P]),
+    "we_peer_open": (C.c_int, [_P, _P]),
+    "we_peer_region": (C.c_void_p, [_P]),
+    "we_peer_exchange": (C.c_int, [_P, _P, _P, C.c_int32, C.c_uint64]),
+    "we_peer_destroy": (C.c_int, [_P]),
     "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
                                         C.c_uint32, C.c_char_p, C.c_size_t]),
 }

@@ -132,17 +132,25 @@ def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.
     raise ValueError(f"unknown block dtype {dtype}")
 
 
-def _attend_sp(graph, sp, q, k, v, o, t: int, cfg: BlockConfig) -> None:
-    """Attention of one image whose rows are sharded over sp's ranks: q/k/v go token shard -> head shard by
-    all-to-all, this rank attends heads / world heads over every token, the output comes back the same way."""
+def _attend_sp(graph, sp, q, k, v, t: int, cfg: BlockConfig):
+    """Attention of one image whose rows are sharded over sp's ranks: q/k/v go token shard -> head shard, this
+    rank attends heads / world heads over every token, the output comes back the same way. Returns this rank's
+    output rows [t, heads x 128] (bf16): in sp's peer region on the peer path, a graph buffer on the nccl one."""
     hb, T = cfg.head_dim * 2, t * sp.world
+    hl, kl = cfg.heads // sp.world, cfg.kv_heads // sp.world
+    if sp.peer:
+        def attend(qh, kh, vh, oh):
+            K.attention(graph, qh, kh, vh, T, hl, kl, cfg.head_dim, oh, dtype="bf16", out_dtype="bf16")
+
+        return sp.exchange_heads(graph, q, k, v, t, cfg.heads, cfg.kv_heads, hb, attend)
+    o = graph.buffer(t * cfg.hidden * 2)
     qh = sp.scatter_heads(graph, q, t, cfg.heads, hb, "q")
     kh = sp.scatter_heads(graph, k, t, cfg.kv_heads, hb, "k")
     vh = sp.scatter_heads(graph, v, t, cfg.kv_heads, hb, "v")
-    oh = sp.buffer("o_heads", T * (cfg.heads // sp.world) * hb)
-    K.attention(graph, qh, kh, vh, T, cfg.heads // sp.world, cfg.kv_heads // sp.world, cfg.head_dim, oh, dtype="bf16",
-                out_dtype="bf16")
+    oh = sp.buffer("o_heads", T * hl * hb)
+    K.attention(graph, qh, kh, vh, T, hl, kl, cfg.head_dim, oh, dtype="bf16", out_dtype="bf16")
     sp.gather_heads(graph, oh, t, cfg.heads, hb, o)
+    return o
 
 
 def _attend_images(graph, q, k, v, o, rows: int, cfg: BlockConfig, images: int, dtype: str) -> None:
@@ -247,11 +255,11 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
                       x_dtype="bf16", out_dtype="bf16")
         K.qknorm_rope(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, cfg.kv_heads, rope.pairs, kp, eps=cfg.eps,
                       x_dtype="bf16", out_dtype="bf16")
-    o = graph.buffer(t * hd * 2)
     if sp is None:
+        o = graph.buffer(t * hd * 2)
         _attend_images(graph, q, k, v, o, t, cfg, images, "bf16")
     else:
-        _attend_sp(graph, sp, q, k, v, o, t, cfg)
+        o = _attend_sp(graph, sp, q, k, v, t, cfg)
     if cfg.attn_gate:  # og = o * sigmoid(gate h), in the gate GEMM's epilogue
         og = graph.buffer(t * hd * 2)
         for p in parts:

@@ -22,6 +22,7 @@ enum : uint32_t {
   DEV_ERR_TIMEOUT_MMA = 2,
   DEV_ERR_TIMEOUT_EPILOGUE = 3,
   DEV_ERR_TIMEOUT_DRAIN = 4,
+  DEV_ERR_TIMEOUT_PEER = 5,  // a peer exchange waited longer than its timeout for another rank's flag
 };
 
 // ---- element decode / encode ----

@@ -10,8 +10,16 @@ heads -> all tokens, H/N heads), each rank attends its heads, and the output com
     [T, H/N, 128]  --all_to_all-->  [N, T/N, H/N, 128]  --we_head_groups-->  [T/N, H, 128]           (o)
 
 Per GPU and block that moves 4 x (N - 1)/N x T/N x H x 256 bytes: 12.4 MB at N = 8 for config 4, against about
-100 MB for the tensor-parallel all-gather / reduce-scatter of the same block. The collectives are NCCL through
-torch.distributed, on the torch stream the library's context uses.
+100 MB for the tensor-parallel all-gather / reduce-scatter of the same block.
+
+Two ways to run the exchange:
+  * peer (default): the library's peer-memory exchange (we_peer_exchange). Each rank's exchange region is opened
+    by every other rank through CUDA IPC, and ONE kernel per exchange writes every (rank, token) chunk of q, k
+    and v straight into the rank that attends those heads, over NVLink, then meets the others at a flag barrier
+    in the same memory; the output comes back the same way. Three launches per block, no collective library on
+    the data path, and the step can be captured in a CUDA graph. The regions alternate between even and odd
+    blocks (a rank can never be two exchanges ahead of another).
+  * nccl: we_head_groups to regroup the rows, then NCCL all_to_all_single through torch.distributed.
 """
 from __future__ import annotations
 
@@ -21,8 +29,73 @@ from . import _lib as L
 from .graph import Graph, addr
 
 
+class PeerExchange:
+    """This rank's exchange region in peer memory and every other rank's, opened once (we_peer_create / export /
+    open; the handles travel through torch.distributed). exchange() runs one we_peer_exchange kernel."""
+
+    def __init__(self, graph: Graph, nbytes: int, group=None):
+        import torch.distributed as dist
+
+        self.graph = graph
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.nbytes = nbytes
+        h = C.c_void_p()
+        L.check(graph.ctx, L.lib().we_peer_create(graph.ctx, self.rank, self.world, nbytes, C.byref(h)))
+        self.handle = h
+        blob = (C.c_ubyte * L.PEER_HANDLE_BYTES)()
+        L.check(graph.ctx, L.lib().we_peer_export(h, blob))
+        blobs = [None] * self.world
+        dist.all_gather_object(blobs, bytes(blob), group=group)
+        allb = (C.c_ubyte * (L.PEER_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(blobs))
+        L.check(graph.ctx, L.lib().we_peer_open(h, allb))
+        self.region = L.lib().we_peer_region(h)
+
+    def exchange(self, copies: list, timeout_ns: int = 0) -> None:
+        """copies: dicts of we_peer_copy fields (src, rows, chunk_bytes, src_row_stride, src_peer_stride,
+        dst_offset, dst_row_stride, dst_rank_stride)."""
+        arr = (L.PeerCopy * len(copies))(*[L.PeerCopy(**c) for c in copies])
+        L.check(self.graph.ctx, L.lib().we_peer_exchange(self.graph.ctx, self.handle, arr, len(copies), timeout_ns))
+
+    def destroy(self) -> None:
+        if self.handle is not None:
+            L.lib().we_peer_destroy(self.handle)
+            self.handle = None
+
+
+def scatter_copy(src: int, t: int, heads: int, head_bytes: int, world: int, dst_offset: int) -> dict:
+    """we_peer_copy of rows [t, heads, head_bytes] -> each rank p receives heads [p H/w, (p+1) H/w) of these rows
+    at rows [rank t, rank t + t) of its [w t, H/w, head_bytes] block at dst_offset."""
+    g = heads // world * head_bytes
+    return dict(src=src, rows=t, chunk_bytes=g, src_row_stride=heads * head_bytes, src_peer_stride=g,
+                dst_offset=dst_offset, dst_row_stride=g, dst_rank_stride=t * g)
+
+
+def gather_copy(src: int, t: int, heads: int, head_bytes: int, world: int, dst_offset: int) -> dict:
+    """we_peer_copy of this rank's heads over every token, [w t, H/w, head_bytes] -> rank p receives rows
+    [p t, p t + t) as heads [rank H/w, ...) of its [t, H, head_bytes] block at dst_offset."""
+    g = heads // world * head_bytes
+    return dict(src=src, rows=t, chunk_bytes=g, src_row_stride=g, src_peer_stride=t * g, dst_offset=dst_offset,
+                dst_row_stride=heads * head_bytes, dst_rank_stride=g)
+
+
+def rows_copy(src: int, nbytes: int, dst_offset: int = 0) -> dict:
+    """we_peer_copy of nbytes to every rank, at dst_offset + rank * nbytes (an all-gather), in chunks that keep
+    many warps busy."""
+    c = _chunk(nbytes)
+    return dict(src=src, rows=nbytes // c, chunk_bytes=c, src_row_stride=c, src_peer_stride=0, dst_offset=dst_offset,
+                dst_row_stride=c, dst_rank_stride=nbytes)
+
+
+def _chunk(nbytes: int, limit: int = 4096) -> int:
+    """The largest power-of-two chunk <= limit (and >= 16) that divides nbytes."""
+    c = limit
+    while c > 16 and nbytes % c:
+        c //= 2
+    return c
+
+
 class SequenceParallel:
-    def __init__(self, group=None, device=None):
+    def __init__(self, group=None, device=None, peer: bool = True):
         import torch
         import torch.distributed as dist
 
@@ -32,6 +105,53 @@ class SequenceParallel:
         self.world = dist.get_world_size(group)
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self._bufs: dict = {}
+        self.peer = peer
+        self._px: dict = {}  # PeerExchange per use ("heads", "rows"), grown collectively when a call needs more
+        self._parity = 0
+
+    def _exchange(self, graph: Graph, key: str, nbytes: int) -> PeerExchange:
+        px = self._px.get(key)
+        if px is None or px.nbytes < nbytes or px.graph is not graph:
+            if px is not None:
+                px.destroy()
+            px = PeerExchange(graph, nbytes, self.group)
+            self._px[key] = px
+        return px
+
+    def destroy(self) -> None:
+        """Frees the peer regions once every rank is done with them (a collective: every rank calls it)."""
+        if self._px:
+            self.torch.cuda.synchronize(self.device)
+            self.dist.barrier(group=self.group)
+        for px in self._px.values():
+            px.destroy()
+        self._px.clear()
+
+    def exchange_heads(self, graph: Graph, q, k, v, local_tokens: int, heads: int, kv_heads: int, head_bytes: int,
+                       attend) -> int:
+        """Peer path of one block's attention: q [t, heads], k / v [t, kv_heads] rows of this rank (head_bytes per
+        head) go to the ranks that attend their heads; attend(qh, kh, vh, oh) runs this rank's heads over every
+        token ([world * t, heads / world] each, oh a buffer it fills); the output comes back. Returns the device
+        address of this rank's output rows [t, heads, head_bytes] (valid until the block after next)."""
+        if heads % self.world or kv_heads % self.world:
+            raise ValueError(f"{heads} / {kv_heads} heads do not split over {self.world} ranks")
+        t, w = local_tokens, self.world
+        T = t * w
+        gq, gk = heads // w * head_bytes, kv_heads // w * head_bytes
+        qb, kb, ob = T * gq, T * gk, t * heads * head_bytes
+        per_set = qb + 2 * kb + ob
+        px = self._exchange(graph, "heads", 2 * per_set)
+        base = self._parity * per_set
+        self._parity ^= 1
+        off_q, off_k, off_v, off_o = base, base + qb, base + qb + kb, base + qb + 2 * kb
+
+        px.exchange([scatter_copy(addr(q).value, t, heads, head_bytes, w, off_q),
+                     scatter_copy(addr(k).value, t, kv_heads, head_bytes, w, off_k),
+                     scatter_copy(addr(v).value, t, kv_heads, head_bytes, w, off_v)])
+        oh = self.buffer("o_heads", qb)
+        attend(px.region + off_q, px.region + off_k, px.region + off_v, oh)
+        px.exchange([gather_copy(oh.data_ptr(), t, heads, head_bytes, w, off_o)])
+        return px.region + off_o
 
     def shard(self, tokens: int) -> tuple:
         """(first row, rows) of this rank: tokens split into equal consecutive shards."""
@@ -73,7 +193,12 @@ class SequenceParallel:
                                                   self.world, gbytes, 0))
 
     def all_gather_rows(self, graph: Graph, local, local_bytes: int):
-        """Every rank's `local_bytes` in rank order (a torch buffer of world * local_bytes)."""
+        """Every rank's `local_bytes` in rank order: a device address (peer path) or a torch buffer (nccl) of
+        world * local_bytes."""
+        if self.peer:
+            px = self._exchange(graph, "rows", self.world * local_bytes)
+            px.exchange([rows_copy(addr(local).value, local_bytes)])
+            return px.region
         src = self.buffer("ag_src", local_bytes)
         graph.copy(local, 0, src.data_ptr(), 0, local_bytes)
         out = self.buffer("ag_out", local_bytes * self.world)
