@@ -295,15 +295,23 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
         step_sp()
         sp_launches = g.stats["launches"] - l0
         nccl_ms = timed(step_sp_nccl, sp_steps, 2) / sp_steps
+        sgr_sp = T.StepGraph(g, model, scfg, side, side, text_tokens, dtype="bf16", sp=sp)
+
+        def step_sp_graph():
+            T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, sp=sp, captured=sgr_sp)
+
+        sp_graph_ms = timed(step_sp_graph, sp_steps, 2) / sp_steps
+        sgr_sp.destroy()
         sp.destroy()
         out["step_config4_sequence_parallel"] = {
             "ms": sp_ms, "median_ms_this_rank": per[len(per) // 2], "steps": sp_steps, "n_gpus": world,
             "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12, "launches_per_step": sp_launches,
-            "nccl_all_to_all_ms": nccl_ms, "clocks": sp_clocks.summary(),
+            "graph_ms": sp_graph_ms, "nccl_all_to_all_ms": nccl_ms, "clocks": sp_clocks.summary(),
             "note": "one 1024x1024 image's step over all GPUs: every rank runs the blocks on 4608 / n_gpus rows; "
                     "q/k/v go to the ranks attending their heads and o comes back through the peer-memory exchange "
-                    "kernel (IPC-mapped HBM of every GPU, one kernel per exchange with a flag barrier); "
-                    "nccl_all_to_all_ms: the same step with NCCL all_to_all_single"}
+                    "kernel (IPC-mapped HBM of every GPU, one kernel per exchange with a flag barrier); graph_ms: this "
+                    "rank's blocks replayed from a CUDA graph; nccl_all_to_all_ms: the same step with NCCL "
+                    "all_to_all_single"}
 
     # config 5's batch: 8 images per step in total, split data-parallel across the ranks (no collective); each
     # rank runs its share as one token stream (every linear one GEMM over all its images' rows)

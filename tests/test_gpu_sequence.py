@@ -53,6 +53,12 @@ def _rank_main(rank, world, port, peer, errq):
         got = g.read(v2, 16 * h * w * 4, np.float32).copy()
         err = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
         assert err < 1e-6, ("sequence-parallel step differs from the one-GPU step", err)
+        if peer:  # the same shard's blocks replayed from a CUDA graph: bit for bit the eager sequence-parallel step
+            sgr = T.StepGraph(g, wts, scfg, h, w, text, dtype="bf16", sp=sp)
+            v3, _ = T.transformer(g, wts, scfg, inp, dtype="bf16", sp=sp, captured=sgr)
+            v3, _ = T.transformer(g, wts, scfg, inp, dtype="bf16", sp=sp, captured=sgr)  # a second replay
+            assert np.array_equal(g.read(v3, 16 * h * w * 4, np.float32), got), "captured SP step differs"
+            sgr.destroy()
         if peer:  # the exchange alone, bit for bit
             t, heads, kvh, hb = 40, 4, 2, 256
             rows = [np.random.default_rng(70 + r).integers(0, 65536, t * heads * 128, dtype=np.uint16)

@@ -127,6 +127,16 @@ class SequenceParallel:
             px.destroy()
         self._px.clear()
 
+    def prepare(self, graph: Graph, local_tokens: int, heads: int, kv_heads: int, head_bytes: int) -> None:
+        """Creates the exchange region and buffers that exchange_heads needs for this geometry now (a collective),
+        so that it allocates nothing later: needed before capturing the blocks in a CUDA graph."""
+        if not self.peer:
+            raise ValueError("only the peer exchange can be captured in a CUDA graph (NCCL calls are not recorded)")
+        t, w = local_tokens, self.world
+        gq, gk = heads // w * head_bytes, kv_heads // w * head_bytes
+        self._exchange(graph, "heads", 2 * (w * t * gq + 2 * w * t * gk + t * heads * head_bytes))
+        self.buffer("o_heads", w * t * gq)
+
     def exchange_heads(self, graph: Graph, q, k, v, local_tokens: int, heads: int, kv_heads: int, head_bytes: int,
                        attend) -> int:
         """Peer path of one block's attention: q [t, heads], k / v [t, kv_heads] rows of this rank (head_bytes per

@@ -153,24 +153,34 @@ class StepGraph:
     issues its ops. It owns the blocks' input rows and timestep vector; a step copies its own into them."""
 
     def __init__(self, graph: Graph, w: TransformerWeights, cfg: StepConfig, height: int, width: int,
-                 text_tokens: int, images: int = 1, dtype: str = "bf16"):
+                 text_tokens: int, images: int = 1, dtype: str = "bf16", sp=None):
+        """sp: a sequence.SequenceParallel (peer exchange) to record this rank's shard of one image's blocks; every
+        rank of the group builds its StepGraph at the same point (the exchange regions are created first)."""
         bc = cfg.block
         rows, cols = patch_grid(height, width)
         image = rows * cols
         T = text_tokens + image
         R = images * T
+        if sp is not None and (images != 1 or dtype != "bf16"):
+            raise ValueError("sequence parallelism splits one image's rows on the bf16 path")
+        r0, n = sp.shard(T) if sp is not None else (0, R)
         self.key = (height, width, text_tokens, images, dtype)
-        self.rows, self.hidden = R, bc.hidden
+        self.sp = sp
+        self.rows, self.hidden = n, bc.hidden
         cos, sin, pairs = _tables(text_tokens, rows, cols, tuple(cfg.axes), float(cfg.theta))
-        self.x_in = graph.buffer(R * bc.hidden * 4)
+        self.x_in = graph.buffer(n * bc.hidden * 4)
         self.tvec = graph.buffer(6 * bc.hidden * 4)
-        self.cos, self.sin = graph.buffer(np.tile(cos, images)), graph.buffer(np.tile(sin, images))
-        rope = ops.Rope(self.cos, self.sin, pairs, R)
+        if sp is not None:
+            self.cos, self.sin = graph.buffer(cos[r0 * pairs:(r0 + n) * pairs]), graph.buffer(sin[r0 * pairs:(r0 + n) * pairs])
+            sp.prepare(graph, n, bc.heads, bc.kv_heads, bc.head_dim * 2)
+        else:
+            self.cos, self.sin = graph.buffer(np.tile(cos, images)), graph.buffer(np.tile(sin, images))
+        rope = ops.Rope(self.cos, self.sin, pairs, n)
         with graph.capture() as cap:
             x = self.x_in
-            for parts in _layers(w, images, T, text_tokens, image, 0, R):
+            for parts in _layers(w, images, T, text_tokens, image, r0, n):
                 bm = graph.mark()
-                nxt = joint_block(graph, parts, bc, x, self.tvec, rope, dtype, images=images)
+                nxt = joint_block(graph, parts, bc, x, self.tvec, rope, dtype, images=images, sp=sp)
                 graph.release(bm, [nxt])
                 if x is not self.x_in:
                     graph.free(x)
@@ -244,8 +254,8 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
         rope = ops.Rope(graph.buffer(np.tile(cos, B)), graph.buffer(np.tile(sin, B)), pairs, R)
 
     if captured is not None:
-        if captured.key != (b0.height, b0.width, Lt, B, dtype) or sp is not None:
-            raise ValueError("the captured step is for another geometry, batch or dtype")
+        if captured.key != (b0.height, b0.width, Lt, B, dtype) or captured.sp is not sp:
+            raise ValueError("the captured step is for another geometry, batch, dtype or sequence-parallel group")
         x = captured.run(graph, x, tvec)  # graph-owned; the last layer reads it
     else:
         for i, parts in enumerate(_layers(w, B, T, Lt, image, r0, n)):
