@@ -165,7 +165,7 @@ def random_block(we, g, torch, dev, gen, bc):
     for name, d, std in (("norm1", hid, 0.5), ("norm2", hid, 0.5), ("norm_q", hd, 0.5), ("norm_k", hd, 0.5),
                          ("table", 6 * hid, 0.3)):
         w[name] = torch.randn(d, generator=gen, device=dev) * std
-    return we.blocks.BlockWeights(**w)
+    return we.blocks.fuse_qkv(g, we.blocks.BlockWeights(**w))
 
 
 def random_model(we, g, torch, dev, gen, scfg):

@@ -152,6 +152,12 @@ typedef struct {
   int32_t y_dtype;  /* WE_F32 | WE_BF16 */
   uint32_t flags;   /* WE_MM_ACCUMULATE */
   we_epilogue epi;  /* fused per-value steps (zero = none) */
+  /* Split output (part_n[0] > 0; y and y_stride unused): the first part_n[0] channels go to y_parts[0], the next
+     part_n[1] to y_parts[1], the rest (part_n[2]) to y_parts[2], each with rows part_n[i] values apart, so one
+     GEMM over concatenated weights (the q, k and v projections) fills separate buffers. The parts' widths sum
+     to n; the boundaries between parts are multiples of 256; no aux operand. */
+  void* y_parts[3];
+  int64_t part_n[3];
 } we_gemm_fp8_desc;
 int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* desc);
 /* kSplitFor (src/model/ops.ts:42-45). */

@@ -162,6 +162,69 @@ def test_block_bf16_fused_path(we, graph, mlp_act, kv_heads, per_channel):
     assert c["cosine"] >= 0.9999 and rel < 1e-2, (c, rel)
 
 
+@pytest.mark.parametrize("pair", ["0", "2"], ids=["1sm", "pair"])
+@pytest.mark.parametrize("m", [150, 1000])
+def test_gemm_split_output(we, graph, monkeypatch, pair, m):
+    """we_gemm_fp8 with a split output writes channels [0, 512), [512, 768), [768, 1024) to three buffers with rows
+    as wide as each part, bit for bit the columns of the unsplit output; bad splits are refused."""
+    monkeypatch.setenv("WE_TC_2SM", pair)
+    n, k = 1024, 256
+    x = bf16_round(randn(m * k, 31))
+    w = fast_fp8(n * k, 32)
+    cs = (np.abs(randn(n, 33, 0.004)) + np.float32(1e-3)).astype(np.float32)
+    bias = randn(n, 34)
+    mark = graph.mark()
+    hi, lo, rs = graph.buffer(m * k), graph.buffer(m * k), graph.buffer(m * 4)
+    we.kernels.quantize_act(graph, graph.buffer(bf16(x)), m, k, hi, lo, rs, terms=2)
+    wb, csb, bb = graph.buffer(w), graph.buffer(cs), graph.buffer(bias)
+    whole = graph.buffer(m * n * 2)
+    we.kernels.gemm_fp8(graph, hi, lo, rs, wb, whole, m, n, k, chan_scale=csb, bias=bb, y_dtype="bf16")
+    want = graph.read(whole, m * n * 2, np.uint16).reshape(m, n)
+    widths = (512, 256, 256)
+    parts = [(graph.buffer(m * wd * 2), wd) for wd in widths]
+    we.kernels.gemm_fp8(graph, hi, lo, rs, wb, None, m, n, k, chan_scale=csb, bias=bb, y_dtype="bf16", parts=parts)
+    c0 = 0
+    for buf, wd in parts:
+        got = graph.read(buf, m * wd * 2, np.uint16).reshape(m, wd)
+        assert np.array_equal(got, want[:, c0:c0 + wd])
+        c0 += wd
+    for bad in ([(parts[0][0], 384), (parts[1][0], 640)], [(parts[0][0], 512), (parts[1][0], 256)]):
+        with pytest.raises(we._lib.WeError, match="split output"):
+            we.kernels.gemm_fp8(graph, hi, lo, rs, wb, None, m, n, k, chan_scale=csb, y_dtype="bf16", parts=bad)
+    assert graph.device_error() == 0
+    graph.release(mark)
+
+
+@pytest.mark.parametrize("mlp_act,kv_heads,per_channel", [("swiglu", 2, False), ("gelu", 4, True)])
+def test_fused_qkv_equals_three_gemms(we, graph, mlp_act, kv_heads, per_channel):
+    """The block with wq, wk and wv fused into one GEMM (split epilogue, fuse_qkv) gives the same bits as with
+    three GEMMs: each output channel's dot product and scale are the same."""
+    cfg = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=kv_heads, head_dim=128, mlp_act=mlp_act,
+                                attn_gate=mlp_act == "swiglu")
+    text, side = 16, 20
+    tokens = text + side * side
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(text, side, side), (32, 48, 48), 1e4)
+    _, bw = make_block(we, graph, cfg, 210, per_channel, fuse=False)
+    x, temb = randn(tokens * cfg.hidden, 5, 1.0), randn(6 * cfg.hidden, 6, 0.3)
+    rope = we.Rope(graph.buffer(cos), graph.buffer(sin), pairs, tokens)
+    xb, tb = graph.buffer(x), graph.buffer(temb)
+
+    def run():
+        mark = graph.mark()
+        out = we.blocks.block(graph, bw, cfg, xb, tb, rope, dtype="bf16")
+        got = graph.read(out, tokens * cfg.hidden * 4, np.float32).copy()
+        graph.release(mark)
+        return got
+
+    three = run()
+    assert bw.wqkv is None
+    we.blocks.fuse_qkv(graph, bw)
+    assert bw.wqkv is not None and bw.wqkv.n == (cfg.heads + 2 * kv_heads) * 128
+    fused = run()
+    assert np.array_equal(three, fused)
+    assert graph.device_error() == 0
+
+
 @pytest.mark.parametrize("rows,d", [(300, 3072), (33, 512), (7, 64)])
 def test_add_norm_split_equals_add_then_norm_split(we, graph, rows, d):
     """we_add_norm_split: xo = x + r exactly, and the planes of norm(xo) exactly as we_norm_split makes them."""

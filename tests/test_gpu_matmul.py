@@ -172,7 +172,9 @@ PAIR_SHAPES = [(256, 256, 128), (37, 70, 128), (300, 520, 384), (130, 65, 144), 
 
 @pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
 @pytest.mark.parametrize("terms", [2, 1])
-def test_tc_pair_kernel_fp8(we, graph, force_pair_kernel, m, n, k, terms):
+@pytest.mark.parametrize("pair_bt", ["256", "128"])
+def test_tc_pair_kernel_fp8(we, graph, force_pair_kernel, monkeypatch, m, n, k, terms, pair_bt):
+    monkeypatch.setenv("WE_TC_PAIR_BT", pair_bt)  # 256 or 128 tokens per pair tile
     x = bf16_round(randn(m * k, 21))
     w = fast_fp8(n * k, 22)
     y, path = run_tc(we, graph, x, w, m, n, k, "fp8", scale=0.002, fast=terms == 1)
@@ -185,7 +187,9 @@ def test_tc_pair_kernel_fp8(we, graph, force_pair_kernel, m, n, k, terms):
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 256, 64), (200, 300, 264), (512, 512, 3072)])
-def test_tc_pair_kernel_bf16_and_epilogue(we, graph, force_pair_kernel, m, n, k):
+@pytest.mark.parametrize("pair_bt", ["256", "128"])
+def test_tc_pair_kernel_bf16_and_epilogue(we, graph, force_pair_kernel, monkeypatch, m, n, k, pair_bt):
+    monkeypatch.setenv("WE_TC_PAIR_BT", pair_bt)
     x = bf16_round(randn(m * k, 23))
     wf = bf16_round(randn(n * k, 24, 0.05))
     bias = randn(n, 25)

@@ -59,7 +59,7 @@ def make_linear(we, graph, n, k, seed, per_channel=True, std=0.02):
     return {"bytes": q, "n": n, "k": k, "scale": sc}, we.Linear(graph.buffer(q), "fp8", sc, n, k)
 
 
-def make_block(we, graph, cfg, seed, per_channel=False):
+def make_block(we, graph, cfg, seed, per_channel=False, fuse=True):
     """Random fp8 block weights on the device plus their host copies for the float64 reference."""
     hid, mlp, heads, kvh, hd = cfg.hidden, cfg.mlp, cfg.heads, cfg.kv_heads, cfg.head_dim
     shapes = {"wq": (heads * hd, hid), "wk": (kvh * hd, hid), "wv": (kvh * hd, hid), "wo": (hid, hid),
@@ -75,7 +75,7 @@ def make_block(we, graph, cfg, seed, per_channel=False):
            "norm_k": randn(hd, seed + 53, 0.5), "table": randn(6 * hid, seed + 54, 0.3)}
     host.update(vec)
     bw = we.blocks.BlockWeights(**dev, **{k: graph.buffer(v) for k, v in vec.items()})
-    return host, bw
+    return host, (we.blocks.fuse_qkv(graph, bw) if fuse else bw)
 
 
 def make_step(we, graph, scfg, seed, per_channel=False):

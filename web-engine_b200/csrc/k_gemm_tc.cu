@@ -50,7 +50,21 @@ struct Params {
   EpiOps epi;
   int epi_vec_ok;  // aux rows and the gate vector allow 16-byte loads
   uint32_t* err;
+  void* ys[3];         // split output (ys[0] set): channels [seg_end[i-1], seg_end[i]) go to ys[i], rows as wide
+  int64_t seg_end[3];  // as the part apart
 };
+
+// Where a tile's outputs go: the buffer, its first channel and its row stride (values).
+struct YOut {
+  void* y;
+  int64_t cofs, stride;
+};
+__device__ __forceinline__ YOut y_out(const Params& p, int64_t ch_base) {
+  if (!p.ys[0]) return YOut{p.y, 0, p.y_stride};
+  const int s = (ch_base >= p.seg_end[0]) + (ch_base >= p.seg_end[1]);
+  const int64_t lo = s ? p.seg_end[s - 1] : 0;
+  return YOut{p.ys[s], lo, p.seg_end[s] - lo};
+}
 
 template <int BT, int TERMS>
 struct Layout {
@@ -92,15 +106,15 @@ __device__ __forceinline__ bool epi_fast(const Params& p, int64_t tok, int64_t c
 }
 
 __device__ __forceinline__ void epi_fetch_iter(EpiFetch& f, int it, int lane, int64_t tok0, int64_t c0,
-                                               const Params& p) {
+                                               const YOut& yo, const Params& p) {
   const int64_t tok = tok0 + it * 8 + (lane >> 2);
   if (!epi_fast(p, tok, c0)) return;
-  const int64_t o = tok * p.y_stride + c0;
+  const int64_t o = tok * yo.stride + c0 - yo.cofs;
   if (p.accumulate) {
     if (p.y_dtype == WE_BF16) {
-      f.y[it][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.y) + o);
+      f.y[it][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(yo.y) + o);
     } else {
-      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const float*>(p.y) + o);
+      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const float*>(yo.y) + o);
       f.y[it][0] = q[0];
       f.y[it][1] = q[1];
     }
@@ -147,7 +161,7 @@ __device__ __forceinline__ void epi_gate(float (&gt)[8], int lane, int64_t ch_ba
 // `more`: the warp goes on to the chunk at tok0 + 32, whose operands are fetched into f as slots free up
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch& f, const float (&gt)[8],
                                                bool more, float* stage, int lane, int64_t tok0, int64_t ch_base,
-                                               float cs, float bias, const Params& p) {
+                                               float cs, float bias, const YOut& yo, const Params& p) {
   const int cg = (lane & 3) * 8;
   const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
   if (p.epi.act == WE_ACT_GELU_TANH) {
@@ -177,7 +191,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch
     const float4 b = *reinterpret_cast<const float4*>(stage + tr * EPI_LD + cg + 4);
     float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     if (epi_fast(p, tok, c0)) {
-      const int64_t o = tok * p.y_stride + c0;
+      const int64_t o = tok * yo.stride + c0 - yo.cofs;
       if (p.epi.aux_op) {
         float ax[8];
         unpack8(f.a[it], abf, ax);
@@ -200,11 +214,11 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch
         for (int e = 0; e < 8; e++) v[e] += yo[e];
       }
       if (ybf) {
-        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + o) =
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(yo.y) + o) =
             make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
                        pack_bf16x2(v[6], v[7]));
       } else {
-        float4* y = reinterpret_cast<float4*>(static_cast<float*>(p.y) + o);
+        float4* y = reinterpret_cast<float4*>(static_cast<float*>(yo.y) + o);
         y[0] = make_float4(v[0], v[1], v[2], v[3]);
         y[1] = make_float4(v[4], v[5], v[6], v[7]);
       }
@@ -213,7 +227,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch
 #pragma unroll
       for (int e = 0; e < 8; e++) {
         if (c0 + e >= p.n) break;
-        const int64_t o = tok * p.y_stride + c0 + e;
+        const int64_t o = tok * yo.stride + c0 + e - yo.cofs;
         float val = v[e];
         if (p.epi.aux_op) {
           const float ax = abf ? load_act<WE_BF16>(p.epi.aux, o) : load_act<WE_F32>(p.epi.aux, o);
@@ -221,25 +235,25 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch
         }
         if (p.epi.gate) val *= gt[e];
         if (ybf) {
-          uint16_t* y = static_cast<uint16_t*>(p.y);
+          uint16_t* y = static_cast<uint16_t*>(yo.y);
           y[o] = f32_to_bf16_bits(val + (p.accumulate ? bf16_bits_to_f32(y[o]) : 0.f));
         } else {
-          float* y = static_cast<float*>(p.y);
+          float* y = static_cast<float*>(yo.y);
           y[o] = val + (p.accumulate ? y[o] : 0.f);
         }
       }
     }
-    if (more && (p.accumulate || p.epi.aux_op)) epi_fetch_iter(f, it, lane, tok0 + 32, c0, p);
+    if (more && (p.accumulate || p.epi.aux_op)) epi_fetch_iter(f, it, lane, tok0 + 32, c0, yo, p);
   }
 }
 
 // Operands of a tile's first chunk, issued before the wait for its accumulator
 __device__ __forceinline__ void epi_fetch_first(EpiFetch& f, int lane, int64_t tok0, int64_t ch_base,
-                                                const Params& p) {
+                                                const YOut& yo, const Params& p) {
   if (!(p.accumulate || p.epi.aux_op)) return;
   const int64_t c0 = ch_base + (lane & 3) * 8;
 #pragma unroll
-  for (int it = 0; it < 4; it++) epi_fetch_iter(f, it, lane, tok0, c0, p);
+  for (int it = 0; it < 4; it++) epi_fetch_iter(f, it, lane, tok0, c0, yo, p);
 }
 
 // ---------------- the kernel ----------------
@@ -385,7 +399,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
       EpiFetch f;
       float gt[8];
-      epi_fetch_first(f, lane, tok_base, ch_base, p);
+      const YOut yo = y_out(p, ch_base);
+      epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
       epi_gate(gt, lane, ch_base, p);
       bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
@@ -403,7 +418,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(TEMPTY(ab));
         }
-        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, p);
+        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, yo, p);
         __syncwarp();
       }
       if (++ab == 2) {
@@ -678,7 +693,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
       EpiFetch f;
       float gt[8];
-      epi_fetch_first(f, lane, tok_base, ch_base, p);
+      const YOut yo = y_out(p, ch_base);
+      epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
       epi_gate(gt, lane, ch_base, p);
       bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
@@ -695,7 +711,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(map_rank(TEMPTY(ab), 0));
         }
-        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, p);
+        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, yo, p);
         __syncwarp();
       }
       if (++ab == 2) {
@@ -763,6 +779,14 @@ static Params make_params(const TcGemmArgs& a) {
   p.accumulate = a.accumulate;
   const int esz = a.y_dtype == WE_BF16 ? 2 : 4;
   p.vec_ok = ((uintptr_t)a.y % 16 == 0) && ((a.y_stride * esz) % 16 == 0);
+  for (int i = 0; i < 3; i++) {
+    p.ys[i] = a.ys[i];
+    p.seg_end[i] = a.seg_end[i];
+    if (a.ys[0] && a.ys[i]) {
+      const int64_t w = a.seg_end[i] - (i ? a.seg_end[i - 1] : 0);
+      p.vec_ok = p.vec_ok && ((uintptr_t)a.ys[i] % 16 == 0) && ((w * esz) % 16 == 0);
+    }
+  }
   p.epi = a.epi;
   const int asz = a.epi.aux_dtype == WE_BF16 ? 2 : 4;
   p.epi_vec_ok = (!a.epi.aux || (((uintptr_t)a.epi.aux % 16 == 0) && ((a.y_stride * asz) % 16 == 0))) &&
@@ -856,6 +880,19 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
     pair = v == 2 ? true : (v == 0 ? false : pair);
   }
   if (pair) {
+    // 256 tokens per pair tile. 128 fills the last wave better on some shapes (2304 tokens x 3072 channels:
+    // 2.92 waves of 74 pairs against 1.46) but halves each tile's reuse of W from L2 and measured slower on every
+    // shape tried (2304 x 3072 x 3072: 61.4 against 58.1 us; 4608 x 3072 x 3072: 100.7 against 73.4 us).
+    int pbt = 256;
+    if (const char* env = getenv("WE_TC_PAIR_BT")) {  // tuning / test override: 128 or 256 tokens per pair tile
+      const int v = atoi(env);
+      if (v == 128 || v == 256) pbt = v;
+    }
+    if (pbt == 128) {
+      if (a.kind_f16) return tc::run_pair<128, 1, true>(a, sms, st);
+      if (a.terms > 1) return tc::run_pair<128, 2, false>(a, sms, st);
+      return tc::run_pair<128, 1, false>(a, sms, st);
+    }
     if (a.kind_f16) return tc::run_pair<256, 1, true>(a, sms, st);
     if (a.terms > 1) return tc::run_pair<256, 2, false>(a, sms, st);
     return tc::run_pair<256, 1, false>(a, sms, st);

@@ -50,6 +50,8 @@ struct TcGemmArgs {
   int accumulate;
   EpiOps epi;
   uint32_t* dev_err;        // device error word
+  void* ys[3];              // split output (ys[0] set): channels [seg_end[i-1], seg_end[i]) to ys[i], rows as
+  int64_t seg_end[3];       // wide as the part apart; inner ends multiples of 256 (no tile straddles two parts)
 };
 // Returns cudaErrorNotSupported when the layout cannot go through TMA (alignment) so the caller can
 // use the CUDA-core kernel instead.

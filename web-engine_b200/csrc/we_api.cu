@@ -515,8 +515,24 @@ int we_matmul(we_ctx* ctx, const we_matmul_desc* d, const void* x, const void* w
 
 int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
   if (!ctx) return WE_EINVAL;
-  if (!d || !d->x_hi || !d->w || !d->y) return fail(ctx, WE_EINVAL, "we_gemm_fp8: missing operand");
+  const bool split = d && d->part_n[0] > 0;
+  if (!d || !d->x_hi || !d->w || (!d->y && !split)) return fail(ctx, WE_EINVAL, "we_gemm_fp8: missing operand");
   if (!act_dtype_ok(d->y_dtype)) return fail(ctx, WE_EINVAL, "y must be f32 or bf16");
+  int64_t ends[3] = {0, 0, 0};
+  if (split) {
+    bool ok = !d->epi.aux_op;
+    int64_t end = 0;
+    for (int i = 0; i < 3; i++) {
+      if (d->part_n[i] < 0) ok = false;
+      if (d->part_n[i] > 0 && !d->y_parts[i]) ok = false;
+      if (i > 0 && d->part_n[i] > 0 && end % 256) ok = false;  // a boundary inside a 256-channel tile
+      end += d->part_n[i];
+      ends[i] = end;
+    }
+    if (!ok || end != d->n)
+      return fail(ctx, WE_EINVAL, "split output needs parts whose widths sum to n, boundaries at multiples of 256, "
+                                  "a buffer for every part and no aux operand");
+  }
   if (d->m == 0 || d->n == 0) return WE_OK;
   we::TcGemmArgs t{};
   t.m = d->m;
@@ -535,6 +551,14 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
   t.bias = d->bias;
   t.y = d->y;
   t.y_stride = d->y_stride ? d->y_stride : d->n;
+  if (split) {
+    for (int i = 0; i < 3; i++) {
+      t.ys[i] = d->y_parts[i];
+      t.seg_end[i] = ends[i];
+    }
+    t.y = d->y_parts[0];
+    t.y_stride = d->part_n[0];
+  }
   t.y_dtype = d->y_dtype;
   t.accumulate = (d->flags & WE_MM_ACCUMULATE) ? 1 : 0;
   t.epi.act = d->epi.act;

@@ -214,15 +214,15 @@ def load_linear(graph: Graph, st: Safetensors, name: str) -> Linear:
 def load_block(graph: Graph, st: Safetensors, prefix: str, gate: bool = True, mlp_gate: bool = True):
     """One block's weights by the reference's names (loadAttentionMlp + loadBlock, weights.ts:70-91): attn.wq/wk/wv/
     gate/wo, mlp.gate/up/down, prenorm/postnorm scales, qk-norm scales and the modulation table mod.lin."""
-    from .block import BlockWeights
+    from .block import BlockWeights, fuse_qkv
 
     lin = lambda n: load_linear(graph, st, f"{prefix}.{n}")  # noqa: E731
     vec = lambda n: graph.buffer(load_floats(st, f"{prefix}.{n}"))  # noqa: E731
-    return BlockWeights(wq=lin("attn.wq"), wk=lin("attn.wk"), wv=lin("attn.wv"), wo=lin("attn.wo"),
+    return fuse_qkv(graph, BlockWeights(wq=lin("attn.wq"), wk=lin("attn.wk"), wv=lin("attn.wv"), wo=lin("attn.wo"),
                         mlp_up=lin("mlp.up"), mlp_down=lin("mlp.down"), norm1=vec("prenorm.scale"),
                         norm2=vec("postnorm.scale"), norm_q=vec("attn.qknorm.qnorm.scale"),
                         norm_k=vec("attn.qknorm.knorm.scale"), table=vec("mod.lin"),
-                        gate=lin("attn.gate") if gate else None, mlp_gate=lin("mlp.gate") if mlp_gate else None)
+                        gate=lin("attn.gate") if gate else None, mlp_gate=lin("mlp.gate") if mlp_gate else None))
 
 
 # ---------------- writing ----------------
