@@ -138,6 +138,7 @@ int we_matmul_check(we_ctx* ctx, const we_matmul_desc* desc);
    writes the split directly): y = (x_hi + x_lo) . W^T * row_scale[m] * (chan_scale[n] | scale) (+ bias)
    (+ y with WE_MM_ACCUMULATE). x_lo NULL = one term. K % 16 == 0, rows 16-byte aligned. The matmul
    of matmulWgsl (src/kernels/matmul.ts:118-178) with its activation quantisation hoisted out. */
+#define WE_GEMM_MAX_SEGMENTS 32
 typedef struct {
   int64_t m, n, k;
   const uint8_t* x_hi;
@@ -158,6 +159,19 @@ typedef struct {
      to n; the boundaries between parts are multiples of 256; no aux operand. */
   void* y_parts[3];
   int64_t part_n[3];
+  /* Two weight sets (nseg > 0): token rows [row_end[i - 1], row_end[i]) use set row_set[i] (row_end increasing, the
+     last one m, at most WE_GEMM_MAX_SEGMENTS segments). Set 0 is w, scale / chan_scale, bias and epi.gate above;
+     set 1 is w2 (same [n, k] layout), scale2 / chan_scale2, bias2 and gate2 (given iff epi.gate is). One GEMM
+     then runs a double block's text and image rows, or every image of a batch, each with its own weights. Inner
+     boundaries must be multiples of 64 rows (of 256 for the 2-SM kernel to be used). */
+  const uint8_t* w2;
+  float scale2;
+  const float* chan_scale2;
+  const float* bias2;
+  const float* gate2;
+  int32_t nseg;
+  int64_t row_end[WE_GEMM_MAX_SEGMENTS];
+  int32_t row_set[WE_GEMM_MAX_SEGMENTS];
 } we_gemm_fp8_desc;
 int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* desc);
 /* kSplitFor (src/model/ops.ts:42-45). */

@@ -84,6 +84,42 @@ def test_double_block_bf16(we, graph, mlp_act, gate):
     assert c["cosine"] >= 0.9999 and rel < 1e-2, (c, rel)
 
 
+@pytest.mark.parametrize("text,side,images,pair", [(64, 16, 1, "0"), (256, 16, 2, "2"), (64, 8, 3, "0")],
+                         ids=["1sm", "pair-2img", "3img"])
+@pytest.mark.parametrize("mlp_act,gate", [("gelu", False), ("swiglu", True)])
+def test_double_block_two_weight_sets_equal_per_part(we, graph, monkeypatch, text, side, images, pair, mlp_act, gate):
+    """A double block's text and image rows (for every image of a batch) run each linear as ONE GEMM whose token
+    tiles pick the text or image weights, scales and gates (we_gemm_fp8 row segments); the result equals the
+    per-part GEMMs bit for bit, with fused q/k/v and GQA."""
+    monkeypatch.setenv("WE_TC_2SM", pair)
+    cfg = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=2, head_dim=128, mlp_act=mlp_act,
+                                attn_gate=gate)
+    T = text + side * side
+    R = images * T
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(text, side, side), (16, 56, 56), 1e4)
+    _, dt_ = make_block(we, graph, cfg, 600, True)
+    _, di = make_block(we, graph, cfg, 677, False)
+    x, temb = randn(R * cfg.hidden, 601, 1.0), randn(6 * cfg.hidden, 602, 0.3)
+    parts = [p for i in range(images) for p in (we.blocks.Part(i * T, text, dt_), we.blocks.Part(i * T + text,
+                                                                                              T - text, di))]
+    assert we.blocks._weight_plan(parts, R)[0] == "two"
+    xb, tb = graph.buffer(x), graph.buffer(temb)
+    rope = we.Rope(graph.buffer(np.tile(cos, images)), graph.buffer(np.tile(sin, images)), pairs, R)
+
+    def run():
+        mark = graph.mark()
+        out = we.blocks.joint_block(graph, parts, cfg, xb, tb, rope, "bf16", images=images)
+        got = graph.read(out, R * cfg.hidden * 4, np.float32).copy()
+        graph.release(mark)
+        return got
+
+    grouped = run()
+    monkeypatch.setattr(we.blocks, "_weight_plan", lambda parts, t: None)
+    per_part = run()
+    assert np.array_equal(grouped, per_part)
+    assert graph.device_error() == 0
+
+
 def _step_case(we, graph, scfg, h, w, text, seed, dtype, per_channel=False):
     T = we.transformer
     host, wts = make_step(we, graph, scfg, seed, per_channel)

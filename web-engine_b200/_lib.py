@@ -52,11 +52,17 @@ class MatmulDesc(C.Structure):
         ("epi", Epilogue)]
 
 
+GEMM_MAX_SEGMENTS = 32
+
+
 class GemmFp8Desc(C.Structure):
     _fields_ = [("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64), ("x_hi", C.c_void_p), ("x_lo", C.c_void_p),
                 ("row_scale", C.c_void_p), ("w", C.c_void_p), ("scale", C.c_float), ("chan_scale", C.c_void_p),
                 ("bias", C.c_void_p), ("y", C.c_void_p), ("y_stride", C.c_int64), ("y_dtype", C.c_int32),
-                ("flags", C.c_uint32), ("epi", Epilogue), ("y_parts", C.c_void_p * 3), ("part_n", C.c_int64 * 3)]
+                ("flags", C.c_uint32), ("epi", Epilogue), ("y_parts", C.c_void_p * 3), ("part_n", C.c_int64 * 3),
+                ("w2", C.c_void_p), ("scale2", C.c_float), ("chan_scale2", C.c_void_p), ("bias2", C.c_void_p),
+                ("gate2", C.c_void_p), ("nseg", C.c_int32), ("row_end", C.c_int64 * GEMM_MAX_SEGMENTS),
+                ("row_set", C.c_int32 * GEMM_MAX_SEGMENTS)]
 
 
 class LinearDesc(C.Structure):

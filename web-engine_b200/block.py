@@ -260,10 +260,64 @@ def _joint_f32(graph, parts, cfg, x, tvec, rope, images=1):
     return out
 
 
-def _gemm(graph, split, lin: ops.Linear, y, t, y_dtype, **epi):
-    hi, lo, rs = split
-    K.gemm_fp8(graph, hi, lo, rs, lin.buffer, y, t, lin.n, lin.k, lin.scale, chan_scale=lin.chan_scale,
-               bias=lin.bias, y_dtype=y_dtype, **epi)
+def _weight_plan(parts, t: int):
+    """How a block's linears run over its parts: ("one", w) when one weight set covers rows [0, t) (one GEMM);
+    ("two", segments, w0, w1) when two weight sets tile [0, t) in row segments at multiples of 64 (one GEMM whose
+    token tiles pick their weights: a double block's text and image rows, for every image of a batch); None: one
+    GEMM per part."""
+    end = 0
+    for p in parts:
+        if p.row0 != end:
+            return None
+        end += p.rows
+    if end != t:
+        return None
+    ws: list = []
+    for p in parts:
+        if not any(p.w is w for w in ws):
+            ws.append(p.w)
+    if len(ws) == 1:
+        return ("one", ws[0])
+    if len(ws) != 2:
+        return None
+    segs: list = []
+    for p in parts:
+        st = 0 if p.w is ws[0] else 1
+        if segs and segs[-1][1] == st:
+            segs[-1] = (p.row0 + p.rows, st)
+        else:
+            segs.append((p.row0 + p.rows, st))
+    if len(segs) > 32 or any(e % 64 for e, _ in segs[:-1]):
+        return None
+    return ("two", segs, ws[0], ws[1])
+
+
+def _gemm_all(graph, plan, parts, split, width: int, lin, outs, y_dtype: str, mods=None, gate_key=None, aux=None,
+              aux_row_bytes: int = 0, **epi):
+    """The linear lin(w) of every part, over all rows: split holds the e4m3 planes of rows [0, t) (width values a
+    row), outs = [(buffer, channels), ...] the output rows (one buffer, or the q / k / v parts of a split output),
+    mods[id(w)][gate_key] the per-channel gate of a weight set, aux an epilogue operand over all rows."""
+    es = 2 if y_dtype == "bf16" else 4
+
+    def call(sr, rows, w, ys, aux_p, **more):
+        ln = lin(w)
+        gate = mods[id(w)][gate_key] if gate_key else None
+        y, pt = (ys[0][0], None) if len(ys) == 1 else (None, ys)
+        K.gemm_fp8(graph, *sr, ln.buffer, y, rows, ln.n, ln.k, ln.scale, chan_scale=ln.chan_scale, bias=ln.bias,
+                   y_dtype=y_dtype, gate=gate, aux=aux_p, parts=pt, **epi, **more)
+
+    if plan is not None and plan[0] == "one":
+        call(split, parts[-1].row0 + parts[-1].rows, plan[1], outs, aux)
+    elif plan is not None:
+        _, segs, w0, w1 = plan
+        l1 = lin(w1)
+        set2 = dict(w=l1.buffer, scale=l1.scale, chan_scale=l1.chan_scale, bias=l1.bias,
+                    gate=mods[id(w1)][gate_key] if gate_key else None)
+        call(split, segs[-1][0], w0, outs, aux, set2=set2, segments=segs)
+    else:
+        for p in parts:
+            call(_split_rows(split, p, width), p.rows, p.w, [(rows_at(b, p.row0, n * es), n) for b, n in outs],
+                 rows_at(aux, p.row0, aux_row_bytes) if aux is not None else None)
 
 
 def _split_rows(split, p: Part, width: int):
@@ -281,19 +335,19 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
         if id(p.w) not in shared:
             shared[id(p.w)] = modulation(graph, tvec, p.w.table, hd)
         mods.append(shared[id(p.w)])
+    plan = _weight_plan(parts, t)
     split = (graph.buffer(t * hd), graph.buffer(t * hd), graph.buffer(t * 4))
     q, k, v = graph.buffer(t * qw * 2), graph.buffer(t * kw * 2), graph.buffer(t * kw * 2)
     for p, mod in zip(parts, mods):
-        sr = _split_rows(split, p, hd)
-        K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *sr, scale=mod["prescale"],
-                     shift=mod["preshift"], eps=cfg.eps)
-        qp, kp, vp = rows_at(q, p.row0, qw * 2), rows_at(k, p.row0, kw * 2), rows_at(v, p.row0, kw * 2)
-        if p.w.wqkv is not None:  # one GEMM, its epilogue writing q, k and v
-            _gemm(graph, sr, p.w.wqkv, None, p.rows, "bf16", parts=[(qp, qw), (kp, kw), (vp, kw)])
-        else:
-            _gemm(graph, sr, p.w.wq, qp, p.rows, "bf16")
-            _gemm(graph, sr, p.w.wk, kp, p.rows, "bf16")
-            _gemm(graph, sr, p.w.wv, vp, p.rows, "bf16")
+        K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(split, p, hd),
+                     scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
+    if all(p.w.wqkv is not None for p in parts):  # one GEMM, its epilogue writing q, k and v
+        _gemm_all(graph, plan, parts, split, hd, lambda w: w.wqkv, [(q, qw), (k, kw), (v, kw)], "bf16")
+    else:
+        for name, buf, n in (("wq", q, qw), ("wk", k, kw), ("wv", v, kw)):
+            _gemm_all(graph, plan, parts, split, hd, lambda w, nm=name: getattr(w, nm), [(buf, n)], "bf16")
+    for p in parts:
+        qp, kp = rows_at(q, p.row0, qw * 2), rows_at(k, p.row0, kw * 2)
         pr = part_rope(rope, p)
         K.qknorm_rope(graph, qp, p.w.norm_q, pr.cos, pr.sin, p.rows, cfg.heads, rope.pairs, qp, eps=cfg.eps,
                       x_dtype="bf16", out_dtype="bf16")
@@ -306,34 +360,29 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
         o = _attend_sp(graph, sp, q, k, v, t, cfg)
     if cfg.attn_gate:  # og = o * sigmoid(gate h), in the gate GEMM's epilogue
         og = graph.buffer(t * hd * 2)
-        for p in parts:
-            _gemm(graph, _split_rows(split, p, hd), p.w.gate, rows_at(og, p.row0, hd * 2), p.rows, "bf16",
-                  aux_op="sigmoid_gate", aux=rows_at(o, p.row0, hd * 2), aux_dtype="bf16")
+        _gemm_all(graph, plan, parts, split, hd, lambda w: w.gate, [(og, hd)], "bf16", aux=o, aux_row_bytes=hd * 2,
+                  aux_op="sigmoid_gate", aux_dtype="bf16")
         o = og
     K.quantize_act(graph, o, t, hd, *split, terms=2)
-    a = graph.buffer(t * hd * 4)
-    for p, mod in zip(parts, mods):  # a = pregate wo(o), the gate in the epilogue
-        _gemm(graph, _split_rows(split, p, hd), p.w.wo, rows_at(a, p.row0, hd * 4), p.rows, "f32", gate=mod["pregate"])
+    a = graph.buffer(t * hd * 4)  # a = pregate wo(o), the gate in the epilogue
+    _gemm_all(graph, plan, parts, split, hd, lambda w: w.wo, [(a, hd)], "f32", shared, "pregate")
     x1 = graph.buffer(t * hd * 4)
     u = graph.buffer(t * cfg.mlp * 2)
-    g = graph.buffer(t * cfg.mlp * 2) if cfg.mlp_act == "swiglu" else None
     for p, mod in zip(parts, mods):  # x1 = x + a, and the norm + split of x1, in one pass
-        sr = _split_rows(split, p, hd)
         K.add_norm_split(graph, rows_at(x, p.row0, hd * 4), rows_at(a, p.row0, hd * 4), rows_at(x1, p.row0, hd * 4),
-                         p.w.norm2, p.rows, hd, *sr, scale=mod["postscale"], shift=mod["postshift"], eps=cfg.eps)
-        up = rows_at(u, p.row0, cfg.mlp * 2)
-        if cfg.mlp_act == "swiglu":
-            gp = rows_at(g, p.row0, cfg.mlp * 2)
-            _gemm(graph, sr, p.w.mlp_gate, gp, p.rows, "bf16")
-            _gemm(graph, sr, p.w.mlp_up, up, p.rows, "bf16", aux_op="swiglu", aux=gp, aux_dtype="bf16")
-        else:
-            _gemm(graph, sr, p.w.mlp_up, up, p.rows, "bf16", act="gelu_tanh")
+                         p.w.norm2, p.rows, hd, *_split_rows(split, p, hd), scale=mod["postscale"],
+                         shift=mod["postshift"], eps=cfg.eps)
+    if cfg.mlp_act == "swiglu":
+        g = graph.buffer(t * cfg.mlp * 2)
+        _gemm_all(graph, plan, parts, split, hd, lambda w: w.mlp_gate, [(g, cfg.mlp)], "bf16")
+        _gemm_all(graph, plan, parts, split, hd, lambda w: w.mlp_up, [(u, cfg.mlp)], "bf16", aux=g,
+                  aux_row_bytes=cfg.mlp * 2, aux_op="swiglu", aux_dtype="bf16")
+    else:
+        _gemm_all(graph, plan, parts, split, hd, lambda w: w.mlp_up, [(u, cfg.mlp)], "bf16", act="gelu_tanh")
     msplit = (graph.buffer(t * cfg.mlp), graph.buffer(t * cfg.mlp), split[2])
     K.quantize_act(graph, u, t, cfg.mlp, *msplit, terms=2)
-    dn = graph.buffer(t * hd * 4)
-    for p, mod in zip(parts, mods):  # dn = postgate down(m)
-        _gemm(graph, _split_rows(msplit, p, cfg.mlp), p.w.mlp_down, rows_at(dn, p.row0, hd * 4), p.rows, "f32",
-              gate=mod["postgate"])
+    dn = graph.buffer(t * hd * 4)  # dn = postgate down(m)
+    _gemm_all(graph, plan, parts, msplit, cfg.mlp, lambda w: w.mlp_down, [(dn, hd)], "f32", shared, "postgate")
     out = ops.add(graph, x1, dn, t * hd)  # x1 + postgate down(m): the block's output
     graph.release(mark, [out])
     return out

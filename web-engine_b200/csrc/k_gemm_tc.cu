@@ -52,7 +52,52 @@ struct Params {
   uint32_t* err;
   void* ys[3];         // split output (ys[0] set): channels [seg_end[i-1], seg_end[i]) go to ys[i], rows as wide
   int64_t seg_end[3];  // as the part apart
+  // second weight set: token rows in segments marked 1 use W2 (a second tensor map) with these scales, bias and
+  // gate; segments [row_end[i-1], row_end[i]) with row_end multiples of the token tile
+  const float* chan_scale2;
+  float scale2;
+  const float* bias2;
+  const float* gate2;
+  int nseg;
+  int32_t row_end[WE_GEMM_MAX_SEGMENTS];
+  uint8_t row_set[WE_GEMM_MAX_SEGMENTS];
 };
+
+// The token tile of the i-th tile in schedule order. With two weight sets the tiles of set 0 come first, then those
+// of set 1, so the CTAs sweep one set's weights at a time and keep them in L2 (alternating text and image rows of
+// a batch would otherwise switch weights every few tiles). Inner segment ends are multiples of bt.
+__device__ __forceinline__ int64_t tile_m(const Params& p, int64_t i, int bt) {
+  if (p.nseg <= 0) return i;
+  for (int set = 0; set < 2; set++) {
+    int64_t start = 0;
+    for (int k = 0; k < p.nseg; k++) {
+      const int64_t n = (p.row_end[k] - start + bt - 1) / bt;
+      if (p.row_set[k] == set) {
+        if (i < n) return start / bt + i;
+        i -= n;
+      }
+      start = p.row_end[k];
+    }
+  }
+  return 0;  // not reached: i < the number of token tiles
+}
+
+// The weight set of the token tile starting at tok_base (0 without segments).
+__device__ __forceinline__ int row_set(const Params& p, int64_t tok_base) {
+  for (int i = 0; i < p.nseg; i++)
+    if (tok_base < p.row_end[i]) return p.row_set[i];
+  return 0;
+}
+// The epilogue's per-channel operands of one weight set.
+struct SetOps {
+  const float* chan_scale;
+  float scale;
+  const float* bias;
+  const float* gate;
+};
+__device__ __forceinline__ SetOps set_ops(const Params& p, int set) {
+  return set ? SetOps{p.chan_scale2, p.scale2, p.bias2, p.gate2} : SetOps{p.chan_scale, p.scale, p.bias, p.epi.gate};
+}
 
 // Where a tile's outputs go: the buffer, its first channel and its row stride (values).
 struct YOut {
@@ -147,14 +192,15 @@ __device__ __forceinline__ void unpack8(const uint4 (&w)[2], bool bf16, float (&
 }
 
 // the per-tile channel gate of this lane's 8 post-transpose channels (zeros past n)
-__device__ __forceinline__ void epi_gate(float (&gt)[8], int lane, int64_t ch_base, const Params& p) {
+__device__ __forceinline__ void epi_gate(float (&gt)[8], int lane, int64_t ch_base, const float* gate,
+                                         const Params& p) {
   const int64_t c0 = ch_base + (lane & 3) * 8;
-  if (!p.epi.gate) return;
+  if (!gate) return;
   if (p.epi_vec_ok && c0 + 8 <= p.n) {
-    load8f(p.epi.gate, c0, gt);
+    load8f(gate, c0, gt);
   } else {
 #pragma unroll
-    for (int e = 0; e < 8; e++) gt[e] = (c0 + e < p.n) ? p.epi.gate[c0 + e] : 0.f;
+    for (int e = 0; e < 8; e++) gt[e] = (c0 + e < p.n) ? gate[c0 + e] : 0.f;
   }
 }
 
@@ -260,7 +306,8 @@ __device__ __forceinline__ void epi_fetch_first(EpiFetch& f, int lane, int64_t t
 template <int BT, int TERMS, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x0,
-                   const __grid_constant__ CUtensorMap tm_x1, const Params p) {
+                   const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_w2,
+                   const Params p) {
   using L = Layout<BT, TERMS>;
   constexpr int STAGES = L::STAGES;
   constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;
@@ -315,7 +362,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       int issued = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int32_t row_w = (int32_t)((t % tiles_n) * BM), row_x = (int32_t)((t / tiles_n) * BT);
+        const int32_t row_w = (int32_t)((t % tiles_n) * BM), row_x = (int32_t)(tile_m(p, t / tiles_n, BT) * BT);
+        const CUtensorMap* mw = row_set(p, row_x) ? &tm_w2 : &tm_w;
         for (int kb = 0; kb < p.num_kb; kb++) {
           if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
             ok = false;
@@ -324,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
           mbar_expect_tx(FULL(s), L::STAGE_BYTES);
           const int32_t kc = kb * KB_ELEMS;
-          tma_load_2d(st, &tm_w, FULL(s), kc, row_w);
+          tma_load_2d(st, mw, FULL(s), kc, row_w);
           tma_load_2d(st + L::W_BYTES, &tm_x0, FULL(s), kc, row_x);
           if (TERMS > 1) tma_load_2d(st + L::W_BYTES + L::X_BYTES, &tm_x1, FULL(s), kc, row_x);
           issued_ph[s] = ph;
@@ -393,15 +441,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       // everything that does not need the accumulator is loaded before waiting for it
       const int64_t ch_base = (t % tiles_n) * BM + q * 32;  // first output channel of this warp
       const int64_t ch = ch_base + lane;
-      const int64_t tok_base = (t / tiles_n) * BT;
+      const int64_t tok_base = tile_m(p, t / tiles_n, BT) * BT;
       const bool ch_ok = ch < p.n;
-      const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
-      const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+      const SetOps so = set_ops(p, row_set(p, tok_base));
+      const float cs = ch_ok ? (so.chan_scale ? so.chan_scale[ch] : so.scale) : 0.f;
+      const float bias = (ch_ok && so.bias) ? so.bias[ch] : 0.f;
       EpiFetch f;
       float gt[8];
       const YOut yo = y_out(p, ch_base);
       epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
-      epi_gate(gt, lane, ch_base, p);
+      epi_gate(gt, lane, ch_base, so.gate, p);
       bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -542,7 +591,8 @@ __host__ __device__ constexpr uint32_t make_idesc_pair() {
 template <int BT, int TERMS, bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x0,
-                    const __grid_constant__ CUtensorMap tm_x1, const Params p) {
+                    const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_w2,
+                    const Params p) {
   constexpr int ATOMS = F16 ? 2 : 1;
   using L = Layout2<BT, TERMS, ATOMS>;
   constexpr int STAGES = L::STAGES;
@@ -604,7 +654,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int64_t t = cid; t < tiles && ok; t += ncl) {
         const int32_t row_w = (int32_t)((t % tiles_n) * 2 * BM + rank * BM);
-        const int32_t row_x = (int32_t)((t / tiles_n) * BT + rank * (BT / 2));
+        const int64_t tok_tile = tile_m(p, t / tiles_n, BT) * BT;
+        const int32_t row_x = (int32_t)(tok_tile + rank * (BT / 2));
+        const CUtensorMap* mw = row_set(p, tok_tile) ? &tm_w2 : &tm_w;
         for (int kb = 0; kb < num_stages; kb++) {
           if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
             ok = false;
@@ -616,7 +668,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int a = 0; a < ATOMS; a++) {
             const int32_t kc = (kb * ATOMS + a) * KB_ELEMS;
-            tma_load_2d_pair(st + a * L::W_ATOM, &tm_w, bar, kc, row_w);
+            tma_load_2d_pair(st + a * L::W_ATOM, mw, bar, kc, row_w);
             tma_load_2d_pair(st + L::W_BYTES + a * L::X_ATOM, &tm_x0, bar, kc, row_x);
             if (TERMS > 1) tma_load_2d_pair(st + L::W_BYTES + L::X_BYTES + a * L::X_ATOM, &tm_x1, bar, kc, row_x);
           }
@@ -687,15 +739,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int64_t t = cid; t < tiles; t += ncl) {
       const int64_t ch_base = (t % tiles_n) * 2 * BM + rank * BM + q * 32;
       const int64_t ch = ch_base + lane;
-      const int64_t tok_base = (t / tiles_n) * BT;
+      const int64_t tok_base = tile_m(p, t / tiles_n, BT) * BT;
       const bool ch_ok = ch < p.n;
-      const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
-      const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+      const SetOps so = set_ops(p, row_set(p, tok_base));
+      const float cs = ch_ok ? (so.chan_scale ? so.chan_scale[ch] : so.scale) : 0.f;
+      const float bias = (ch_ok && so.bias) ? so.bias[ch] : 0.f;
       EpiFetch f;
       float gt[8];
       const YOut yo = y_out(p, ch_base);
       epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
-      epi_gate(gt, lane, ch_base, p);
+      epi_gate(gt, lane, ch_base, so.gate, p);
       bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -790,7 +843,16 @@ static Params make_params(const TcGemmArgs& a) {
   p.epi = a.epi;
   const int asz = a.epi.aux_dtype == WE_BF16 ? 2 : 4;
   p.epi_vec_ok = (!a.epi.aux || (((uintptr_t)a.epi.aux % 16 == 0) && ((a.y_stride * asz) % 16 == 0))) &&
-                 (!a.epi.gate || (uintptr_t)a.epi.gate % 16 == 0);
+                 (!a.epi.gate || (uintptr_t)a.epi.gate % 16 == 0) && (!a.gate2 || (uintptr_t)a.gate2 % 16 == 0);
+  p.chan_scale2 = a.chan_scale2;
+  p.scale2 = a.scale2;
+  p.bias2 = a.bias2;
+  p.gate2 = a.gate2;
+  p.nseg = a.nseg;
+  for (int i = 0; i < WE_GEMM_MAX_SEGMENTS; i++) {
+    p.row_end[i] = i < a.nseg ? (int32_t)a.row_end[i] : 0;
+    p.row_set[i] = i < a.nseg ? (uint8_t)a.row_set[i] : 0;
+  }
   p.err = a.dev_err;
   return p;
 }
@@ -806,13 +868,15 @@ static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
   } else {
     mx1 = mx0;
   }
+  CUtensorMap mw2 = mw;
+  if (a.nseg > 0 && !make_map(&mw2, a.w2, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
   Params p = make_params<F16>(a);
   auto kern = gemm_tc_kernel<BT, TERMS, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
   if (e != cudaSuccess) return e;
   const int64_t tiles = ((a.n + BM - 1) / BM) * ((a.m + BT - 1) / BT);
   const int grid = (int)(tiles < sms ? tiles : sms);
-  kern<<<grid, THREADS, L::ALLOC, st>>>(mw, mx0, mx1, p);
+  kern<<<grid, THREADS, L::ALLOC, st>>>(mw, mx0, mx1, mw2, p);
   return cudaGetLastError();
 }
 
@@ -828,6 +892,8 @@ static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
   } else {
     mx1 = mx0;
   }
+  CUtensorMap mw2 = mw;
+  if (a.nseg > 0 && !make_map(&mw2, a.w2, F16, a.k, a.n, a.w_stride_bytes, BM)) return cudaErrorNotSupported;
   Params p = make_params<F16>(a);
   auto kern = gemm_tc2_kernel<BT, TERMS, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
@@ -852,7 +918,7 @@ static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
     clusters = max_clusters;
   if (tiles < clusters) clusters = (int)tiles;
   cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, mw, mx0, mx1, p);
+  e = cudaLaunchKernelEx(&cfg, kern, mw, mx0, mx1, mw2, p);
   return e == cudaSuccess ? cudaGetLastError() : e;
 }
 }  // namespace tc
@@ -866,15 +932,28 @@ bool gemm_tc_supported(const TcGemmArgs& a) {
   if (a.w_stride_bytes < a.k * es || a.x_stride_bytes < a.k * es) return false;
   if (!al(a.w) || !al(a.x[0]) || (a.terms > 1 && !al(a.x[1]))) return false;
   if (a.m > 0x7fffffffLL || a.n > 0x7fffffffLL || a.k > 0x7fffffffLL) return false;
+  if (a.nseg < 0 || a.nseg > WE_GEMM_MAX_SEGMENTS || (a.nseg > 0 && (!a.w2 || !al(a.w2)))) return false;
+  if (a.nseg > 0 && (!a.epi.gate) != (!a.gate2)) return false;
   return true;
+}
+
+// The largest token tile (of 256 / 128 / 64) that every segment boundary of a two-weight-set GEMM is a multiple of
+// (256 without segments); 0 if none.
+static int seg_tile(const TcGemmArgs& a) {
+  int bt = 256;
+  for (int i = 0; i + 1 < a.nseg; i++)
+    while (bt >= 64 && a.row_end[i] % bt) bt /= 2;
+  return bt >= 64 ? bt : 0;
 }
 
 // Token tile: the largest of 256 / 128 / 64 that still gives every SM a tile, else 64.
 cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (!gemm_tc_supported(a)) return cudaErrorNotSupported;
+  const int max_bt = seg_tile(a);  // token tiles may not straddle two weight sets
+  if (max_bt == 0) return cudaErrorNotSupported;
   // 2-SM pairs (256 weight rows x 256 tokens per pair) when there are enough pair tiles to fill the
   // GPU; otherwise 1-SM tiles with the largest token tile (256 / 128 / 64) that gives every SM a tile.
-  bool pair = ((a.n + 255) / 256) * ((a.m + 255) / 256) >= sms / 2;
+  bool pair = max_bt == 256 && ((a.n + 255) / 256) * ((a.m + 255) / 256) >= sms / 2;
   if (const char* env = getenv("WE_TC_2SM")) {  // tuning / test override: 0 never, 2 always
     const int v = atoi(env);
     pair = v == 2 ? true : (v == 0 ? false : pair);
@@ -900,6 +979,7 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
   auto tiles = [&](int bt) { return tn * ((a.m + bt - 1) / bt); };
   int bt = tiles(256) >= sms ? 256 : (tiles(128) >= sms ? 128 : 64);
+  if (bt > max_bt) bt = max_bt;
   if (const char* env = getenv("WE_TC_BT")) {  // tuning override: 64, 128 or 256 tokens per tile
     const int v = atoi(env);
     if (v == 64 || v == 128 || v == 256) bt = v;

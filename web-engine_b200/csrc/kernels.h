@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/we_b200.h"
+
 namespace we {
 
 // Fused epilogue steps after v = acc * scales + bias (see we_epilogue in the public header).
@@ -52,6 +54,16 @@ struct TcGemmArgs {
   uint32_t* dev_err;        // device error word
   void* ys[3];              // split output (ys[0] set): channels [seg_end[i-1], seg_end[i]) to ys[i], rows as
   int64_t seg_end[3];       // wide as the part apart; inner ends multiples of 256 (no tile straddles two parts)
+  // second weight set (nseg > 0): token rows [row_end[i-1], row_end[i]) use set row_set[i]; set 1 takes w2 (same
+  // shape and stride as w), chan_scale2 / scale2, bias2 and gate2 (gate2 present iff epi.gate is)
+  const void* w2;
+  const float* chan_scale2;
+  float scale2;
+  const float* bias2;
+  const float* gate2;
+  int nseg;
+  int64_t row_end[WE_GEMM_MAX_SEGMENTS];
+  int row_set[WE_GEMM_MAX_SEGMENTS];
 };
 // Returns cudaErrorNotSupported when the layout cannot go through TMA (alignment) so the caller can
 // use the CUDA-core kernel instead.

@@ -533,12 +533,37 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
       return fail(ctx, WE_EINVAL, "split output needs parts whose widths sum to n, boundaries at multiples of 256, "
                                   "a buffer for every part and no aux operand");
   }
+  if (d->nseg < 0 || d->nseg > WE_GEMM_MAX_SEGMENTS)
+    return fail(ctx, WE_EINVAL, "two weight sets take 1 to " + std::to_string(WE_GEMM_MAX_SEGMENTS) + " row segments");
+  if (d->nseg > 0) {
+    bool ok = (!d->epi.gate) == (!d->gate2), any1 = false;
+    for (int i = 0; i < d->nseg; i++) {
+      ok = ok && d->row_end[i] > (i ? d->row_end[i - 1] : 0) && (d->row_set[i] == 0 || d->row_set[i] == 1);
+      any1 = any1 || d->row_set[i] == 1;
+    }
+    ok = ok && d->row_end[d->nseg - 1] == d->m && (!any1 || d->w2);
+    if (!ok)
+      return fail(ctx, WE_EINVAL, "row segments must increase to m, name set 0 or 1, have w2 for set 1, and give "
+                                  "gate2 iff epi.gate");
+  }
   if (d->m == 0 || d->n == 0) return WE_OK;
   we::TcGemmArgs t{};
   t.m = d->m;
   t.n = d->n;
   t.k = d->k;
   t.kind_f16 = 0;
+  if (d->nseg > 0) {
+    t.w2 = d->w2 ? d->w2 : d->w;
+    t.scale2 = d->scale2;
+    t.chan_scale2 = d->chan_scale2;
+    t.bias2 = d->bias2;
+    t.gate2 = d->gate2;
+    t.nseg = d->nseg;
+    for (int i = 0; i < d->nseg; i++) {
+      t.row_end[i] = d->row_end[i];
+      t.row_set[i] = d->row_set[i];
+    }
+  }
   t.terms = d->x_lo ? 2 : 1;
   t.x[0] = d->x_hi;
   t.x[1] = d->x_lo ? d->x_lo : d->x_hi;
@@ -569,7 +594,10 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
   t.dev_err = ctx->dev_err;
   if (!we::gemm_tc_supported(t))
     return fail(ctx, WE_EINVAL, "we_gemm_fp8 needs K a multiple of 16 and 16-byte aligned operands");
-  CK(we::launch_gemm_tc(t, ctx->sms, ctx->stream), "tcgen05 gemm");
+  const cudaError_t e = we::launch_gemm_tc(t, ctx->sms, ctx->stream);
+  if (e == cudaErrorNotSupported && t.nseg > 0)
+    return fail(ctx, WE_EINVAL, "row segment boundaries must be multiples of 64 rows");
+  CK(e, "tcgen05 gemm");
   ctx->stats.launches++;
   ctx->stats.tc_gemms++;
   return WE_OK;

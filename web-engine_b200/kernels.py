@@ -217,9 +217,12 @@ def quantize_act(graph: Graph, x, m: int, k: int, hi, lo, row_scale, terms: int 
 
 def gemm_fp8(graph: Graph, x_hi, x_lo, row_scale, w, y, m: int, n: int, k: int, scale: float = 1.0,
              chan_scale=None, bias=None, y_dtype="f32", y_stride: int = 0, accumulate: bool = False,
-             act=None, aux_op=None, aux=None, aux_dtype="f32", gate=None, parts=None) -> None:
+             act=None, aux_op=None, aux=None, aux_dtype="f32", gate=None, parts=None, set2=None,
+             segments=None) -> None:
     """The tcgen05 GEMM on an already-split activation (we_gemm_fp8); x_lo None = one term. parts: a split output,
-    [(buffer, width), ...] taking the channels in order (y is then unused)."""
+    [(buffer, width), ...] taking the channels in order (y is then unused). set2 / segments: a second weight set,
+    set2 = dict(w=, scale=, chan_scale=, bias=, gate=) used by the row segments marked 1 in segments =
+    [(row_end, set), ...]."""
     d = L.GemmFp8Desc(m, n, k, addr(x_hi).value, addr(x_lo).value, addr(row_scale).value, addr(w).value, scale,
                       addr(chan_scale).value, addr(bias).value, addr(y).value, y_stride, L.DTYPES[y_dtype],
                       L.MM_ACCUMULATE if accumulate else 0, epilogue(act, aux_op, aux, aux_dtype, gate))
@@ -227,6 +230,13 @@ def gemm_fp8(graph: Graph, x_hi, x_lo, row_scale, w, y, m: int, n: int, k: int, 
         for i, (pt, width) in enumerate(parts):
             d.y_parts[i] = addr(pt).value
             d.part_n[i] = width
+    if segments:
+        s2 = set2 or {}
+        d.w2, d.scale2 = addr(s2.get("w")).value, s2.get("scale", 1.0)
+        d.chan_scale2, d.bias2, d.gate2 = (addr(s2.get(x)).value for x in ("chan_scale", "bias", "gate"))
+        d.nseg = len(segments)
+        for i, (end, st) in enumerate(segments):
+            d.row_end[i], d.row_set[i] = end, st
     L.check(graph.ctx, L.lib().we_gemm_fp8(graph.ctx, C.byref(d)))
 
 
