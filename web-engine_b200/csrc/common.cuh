@@ -138,6 +138,34 @@ __device__ __forceinline__ float gelu_tanh_fast(float v) {
   return __fdividef(v, 1.f + __expf(-2.f * u));
 }
 
+// The hardware 2^x and 1/x (MUFU.EX2, MUFU.RCP; subnormal results flush to zero).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// GELU (tanh form) of two values with packed f32x2 arithmetic: v sigma(2u) = v / (1 + 2^x), where
+// x = -2 log2(e) sqrt(2/pi) (v + 0.044715 v^3) = v (K1 + K2 v^2). Same function as gelu_tanh_fast, about half the
+// instructions: the GEMM epilogue that applies it is bound by instruction issue.
+__device__ __forceinline__ float2 gelu_tanh2(float2 v) {
+  constexpr float K1 = -2.302208198144325f, K2 = -0.1029432395800235f;
+  const float2 x = __fmul2_rn(v, __ffma2_rn(__fmul2_rn(v, v), make_float2(K2, K2), make_float2(K1, K1)));
+  const float2 d = __fadd2_rn(make_float2(ex2_ftz(x.x), ex2_ftz(x.y)), make_float2(1.f, 1.f));
+  return __fmul2_rn(v, make_float2(rcp_ftz(d.x), rcp_ftz(d.y)));
+}
+// SiLU of two values: v / (1 + 2^(-v log2 e)).
+__device__ __forceinline__ float2 silu2(float2 v) {
+  constexpr float NL2E = -1.4426950408889634f;
+  const float2 x = __fmul2_rn(v, make_float2(NL2E, NL2E));
+  const float2 d = __fadd2_rn(make_float2(ex2_ftz(x.x), ex2_ftz(x.y)), make_float2(1.f, 1.f));
+  return __fmul2_rn(v, make_float2(rcp_ftz(d.x), rcp_ftz(d.y)));
+}
+
 // ---- warp reductions ----
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

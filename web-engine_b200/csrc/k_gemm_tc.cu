@@ -210,21 +210,18 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], EpiFetch
                                                float cs, float bias, const YOut& yo, const Params& p) {
   const int cg = (lane & 3) * 8;
   const float rs_lane = p.row_scale ? ((tok0 + lane < p.m) ? p.row_scale[tok0 + lane] : 0.f) : 1.f;
-  if (p.epi.act == WE_ACT_GELU_TANH) {
+  const float2 cs2 = make_float2(cs, cs), b2 = make_float2(bias, bias);
+  const int act = p.epi.act;
 #pragma unroll
-    for (int j = 0; j < 32; j++)
-      stage[j * EPI_LD + lane] =
-          gelu_tanh_fast(fmaf(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j), cs, bias));
-  } else if (p.epi.act == WE_ACT_SILU) {
-#pragma unroll
-    for (int j = 0; j < 32; j++) {
-      const float v = fmaf(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j), cs, bias);
-      stage[j * EPI_LD + lane] = v * sigmoid_fast(v);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; j++)
-      stage[j * EPI_LD + lane] = fmaf(__uint_as_float(r[j]) * __shfl_sync(0xffffffffu, rs_lane, j), cs, bias);
+  for (int j = 0; j < 32; j += 2) {
+    float2 v = __ffma2_rn(__fmul2_rn(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])),
+                                     make_float2(__shfl_sync(0xffffffffu, rs_lane, j),
+                                                 __shfl_sync(0xffffffffu, rs_lane, j + 1))),
+                          cs2, b2);
+    if (act == WE_ACT_GELU_TANH) v = gelu_tanh2(v);
+    else if (act == WE_ACT_SILU) v = silu2(v);
+    stage[j * EPI_LD + lane] = v.x;
+    stage[(j + 1) * EPI_LD + lane] = v.y;
   }
   __syncwarp();
   const int64_t c0 = ch_base + cg;
