@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int32_t row_w = (int32_t)((t % tiles_n) * BM), row_x = (int32_t)(tile_m(p, t / tiles_n, BT) * BT);
         const CUtensorMap* mw = row_set(p, row_x) ? &tm_w2 : &tm_w;
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
+          if (!wait_fast(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
             ok = false;
             break;
           }
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!ok) {  // let the loads already issued land before the CTA can exit
         for (int i = 0; i < STAGES && i < issued; i++)
-          wait_bounded(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+          wait_fast(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
       }
     }
     __syncwarp();
@@ -393,11 +393,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       int ab = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        if (!wait_bounded(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
+        if (!wait_fast(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BT);
         for (int kb = 0; kb < p.num_kb; kb++) {
-          if (!wait_bounded(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
+          if (!wait_fast(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
             ok = false;
             break;
           }
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // all MMAs issued by this thread complete before TMEM can be freed
       umma_commit(DRAIN);
-      wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      wait_fast(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
     }
     __syncwarp();
   } else {
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const YOut yo = y_out(p, ch_base);
       epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
       epi_gate(gt, lane, ch_base, so.gate, p);
-      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      bool ok = wait_fast(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
 #pragma unroll 1
@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int32_t row_x = (int32_t)(tok_tile + rank * (BT / 2));
         const CUtensorMap* mw = row_set(p, tok_tile) ? &tm_w2 : &tm_w;
         for (int kb = 0; kb < num_stages; kb++) {
-          if (!wait_bounded(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
+          if (!wait_fast(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
             ok = false;
             break;
           }
@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!ok && leader) {  // the pair's loads already issued land before the CTAs can exit
         for (int i = 0; i < STAGES && i < issued; i++)
-          wait_bounded(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+          wait_fast(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
       }
     }
     __syncwarp();
@@ -690,11 +690,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       int ab = 0;
       bool ok = true;
       for (int64_t t = cid; t < tiles && ok; t += ncl) {
-        if (!wait_bounded(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
+        if (!wait_fast(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BT);
         for (int kb = 0; kb < num_stages; kb++) {
-          if (!wait_bounded(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
+          if (!wait_fast(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
             ok = false;
             break;
           }
@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       umma_commit_pair_local(DRAIN);
-      wait_bounded(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      wait_fast(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
     }
     __syncwarp();
   } else {
@@ -746,7 +746,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const YOut yo = y_out(p, ch_base);
       epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
       epi_gate(gt, lane, ch_base, so.gate, p);
-      bool ok = wait_bounded(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      bool ok = wait_fast(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
 #pragma unroll 1
