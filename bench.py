@@ -530,8 +530,8 @@ def main() -> None:
     roofline = {"bound": "tensor", "achieved": gemm_tflops, "peak": bf16_peak, "unit": "TFLOP/s",
                 "frac": gemm_tflops / bf16_peak,
                 # dram__bytes_read.sum + dram__bytes_write.sum of this kernel, one ncu --set full capture of
-                # `python bench.py --profile-case` (cold caches): 87.2 MB + 83.5 MB per launch
-                "traffic": 170.7e6, "traffic_unit": "bytes per launch",
+                # `python bench.py --profile-case` (cold caches): 88.5 MB + 84.6 MB per launch
+                "traffic": 173.1e6, "traffic_unit": "bytes per launch",
                 "algorithmic_bytes_per_launch": N * K + 2 * M * K + 4 * M + 2 * M * N,
                 "kernel": "gemm_tc2_kernel<256, 2, kind::f8f6f4> (cta_group::2 pairs)",
                 "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst; two e4m3 MMAs per K step = bf16 rate)"
