@@ -476,6 +476,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
 #undef DRAIN
 }
 
+
 // ---------------- host side ----------------
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_attn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -522,9 +523,10 @@ cudaError_t launch_flash_attention(const AttnArgs& a, uint32_t* err, cudaStream_
   p.out = a.out;
   p.out_dtype = a.out_dtype;
   p.err = err;
+  const unsigned blocks = (unsigned)((a.tokens + fa2::QT * fa2::BQ - 1) / (fa2::QT * fa2::BQ));
   cudaError_t e = cudaFuncSetAttribute(flash_attn2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa2::ALLOC);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((a.tokens + fa2::QT * fa2::BQ - 1) / (fa2::QT * fa2::BQ)), (unsigned)a.heads);
+  dim3 grid(blocks, (unsigned)a.heads);
   flash_attn2_kernel<<<grid, fa2::THREADS, fa2::ALLOC, st>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
