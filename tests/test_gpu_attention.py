@@ -76,7 +76,7 @@ def test_flash_attention_bf16(we, graph, tokens, heads, kv_heads):
     k = bf16_round(randn(tokens * kv_heads * dim, 12))
     v = bf16_round(randn(tokens * kv_heads * dim, 13))
     got, launched = run(we, graph, q, k, v, tokens, heads, kv_heads, dim, dtype="bf16")
-    assert launched == 1  # the flash kernel alone: V is read as stored (MN-major operand), no transpose
+    assert launched in (1, 2)  # the flash kernel (V read as stored, no transpose), + the combine if keys split
     check(got, O.attention(q, k, v, tokens, heads, kv_heads, dim))
 
 
@@ -89,6 +89,38 @@ def test_flash_attention_large_scores_rescale(we, graph):
     v = bf16_round(randn(tokens * kv_heads * dim, 23))
     got, _ = run(we, graph, q, k, v, tokens, heads, kv_heads, dim, dtype="bf16")
     check(got, O.attention(q, k, v, tokens, heads, kv_heads, dim))
+
+
+@pytest.mark.parametrize("tokens,heads,kv_heads,splits", [(1000, 2, 1, "3"), (600, 4, 2, "2"), (700, 1, 1, "5")])
+def test_flash_attention_key_splits(we, graph, monkeypatch, tokens, heads, kv_heads, splits):
+    """Keys split over CTAs (WE_FA_SPLITS forces it; the library splits by itself when a grid would not fill the
+    GPU): unnormalised partial rows with their (max, sum), merged by the combine kernel."""
+    monkeypatch.setenv("WE_FA_SPLITS", splits)
+    dim = 128
+    q = bf16_round(randn(tokens * heads * dim, 31))
+    k = bf16_round(randn(tokens * kv_heads * dim, 32))
+    v = bf16_round(randn(tokens * kv_heads * dim, 33))
+    got, launched = run(we, graph, q, k, v, tokens, heads, kv_heads, dim, dtype="bf16")
+    assert launched == 2  # flash kernel + combine
+    check(got, O.attention(q, k, v, tokens, heads, kv_heads, dim))
+
+
+def test_flash_attention_splits_a_small_grid(we, graph):
+    """4608 tokens x 3 heads (one rank's heads at 8-way sequence parallelism): 54 CTAs, so the keys split 3 ways."""
+    tokens, heads, kv_heads, dim = 4608, 3, 3, 128
+    rng = np.random.default_rng(9)
+    q = bf16_round(rng.standard_normal(tokens * heads * dim, dtype=np.float32))
+    k = bf16_round(rng.standard_normal(tokens * heads * dim, dtype=np.float32))
+    v = bf16_round(rng.standard_normal(tokens * heads * dim, dtype=np.float32))
+    got, launched = run(we, graph, q, k, v, tokens, heads, kv_heads, dim, dtype="bf16")
+    assert launched == 2
+    rows = np.concatenate([np.arange(0, 16), rng.choice(tokens, 16, replace=False), np.arange(tokens - 16, tokens)])
+    qq, kk, vv = (a.reshape(tokens, heads, dim).astype(np.float64) for a in (q, k, v))
+    g3 = got.reshape(tokens, heads, dim)
+    for h in range(heads):
+        s = qq[rows, h] @ kk[:, h].T / np.sqrt(dim)
+        p = np.exp(s - s.max(1, keepdims=True))
+        check(g3[rows, h].ravel(), ((p / p.sum(1, keepdims=True)) @ vv[:, h]).ravel())
 
 
 def test_flash_attention_config3_rows(we, graph):

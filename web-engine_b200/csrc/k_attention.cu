@@ -141,6 +141,10 @@ struct Params {
   void* out;
   int out_dtype;
   uint32_t* err;
+  // key splits (gridDim.z > 1): split z takes key tiles [z nt / splits, (z + 1) nt / splits) and writes its
+  // unnormalised O rows (f32) to part_o[z][token][head][dim] and the rows' (max, sum) to part_ml[z][token][head]
+  float* part_o;
+  float* part_ml;
 };
 }  // namespace fa
 
@@ -200,7 +204,9 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
   const int64_t q0 = (int64_t)blockIdx.x * (QT * BQ);
   const int64_t h = blockIdx.y;
   const int64_t g = h / (p.heads / p.kv_heads);
-  const int nt = (int)((p.tokens + BK - 1) / BK);
+  const int nt_all = (int)((p.tokens + BK - 1) / BK);
+  const int j0 = (int)((int64_t)blockIdx.z * nt_all / gridDim.z);  // this split's first key tile
+  const int nt = (int)((int64_t)(blockIdx.z + 1) * nt_all / gridDim.z) - j0;
 
   if (threadIdx.x == 0) {
     mbar_init(Q_FULL, 1);
@@ -242,8 +248,8 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
           return false;
         const uint32_t dst = sbase + K_OFF + st * TILE;
         mbar_expect_tx(K_FULL(st), TILE);
-        tma_load_2d(dst, &tm_k, K_FULL(st), (int32_t)(g * D), t * BK);
-        tma_load_2d(dst + ATOM, &tm_k, K_FULL(st), (int32_t)(g * D + 64), t * BK);
+        tma_load_2d(dst, &tm_k, K_FULL(st), (int32_t)(g * D), (j0 + t) * BK);
+        tma_load_2d(dst + ATOM, &tm_k, K_FULL(st), (int32_t)(g * D + 64), (j0 + t) * BK);
         return true;
       };
       auto load_v = [&](int t) -> bool {
@@ -253,8 +259,8 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
           return false;
         const uint32_t dst = sbase + V_OFF + st * TILE;
         mbar_expect_tx(V_FULL(st), TILE);
-        tma_load_2d(dst, &tm_v, V_FULL(st), (int32_t)(g * D), t * BK);  // V as stored: keys x 64 dims per box
-        tma_load_2d(dst + ATOM, &tm_v, V_FULL(st), (int32_t)(g * D + 64), t * BK);
+        tma_load_2d(dst, &tm_v, V_FULL(st), (int32_t)(g * D), (j0 + t) * BK);  // V as stored: keys x 64 dims per box
+        tma_load_2d(dst + ATOM, &tm_v, V_FULL(st), (int32_t)(g * D + 64), (j0 + t) * BK);
         return true;
       };
       int k_issued = 0, v_issued = 0;
@@ -359,7 +365,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
       tmem_ld32_async(tmem + lane_addr + s_col + (uint32_t)(half * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(sc + 32));
       tmem_wait_ld(*reinterpret_cast<uint32_t(*)[32]>(sc));
       reg_fence(*reinterpret_cast<uint32_t(*)[32]>(sc + 32));
-      const int64_t valid = p.tokens - (int64_t)j * BK - half * 64;  // keys of this half that exist (warp-uniform)
+      const int64_t valid = p.tokens - (int64_t)(j0 + j) * BK - half * 64;  // keys of this half that exist (uniform)
       if (valid < 64) {
 #pragma unroll
         for (int c = 0; c < 64; c++)
@@ -434,6 +440,25 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
         tc_fence_after();
         const int64_t qi = q0 + grp * BQ + r;
         const float inv = 1.f / l;
+        if (p.part_o) {  // a key split: the unnormalised rows and (max, sum), merged by flash_combine_kernel
+          const int64_t row = ((int64_t)blockIdx.z * p.tokens + qi) * p.heads + h;
+#pragma unroll
+          for (int c = 0; c < 2; c++) {
+            uint32_t u[32];
+            tmem_ld32(tmem + lane_addr + o_col + (uint32_t)(c * 32), u);
+            if (qi < p.tokens) {
+              float4* dst = reinterpret_cast<float4*>(p.part_o + row * D + half * 64 + c * 32);
+#pragma unroll
+              for (int e = 0; e < 8; e++)
+                dst[e] = make_float4(__uint_as_float(u[4 * e]), __uint_as_float(u[4 * e + 1]),
+                                     __uint_as_float(u[4 * e + 2]), __uint_as_float(u[4 * e + 3]));
+            }
+          }
+          if (qi < p.tokens && half == 0) {
+            p.part_ml[2 * row] = m_used;
+            p.part_ml[2 * row + 1] = l;
+          }
+        } else {
 #pragma unroll
         for (int c = 0; c < 2; c++) {  // this half's 64 output dims
           uint32_t u[32];
@@ -457,6 +482,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
             }
           }
         }
+        }
       }
     }
   }
@@ -476,6 +502,39 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
 #undef DRAIN
 }
 
+
+// Merges the key splits of flash_attn2_kernel: per (token, head) row, with M the largest split maximum,
+// O = sum_z 2^(m_z - M) O_z / sum_z 2^(m_z - M) l_z (the maxima are in log2 units). One warp per row, 4 dims a lane.
+template <int OT>
+__global__ void __launch_bounds__(256) flash_combine_kernel(const float* __restrict__ part_o,
+                                                            const float* __restrict__ part_ml, int splits,
+                                                            int64_t rows, void* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float mx = -INFINITY;
+  for (int z = 0; z < splits; z++) mx = fmaxf(mx, part_ml[2 * ((int64_t)z * rows + row)]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float lsum = 0.f;
+  for (int z = 0; z < splits; z++) {
+    const int64_t zr = (int64_t)z * rows + row;
+    const float w = exp2f(part_ml[2 * zr] - mx);
+    lsum = fmaf(part_ml[2 * zr + 1], w, lsum);
+    const float4 o = reinterpret_cast<const float4*>(part_o + zr * 128)[lane];
+    acc.x = fmaf(o.x, w, acc.x);
+    acc.y = fmaf(o.y, w, acc.y);
+    acc.z = fmaf(o.z, w, acc.z);
+    acc.w = fmaf(o.w, w, acc.w);
+  }
+  const float inv = 1.f / lsum;
+  if (OT == WE_BF16) {
+    uint2* dst = reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + row * 128) + lane;
+    *dst = make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+  } else {
+    reinterpret_cast<float4*>(static_cast<float*>(out) + row * 128)[lane] =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  }
+}
 
 // ---------------- host side ----------------
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn_attn() {
@@ -509,7 +568,35 @@ bool flash_attention_supported(const AttnArgs& a) {
          al(a.out) && a.heads % a.kv_heads == 0 && a.tokens <= 0x7fffffffLL;
 }
 
-cudaError_t launch_flash_attention(const AttnArgs& a, uint32_t* err, cudaStream_t st) {
+int flash_attention_splits(const AttnArgs& a, int sms) {
+  const int64_t blocks = (a.tokens + fa2::QT * fa2::BQ - 1) / (fa2::QT * fa2::BQ);
+  const int64_t nt = (a.tokens + fa2::BK - 1) / fa2::BK;
+  const int64_t ctas = blocks * a.heads;
+  // A CTA (one per SM) costs about 15 key tiles of fixed work plus its key tiles (measured at 4608 tokens: 25 us +
+  // 1.7 us a tile), so splitting the keys pays only when it adds CTAs without adding a wave: pick the split count
+  // with the least waves x (15 + tiles per split), the combine costing about 3 tiles.
+  int splits = 1;
+  int64_t best = -1;
+  for (int s = 1; s <= 8 && s <= nt; s++) {
+    const int64_t waves = (ctas * s + sms - 1) / sms;
+    const int64_t cost = waves * (15 + (nt + s - 1) / s) + (s > 1 ? 3 : 0);
+    if (best < 0 || cost < best) {
+      best = cost;
+      splits = s;
+    }
+  }
+  if (const char* env = getenv("WE_FA_SPLITS")) {  // test / tuning override
+    const int v = atoi(env);
+    if (v >= 1 && v <= 8 && v <= nt) splits = v;
+  }
+  return splits;
+}
+
+int64_t flash_attention_scratch_bytes(const AttnArgs& a, int splits) {
+  return splits > 1 ? (int64_t)splits * a.tokens * a.heads * (fa2::D + 2) * 4 : 0;
+}
+
+cudaError_t launch_flash_attention(const AttnArgs& a, int splits, void* scratch, uint32_t* err, cudaStream_t st) {
   CUtensorMap mq, mk, mv;
   if (!bf16_map(&mq, a.q, a.heads * a.dim, a.tokens, a.heads * a.dim * 2) ||
       !bf16_map(&mk, a.k, a.kv_heads * a.dim, a.tokens, a.kv_heads * a.dim * 2) ||
@@ -523,11 +610,21 @@ cudaError_t launch_flash_attention(const AttnArgs& a, uint32_t* err, cudaStream_
   p.out = a.out;
   p.out_dtype = a.out_dtype;
   p.err = err;
+  p.part_o = splits > 1 ? static_cast<float*>(scratch) : nullptr;
+  p.part_ml = splits > 1 ? static_cast<float*>(scratch) + (int64_t)splits * a.tokens * a.heads * fa2::D : nullptr;
   const unsigned blocks = (unsigned)((a.tokens + fa2::QT * fa2::BQ - 1) / (fa2::QT * fa2::BQ));
   cudaError_t e = cudaFuncSetAttribute(flash_attn2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa2::ALLOC);
   if (e != cudaSuccess) return e;
-  dim3 grid(blocks, (unsigned)a.heads);
+  dim3 grid(blocks, (unsigned)a.heads, (unsigned)splits);
   flash_attn2_kernel<<<grid, fa2::THREADS, fa2::ALLOC, st>>>(mq, mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || splits == 1) return e;
+  const int64_t rows = a.tokens * a.heads;
+  const unsigned cb = (unsigned)((rows + 7) / 8);
+  if (a.out_dtype == WE_BF16)
+    flash_combine_kernel<WE_BF16><<<cb, 256, 0, st>>>(p.part_o, p.part_ml, splits, rows, a.out);
+  else
+    flash_combine_kernel<WE_F32><<<cb, 256, 0, st>>>(p.part_o, p.part_ml, splits, rows, a.out);
   return cudaGetLastError();
 }
 

@@ -118,7 +118,11 @@ struct AttnArgs {
   int dtype, out_dtype;
 };
 bool flash_attention_supported(const AttnArgs& a);
-cudaError_t launch_flash_attention(const AttnArgs& a, uint32_t* err, cudaStream_t st);
+// key splits for a grid that would not fill `sms` SMs (1 = none), the scratch they need, and the launch (the flash
+// kernel, then the combine kernel when splits > 1)
+int flash_attention_splits(const AttnArgs& a, int sms);
+int64_t flash_attention_scratch_bytes(const AttnArgs& a, int splits);
+cudaError_t launch_flash_attention(const AttnArgs& a, int splits, void* scratch, uint32_t* err, cudaStream_t st);
 cudaError_t launch_attention_simt(const AttnArgs& a, int sms, cudaStream_t st);
 
 }  // namespace we

@@ -1041,9 +1041,16 @@ int we_attention(we_ctx* ctx, const void* q, const void* k, const void* v, int32
   if (tokens <= 0 || heads <= 0) return WE_OK;
   we::AttnArgs a{q, k, v, out, tokens, heads, kv_heads, dim, causal ? 1 : 0, dtype, out_dtype};
   if (we::flash_attention_supported(a)) {
-    cudaError_t e = we::launch_flash_attention(a, ctx->dev_err, ctx->stream);
+    const int splits = we::flash_attention_splits(a, ctx->sms);
+    Scratch scratch(ctx);
+    void* part = nullptr;
+    if (splits > 1) {
+      int rc = scratch.take((size_t)we::flash_attention_scratch_bytes(a, splits), &part);
+      if (rc != WE_OK) return rc;
+    }
+    cudaError_t e = we::launch_flash_attention(a, splits, part, ctx->dev_err, ctx->stream);
     if (e == cudaSuccess) {
-      ctx->stats.launches++;
+      ctx->stats.launches += splits > 1 ? 2 : 1;
       return WE_OK;
     }
     if (e != cudaErrorNotSupported) return cuda_fail(ctx, e, "flash attention");
