@@ -882,12 +882,31 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (!gemm_tc_supported(a)) return cudaErrorNotSupported;
   const int max_bt = seg_tile(a);  // token tiles may not straddle two weight sets
   if (max_bt == 0) return cudaErrorNotSupported;
-  // 2-SM pairs (256 weight rows x 256 tokens per pair) when there are enough pair tiles to fill the
-  // GPU; otherwise 1-SM tiles with the largest token tile (256 / 128 / 64) that gives every SM a tile.
-  bool pair = max_bt == 256 && ((a.n + 255) / 256) * ((a.m + 255) / 256) >= sms / 2;
-  if (const char* env = getenv("WE_TC_2SM")) {  // tuning / test override: 0 never, 2 always
+  // Kernel and token tile by a cost model of waves x per-SM tile cost: a 1-SM tile (128 channels x bt tokens) costs
+  // 1.2 bt + 96 token-units, a pair tile (256 channels x 256 tokens on two SMs, half the shared-memory bytes per
+  // FLOP) 256 + 96. Fitted on 576 to 4608 tokens x N 3072 / 9216 / 12288: it picks the measured fastest choice, e.g.
+  // 576 x 3072 x 12288: 128-token 1-SM tiles, 65 us (64-token tiles 103 us, pairs 85 us).
+  const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
+  auto waves = [&](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
+  double best_cost = -1.0;
+  bool pair = false;
+  int bt = 64;
+  if (max_bt == 256) {
+    best_cost = (double)waves(((a.n + 255) / 256) * ((a.m + 255) / 256), sms / 2) * (256.0 + 96.0);
+    pair = true;
+  }
+  for (int c = 256; c >= 64; c /= 2) {
+    if (c > max_bt) continue;
+    const double cost = (double)waves(tn * ((a.m + c - 1) / c), sms) * (1.2 * c + 96.0);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      pair = false;
+      bt = c;
+    }
+  }
+  if (const char* env = getenv("WE_TC_2SM")) {  // tuning / test override: 0 never, 2 always (where tiles allow)
     const int v = atoi(env);
-    pair = v == 2 ? true : (v == 0 ? false : pair);
+    pair = v == 2 ? max_bt == 256 : (v == 0 ? false : pair);
   }
   if (pair) {
     // 256 tokens per pair tile. 128 fills the last wave better on some shapes (2304 tokens x 3072 channels:
@@ -907,10 +926,6 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
     if (a.terms > 1) return tc::run_pair<256, 2, false>(a, sms, st);
     return tc::run_pair<256, 1, false>(a, sms, st);
   }
-  const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
-  auto tiles = [&](int bt) { return tn * ((a.m + bt - 1) / bt); };
-  int bt = tiles(256) >= sms ? 256 : (tiles(128) >= sms ? 128 : 64);
-  if (bt > max_bt) bt = max_bt;
   if (const char* env = getenv("WE_TC_BT")) {  // tuning override: 64, 128 or 256 tokens per tile
     const int v = atoi(env);
     if (v == 64 || v == 128 || v == 256) bt = v;
