@@ -166,6 +166,16 @@ __device__ __forceinline__ float2 silu2(float2 v) {
   return __fmul2_rn(v, make_float2(rcp_ftz(d.x), rcp_ftz(d.y)));
 }
 
+// Grid of a row-loop kernel: as many CTAs as fit on the SMs at once (each then walks its rows, and a kernel that
+// prefetches its next row keeps those loads in flight), at most one per row.
+template <typename K>
+static inline unsigned resident_grid(K kernel, int threads, int sms, int64_t rows) {
+  int per = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, 0) != cudaSuccess || per < 1) per = 1;
+  const int64_t g = (int64_t)per * sms;
+  return (unsigned)(rows < g ? rows : g);
+}
+
 // ---- warp reductions ----
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -193,19 +193,36 @@ __global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restr
       sf[c][j] = hv[j];
     }
   }
+  // software-pipelined over rows: the next row's loads are in flight while this row is reduced and stored
+  float nx[CH][4], nr[CH][4];
+  auto fetch = [&](int64_t row) {
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i < d && row < rows) {
+        load4<DT>(x, row * d + i, nx[c]);
+        if (RES) {
+          const float4 u = *reinterpret_cast<const float4*>(r + row * d + i);
+          nr[c][0] = u.x; nr[c][1] = u.y; nr[c][2] = u.z; nr[c][3] = u.w;
+        }
+      }
+    }
+  };
+  fetch(blockIdx.x);
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     float v[CH][4];
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < CH; c++) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[c][j] = RES ? nx[c][j] + nr[c][j] : nx[c][j];
+    }
+    fetch(row + gridDim.x);
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
       const int64_t i = (int64_t)(c * 256 + tid) * 4;
       if (i < d) {
-        load4<DT>(x, row * d + i, v[c]);
-        if (RES) {
-          const float4 u = *reinterpret_cast<const float4*>(r + row * d + i);
-          v[c][0] += u.x; v[c][1] += u.y; v[c][2] += u.z; v[c][3] += u.w;
-          *reinterpret_cast<float4*>(xo + row * d + i) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
-        }
+        if (RES) *reinterpret_cast<float4*>(xo + row * d + i) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
         ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
         ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
       }
@@ -261,14 +278,20 @@ __global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restr
 template <int DT, int TERMS>
 static bool norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
                            float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs, int sms, cudaStream_t st) {
-  const unsigned g = (unsigned)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
   const int64_t ch = (d / 4 + 255) / 256;
-  if (ch <= 2) norm_split_row_kernel<DT, TERMS, 2><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (ch <= 3) norm_split_row_kernel<DT, TERMS, 3><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (ch <= 4) norm_split_row_kernel<DT, TERMS, 4><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (ch <= 6) norm_split_row_kernel<DT, TERMS, 6><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (ch <= 8) norm_split_row_kernel<DT, TERMS, 8><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
+#define WE_NS(CH)                                                                                              \
+  {                                                                                                            \
+    auto k = norm_split_row_kernel<DT, TERMS, CH>;                                                             \
+    k<<<resident_grid(k, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, nullptr, \
+                                                         nullptr);                                             \
+  }
+  if (ch <= 2) WE_NS(2)
+  else if (ch <= 3) WE_NS(3)
+  else if (ch <= 4) WE_NS(4)
+  else if (ch <= 6) WE_NS(6)
+  else if (ch <= 8) WE_NS(8)
   else return false;
+#undef WE_NS
   return true;
 }
 
@@ -295,14 +318,16 @@ cudaError_t launch_add_norm_split(const float* x, const float* r, float* xo, con
   if (d % 8 || d > 8192 || !al(x) || !al(r) || !al(xo) || !al(w) || (sc && !al(sc)) || (sh && !al(sh)) ||
       ((uintptr_t)hi & 7) || (lo && ((uintptr_t)lo & 7)))
     return cudaErrorNotSupported;
-  const unsigned g = (unsigned)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
   const int64_t ch = (d / 4 + 255) / 256;
 #define WE_ANS(CH)                                                                                                  \
   {                                                                                                                 \
-    if (terms > 1)                                                                                                  \
-      norm_split_row_kernel<WE_F32, 2, CH, true><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo); \
-    else                                                                                                            \
-      norm_split_row_kernel<WE_F32, 1, CH, true><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo); \
+    if (terms > 1) {                                                                                                \
+      auto k = norm_split_row_kernel<WE_F32, 2, CH, true>;                                                          \
+      k<<<resident_grid(k, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo);   \
+    } else {                                                                                                        \
+      auto k = norm_split_row_kernel<WE_F32, 1, CH, true>;                                                          \
+      k<<<resident_grid(k, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo);   \
+    }                                                                                                               \
   }
   if (ch <= 2) WE_ANS(2)
   else if (ch <= 3) WE_ANS(3)

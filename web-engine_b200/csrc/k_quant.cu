@@ -318,23 +318,35 @@ __global__ void __launch_bounds__(128, 6) quant_act_warp_kernel(const uint16_t* 
 
 // CTA-per-row split for long bf16 rows (k % 8 == 0, k <= 2048 CH, 16-byte aligned rows): 256 threads, thread t
 // keeps the row's 16-byte chunks t, t + 256, ... in registers (few registers: many rows in flight per SM); the
-// row max is a warp shuffle then a shared-memory reduction over the 8 warps.
-template <int TERMS, int CH, int NT = 256>
+// row max is a warp shuffle then a shared-memory reduction over the 8 warps. PF: the next row's chunks are
+// loaded while this row is split (pays for short rows; at 6+ chunks the doubled registers cost more than it gains).
+template <int TERMS, int CH, int NT = 256, bool PF = false>
 __global__ void __launch_bounds__(NT) quant_act_row_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
                                                            int64_t stride, uint8_t* __restrict__ hi,
                                                            uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
   constexpr int NW = NT / 32;
   __shared__ float red[8];
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  uint4 nv[CH];
+  auto fetch = [&](int64_t row) {
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t t = (int64_t)(c * NT + tid) * 8;
+      if (t < k && row < m) nv[c] = *reinterpret_cast<const uint4*>(x + row * stride + t);
+    }
+  };
+  if (PF) fetch(blockIdx.x);
   for (int64_t row = blockIdx.x; row < m; row += gridDim.x) {
-    const uint16_t* xr = x + row * stride;
     uint4 v[CH];
     uint32_t mx = 0;
+    if (!PF) fetch(row);
+#pragma unroll
+    for (int c = 0; c < CH; c++) v[c] = nv[c];
+    if (PF) fetch(row + gridDim.x);
 #pragma unroll
     for (int c = 0; c < CH; c++) {
       const int64_t t = (int64_t)(c * NT + tid) * 8;
       if (t < k) {
-        v[c] = *reinterpret_cast<const uint4*>(xr + t);
         // |bf16| max on the bit patterns: clear the sign bits, compare as integers
         mx = __vmaxu2(mx, __vmaxu2(__vmaxu2(v[c].x & 0x7fff7fffu, v[c].y & 0x7fff7fffu),
                                    __vmaxu2(v[c].z & 0x7fff7fffu, v[c].w & 0x7fff7fffu)));
@@ -384,22 +396,29 @@ __global__ void __launch_bounds__(NT) quant_act_row_kernel(const uint16_t* __res
 template <int TERMS>
 static bool quant_act_row(const uint16_t* x, int64_t m, int64_t k, int64_t stride, uint8_t* hi, uint8_t* lo, float* rs,
                           int sms, cudaStream_t st) {
+  // short rows: next-row prefetch on a grid of every resident CTA; long rows: one row at a time on 8 CTAs per SM
+#define WE_QAR(CH, NT)                                                                                   \
+  {                                                                                                      \
+    constexpr bool pf = NT == 128;                                                                       \
+    auto kern = quant_act_row_kernel<TERMS, CH, NT, pf>;                                                 \
+    const int g = pf ? resident_grid(kern, NT, sms, m) : (int)std::min<int64_t>(m, (int64_t)sms * 8);    \
+    kern<<<g, NT, 0, st>>>(x, m, k, stride, hi, lo, rs);                                                 \
+  }
   if (k <= 128 * 8 * 4) {  // up to 4096 values: 128 threads, every thread busy at k = 3072
-    const int g = (int)std::min<int64_t>(m, (int64_t)sms * 16);
     const int64_t ch = (k / 8 + 127) / 128;
-    if (ch <= 2) quant_act_row_kernel<TERMS, 2, 128><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
-    else if (ch <= 3) quant_act_row_kernel<TERMS, 3, 128><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
-    else quant_act_row_kernel<TERMS, 4, 128><<<g, 128, 0, st>>>(x, m, k, stride, hi, lo, rs);
+    if (ch <= 2) WE_QAR(2, 128)
+    else if (ch <= 3) WE_QAR(3, 128)
+    else WE_QAR(4, 128)
     return true;
   }
-  const int g = (int)std::min<int64_t>(m, (int64_t)sms * 8);
   const int64_t ch = (k / 8 + 255) / 256;
-  if (ch <= 2) quant_act_row_kernel<TERMS, 2><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
-  else if (ch <= 3) quant_act_row_kernel<TERMS, 3><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
-  else if (ch <= 4) quant_act_row_kernel<TERMS, 4><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
-  else if (ch <= 6) quant_act_row_kernel<TERMS, 6><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
-  else if (ch <= 8) quant_act_row_kernel<TERMS, 8><<<g, 256, 0, st>>>(x, m, k, stride, hi, lo, rs);
+  if (ch <= 2) WE_QAR(2, 256)
+  else if (ch <= 3) WE_QAR(3, 256)
+  else if (ch <= 4) WE_QAR(4, 256)
+  else if (ch <= 6) WE_QAR(6, 256)
+  else if (ch <= 8) WE_QAR(8, 256)
   else return false;
+#undef WE_QAR
   return true;
 }
 
