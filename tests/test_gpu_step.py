@@ -120,6 +120,41 @@ def test_double_block_two_weight_sets_equal_per_part(we, graph, monkeypatch, tex
     assert graph.device_error() == 0
 
 
+@pytest.mark.parametrize("images", [1, 2])
+def test_deferred_residual_chain_is_bit_identical(we, graph, images):
+    """Chained bf16 blocks (a double block, then a single block) with the first block's output left as a Residual
+    (x1, dn) that the second block's first norm pass adds (we_add_norm_split): the second block's output, and its
+    input rows, equal the plain chain (add, then norm + split) bit for bit."""
+    cfg = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=4, head_dim=128, mlp_act="gelu",
+                                attn_gate=False)
+    text, side = 24, 8
+    T = text + side * side
+    R = images * T
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(text, side, side), (16, 56, 56), 1e4)
+    _, dt_ = make_block(we, graph, cfg, 700, True)
+    _, di = make_block(we, graph, cfg, 701, True)
+    _, ds = make_block(we, graph, cfg, 702, True)
+    x, temb = randn(R * cfg.hidden, 703, 1.0), randn(6 * cfg.hidden, 704, 0.3)
+    xb, tb = graph.buffer(x), graph.buffer(temb)
+    rope = we.Rope(graph.buffer(np.tile(cos, images)), graph.buffer(np.tile(sin, images)), pairs, R)
+    double = [p for i in range(images) for p in (we.blocks.Part(i * T, text, dt_), we.blocks.Part(i * T + text,
+                                                                                              T - text, di))]
+    single = [we.blocks.Part(0, R, ds)]
+
+    def chain(defer):
+        mark = graph.mark()
+        mid = we.blocks.joint_block(graph, double, cfg, xb, tb, rope, "bf16", images=images, defer=defer)
+        assert isinstance(mid, we.blocks.Residual) == defer
+        out = we.blocks.joint_block(graph, single, cfg, mid, tb, rope, "bf16", images=images)
+        got = graph.read(out, R * cfg.hidden * 4, np.float32).copy()
+        graph.release(mark)
+        return got
+
+    plain, deferred = chain(False), chain(True)
+    assert np.isfinite(plain).all() and np.array_equal(plain, deferred)
+    assert graph.device_error() == 0
+
+
 def _step_case(we, graph, scfg, h, w, text, seed, dtype, per_channel=False):
     T = we.transformer
     host, wts = make_step(we, graph, scfg, seed, per_channel)

@@ -17,7 +17,8 @@ reference's f32 semantics, src/model/block.ts:91-105). `dtype="bf16"` is the B20
 - q/k get the fused norm + RoPE;
 - attention runs on the tcgen05 flash kernel;
 - the sigmoid gate, the MLP activation and the residual gates run inside the GEMM epilogues; the first residual
-  add is fused with the second RMSNorm + split (we_add_norm_split), the second is one f32 add.
+  add is fused with the second RMSNorm + split (we_add_norm_split), the second is one f32 add, or, when the
+  caller chains blocks (`defer=True`), is left to the next block's first RMSNorm + split (a `Residual`).
 The residual stream stays f32.
 """
 from __future__ import annotations
@@ -29,6 +30,23 @@ import numpy as np
 from . import kernels as K
 from . import ops
 from .graph import Buffer, Graph, addr
+
+
+@dataclass
+class Residual:
+    """A bf16 block's output y = x1 + dn with the add not yet done: the next block's first norm pass adds the two
+    (we_add_norm_split), which saves the add's launch and one read of y. Both buffers are the caller's."""
+
+    x1: Buffer
+    dn: Buffer
+
+    def buffers(self) -> list:
+        return [self.x1, self.dn]
+
+
+def buffers_of(x) -> list:
+    """The graph buffers that hold a block's output (one Buffer, or a Residual's two)."""
+    return x.buffers() if isinstance(x, Residual) else [x]
 
 
 @dataclass
@@ -155,10 +173,12 @@ def double_block(graph: Graph, txt: BlockWeights, img: BlockWeights, cfg: BlockC
 
 
 def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32",
-                images: int = 1, sp=None) -> Buffer:
+                images: int = 1, sp=None, defer: bool = False):
     """Rows of `images` sequences of rope.tokens / images tokens each, stacked; each part covers a row range with its
     own weights, attention runs within each image. rope: cos/sin for all stacked rows (per image, tiled).
-    sp: a sequence.SequenceParallel when the rows are this rank's shard of one image (bf16 path)."""
+    sp: a sequence.SequenceParallel when the rows are this rank's shard of one image (bf16 path).
+    x: a Buffer [tokens, hidden] f32 or the Residual a previous block deferred. defer: on the bf16 path, return
+    the output as a Residual for the next block instead of adding it here (the f32 path always returns a Buffer)."""
     parts = [p for p in parts if p.rows > 0]
     if sum(p.rows for p in parts) != rope.tokens:
         raise ValueError("the parts must cover the rope's tokens")
@@ -167,9 +187,11 @@ def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.
     if sp is not None and (dtype != "bf16" or images != 1):
         raise ValueError("a sequence-parallel block runs one image on the bf16 path")
     if dtype == "f32":
+        if isinstance(x, Residual):
+            x = ops.add(graph, x.x1, x.dn, rope.tokens * cfg.hidden)
         return _joint_f32(graph, parts, cfg, x, tvec, rope, images)
     if dtype == "bf16":
-        return _joint_bf16(graph, parts, cfg, x, tvec, rope, images, sp)
+        return _joint_bf16(graph, parts, cfg, x, tvec, rope, images, sp, defer)
     raise ValueError(f"unknown block dtype {dtype}")
 
 
@@ -325,10 +347,13 @@ def _split_rows(split, p: Part, width: int):
     return (rows_at(split[0], p.row0, width), rows_at(split[1], p.row0, width), rows_at(split[2], p.row0, 4))
 
 
-def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
+def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None, defer=False):
     t, hd, hdim = rope.tokens, cfg.hidden, cfg.head_dim
     qw, kw = cfg.heads * hdim, cfg.kv_heads * hdim
     mark = graph.mark()
+    res = None
+    if isinstance(x, Residual):  # x = x1 + dn of the previous block, written by the first norm pass below
+        res, x = x, graph.buffer(t * hd * 4)
     shared: dict = {}  # parts with the same weights (the images of a batch) share one modulation
     mods = []
     for p in parts:
@@ -339,8 +364,13 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
     split = (graph.buffer(t * hd), graph.buffer(t * hd), graph.buffer(t * 4))
     q, k, v = graph.buffer(t * qw * 2), graph.buffer(t * kw * 2), graph.buffer(t * kw * 2)
     for p, mod in zip(parts, mods):
-        K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(split, p, hd),
-                     scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
+        if res is None:
+            K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(split, p, hd),
+                         scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
+        else:
+            K.add_norm_split(graph, rows_at(res.x1, p.row0, hd * 4), rows_at(res.dn, p.row0, hd * 4),
+                             rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(split, p, hd),
+                             scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
     if all(p.w.wqkv is not None for p in parts):  # one GEMM, its epilogue writing q, k and v
         _gemm_all(graph, plan, parts, split, hd, lambda w: w.wqkv, [(q, qw), (k, kw), (v, kw)], "bf16")
     else:
@@ -383,6 +413,9 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None):
     K.quantize_act(graph, u, t, cfg.mlp, *msplit, terms=2)
     dn = graph.buffer(t * hd * 4)  # dn = postgate down(m)
     _gemm_all(graph, plan, parts, msplit, cfg.mlp, lambda w: w.mlp_down, [(dn, hd)], "f32", shared, "postgate")
+    if defer:  # the next block adds x1 + dn in its first norm pass
+        graph.release(mark, [x1, dn])
+        return Residual(x1, dn)
     out = ops.add(graph, x1, dn, t * hd)  # x1 + postgate down(m): the block's output
     graph.release(mark, [out])
     return out

@@ -28,7 +28,7 @@ import numpy as np
 from . import _lib as L
 from . import kernels as K
 from . import ops
-from .block import BlockConfig, BlockWeights, Part, block_flops, joint_block
+from .block import BlockConfig, BlockWeights, Part, block_flops, buffers_of, joint_block
 from .graph import Buffer, Graph, addr
 
 LATENT_CHANNELS = 16
@@ -178,12 +178,15 @@ class StepGraph:
         rope = ops.Rope(self.cos, self.sin, pairs, n)
         with graph.capture() as cap:
             x = self.x_in
-            for parts in _layers(w, images, T, text_tokens, image, r0, n):
+            layers = _layers(w, images, T, text_tokens, image, r0, n)
+            for i, parts in enumerate(layers):
                 bm = graph.mark()
-                nxt = joint_block(graph, parts, bc, x, self.tvec, rope, dtype, images=images, sp=sp)
-                graph.release(bm, [nxt])
+                nxt = joint_block(graph, parts, bc, x, self.tvec, rope, dtype, images=images, sp=sp,
+                                  defer=i + 1 < len(layers))
+                graph.release(bm, buffers_of(nxt))
                 if x is not self.x_in:
-                    graph.free(x)
+                    for b in buffers_of(x):
+                        graph.free(b)
                 x = nxt
         self.captured, self.out = cap, x
 
@@ -258,11 +261,14 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
             raise ValueError("the captured step is for another geometry, batch, dtype or sequence-parallel group")
         x = captured.run(graph, x, tvec)  # graph-owned; the last layer reads it
     else:
-        for i, parts in enumerate(_layers(w, B, T, Lt, image, r0, n)):
+        layers = _layers(w, B, T, Lt, image, r0, n)
+        for i, parts in enumerate(layers):
             bm = graph.mark()
-            nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp)
-            graph.release(bm, [nxt])
-            graph.free(x)
+            # between blocks the output stays a Residual: the next block's first norm pass adds it
+            nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp, defer=i + 1 < len(layers))
+            graph.release(bm, buffers_of(nxt))
+            for b in buffers_of(x):
+                graph.free(b)
             x = nxt
             if on_block:
                 on_block(i)
