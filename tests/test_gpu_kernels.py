@@ -243,10 +243,12 @@ def test_qknorm_rope_block_size_bf16(we, graph, pairing):
 
 @pytest.mark.parametrize("head_dim,pairing,axes,heads", [
     (128, "interleaved", (32, 48, 48), 4), (128, "half", (32, 48, 48), 4), (128, "interleaved", (32, 48, 48), 3),
-    (128, "half", (32, 48, 48), 3), (64, "interleaved", (16, 24, 24), 4), (256, "interleaved", (64, 96, 96), 4),
-    (96, "interleaved", (32, 32, 32), 4)])
+    (128, "half", (32, 48, 48), 3), (128, "interleaved", (32, 48, 48), 8), (128, "half", (32, 48, 48), 16),
+    (64, "interleaved", (16, 24, 24), 4), (256, "interleaved", (64, 96, 96), 4), (96, "interleaved", (32, 32, 32), 4)])
 def test_qknorm_rope_matches_norm_then_rotate(we, graph, head_dim, pairing, axes, heads):
-    tokens = 2 + 5 * 7  # with 3 heads: an odd number of head rows
+    """With 3 heads an odd number of head rows; with 8 and 16 heads of 128 the kernel takes a token's 8 heads per
+    warp step (its cos/sin loaded once for them)."""
+    tokens = 2 + 5 * 7
     cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(2, 5, 7), axes, 1000.0)
     assert 2 * pairs == head_dim
     x = lcg_floats(tokens * heads * head_dim, 5, 3.0)

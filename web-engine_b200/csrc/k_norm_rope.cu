@@ -232,9 +232,10 @@ __global__ void __launch_bounds__(256) rmsnorm_row_kernel(const void* __restrict
 // q/k norm + RoPE for 128-wide heads (NORM false: RoPE alone): 16 lanes per head row, 8 values (16 bytes of
 // bf16) per lane; a warp takes 2 R rows per step (R per half-warp) and issues all their loads (rows and cos/sin)
 // before any arithmetic, so each warp keeps R x 48 bytes per lane in flight. Interleaved pairs stay in a lane;
-// half pairing exchanges with lane ^ 8.
-template <int DT, int OT, int PAIRING, bool NORM>
-__global__ void __launch_bounds__(256, 3) qknorm_rope128_kernel(const void* __restrict__ x, const float* __restrict__ w,
+// half pairing exchanges with lane ^ 8. TOK (heads % 8 == 0): a step's 8 rows are 8 heads of one token, so the
+// token's cos/sin values are loaded once per step instead of once per row (they are twice a row's own bytes).
+template <int DT, int OT, int PAIRING, bool NORM, bool TOK = false>
+__global__ void __launch_bounds__(256, TOK ? 3 : 2) qknorm_rope128_kernel(const void* __restrict__ x, const float* __restrict__ w,
                                                              float eps, float offset, const float* __restrict__ cs,
                                                              const float* __restrict__ sn, int64_t tokens,
                                                              int64_t heads, void* __restrict__ out) {
@@ -254,6 +255,31 @@ __global__ void __launch_bounds__(256, 3) qknorm_rope128_kernel(const void* __re
     float v[R][8], c[R][8], sv[R][8];
     int64_t base[R];
     bool live[R];
+    if constexpr (TOK) {  // rows t heads + [8 k, 8 k + 8) of token t = gi / (heads / 8): every row live
+      const int64_t t = gi / (heads >> 3);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        base[r] = (gi * 2 * R + 2 * r + half) * D + sub * 8;
+        live[r] = true;
+        load8<DT>(x, base[r], v[r]);
+      }
+      if (PAIRING == WE_ROPE_INTERLEAVED) {
+        const float4 cc = *reinterpret_cast<const float4*>(cs + t * P + sub * 4);
+        const float4 ss4 = *reinterpret_cast<const float4*>(sn + t * P + sub * 4);
+        c[0][0] = cc.x; c[0][1] = cc.y; c[0][2] = cc.z; c[0][3] = cc.w;
+        sv[0][0] = ss4.x; sv[0][1] = ss4.y; sv[0][2] = ss4.z; sv[0][3] = ss4.w;
+      } else {
+        load8f(cs, t * P + (sub & 7) * 8, c[0]);
+        load8f(sn, t * P + (sub & 7) * 8, sv[0]);
+      }
+#pragma unroll
+      for (int r = 1; r < R; r++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          c[r][e] = c[0][e];
+          sv[r][e] = sv[0][e];
+        }
+    } else {
 #pragma unroll
     for (int r = 0; r < R; r++) {
       const int64_t row0 = gi * 2 * R + 2 * r + half;
@@ -271,6 +297,7 @@ __global__ void __launch_bounds__(256, 3) qknorm_rope128_kernel(const void* __re
         load8f(cs, t * P + (sub & 7) * 8, c[r]);
         load8f(sn, t * P + (sub & 7) * 8, sv[r]);
       }
+    }
     }
 #pragma unroll
     for (int r = 0; r < R; r++) {
@@ -458,15 +485,36 @@ cudaError_t launch_rmsnorm(const void* x, int xdt, const float* w, const float* 
   return cudaGetLastError();
 }
 
+// the 128-wide head kernel: token-grouped rows when heads % 8 == 0 (WE_QK_TOK=0 turns that off for tests),
+// on a grid of every resident CTA (each warp strides over groups of 8 rows)
+template <int DT, int OT, bool NORM>
+static void launch_qk128(const void* x, const float* w, float eps, float offset, const float* cs, const float* sn,
+                         int64_t tokens, int64_t heads, int pairing, void* out, int sms, cudaStream_t st) {
+  static const bool tok_ok = [] {
+    const char* e = getenv("WE_QK_TOK");
+    return !(e && atoi(e) == 0);
+  }();
+  const int64_t groups = (tokens * heads + 7) / 8;
+#define WE_QK(PAIR, TOK)                                                                                       \
+  {                                                                                                            \
+    auto kern = qknorm_rope128_kernel<DT, OT, PAIR, NORM, TOK>;                                                \
+    kern<<<resident_grid(kern, 256, sms, (groups + 7) / 8), 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens,   \
+                                                                          heads, out);                          \
+  }
+  const bool tok = tok_ok && heads % 8 == 0;
+  if (pairing == WE_ROPE_INTERLEAVED) {
+    if (tok) WE_QK(WE_ROPE_INTERLEAVED, true) else WE_QK(WE_ROPE_INTERLEAVED, false)
+  } else {
+    if (tok) WE_QK(WE_ROPE_HALF, true) else WE_QK(WE_ROPE_HALF, false)
+  }
+#undef WE_QK
+}
+
 template <int DT, int OT>
 static void rope_dispatch(const void* x, const float* cs, const float* sn, int64_t tokens, int64_t heads, int64_t pairs,
                           int pairing, void* out, bool vec, int sms, cudaStream_t st) {
   if (pairs == 64 && vec && ((uintptr_t)cs & 15) == 0 && ((uintptr_t)sn & 15) == 0) {  // 128-wide heads: row layout
-    const int g = capped((tokens * heads + 63) / 64, sms, 8);
-    if (pairing == WE_ROPE_INTERLEAVED)
-      qknorm_rope128_kernel<DT, OT, WE_ROPE_INTERLEAVED, false><<<g, 256, 0, st>>>(x, nullptr, 0.f, 0.f, cs, sn, tokens, heads, out);
-    else
-      qknorm_rope128_kernel<DT, OT, WE_ROPE_HALF, false><<<g, 256, 0, st>>>(x, nullptr, 0.f, 0.f, cs, sn, tokens, heads, out);
+    launch_qk128<DT, OT, false>(x, nullptr, 0.f, 0.f, cs, sn, tokens, heads, pairing, out, sms, st);
     return;
   }
   int threads = 128;
@@ -511,12 +559,7 @@ static bool qk_dispatch(const void* x, const float* w, float eps, float offset, 
                         int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out, int sms, cudaStream_t st) {
   if (pairs * 2 == 128 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0 && ((uintptr_t)cs & 15) == 0 &&
       ((uintptr_t)sn & 15) == 0) {
-    const int64_t rows = tokens * heads;
-    const int g = capped((rows + 63) / 64, sms, 8);
-    if (pairing == WE_ROPE_INTERLEAVED)
-      qknorm_rope128_kernel<DT, OT, WE_ROPE_INTERLEAVED, true><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
-    else
-      qknorm_rope128_kernel<DT, OT, WE_ROPE_HALF, true><<<g, 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens, heads, out);
+    launch_qk128<DT, OT, true>(x, w, eps, offset, cs, sn, tokens, heads, pairing, out, sms, st);
     return true;
   }
   switch (pairs * 2) {
