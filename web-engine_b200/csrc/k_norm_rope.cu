@@ -4,6 +4,8 @@
 // q/k path of attend() (src/model/block.ts:53-56: linear -> norm(qNorm, rows*heads, 128) -> rotate).
 // These are HBM-bandwidth kernels. Row sums of squares are accumulated in fp32 like the reference
 // shader (tree order differs; the result stays within the reference test's 1e-5).
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -187,21 +189,37 @@ __global__ void __launch_bounds__(256) rmsnorm_row_kernel(const void* __restrict
       sf[c][j] = hv[j];
     }
   }
+  // software-pipelined over rows: the next row's chunks are loaded (raw words) while this row is reduced and stored
+  using Raw = typename std::conditional<DT == WE_F32, float4, uint2>::type;
+  Raw nx[CH];
+  auto fetch = [&](int64_t row) {
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
+      const int64_t i = (int64_t)(c * 256 + tid) * 4;
+      if (i < d && row < rows) {
+        if constexpr (DT == WE_F32) nx[c] = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + row * d + i);
+        else nx[c] = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + row * d + i);
+      }
+    }
+  };
+  fetch(blockIdx.x);
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     float v[CH][4];
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < CH; c++) {
+      if constexpr (DT == WE_F32) {
+        v[c][0] = nx[c].x; v[c][1] = nx[c].y; v[c][2] = nx[c].z; v[c][3] = nx[c].w;
+      } else {
+        v[c][0] = __uint_as_float(nx[c].x << 16); v[c][1] = __uint_as_float(nx[c].x & 0xffff0000u);
+        v[c][2] = __uint_as_float(nx[c].y << 16); v[c][3] = __uint_as_float(nx[c].y & 0xffff0000u);
+      }
+    }
+    fetch(row + gridDim.x);
+#pragma unroll
+    for (int c = 0; c < CH; c++) {
       const int64_t i = (int64_t)(c * 256 + tid) * 4;
       if (i < d) {
-        if constexpr (DT == WE_F32) {
-          const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + row * d + i);
-          v[c][0] = a.x; v[c][1] = a.y; v[c][2] = a.z; v[c][3] = a.w;
-        } else {
-          const uint2 a = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + row * d + i);
-          v[c][0] = __uint_as_float(a.x << 16); v[c][1] = __uint_as_float(a.x & 0xffff0000u);
-          v[c][2] = __uint_as_float(a.y << 16); v[c][3] = __uint_as_float(a.y & 0xffff0000u);
-        }
         ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
         ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
       }
@@ -439,13 +457,18 @@ template <int DT, int OT>
 static void rmsnorm_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
                              float eps, float offset, void* out, bool vec, int sms, cudaStream_t st) {
   if (vec && d >= 2048 && d % 4 == 0 && d <= 8192) {  // CTA per row, weights held across rows
-    const unsigned g = (unsigned)(rows < (int64_t)sms * 8 ? rows : (int64_t)sms * 8);
     const int64_t ch = (d / 4 + 255) / 256;
-    if (ch <= 2) rmsnorm_row_kernel<DT, OT, 2><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
-    else if (ch <= 3) rmsnorm_row_kernel<DT, OT, 3><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
-    else if (ch <= 4) rmsnorm_row_kernel<DT, OT, 4><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
-    else if (ch <= 6) rmsnorm_row_kernel<DT, OT, 6><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
-    else rmsnorm_row_kernel<DT, OT, 8><<<g, 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out);
+#define WE_RNR(CH)                                                                                  \
+  {                                                                                                 \
+    auto kern = rmsnorm_row_kernel<DT, OT, CH>;                                                     \
+    kern<<<resident_grid(kern, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out); \
+  }
+    if (ch <= 2) WE_RNR(2)
+    else if (ch <= 3) WE_RNR(3)
+    else if (ch <= 4) WE_RNR(4)
+    else if (ch <= 6) WE_RNR(6)
+    else WE_RNR(8)
+#undef WE_RNR
     return;
   }
   if constexpr (DT == WE_BF16) {
