@@ -390,8 +390,8 @@ int we_peer_exchange(we_ctx* ctx, we_peer* peer, const we_peer_copy* copies, int
 int we_peer_destroy(we_peer* peer);
 
 /* ---------------- allocation-free linear (no counterpart in the reference) ----------------
-   For callers that cannot allocate device memory: code inside someone else's CUDA-graph capture, a
-   serving loop with a fixed memory budget, or a runtime whose allocator owns all device memory.
+   For callers that cannot allocate device memory: a serving loop whose memory budget is fixed when it
+   starts, or a host runtime (a plugin handed only streams and pointers) whose allocator owns all of it.
    y = x . W^T * scale (+ bias) for bf16 x [m, k] (row stride x_stride values, 0 = k) and e4m3 W [n, k]
    with f32 scale or per-channel chan_scale [n]: the same activation split and tcgen05 GEMM as
    we_matmul, but with no context and no allocation. The split lives in one static device array of

@@ -1,7 +1,8 @@
 """The allocation-free linear, we_matmul_fp8_noalloc, against the regular entry point we_matmul.
 
-Callers such as code running inside someone else's CUDA-graph capture, or a runtime whose allocator
-owns all device memory, cannot call cudaMalloc. For them the library keeps the activation split in
+Callers such as a serving loop whose device memory budget is fixed at start-up, or a host runtime whose
+own allocator owns all device memory (a plugin that is handed only streams and pointers), cannot call
+cudaMalloc. For them the library keeps the activation split in
 one static device array instead of a pooled buffer. This test (the test itself may allocate; the
 entry point under test does not) checks that two calls in a row, on different data and sizes, give
 the same output as we_matmul on the same inputs, and that a request larger than the static scratch

@@ -1,9 +1,9 @@
 // we_matmul_fp8_noalloc: the bf16 x fp8 linear (activation split + tcgen05 GEMM) for callers that cannot
 // allocate device memory.
 //
-// Some hosts of this library may not call cudaMalloc at all: code running inside a CUDA-graph capture
-// owned by someone else, a real-time or serving loop with a fixed memory budget, or an embedding
-// runtime whose allocator owns every byte of device memory. The regular path (we_matmul /
+// Some hosts of this library may not call cudaMalloc at all: a real-time or serving loop whose device
+// memory budget is fixed when it starts, or an embedding runtime (a framework plugin that is handed only
+// streams and tensor pointers) whose own allocator owns every byte of device memory. The regular path (we_matmul /
 // we_linear_forward) takes its scratch for the activation split from the context's pool, and that
 // pool grows with cudaMalloc. This entry point needs no context and allocates nothing. Its scratch is
 // one file-scope device array of WE_NOALLOC_SCRATCH_BYTES, which the CUDA runtime creates on every GPU
