@@ -197,7 +197,7 @@ int we_linear_forward(we_ctx* ctx, const void* x, int32_t x_dtype, const we_line
 /* linear from host memory to host memory: y_host [m, n] = linear(x_host [m, k]). One call does the upload of x,
    the linear and the read-back of y. A caller of ops.ts:61-73 does the same with queue.writeBuffer before the
    dispatch and a mapped read after it (graph.ts:37-47, graph.ts:108-119). Rows go in chunks of chunk_rows
-   (0: about m / 8, a multiple of 128) through three streams, so the host -> device copy of chunk c + 1, the GEMM
+   (0: about m / 12, a multiple of 128) through three streams, so the host -> device copy of chunk c + 1, the GEMM
    of chunk c and the device -> host copy of chunk c - 1 overlap. Returns when y_host holds the result. Copies
    overlap only when both host buffers are page-locked (cudaHostAlloc / cudaHostRegister); pageable buffers give
    the same result. Each chunk is the linear of its rows, as we_linear_forward computes it for that many rows.

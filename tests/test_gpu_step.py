@@ -155,6 +155,29 @@ def test_deferred_residual_chain_is_bit_identical(we, graph, images):
     assert graph.device_error() == 0
 
 
+def test_deferred_residual_into_an_f32_block(we, graph):
+    """A bf16 block's deferred Residual handed to the f32 path: the f32 block adds x1 + dn first, so its output
+    equals the one it gives on the bf16 block's plain output, bit for bit."""
+    cfg = we.blocks.BlockConfig(hidden=256, mlp=1024, heads=2, kv_heads=2, head_dim=128, mlp_act="gelu",
+                                attn_gate=False)
+    tokens = 40
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(8, 4, 8), (16, 56, 56), 1e4)
+    _, d1 = make_block(we, graph, cfg, 720, True)
+    _, d2 = make_block(we, graph, cfg, 721, True)
+    x, temb = randn(tokens * cfg.hidden, 722, 1.0), randn(6 * cfg.hidden, 723, 0.3)
+    xb, tb = graph.buffer(x), graph.buffer(temb)
+    rope = we.Rope(graph.buffer(cos), graph.buffer(sin), pairs, tokens)
+    outs = []
+    for defer in (False, True):
+        mark = graph.mark()
+        mid = we.blocks.joint_block(graph, [we.blocks.Part(0, tokens, d1)], cfg, xb, tb, rope, "bf16", defer=defer)
+        out = we.blocks.joint_block(graph, [we.blocks.Part(0, tokens, d2)], cfg, mid, tb, rope, "f32")
+        outs.append(graph.read(out, tokens * cfg.hidden * 4, np.float32).copy())
+        graph.release(mark)
+    assert np.isfinite(outs[0]).all() and np.array_equal(outs[0], outs[1])
+    assert graph.device_error() == 0
+
+
 def _step_case(we, graph, scfg, h, w, text, seed, dtype, per_channel=False):
     T = we.transformer
     host, wts = make_step(we, graph, scfg, seed, per_channel)
