@@ -392,17 +392,20 @@ int we_peer_destroy(we_peer* peer);
 /* ---------------- allocation-free linear (no counterpart in the reference) ----------------
    For callers that cannot allocate device memory: a serving loop whose memory budget is fixed when it
    starts, or a host runtime (a plugin handed only streams and pointers) whose allocator owns all of it.
-   y = x . W^T * scale (+ bias) for bf16 x [m, k] (row stride x_stride values, 0 = k) and e4m3 W [n, k]
-   with f32 scale or per-channel chan_scale [n]: the same activation split and tcgen05 GEMM as
-   we_matmul, but with no context and no allocation. The split lives in one static device array of
-   WE_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until the process exits; calls
-   needing more (2 m k + 4 m bytes, m k + 4 m with WE_MM_FP8_FAST) return WE_EINVAL. All calls on a
-   device share that array, so calls that overlap on the GPU (other streams, other threads) race:
-   serialise them. The first call on each device looks up the array's device address with that
-   device current; make that first call before any stream capture. `stream` is a cudaStream_t on the
-   current device. flags: WE_MM_FP8_FAST, WE_MM_ACCUMULATE, WE_NOALLOC_SYNC (wait for the stream and
-   return WE_ETIMEOUT if a bounded wait in the GEMM gave up). errbuf (may be NULL) receives a message
-   on failure. */
+   y = x . W^T * scale (+ bias) for bf16 x [m, k] (row stride x_stride values: 0 = k, else >= k) and e4m3
+   W [n, k] with f32 scale or per-channel chan_scale [n], into y [m, n] (row stride y_stride: 0 = n, else
+   >= n): the same activation split and tcgen05 GEMM as we_matmul, but with no context and no allocation.
+   The split lives in one static device array of WE_NOALLOC_SCRATCH_BYTES that every GPU loading this
+   library holds until the process exits; calls needing more (2 m k + 4 m bytes, m k + 4 m with
+   WE_MM_FP8_FAST) return WE_EINVAL, and so do layouts the tensor-core GEMM cannot take (K % 16 != 0, w
+   not 16-byte aligned), with a message. All calls on a device share that array, so calls that overlap on
+   the GPU (other streams, other threads) race: serialise them. The first call in each CUDA context (per
+   device; again after cudaDeviceReset, or in a context the host made itself) looks up the array's device
+   address with that device current; make that first call before any stream capture. `stream` is a
+   cudaStream_t of the current context. flags: WE_MM_FP8_FAST, WE_MM_ACCUMULATE, WE_NOALLOC_SYNC (wait for
+   the stream, read the GEMM's error word on it, and return WE_ETIMEOUT if a bounded wait gave up). Without
+   WE_NOALLOC_SYNC the call returns once the work is queued and a bounded-wait timeout goes unreported (the
+   next call clears the word). errbuf (may be NULL) receives a message on failure. */
 #define WE_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 enum { WE_NOALLOC_SYNC = 1u << 3 };
 int we_matmul_fp8_noalloc(void* stream, const void* x, int64_t m, int64_t k, int64_t x_stride, const uint8_t* w,

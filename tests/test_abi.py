@@ -78,3 +78,24 @@ def test_rope_tables_and_positions_match_oracle(we):
 def test_without_a_gpu_the_library_fails_loudly(we):
     with pytest.raises(we._lib.WeError):
         we.Graph(0)
+
+
+def test_noalloc_refuses_bad_arguments_before_touching_the_gpu(we):
+    """we_matmul_fp8_noalloc checks its arguments before any CUDA call, so these refusals need no GPU: negative
+    sizes, row strides shorter than a row (or negative), K not a multiple of 16, an unaligned w."""
+    lib = we._lib.lib()
+    dummy = C.c_void_p(256)  # never dereferenced: every case below is refused first
+
+    def call(m, k, x_stride, n, y_stride, w=dummy):
+        err = C.create_string_buffer(200)
+        rc = lib.we_matmul_fp8_noalloc(None, dummy, m, k, x_stride, w, n, 1.0, None, None, dummy, y_stride,
+                                       we._lib.DTYPES["bf16"], 0, err, 200)
+        return rc, err.value.decode()
+
+    for args, words in [((-1, 64, 0, 16, 0), "negative"), ((4, 64, 32, 16, 0), "x_stride"),
+                        ((4, 64, -64, 16, 0), "x_stride"), ((4, 64, 0, 16, 8), "y_stride"),
+                        ((4, 64, 0, 16, -1), "y_stride"), ((4, 40, 0, 16, 0), "multiple of 16")]:
+        rc, msg = call(*args)
+        assert rc == we._lib.WE_EINVAL and words in msg, (args, msg)
+    rc, msg = call(4, 64, 0, 16, 0, w=C.c_void_p(257))
+    assert rc == we._lib.WE_EINVAL and "aligned" in msg
