@@ -326,10 +326,20 @@ def _gelu(u):
     return 0.5 * u * (1.0 + np.tanh(0.7978845608028654 * (u + 0.044715 * u ** 3)))
 
 
-def joint_block_reference(x, parts: list, cfg: dict, temb, cos, sin) -> np.ndarray:
+def block_rows_reference(x, w: dict, cfg: dict, temb, cos, sin, rows) -> np.ndarray:
+    """The float64 single-stream block's output on the given rows only: keys and values come from every token, the
+    queries and everything after attention from `rows` alone (the same formulas as joint_block_reference, for
+    checking a few rows of a full-size block without the full block's float64 cost)."""
+    return joint_block_reference(x, [(0, x.shape[0], w)], cfg, temb, cos, sin, rows=rows)
+
+
+def joint_block_reference(x, parts: list, cfg: dict, temb, cos, sin, rows=None) -> np.ndarray:
     """float64 block over a token sequence split into parts (row0, rows, w): each part has its own weights and
     modulation, attention runs over all rows. One part = the single-stream block of tests/gpu/block.test.ts:26-100;
-    two parts (text rows, image rows) = the double-stream block built from the same ops."""
+    two parts (text rows, image rows) = the double-stream block built from the same ops. rows: a list of row
+    indices (one part only) to return the output of just those rows, in that order."""
+    if rows is not None:
+        return _block_rows(np.asarray(x, np.float64), parts, cfg, temb, cos, sin, np.asarray(rows))
     t, hid, heads, kvh, hd = x.shape[0], cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
     eps = cfg.get("eps", 1e-5)
     pairs = hd // 2
@@ -377,6 +387,50 @@ def joint_block_reference(x, parts: list, cfg: dict, temb, cos, sin) -> np.ndarr
             m = _gelu(_mm(h2, w["mlp_up"]))
         out[r0:r0 + n] = x1 + postgate * _mm(m, w["mlp_down"])
     return out
+
+
+def _block_rows(x, parts, cfg, temb, cos, sin, rows):
+    """joint_block_reference restricted to output rows `rows` of a one-part block."""
+    if len(parts) != 1:
+        raise ValueError("row sampling takes a one-part block")
+    (_, t, w), = parts
+    hid, heads, kvh, hd = cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+    eps, pairs = cfg.get("eps", 1e-5), hd // 2
+    mod = [(np.asarray(temb[i * hid:(i + 1) * hid], np.float64) + w["table"][i * hid:(i + 1) * hid]) for i in range(6)]
+    prescale, preshift, pregate, postscale, postshift, postgate = mod
+    cs, sn = (np.asarray(a, np.float64).reshape(-1, pairs) for a in (cos, sin))
+
+    def rope_np(a, idx, nh):
+        a = a.reshape(len(idx), nh, pairs, 2)
+        c, s = cs[idx][:, None, :], sn[idx][:, None, :]
+        out = np.empty_like(a)
+        out[..., 0] = a[..., 0] * c - a[..., 1] * s
+        out[..., 1] = a[..., 1] * c + a[..., 0] * s
+        return out.reshape(len(idx), nh, hd)
+
+    allr = np.arange(t)
+    h = _rms(x, w["norm1"], t, hid, prescale, preshift, eps)
+    k = rope_np(_rms(_mm(h, w["wk"]), w["norm_k"], t * kvh, hd, eps=eps), allr, kvh)
+    v = _mm(h, w["wv"]).reshape(t, kvh, hd)
+    hr = h[rows]
+    q = rope_np(_rms(_mm(hr, w["wq"]), w["norm_q"], len(rows) * heads, hd, eps=eps), rows, heads)
+    o = np.empty((len(rows), heads, hd))
+    for hh in range(heads):
+        g = hh // (heads // kvh)
+        s = q[:, hh] @ k[:, g].T / np.sqrt(hd)
+        p = np.exp(s - s.max(1, keepdims=True))
+        o[:, hh] = (p / p.sum(1, keepdims=True)) @ v[:, g]
+    op = o.reshape(len(rows), hid)
+    if cfg.get("attn_gate", True):
+        op = op / (1.0 + np.exp(-_mm(hr, w["gate"])))
+    x1 = x[rows] + pregate * _mm(op, w["wo"])
+    h2 = _rms(x1, w["norm2"], len(rows), hid, postscale, postshift, eps)
+    if cfg.get("mlp_act", "swiglu") == "swiglu":
+        gg = _mm(h2, w["mlp_gate"])
+        m = gg / (1.0 + np.exp(-gg)) * _mm(h2, w["mlp_up"])
+    else:
+        m = _gelu(_mm(h2, w["mlp_up"]))
+    return x1 + postgate * _mm(m, w["mlp_down"])
 
 
 # ---------------- the step driver's host parts (src/model/transformer.ts, src/model/sampler.ts) ----------------

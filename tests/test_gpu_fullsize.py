@@ -1,0 +1,222 @@
+"""Parity at the sizes the benchmark times.
+
+The float64 oracle cannot run a 4608-token block or a 57-block step in a test's time, so the full-size reference is
+the library's own f32 path: CUDA-core GEMMs (k_gemm_simt.cu, fp32 FMA over the same fp8 weights) and the fp32
+CUDA-core attention, the reference's op-by-op f32 semantics (src/model/block.ts:91-105), which the other tests pin
+to the float64 oracle at small shapes (test_block_f32_matches_the_float64_block, test_step_f32_matches_the_float64_
+step). Against it, the B200 bf16 path (fused norm + split, tcgen05 fp8 GEMMs with fused epilogues, q/k norm + RoPE,
+flash attention) must reach the north star's bounds: cosine >= 0.9999 and max-abs-rel < 1e-2 (max |a - b| over
+max |b|). A few rows of the config 3 block are also checked against the float64 oracle directly.
+
+- config 2, int4 group-64 variant in full (M=4608, K=3072, N=12288): the tcgen05 path against the CUDA-core kernel
+  on the whole output, and 8 rows against the float64 oracle (relErr < 1e-5, the matmul tolerance);
+- the activation split on rows with a wide dynamic range (an outlier of 1e3 among N(0, 1) values, and log-uniform
+  magnitudes over 9 decades): exact for every value at or above 2^(e-2) (2^e the row's power-of-two scale, about
+  2^-11 of the row maximum), within 2^(e-10) below; the two-term GEMM on such rows stays within that bound;
+- config 3: one single-stream block, 4608 tokens (512 text + 64 x 64 image), hidden 3072, 24 x 128 heads, 4x GELU
+  MLP, fp8 per-channel linears;
+- config 4: one denoising step of the 19 double + 38 single block model at 1024 x 1024, eagerly and replayed from a
+  CUDA graph (StepGraph), velocity against the f32 step.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from util import bf16, bf16_round, randn
+
+pytestmark = pytest.mark.gpu
+
+EXACT_REL = 1e-5
+COS, MAXREL = 0.9999, 1e-2  # the north star's GEMM / block / step tolerance
+
+
+def _cmp(a, b):
+    a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
+    return O.compare(a, b)["cosine"], float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
+
+
+def test_config2_int4_in_full_against_cuda_core_and_oracle_rows(we, graph):
+    m, n, k = 4608, 12288, 3072
+    rng = np.random.default_rng(3)
+    x = bf16_round(rng.standard_normal(m * k, dtype=np.float32))
+    packed = rng.integers(0, 256, n * k // 2, dtype=np.uint8)
+    # group scales as absmax / 7 of N(0, 0.02) groups give them: about 0.006 .. 0.012
+    scales = np.array([O.f32_to_f16(v) for v in rng.uniform(0.006, 0.012, 4096)], np.uint16)
+    scales = scales[rng.integers(0, 4096, n * k // 64)]
+    mark = graph.mark()
+    xb, wb, sb = graph.buffer(bf16(x)), graph.buffer(packed), graph.buffer(scales)
+    y_tc, y_ref = graph.buffer(m * n * 4), graph.buffer(m * n * 4)
+    t0 = graph.stats["tcGemms"]
+    we.kernels.matmul(graph, xb, wb, y_tc, m, n, k, 1.0, x_dtype="bf16", w_dtype="int4", group_scale=sb)
+    assert graph.stats["tcGemms"] == t0 + 1
+    we.kernels.matmul(graph, xb, wb, y_ref, m, n, k, 1.0, x_dtype="bf16", w_dtype="int4", group_scale=sb,
+                      force_simt=True)
+    a = graph.read(y_tc, m * n * 4, np.float32).reshape(m, n)
+    b = graph.read(y_ref, m * n * 4, np.float32).reshape(m, n)
+    assert graph.device_error() == 0
+    graph.release(mark)
+    assert np.max(np.abs(a - b)) / np.max(np.abs(b)) < EXACT_REL
+    rows = [0, 1, 255, 256, 2047, 3001, 4606, 4607]
+    want = O.matmul(x.reshape(m, k)[rows].ravel(), O.INT4G64, packed, len(rows), n, k, gscale=scales, threads=0)
+    assert O.rel_error(a[rows].ravel(), want) < EXACT_REL
+
+
+def _wide_rows(k):
+    rng = np.random.default_rng(11)
+    r0 = rng.standard_normal(k).astype(np.float32)
+    r0[17] = 1000.0  # one outlier among N(0, 1): the realistic post-norm case
+    r1 = rng.standard_normal(k).astype(np.float32)
+    r1[k - 3] = -1000.0
+    mag = 10.0 ** rng.uniform(-6, 3, k)  # 9 decades of magnitude
+    r2 = (mag * np.sign(rng.standard_normal(k))).astype(np.float32)
+    r3 = rng.standard_normal(k).astype(np.float32)  # an ordinary row
+    return bf16_round(np.stack([r0, r1, r2, r3]).ravel())
+
+
+def test_split_on_a_wide_dynamic_range(we, graph):
+    """What "exact" covers: hi + lo reproduces every bf16 value v with |v| >= 2^(e-2) (2^e the row scale, the
+    smallest power of two with max|x| 2^-e <= 448), and is within 2^(e-10) of the rest (lo's subnormal step)."""
+    m, k, n = 4, 3072, 512
+    x = _wide_rows(k)
+    mark = graph.mark()
+    xb = graph.buffer(bf16(x))
+    hi, lo, rs = graph.buffer(m * k), graph.buffer(m * k), graph.buffer(m * 4)
+    we.kernels.quantize_act(graph, xb, m, k, hi, lo, rs, terms=2)
+    h, l_, s = graph.read(hi, m * k).copy(), graph.read(lo, m * k).copy(), graph.read(rs, m * 4, np.float32).copy()
+    e4 = O.e4m3_table()
+    rec = (e4[h] + e4[l_]).reshape(m, k) * s[:, None]
+    xr = x.reshape(m, k).astype(np.float64)
+    for r in range(m):
+        e = int(np.ceil(np.log2(np.abs(xr[r]).max() / 448.0)))
+        assert s[r] == 2.0 ** e
+        big = np.abs(xr[r]) >= 2.0 ** (e - 2)
+        assert np.array_equal(rec[r][big], xr[r][big]), r
+        assert np.all(np.abs(rec[r] - xr[r]) <= 2.0 ** (e - 10)), r
+    # the two-term GEMM on these rows: within sum_k |W[n, k]| 2^(e - 10) (plus fp32 accumulation) of float64
+    w = np.random.default_rng(12).integers(0, 256, n * k, dtype=np.uint8)
+    w[(w & 0x7F) == 0x7F] -= 1
+    wb = graph.buffer(w)
+    y = graph.buffer(m * n * 4)
+    we.kernels.matmul(graph, xb, wb, y, m, n, k, 0.002, x_dtype="bf16", w_dtype="fp8")
+    got = graph.read(y, m * n * 4, np.float32).reshape(m, n).astype(np.float64)
+    graph.release(mark)
+    want = O.matmul(x, O.FP8, w, m, n, k, scale=0.002, threads=0).reshape(m, n)
+    wabs = np.abs(e4[w].reshape(n, k)).sum(1) * 0.002
+    for r in range(m):
+        e = int(np.log2(s[r]))
+        bound = wabs * 2.0 ** (e - 10) + 1e-6 * np.abs(want[r]).max()
+        assert np.all(np.abs(got[r] - want[r]) <= bound), r
+    assert O.rel_error(got[3], want[3]) < EXACT_REL  # the ordinary row: exact as on every N(0, 1) test
+
+
+@pytest.fixture
+def torch_on_graph(graph):
+    """torch with the graph's stream as its current stream, so that torch's tensor ops and the library's kernels
+    are ordered on one stream."""
+    torch = pytest.importorskip("torch")
+    with torch.cuda.stream(torch.cuda.ExternalStream(graph.stream, device=torch.device("cuda", 0))):
+        yield torch
+    torch.cuda.synchronize()
+
+
+def _device_linear(we, g, torch, gen, dev, n, k):
+    w32 = torch.randn(n, k, generator=gen, device=dev) * 0.02
+    q = torch.empty(n, k, dtype=torch.uint8, device=dev)
+    s = torch.empty(n, dtype=torch.float32, device=dev)
+    we.kernels.quantize_fp8(g, w32, n, k, q, s, per_channel=True, w_dtype="f32")
+    return we.Linear(q, "fp8", 1.0, n, k, chan_scale=s)
+
+
+def _device_block(we, g, torch, gen, dev, bc):
+    hid, hd = bc.hidden, bc.head_dim
+    shapes = {"wq": (bc.heads * hd, hid), "wk": (bc.kv_heads * hd, hid), "wv": (bc.kv_heads * hd, hid),
+              "wo": (hid, hid), "mlp_up": (bc.mlp, hid), "mlp_down": (hid, bc.mlp)}
+    w = {name: _device_linear(we, g, torch, gen, dev, n, k) for name, (n, k) in shapes.items()}
+    for name, d, std in (("norm1", hid, 0.5), ("norm2", hid, 0.5), ("norm_q", hd, 0.5), ("norm_k", hd, 0.5),
+                         ("table", 6 * hid, 0.3)):
+        w[name] = torch.randn(d, generator=gen, device=dev) * std
+    return we.blocks.fuse_qkv(g, we.blocks.BlockWeights(**w))
+
+
+def _host_block(w):
+    """Host copies of a device block for the float64 oracle."""
+    out = {}
+    for name in ("wq", "wk", "wv", "wo", "mlp_up", "mlp_down"):
+        lin = getattr(w, name)
+        out[name] = {"bytes": lin.buffer.cpu().numpy().ravel(), "n": lin.n, "k": lin.k,
+                     "chan_scale": lin.chan_scale.cpu().numpy()}
+    for name in ("norm1", "norm2", "norm_q", "norm_k", "table"):
+        out[name] = getattr(w, name).cpu().numpy()
+    return out
+
+
+def test_config3_block_in_full(we, graph, torch_on_graph):
+    torch = torch_on_graph
+    T = we.transformer
+    bc = T.FLUX_BLOCK
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(31)
+    rows, cols = T.patch_grid(128, 128)
+    tokens = 512 + rows * cols
+    bw = _device_block(we, graph, torch, gen, dev, bc)
+    x = torch.randn(tokens, bc.hidden, generator=gen, device=dev)
+    tvec = torch.randn(6 * bc.hidden, generator=gen, device=dev) * 0.3
+    cos, sin, pairs = we.kernels.rope_tables(we.kernels.positions(512, rows, cols), (16, 56, 56), 1e4)
+    rope = we.Rope(torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev), pairs, tokens)
+    outs = {}
+    for dt in ("bf16", "f32"):
+        mark = graph.mark()
+        out = we.blocks.block(graph, bw, bc, x, tvec, rope, dtype=dt)
+        outs[dt] = graph.read(out, tokens * bc.hidden * 4, np.float32).reshape(tokens, -1).copy()
+        graph.release(mark)
+    assert graph.device_error() == 0
+    xh = x.cpu().numpy()
+    cos_, rel = _cmp(outs["bf16"] - xh, outs["f32"] - xh)
+    assert cos_ >= COS and rel < MAXREL, (cos_, rel)
+    # 24 rows (text and image, first and last) of the f32 path against the float64 oracle
+    sel = [0, 1, 255, 511, 512, 513, 1000, 2048, 2049, 3000, 3071, 3072, 3500, 4000, 4100, 4200, 4300, 4400, 4500,
+           4550, 4600, 4605, 4606, 4607]
+    want = O.block_rows_reference(xh, _host_block(bw), vars(bc), tvec.cpu().numpy(), cos, sin, sel)
+    c64, rel64 = _cmp(outs["f32"][sel] - xh[sel], want - xh[sel])
+    assert c64 > 0.99999 and rel64 < 1e-4, (c64, rel64)  # the reference block test's bound (block.test.ts:131-132)
+    cb, relb = _cmp(outs["bf16"][sel] - xh[sel], want - xh[sel])
+    assert cb >= COS and relb < MAXREL, (cb, relb)
+
+
+def test_config4_step_in_full(we, graph, torch_on_graph):
+    torch = torch_on_graph
+    T = we.transformer
+    scfg = T.StepConfig()
+    bc, hid, ch = scfg.block, scfg.block.hidden, scfg.channels
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(41)
+    edge = {name: _device_linear(we, graph, torch, gen, dev, n, k) for name, (n, k) in
+            (("first", (hid, 4 * ch)), ("tmlp0", (hid, scfg.time_dim)), ("tmlp2", (hid, hid)),
+             ("tproj", (6 * hid, hid)), ("txt_in", (hid, scfg.ctx_dim)), ("last_linear", (4 * ch, hid)))}
+    double = [(_device_block(we, graph, torch, gen, dev, bc), _device_block(we, graph, torch, gen, dev, bc))
+              for _ in range(scfg.double)]
+    single = [_device_block(we, graph, torch, gen, dev, bc) for _ in range(scfg.single)]
+    vec = {name: torch.randn(hid, generator=gen, device=dev) * 0.3 for name in ("last_norm", "last_scale", "last_shift")}
+    model = T.TransformerWeights(double=double, single=single, **edge, **vec)
+    side, text = 128, 512
+    lat = torch.randn(ch, side, side, generator=gen, device=dev).to(torch.bfloat16)
+    ctx = torch.randn(text, scfg.ctx_dim, generator=gen, device=dev).to(torch.bfloat16)
+    vel = {}
+    for name, dt, latent, context in (("bf16", "bf16", lat, ctx), ("f32", "f32", lat.float(), ctx.float())):
+        v = torch.empty(ch, side, side, dtype=torch.float32, device=dev)
+        T.transformer(graph, model, scfg, T.StepInputs(latent, side, side, 0.7, context, text), dtype=dt, velocity=v)
+        graph.sync()
+        vel[name] = v.cpu().numpy().copy()
+    sgr = T.StepGraph(graph, model, scfg, side, side, text, dtype="bf16")
+    v = torch.empty(ch, side, side, dtype=torch.float32, device=dev)
+    for _ in range(2):  # two replays: the graph's buffers are reused
+        T.transformer(graph, model, scfg, T.StepInputs(lat, side, side, 0.7, ctx, text), dtype="bf16", velocity=v,
+                      captured=sgr)
+    graph.sync()
+    vel["graph"] = v.cpu().numpy().copy()
+    sgr.destroy()
+    assert graph.device_error() == 0
+    assert np.isfinite(vel["f32"]).all()
+    cos_, rel = _cmp(vel["bf16"], vel["f32"])
+    assert cos_ >= COS and rel < MAXREL, ("eager bf16 step vs f32 step", cos_, rel)
+    assert np.array_equal(vel["graph"], vel["bf16"])  # the replay runs the same kernels on the same inputs
