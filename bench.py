@@ -552,7 +552,29 @@ def main() -> None:
 
         i4_ms = timed(step_int4, args.steps, 2) / args.steps
         variants["int4_g64_linear"] = {"tflops": FLOPS / (i4_ms * 1e-3) / 1e12, "ms": i4_ms,
-                                       "note": "int4 group-64 decode to bf16 + tcgen05 kind::f16"}
+                                       "note": "int4 group-64 at config 2's size: decode to bf16 in HBM + tcgen05 "
+                                               "kind::f16 (the library's choice at 18 token tiles)"}
+        os.environ["WE_TC_I4"] = "1"  # the in-kernel unpack at the same size, for comparison
+        i4k_ms = timed(step_int4, args.steps, 2) / args.steps
+        del os.environ["WE_TC_I4"]
+        variants["int4_g64_linear"]["in_kernel_unpack_ms"] = i4k_ms
+        # one token tile (M = 256): the library unpacks W inside the GEMM (converter warps -> shared memory)
+        x256 = x[:256]
+
+        def step_int4_256():
+            mark = g.mark()
+            we.linear(g, x256, lin4, 256, x_dtype="bf16", y_dtype="bf16")
+            g.release(mark)
+
+        i4s_ms = timed(step_int4_256, args.steps, 2) / args.steps
+        os.environ["WE_TC_I4"] = "0"
+        i4s_dec_ms = timed(step_int4_256, args.steps, 2) / args.steps
+        del os.environ["WE_TC_I4"]
+        variants["int4_g64_linear_m256"] = {"ms": i4s_ms, "tflops": 2.0 * 256 * N * K / (i4s_ms * 1e-3) / 1e12,
+                                            "decode_first_ms": i4s_dec_ms,
+                                            "note": "M=256 (one token tile): W unpacked inside the GEMM, the "
+                                                    "library's choice here; decode_first_ms: decoding W to bf16 in "
+                                                    "HBM first"}
 
     # ---- the bandwidth kernels around the GEMM at block size (config 3: 4608 tokens, hidden 3072, 24 heads) ----
     hbm = float(peaks.get("hbm_gbs", 6650.0))

@@ -289,3 +289,62 @@ def test_tc_config2_full_against_cuda_core_and_oracle_rows(we, graph):
     rows = [0, 1, 127, 128, 2047, 3000, 4606, 4607]
     want = O.matmul(x.reshape(m, k)[rows].ravel(), O.FP8, q, len(rows), n, k, scale=0.002, threads=0)
     assert O.rel_error(a[rows].ravel(), want) < EXACT_REL
+
+
+@pytest.mark.parametrize("warps", ["8", "4"])
+@pytest.mark.parametrize("m,n,k", [(70, 300, 192), (256, 512, 3072), (513, 1000, 1024), (4608, 768, 3072)])
+def test_int4_unpacked_in_the_gemm_equals_decode_then_bf16_gemm(we, graph, monkeypatch, warps, m, n, k):
+    """int4 group-64 weights are unpacked by the GEMM's converter warps (8, or 4) into shared memory (bf16_rne(q * s)
+    in the tensor-core operand layout): the output equals, bit for bit, decoding W to bf16 in HBM (we_unpack_int4)
+    and running the bf16 GEMM on the same kernel form (1-SM, 256-token tiles), on ragged shapes (N past the last
+    tile, K past the last stage), with bias, per-channel scale, an activation and bf16 output."""
+    monkeypatch.setenv("WE_TC_I4", "1")  # the in-kernel unpack at every size (by default only where it is faster)
+    monkeypatch.setenv("WE_TC_I4_WARPS", warps)
+    monkeypatch.setenv("WE_TC_2SM", "0")  # the decoded path on the same kernel form: same MMA order
+    monkeypatch.setenv("WE_TC_BT", "256")
+    x = bf16_round(randn(m * k, 51))
+    packed, scales = O.quant_int4_g64(randn(n * k, 52, 0.02), n, k)
+    cs = (np.abs(randn(n, 53, 0.5)) + np.float32(0.5)).astype(np.float32)
+    bias = randn(n, 54)
+    mark = graph.mark()
+    xb, pb, sb, csb, bb = (graph.buffer(a) for a in (bf16(x), packed, scales, cs, bias))
+    wd = graph.buffer(n * k * 2)
+    we.kernels.unpack_int4(graph, pb, sb, n, k, wd)
+    for y_dtype, act in (("f32", None), ("bf16", "gelu_tanh")):
+        ysz = 4 if y_dtype == "f32" else 2
+        y4, yd = graph.buffer(m * n * ysz), graph.buffer(m * n * ysz)
+        t0 = graph.stats["tcGemms"]
+        we.kernels.matmul(graph, xb, pb, y4, m, n, k, 1.0, x_dtype="bf16", w_dtype="int4", group_scale=sb,
+                          chan_scale=csb, bias=bb, y_dtype=y_dtype, act=act)
+        we.kernels.matmul(graph, xb, wd, yd, m, n, k, 1.0, x_dtype="bf16", w_dtype="bf16", chan_scale=csb, bias=bb,
+                          y_dtype=y_dtype, act=act)
+        assert graph.stats["tcGemms"] == t0 + 2
+        a, b = graph.read(y4, m * n * ysz).copy(), graph.read(yd, m * n * ysz).copy()
+        assert np.array_equal(a, b), y_dtype
+    if m <= 513:
+        y = graph.buffer(m * n * 4)
+        we.kernels.matmul(graph, xb, pb, y, m, n, k, 1.0, x_dtype="bf16", w_dtype="int4", group_scale=sb)
+        want = O.matmul(x, O.INT4G64, packed, m, n, k, gscale=scales, threads=0)
+        assert O.rel_error(graph.read(y, m * n * 4, np.float32), want) < EXACT_REL
+    assert graph.device_error() == 0
+    graph.release(mark)
+
+
+@pytest.mark.parametrize("offset", [1, 4, 8])
+def test_int4_packed_weights_at_any_alignment(we, graph, offset):
+    """Packed int4 weights that do not start on a 16-byte boundary cannot feed the converter warps' 8- and 16-byte
+    loads: 4- and 8-byte aligned ones are decoded to bf16 first (4-byte words), others run on the CUDA-core kernel
+    (byte loads). Every case matches the float64 oracle."""
+    m, n, k = 64, 96, 256
+    x = bf16_round(randn(m * k, 61))
+    packed, scales = O.quant_int4_g64(randn(n * k, 62, 0.02), n, k)
+    mark = graph.mark()
+    base = graph.buffer(n * k // 2 + 32)
+    graph.write(base, np.concatenate([np.zeros(offset, np.uint8), packed]))
+    xb, sb, y = graph.buffer(bf16(x)), graph.buffer(scales), graph.buffer(m * n * 4)
+    we.kernels.matmul(graph, xb, base.ptr + offset, y, m, n, k, 1.0, x_dtype="bf16", w_dtype="int4", group_scale=sb)
+    got = graph.read(y, m * n * 4, np.float32).copy()
+    assert graph.device_error() == 0
+    graph.release(mark)
+    want = O.matmul(x, O.INT4G64, packed, m, n, k, gscale=scales, threads=0)
+    assert O.rel_error(got, want) < EXACT_REL

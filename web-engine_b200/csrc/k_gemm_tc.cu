@@ -61,6 +61,10 @@ struct Params {
   int nseg;
   int32_t row_end[WE_GEMM_MAX_SEGMENTS];
   uint8_t row_set[WE_GEMM_MAX_SEGMENTS];
+  // int4 group-64 weights (gemm_tc_i4_kernel): packed [n, k / 2], f16 group scales [n, k / 64]
+  const uint8_t* w4;
+  const uint16_t* w4_scale;
+  int64_t k;
 };
 
 // The token tile of the i-th tile in schedule order. With two weight sets the tiles of set 0 come first, then those
@@ -718,6 +722,290 @@ __global__ void __launch_bounds__(THREADS, 1)
 #undef DRAIN
 }
 
+// 8 int4 values (one u32: value 2i in bits 8i..8i+3, value 2i+1 in bits 8i+4..8i+7) times the group scale s,
+// rounded to bf16: the same bf16_rne(q * s) as int4_operand, on bf16x2 FMA-pipe math (a float -> bf16 convert per
+// pair would saturate the conversion pipe). A byte permute and a mask build v = 128 + (nib ^ 8) as bf16 (exact),
+// q = v - 136 = (nib ^ 8) - 8 exactly; with s = s_hi + s_lo split exactly into two bf16 values (s_lo has at most
+// 3 significant bits), q * s_lo is exact and fma(q, s_hi, q * s_lo) rounds q * s once, to nearest even.
+struct I4Scale {
+  __nv_bfloat162 hi, lo;
+};
+__device__ __forceinline__ I4Scale i4_scale(float s) {
+  const __nv_bfloat162 hi = __float2bfloat162_rn(s);
+  return I4Scale{hi, __float2bfloat162_rn(s - __low2float(hi))};  // the remainder is exact in bf16
+}
+__device__ __forceinline__ uint4 int4x8_to_bf16x8(uint32_t w, const I4Scale& sc) {
+  const uint32_t w4 = w >> 4;
+  const __nv_bfloat162 m136 = __floats2bfloat162_rn(-136.f, -136.f);
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    // low half: byte j of w (value 2j in its low nibble), high half: byte j of w >> 4 (value 2j + 1); keeping the
+    // low nibbles and flipping bit 3 under the 0x43 high byte gives bf16 128 + (nib ^ 8) in each half
+    const uint32_t v = (__byte_perm(w, w4, (uint32_t)(j | (4 + j) << 8)) & 0x000F000Fu) ^ 0x43084308u;
+    const __nv_bfloat162 q = __hadd2(*reinterpret_cast<const __nv_bfloat162*>(&v), m136);
+    const __nv_bfloat162 r = __hfma2(q, sc.hi, __hmul2(q, sc.lo));
+    o[j] = *reinterpret_cast<const uint32_t*>(&r);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---------------- the 1-SM kernel with int4 group-64 weights unpacked in the kernel ----------------
+// The 1-SM kernel's kind::f16 form (128 weight rows x BT tokens per CTA, one 64-value K atom per stage, which is
+// exactly one int4 group), with W written by CW converter warps (warps 6 .. 6 + CW - 1) instead of TMA. All signals
+// stay inside the CTA: the converters arrive on the stage's full barrier after fencing their stores into the async
+// proxy. (A 2-SM form, where the peer CTA's converters must arrive on the leader's barrier every stage, measured
+// slower than decoding W to bf16 first: the cross-SM release arrive cost 1-3 us per stage.) A converter thread takes
+// 16 / CW items per stage: weight row (128 / CW) cw + 8 i + (lane & 7), values [16 part, 16 part + 16) with
+// part = lane >> 3, i.e. 8 packed bytes (one 8-byte load; a warp reads 32 contiguous bytes of each of 8 rows) and
+// two 16-byte stores (a quarter-warp covers 8 rows of one chunk: 8 different bank groups). The packed bytes and
+// scales of a stage are loaded I4_AHEAD stages before it is written (a ring of register sets), since an L2 load
+// under a running GEMM takes longer than a stage's MMAs.
+constexpr int I4_AHEAD = 3;
+template <int CW>
+struct I4Stage1 {
+  static constexpr int ITEMS = 16 / CW;
+  uint2 w[ITEMS];
+  float s[ITEMS];
+};
+template <int CW>
+__device__ __forceinline__ void i4_load1(I4Stage1<CW>& st, const Params& p, int64_t row0, int kb, int cw, int lane) {
+  const int part = lane >> 3;
+  const int64_t groups = p.k / 64, row_bytes = p.k / 2;
+#pragma unroll
+  for (int i = 0; i < I4Stage1<CW>::ITEMS; i++) {
+    const int64_t row = row0 + cw * (128 / CW) + i * 8 + (lane & 7);
+    if (row < p.n && kb < groups) {
+      st.w[i] = __ldg(reinterpret_cast<const uint2*>(p.w4 + row * row_bytes + (int64_t)kb * 32 + part * 8));
+      st.s[i] = __half2float(__ushort_as_half(__ldg(p.w4_scale + row * groups + kb)));
+    } else {  // past the weight's rows: zeros (the MMA must not see stale bytes)
+      st.w[i] = make_uint2(0x88888888u, 0x88888888u);  // q = 0
+      st.s[i] = 0.f;
+    }
+  }
+}
+template <int CW>
+__device__ __forceinline__ void i4_store1(const I4Stage1<CW>& st, uint8_t* wst, int cw, int lane) {
+  const int part = lane >> 3;
+#pragma unroll
+  for (int i = 0; i < I4Stage1<CW>::ITEMS; i++) {
+    const int r = cw * (128 / CW) + i * 8 + (lane & 7);
+    const I4Scale sc = i4_scale(st.s[i]);
+    const uint32_t wd[2] = {st.w[i].x, st.w[i].y};
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int c = part * 2 + j;  // 16-byte chunk of the 128-byte row
+      *reinterpret_cast<uint4*>(wst + r * 128 + ((c ^ (r & 7)) << 4)) = int4x8_to_bf16x8(wd[j], sc);
+    }
+  }
+}
+
+template <int BT, int CW>
+__global__ void __launch_bounds__(192 + 32 * CW, 1)
+    gemm_tc_i4_kernel(const __grid_constant__ CUtensorMap tm_x0, const Params p) {
+  using L = Layout<BT, 1>;
+  constexpr int STAGES = L::STAGES;
+  constexpr int KB_ELEMS = KB_BYTES / 2;
+  constexpr uint32_t TMEM_COLS = 2 * BT;
+  constexpr uint32_t IDESC = make_idesc<BT, true>();
+  constexpr int MMAS_PER_KB = KB_BYTES / 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + L::BAR_OFFSET;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::BAR_OFFSET + L::NUM_BARS * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+#define FULL(s) (bars + 8u * (s))
+#define EMPTY(s) (bars + 8u * (STAGES + (s)))
+#define TFULL(b) (bars + 8u * (2 * STAGES + (b)))
+#define TEMPTY(b) (bars + 8u * (2 * STAGES + 2 + (b)))
+#define DRAIN (bars + 8u * (2 * STAGES + 4))
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(FULL(s), 1 + CW);  // the producer's arrive.expect_tx + the converter warps
+      mbar_init(EMPTY(s), 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(TFULL(b), 1);
+      mbar_init(TEMPTY(b), 4);
+    }
+    mbar_init(DRAIN, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  const int64_t tiles_n = (p.n + BM - 1) / BM;
+  const int64_t tiles_m = (p.m + BT - 1) / BT;
+  const int64_t tiles = tiles_n * tiles_m;
+
+  if (warp == 0) {
+    if (lane == 0) {  // the token operand by TMA
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm_x0)) : "memory");
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_ph[STAGES];
+      int issued = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int32_t row_x = (int32_t)((t / tiles_n) * BT);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!wait_fast(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
+          mbar_expect_tx(FULL(s), L::X_BYTES);
+          tma_load_2d(st + L::W_BYTES, &tm_x0, FULL(s), kb * KB_ELEMS, row_x);
+          issued_ph[s] = ph;
+          issued++;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {  // the loads already issued land before the CTA can exit
+        for (int i = 0; i < STAGES && i < issued; i++)
+          wait_fast(FULL(i), issued_ph[i], abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, aph = 0;
+      int ab = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!wait_fast(TEMPTY(ab), aph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(ab * BT);
+        for (int kb = 0; kb < p.num_kb; kb++) {
+          if (!wait_fast(FULL(s), ph, abort_flag, p.err, DEV_ERR_TIMEOUT_MMA, WAIT_LIMIT_NS, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sbase + (uint32_t)(s * L::STAGE_BYTES);
+          const uint64_t adesc = sw128_desc(st), bdesc = sw128_desc(st + L::W_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < MMAS_PER_KB; kk++)
+            umma<true>(d, adesc + 2u * kk, bdesc + 2u * kk, IDESC, (kb | kk) != 0);
+          umma_commit(EMPTY(s));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(TFULL(ab));
+        if (++ab == 2) {
+          ab = 0;
+          aph ^= 1u;
+        }
+      }
+      umma_commit(DRAIN);
+      wait_fast(DRAIN, 0, abort_flag, p.err, DEV_ERR_TIMEOUT_DRAIN, DRAIN_LIMIT_NS, false);
+    }
+    __syncwarp();
+  } else if (warp >= 6) {
+    // converters: packed int4 + the stage's group scale -> bf16 W, loads I4_AHEAD stages ahead
+    const int cw = warp - 6;
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    auto put = [&](const I4Stage1<CW>& cur) -> bool {
+      const bool got = wait_fast(EMPTY(s), ph ^ 1u, abort_flag, p.err, DEV_ERR_TIMEOUT_PRODUCER, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, got)) return false;
+      i4_store1<CW>(cur, smem + s * L::STAGE_BYTES, cw, lane);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the MMA's async reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(FULL(s));
+      if (++s == STAGES) {
+        s = 0;
+        ph ^= 1u;
+      }
+      return true;
+    };
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const int64_t row0 = (t % tiles_n) * BM;
+      I4Stage1<CW> ring[I4_AHEAD + 1];
+#pragma unroll
+      for (int u = 0; u < I4_AHEAD; u++)
+        if (u < p.num_kb) i4_load1<CW>(ring[u], p, row0, u, cw, lane);
+      for (int kb = 0; kb < p.num_kb && ok; kb += I4_AHEAD + 1) {
+#pragma unroll
+        for (int u = 0; u <= I4_AHEAD; u++) {  // static ring slots: stage kb + u is in slot u
+          if (!ok || kb + u >= p.num_kb) break;
+          if (kb + u + I4_AHEAD < p.num_kb)
+            i4_load1<CW>(ring[(u + I4_AHEAD) % (I4_AHEAD + 1)], p, row0, kb + u + I4_AHEAD, cw, lane);
+          ok = put(ring[u]);
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    float* stage = reinterpret_cast<float*>(smem + L::EPI_OFFSET) + (warp - 2) * (32 * EPI_LD);
+    int ab = 0;
+    uint32_t aph = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int64_t ch_base = (t % tiles_n) * BM + q * 32;
+      const int64_t ch = ch_base + lane;
+      const int64_t tok_base = (t / tiles_n) * BT;
+      const bool ch_ok = ch < p.n;
+      const float cs = ch_ok ? (p.chan_scale ? p.chan_scale[ch] : p.scale) : 0.f;
+      const float bias = (ch_ok && p.bias) ? p.bias[ch] : 0.f;
+      EpiFetch f;
+      float gt[8];
+      const YOut yo = y_out(p, ch_base);
+      epi_fetch_first(f, lane, tok_base, ch_base, yo, p);
+      epi_gate(gt, lane, ch_base, p.epi.gate, p);
+      bool ok = wait_fast(TFULL(ab), aph, abort_flag, p.err, DEV_ERR_TIMEOUT_EPILOGUE, WAIT_LIMIT_NS, true);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; c++) {
+        const int64_t tok0 = tok_base + c * 32;
+        if (tok0 >= p.m) break;
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BT + c * 32), r);
+        const bool last = c == BT / 32 - 1 || tok0 + 32 >= p.m;
+        if (last) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(TEMPTY(ab));
+        }
+        epilogue_chunk(r, f, gt, !last, stage, lane, tok0, ch_base, cs, bias, yo, p);
+        __syncwarp();
+      }
+      if (++ab == 2) {
+        ab = 0;
+        aph ^= 1u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+#undef FULL
+#undef EMPTY
+#undef TFULL
+#undef TEMPTY
+#undef DRAIN
+}
+
 // ---------------- host side ----------------
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -785,6 +1073,9 @@ static Params make_params(const TcGemmArgs& a) {
     p.row_set[i] = i < a.nseg ? (uint8_t)a.row_set[i] : 0;
   }
   p.err = a.dev_err;
+  p.w4 = a.int4 ? static_cast<const uint8_t*>(a.w) : nullptr;
+  p.w4_scale = a.int4 ? a.group_scale : nullptr;
+  p.k = a.k;
   return p;
 }
 
@@ -852,9 +1143,31 @@ static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
   e = cudaLaunchKernelEx(&cfg, kern, mw, mx0, mx1, mw2, p);
   return e == cudaSuccess ? cudaGetLastError() : e;
 }
+// int4 group-64 weights: the W operand is made by the kernel's converter warps, so only the tokens have a tensor map
+template <int BT, int CW>
+static cudaError_t run_i4(const TcGemmArgs& a, int sms, cudaStream_t st) {
+  using L = Layout<BT, 1>;
+  CUtensorMap mx0;
+  if (!make_map(&mx0, a.x[0], true, a.k, a.m, a.x_stride_bytes, BT)) return cudaErrorNotSupported;
+  Params p = make_params<true>(a);
+  auto kern = gemm_tc_i4_kernel<BT, CW>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = ((a.n + BM - 1) / BM) * ((a.m + BT - 1) / BT);
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  kern<<<grid, 192 + 32 * CW, L::ALLOC, st>>>(mx0, p);
+  return cudaGetLastError();
+}
 }  // namespace tc
 
 bool gemm_tc_supported(const TcGemmArgs& a) {
+  if (a.int4) {  // packed weights read by the converter warps (16-byte loads), bf16 tokens by TMA
+    auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+    return a.kind_f16 && a.terms == 1 && a.nseg == 0 && a.group_scale && ((uintptr_t)a.group_scale & 1) == 0 &&
+           a.m >= 1 && a.n >= 1 && a.k >= 64 &&
+           a.k % 64 == 0 && al(a.w) && al(a.x[0]) && a.x_stride_bytes % 16 == 0 && a.x_stride_bytes >= a.k * 2 &&
+           a.m <= 0x7fffffffLL && a.n <= 0x7fffffffLL && a.k <= 0x7fffffffLL;
+  }
   const int es = a.kind_f16 ? 2 : 1;
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
   if (a.m < 1 || a.n < 1 || a.k < 1) return false;
@@ -880,6 +1193,11 @@ static int seg_tile(const TcGemmArgs& a) {
 // Token tile: the largest of 256 / 128 / 64 that still gives every SM a tile, else 64.
 cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (!gemm_tc_supported(a)) return cudaErrorNotSupported;
+  if (a.int4) {
+    if (const char* env = getenv("WE_TC_I4_WARPS"))  // tuning override: 4 converter warps instead of 8
+      if (atoi(env) == 4) return tc::run_i4<256, 4>(a, sms, st);
+    return tc::run_i4<256, 8>(a, sms, st);
+  }
   const int max_bt = seg_tile(a);  // token tiles may not straddle two weight sets
   if (max_bt == 0) return cudaErrorNotSupported;
   // Kernel and token tile by a cost model of waves x per-SM tile cost: a 1-SM tile (128 channels x bt tokens) costs

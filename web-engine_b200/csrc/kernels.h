@@ -64,6 +64,10 @@ struct TcGemmArgs {
   int nseg;
   int64_t row_end[WE_GEMM_MAX_SEGMENTS];
   int row_set[WE_GEMM_MAX_SEGMENTS];
+  // int4 group-64 weights unpacked inside the GEMM (kind_f16 = 1): w is packed [n, k / 2] (low nibble = even k),
+  // group_scale f16 [n, k / 64]; k % 64 == 0, one weight set
+  int int4;
+  const uint16_t* group_scale;
 };
 // Returns cudaErrorNotSupported when the layout cannot go through TMA (alignment) so the caller can
 // use the CUDA-core kernel instead.

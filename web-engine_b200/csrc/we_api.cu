@@ -389,6 +389,7 @@ int we_matmul_check(we_ctx* ctx, const we_matmul_desc* d) {
     if (d->k % 64) return fail(ctx, WE_EINVAL, "K must be a multiple of 64 for int4 group-64 weights, got " + std::to_string(d->k));
     if (ws != d->k || d->w_offset) return fail(ctx, WE_EINVAL, "int4 group-64 weights must be contiguous [n, k]");
     if (!d->group_scale) return fail(ctx, WE_EINVAL, "int4 group-64 weights need group scales");
+    if ((uintptr_t)d->group_scale & 1) return fail(ctx, WE_EINVAL, "int4 group scales must be 2-byte aligned f16");
   }
   if (d->k_split > 1 && d->bias) return fail(ctx, WE_EINVAL, "bias is not supported with kSplit");
   if (d->epi.act < WE_ACT_NONE || d->epi.act > WE_ACT_SILU) return fail(ctx, WE_EINVAL, "unknown activation");
@@ -483,8 +484,26 @@ static int matmul_impl(we_ctx* ctx, const we_matmul_desc* d, const void* x, cons
       t.w_stride_bytes = a.k * 2;
       t.x[0] = t.x[1] = static_cast<const uint16_t*>(x) + a.x_offset;
       t.x_stride_bytes = a.x_stride * 2;
+      // In-kernel unpack (the GEMM's converter warps write bf16_rne(q * s) into shared memory) converts each weight
+      // once per 256-token tile; decoding W to bf16 in HBM first converts it once and costs n k 4 bytes of traffic.
+      // Measured on config 2's shapes: the in-kernel form wins with one token tile and at least sms / 2 weight-row
+      // tiles (M <= 256, N = 12288: 49 against 58 us), decoding wins everywhere else (M = 4608: 0.27 against 0.43 ms).
+      // Both give the same bf16 operand, so the choice changes no value.
+      bool fuse = a.m <= 256 && ((a.n + 127) / 128) * 2 >= ctx->sms;
+      if (const char* env = getenv("WE_TC_I4"))  // tuning / test override: 1 in-kernel unpack, 0 decode first
+        fuse = atoi(env) == 1;
+      t.int4 = 1;
+      t.w = w;
+      t.group_scale = a.group_scale;
+      ready = fuse && we::gemm_tc_supported(t);
+      t.int4 = 0;
       t.w = reinterpret_cast<void*>(256);
-      if (we::gemm_tc_supported(t)) {
+      if (ready) {
+        t.int4 = 1;
+        t.w = w;
+      } else if (((uintptr_t)w & 3) == 0 && we::gemm_tc_supported(t)) {
+        // packed weights 4- but not 16-byte aligned: decode to bf16 first (the decode reads 4-byte words); less
+        // aligned packed weights go to the CUDA-core kernel, which reads bytes
         void* wb;
         if ((rc = scratch.take((size_t)(a.n * a.k * 2), &wb)) != WE_OK) return rc;
         LK(we::launch_unpack_int4(static_cast<const uint8_t*>(w), a.group_scale, a.n, a.k, (uint16_t*)wb, ctx->sms, st),
