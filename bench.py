@@ -96,50 +96,99 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+def _cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _oracle_sample(O, np, rows: int, threads: int):
+    """One timed float64 oracle matmul over `rows` rows of config 2 (the reference tests' CPU matmul)."""
+    rng = np.random.default_rng(0)
+    w = rng.integers(0, 256, N * K, dtype=np.uint8)
+    w[(w & 0x7F) == 0x7F] = 0
+    cs = np.full(N, 0.002, np.float32)
+    x = O.bf16_round(rng.standard_normal(rows * K, dtype=np.float32))
+    t0 = time.perf_counter()
+    O.matmul(x, O.FP8, w, rows, N, K, chan_scale=cs, threads=threads)
+    return time.perf_counter() - t0
+
+
+def _calibrate_rows(O, np, threads: int, target_s: float) -> int:
+    """Rows of config 2 whose oracle matmul takes about target_s on `threads` threads (untimed calibration)."""
+    rows, dt = 2, 0.0
+    while rows < M:
+        dt = _oracle_sample(O, np, rows, threads)
+        if dt > target_s / 2:
+            break
+        rows = min(M, max(rows * 2, int(rows * target_s / max(dt, 1e-3))))
+    return rows
+
+
 def cpu_baseline(threads: int | None, target_s: float = 12.0) -> dict:
-    """The oracle's float64 matmul (the reference tests' CPU reference) on a bounded row sample of config 2."""
+    """The oracle's float64 matmul (the reference tests' CPU reference) on a bounded row sample of config 2, on all
+    host threads (OpenMP) and on one thread (the reference runs in one JS thread)."""
     sys.path.insert(0, ROOT)
     import numpy as np
 
     from oracle import oracle as O  # the CPU baseline leg: the checker timed as the reference's CPU path
 
-    rng = np.random.default_rng(0)
-    w = rng.integers(0, 256, N * K, dtype=np.uint8)
-    w[(w & 0x7F) == 0x7F] = 0
-    cs = np.full(N, 0.002, np.float32)
     nthreads = threads or os.cpu_count() or 1
-    rows = 2
-    while True:
-        x = O.bf16_round(rng.standard_normal(rows * K, dtype=np.float32))
-        t0 = time.perf_counter()
-        O.matmul(x, O.FP8, w, rows, N, K, chan_scale=cs, threads=nthreads)
-        dt = time.perf_counter() - t0
-        if dt > target_s / 4 or rows >= 4096:
-            break
-        rows = min(4096, max(rows * 2, int(rows * (target_s / 4) / max(dt, 1e-3))))
+    rows = _calibrate_rows(O, np, nthreads, target_s)
+    dt = _oracle_sample(O, np, rows, nthreads)
+    rows1 = max(2, rows // nthreads)
+    dt1 = _oracle_sample(O, np, rows1, 1)
     return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": "TFLOPS", "cores": nthreads, "kind": "port",
-            "sample": f"{rows} of {M} rows of config 2 (float64 oracle, OpenMP {nthreads} threads), {dt:.1f} s"}
+            "sample": f"{rows} of {M} rows of config 2 (float64 oracle, OpenMP {nthreads} threads), {dt:.1f} s",
+            "single_thread": {"value": 2.0 * rows1 * N * K / dt1 / 1e12, "unit": "TFLOPS", "cores": 1,
+                              "sample": f"{rows1} rows, {dt1:.2f} s"},
+            "cpu_model": _cpu_model(), "nproc": os.cpu_count()}
 
 
 def run_reference(args, rank: int) -> None:
+    """The reference arm: every step is one real float64 oracle matmul over a fixed sample of config 2's rows (sized
+    once, untimed, so that warm-up + steps take about a minute), timed step by step; ms_per_step is that measured
+    time, value the sample's FLOPs over it."""
     if rank != 0:
         return
+    sys.path.insert(0, ROOT)
+    import numpy as np
+
+    from oracle import oracle as O  # the reference arm: the reference's CPU path as restated in oracle/
+
     threads = os.cpu_count() or 1
-    per_step = []
-    info = None
+    per_step_s = max(0.5, 60.0 / max(1, args.steps + args.warmup))
+    rows = _calibrate_rows(O, np, threads, per_step_s)
+    times = []
     for i in range(args.warmup + args.steps):
-        info = cpu_baseline(threads, target_s=max(2.0, 60.0 / max(1, args.steps + args.warmup)))
+        dt = _oracle_sample(O, np, rows, threads)
         if i >= args.warmup:
-            per_step.append(info["value"])
-    value = sum(per_step) / len(per_step)
+            times.append(dt)
+    times.sort()
+    med = times[len(times) // 2]
+    value = 2.0 * rows * N * K / med / 1e12
+    rows1 = max(2, rows // threads)
+    dt1 = _oracle_sample(O, np, rows1, 1)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": FLOPS / (value * 1e12) * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": med * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": config_dict(args),
-            "cpu_baseline": {**info, "value": value},
+            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                             "sample": f"each step: {rows} of {M} rows of config 2 (float64 oracle, OpenMP "
+                                       f"{threads} threads), median of {args.steps} timed steps",
+                             "single_thread": {"value": 2.0 * rows1 * N * K / dt1 / 1e12, "unit": "TFLOPS",
+                                               "cores": 1, "sample": f"{rows1} rows, {dt1:.2f} s"},
+                             "cpu_model": _cpu_model(), "nproc": os.cpu_count()},
             "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "rows_per_step": rows, "step_s": times,
             "note": "the reference path is TypeScript/WGSL (no Node or WebGPU on this box); this arm is the C "
-                    "restatement of its float64 CPU matmul reference (tests/gpu/matmul.test.ts:26-35)"}
+                    "restatement of its float64 CPU matmul reference (tests/gpu/matmul.test.ts:26-35); a step is "
+                    "that matmul over rows_per_step rows of config 2, so ms_per_step is the measured time of the "
+                    "sample, not an extrapolation to all 4608 rows"}
     print(json.dumps(line), flush=True)
 
 
@@ -727,7 +776,7 @@ def main() -> None:
                 "clocks": clocks.summary(), "variants": variants,
                 "host_wall_ms_timed_region": wall_headline_ms}
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(None)
+            line["cpu_baseline"] = cpu_baseline(None, target_s=8.0)
     g.destroy()
     if world > 1:
         dist.barrier()
