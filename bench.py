@@ -327,8 +327,14 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
                                    "(1024x1024), random fp8 per-channel weights resident (8.6 GB), bf16 latent/context"}
     # config 4's one image split over all ranks: sequence parallelism (rows sharded, heads exchanged by all-to-all)
     if world > 1:
-        sp = we.sequence.SequenceParallel(device=dev)  # the peer-memory exchange kernel
-        sp_nccl = we.sequence.SequenceParallel(device=dev, peer=False)
+        # the library's NCCL communicator (C ABI); its unique id travels over the bench's own process group
+        import torch.distributed as dist
+
+        uid = [we.comm.unique_id() if dist.get_rank() == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = we.comm.Comm(g, dist.get_rank(), world, uid[0], timeout_ms=120000)
+        sp = we.sequence.SequenceParallel(comm)  # the peer-memory exchange kernel
+        sp_nccl = we.sequence.SequenceParallel(comm, peer=False)
 
         def step_sp():
             T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, sp=sp)
@@ -352,6 +358,8 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
         sp_graph_ms = timed(step_sp_graph, sp_steps, 2) / sp_steps
         sgr_sp.destroy()
         sp.destroy()
+        sp_nccl.destroy()
+        comm.destroy()
         out["step_config4_sequence_parallel"] = {
             "ms": sp_ms, "median_ms_this_rank": per[len(per) // 2], "steps": sp_steps, "n_gpus": world,
             "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12, "launches_per_step": sp_launches,
@@ -457,6 +465,14 @@ def main() -> None:
     yk = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     torch.cuda.synchronize()
 
+    def max_over_ranks(value: float) -> float:
+        """The largest value over the ranks (the bench's own process group; timings are max over ranks)."""
+        if world == 1:
+            return float(value)
+        t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     wall_ms = [0.0]
     step_ms: list = []  # per-step event times of the last timed() call, this rank
 
@@ -479,7 +495,7 @@ def main() -> None:
         wall_ms[0] = (time.perf_counter() - t0) * 1e3
         step_ms[:] = [a.elapsed_time(b) for a, b in ev]
         total = sum(step_ms)
-        return we.parallel.max_over_ranks(total, device=dev)
+        return max_over_ranks(total)
 
     def interleaved(fns: dict, rounds: int, warmup: int) -> dict:
         """Median CUDA-event ms per step of each function, the functions taking turns (one step each per round,
@@ -505,7 +521,7 @@ def main() -> None:
         out = {}
         for name, pairs in ev.items():
             t = sorted(a.elapsed_time(b) for a, b in pairs)
-            out[name] = we.parallel.max_over_ranks(t[len(t) // 2], device=dev)
+            out[name] = max_over_ranks(t[len(t) // 2])
         return out
 
     if args.profile_block:

@@ -389,6 +389,38 @@ void* we_peer_region(const we_peer* peer);
 int we_peer_exchange(we_ctx* ctx, we_peer* peer, const we_peer_copy* copies, int32_t ncopies, uint64_t timeout_ns);
 int we_peer_destroy(we_peer* peer);
 
+/* ---------------- collectives (no counterpart in the reference: it runs on one GPU) ----------------
+   NCCL communicators over NVLink / NVSwitch, one per context (one process per GPU), for the multi-GPU paths: the
+   tensor-parallel linears (all-gather of token shards, reduce-scatter of partial sums), the sequence-parallel
+   attention exchange (all-to-all) and timing reductions. NCCL is loaded when first needed (dlopen libnccl.so.2);
+   without it these calls return WE_EUNSUPPORTED. Rank 0 makes the unique id (we_comm_unique_id, WE_COMM_ID_BYTES)
+   and any host channel carries it to the other ranks, which all call we_comm_init with it. The communicator is
+   non-blocking: each collective returns once queued on the context's stream (device buffers, stream order). A host
+   deadline (timeout_ms, 0 = 60 s) bounds init and every call: a rank that never joins, or an NCCL error, aborts the
+   communicator and returns WE_ETIMEOUT / WE_ENCCL, with the message in we_comm_last_error; an aborted communicator
+   refuses further calls. Every rank must issue the same collectives in the same order. */
+#define WE_COMM_ID_BYTES 128
+typedef struct we_comm we_comm;
+enum { WE_REDUCE_SUM = 0, WE_REDUCE_MAX = 1 };
+int we_comm_unique_id(void* id);
+int we_comm_init(we_ctx* ctx, int32_t nranks, int32_t rank, const void* id, uint64_t timeout_ms, we_comm** out);
+int we_comm_destroy(we_comm* comm);
+int we_comm_abort(we_comm* comm);
+int we_comm_rank(const we_comm* comm, int32_t* rank, int32_t* nranks);
+const char* we_comm_last_error(const we_comm* comm);
+/* y [nranks * bytes] = every rank's x [bytes], in rank order */
+int we_all_gather(we_comm* comm, const void* x, void* y, size_t bytes);
+/* y [count] = this rank's count values of the element-wise sum over ranks of x [nranks * count] (f32 | bf16 | f16) */
+int we_reduce_scatter(we_comm* comm, const void* x, void* y, size_t count, int32_t dtype);
+/* y [count] = the element-wise sum or max over ranks of x [count] (f32 | bf16 | f16); x == y allowed */
+int we_all_reduce(we_comm* comm, const void* x, void* y, size_t count, int32_t dtype, int32_t op);
+/* y [nranks * bytes_per_rank]: chunk p of y is chunk rank of rank p's x (an all-to-all of equal chunks) */
+int we_all_to_all(we_comm* comm, const void* x, void* y, size_t bytes_per_rank);
+/* every rank reaches this point: an all-reduce of one word, then a bounded wait for the context's stream */
+int we_comm_barrier(we_comm* comm);
+/* waits for the context's stream, bounded by the timeout, watching for asynchronous NCCL errors */
+int we_comm_wait(we_comm* comm);
+
 /* ---------------- allocation-free linear (no counterpart in the reference) ----------------
    For callers that cannot allocate device memory: a serving loop whose memory budget is fixed when it
    starts, or a host runtime (a plugin handed only streams and pointers) whose allocator owns all of it.

@@ -1,6 +1,9 @@
-"""Tensor-parallel linear layers on 2 GPUs (one process each, NCCL): column-parallel (N split, token
-all-gather) and row-parallel (K split, reduce-scatter) against the same layer on one GPU.
-Needs two B200s; skipped otherwise (the round-end GPU run has one). NVLS is off (NCCL_NVLS_ENABLE=0)."""
+"""Tensor-parallel linear layers on 2, 4 or 8 GPUs (one process each) through the library's NCCL communicator
+(we_comm_* in the C ABI, web-engine_b200/comm.py): column-parallel (N split, token all-gather) and row-parallel
+(K split, reduce-scatter) against the same layer on one GPU. The unique id travels over comm.rendezvous (plain
+TCP); no framework is involved. Skipped when fewer GPUs are visible (the round-end GPU run has one). NVLS is off
+(NCCL_NVLS_ENABLE=0)."""
+import multiprocessing
 import os
 import socket
 import sys
@@ -18,81 +21,25 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, errq):
+def gpu_count() -> int:
     try:
-        sys.path.insert(0, ROOT)
-        sys.path.insert(0, os.path.join(ROOT, "tests"))
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-        from datetime import timedelta
-
         import torch
-        import torch.distributed as dist
 
-        from conftest import load_package
-        from oracle import oracle as O
-
-        torch.cuda.set_device(rank)
-        dev = torch.device("cuda", rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
-        we = load_package()
-        par = we.parallel
-        g = we.Graph(rank)
-        st = torch.cuda.Stream(device=dev)
-        torch.cuda.set_stream(st)
-        g.set_stream(st.cuda_stream)
-        tp = par.TensorParallel()
-
-        def mm(x, shard, m):
-            w = torch.from_numpy(shard.weight).to(dev)
-            cs = None if shard.chan_scale is None else torch.from_numpy(shard.chan_scale).to(dev)
-            gs = None if shard.group_scale is None else torch.from_numpy(shard.group_scale.view(np.int16)).to(dev)
-            b = None if shard.bias is None else torch.from_numpy(shard.bias).to(dev)
-            y = torch.empty(m, shard.n, dtype=torch.float32, device=dev)
-            we.kernels.matmul(g, x, w, y, m, shard.n, shard.k, shard.scale, x_dtype="bf16", w_dtype=shard.dtype,
-                              chan_scale=cs, group_scale=gs, bias=b)
-            return y
-
-        t, k, n = 1024, 3072, 1536
-        rng = np.random.default_rng(0)
-        xh = O.bf16_round(rng.standard_normal(t * k).astype(np.float32)).reshape(t, k)
-        wf = (rng.standard_normal(n * k) * 0.02).astype(np.float32)
-        q, s = O.quant_fp8_channel(wf, n, k)
-        bias = rng.standard_normal(n).astype(np.float32)
-        x = torch.from_numpy(xh).to(dev).to(torch.bfloat16)
-        full = mm(x, par.Shard(q, "fp8", n, k, chan_scale=s), t) + torch.from_numpy(bias).to(dev)
-
-        tb, te = par.split_range(t, world, rank)
-        nb, ne = par.split_range(n, world, rank)
-        y = tp.column_linear(mm, x[tb:te].contiguous(), par.shard_column(q, "fp8", n, k, world, rank, chan_scale=s,
-                                                                           bias=bias))
-        err = (y - full[:, nb:ne]).abs().max().item() / full.abs().max().item()
-        assert err < 1e-5, ("column", err)
-        kb, ke = par.split_range(k, world, rank, 16)
-        y = tp.row_linear(mm, x[:, kb:ke].contiguous(), par.shard_row(q, "fp8", n, k, world, rank, chan_scale=s),
-                          bias=torch.from_numpy(bias).to(dev))
-        err = (y - full[tb:te]).abs().max().item() / full.abs().max().item()
-        assert err < 1e-5, ("row", err)
-        assert g.device_error() == 0
-        g.destroy()
-        dist.barrier()
-        dist.destroy_process_group()
-    except BaseException as exc:  # noqa: BLE001
-        errq.put(f"rank {rank}: {type(exc).__name__}: {exc}")
-        raise
+        return torch.cuda.device_count()
+    except ImportError:
+        return 0
 
 
-def test_tensor_parallel_linear_on_two_gpus():
-    torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    mp = torch.multiprocessing.get_context("spawn")
+def run_ranks(target, world: int, *args, timeout: float = 300.0) -> None:
+    """Runs target(rank, world, port, errq, *args) in one spawned process per rank; fails on any rank's error."""
+    mp = multiprocessing.get_context("spawn")
     errq = mp.SimpleQueue()
-    world, port = 2, _free_port()
-    procs = [mp.Process(target=_rank_main, args=(r, world, port, errq)) for r in range(world)]
+    port = _free_port()
+    procs = [mp.Process(target=target, args=(r, world, port, errq) + args) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=300)
+        p.join(timeout=timeout)
     alive = [p for p in procs if p.is_alive()]
     for p in alive:
         p.kill()
@@ -100,3 +47,70 @@ def test_tensor_parallel_linear_on_two_gpus():
     while not errq.empty():
         errors.append(errq.get())
     assert not alive and not errors and all(p.exitcode == 0 for p in procs), errors
+
+
+def _rank_main(rank, world, port, errq):
+    try:
+        sys.path.insert(0, ROOT)
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        from conftest import load_package
+        from oracle import oracle as O
+
+        we = load_package()
+        par = we.parallel
+        g = we.Graph(rank)
+        uid = we.comm.rendezvous(rank, world, "127.0.0.1", port)
+        comm = we.comm.Comm(g, rank, world, uid, timeout_ms=60000)
+        tp = par.TensorParallel(comm, g.buffer)
+
+        def mm(x, shard, m):
+            w = g.buffer(shard.weight)
+            cs = None if shard.chan_scale is None else g.buffer(shard.chan_scale)
+            b = None if shard.bias is None else g.buffer(shard.bias)
+            y = g.buffer(m * shard.n * 4)
+            we.kernels.matmul(g, x, w, y, m, shard.n, shard.k, shard.scale, x_dtype="bf16", w_dtype=shard.dtype,
+                              chan_scale=cs, bias=b)
+            return y
+
+        def add_bias(y, bias, rows, n):
+            return we.ops.elementwise(g, "add_bias", y, None, rows * n, g=g.buffer(bias), d=n, dtype="f32",
+                                      out_dtype="f32")
+
+        t, k, n = 1024, 3072, 1536
+        rng = np.random.default_rng(0)
+        xh = O.bf16_round(rng.standard_normal(t * k).astype(np.float32)).reshape(t, k)
+        wf = (rng.standard_normal(n * k) * 0.02).astype(np.float32)
+        q, s = O.quant_fp8_channel(wf, n, k)
+        bias = rng.standard_normal(n).astype(np.float32)
+        full = g.read(mm(g.buffer(O.bf16_bits(xh)), par.Shard(q, "fp8", n, k, chan_scale=s), t), t * n * 4,
+                      np.float32).reshape(t, n) + bias
+
+        tb, te = par.split_range(t, world, rank)
+        nb, ne = par.split_range(n, world, rank)
+        y = tp.column_linear(mm, g.buffer(O.bf16_bits(xh[tb:te])), te - tb, k * 2,
+                             par.shard_column(q, "fp8", n, k, world, rank, chan_scale=s, bias=bias))
+        got = g.read(y, t * (ne - nb) * 4, np.float32).reshape(t, ne - nb)
+        err = np.abs(got - full[:, nb:ne]).max() / np.abs(full).max()
+        assert err < 1e-5, ("column", err)
+        kb, ke = par.split_range(k, world, rank, 16)
+        y = tp.row_linear(mm, g.buffer(O.bf16_bits(np.ascontiguousarray(xh[:, kb:ke]))), t,
+                          par.shard_row(q, "fp8", n, k, world, rank, chan_scale=s), bias=bias, add_bias=add_bias)
+        got = g.read(y, (te - tb) * n * 4, np.float32).reshape(te - tb, n)
+        err = np.abs(got - full[tb:te]).max() / np.abs(full).max()
+        assert err < 1e-5, ("row", err)
+        assert comm.max_over_ranks(1.5 + rank) == 1.5 + (world - 1)
+        assert g.device_error() == 0
+        comm.barrier()
+        comm.destroy()
+        g.destroy()
+    except BaseException as exc:  # noqa: BLE001
+        errq.put(f"rank {rank}: {type(exc).__name__}: {exc}")
+        raise
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_linear_on_gpus(world):
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_ranks(_rank_main, world)

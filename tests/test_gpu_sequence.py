@@ -1,46 +1,38 @@
-"""Sequence parallelism of one image's step on 2 GPUs (one process each): every rank runs the blocks on half of the
-rows, attention exchanges heads all-to-all, through the peer-memory exchange kernel (we_peer_exchange) or NCCL;
-the velocity must equal the one-GPU step's. 80 tokens (8 text + 72 image), so rank 0's shard holds text and image
-rows and rank 1's image rows only. The peer case also checks the exchange itself bit for bit: scattering each
-rank's q rows and gathering them back through an identity "attention" returns them unchanged, and every rank
-receives exactly its heads of every rank's rows. Needs two B200s; skipped otherwise. NVLS is off
-(NCCL_NVLS_ENABLE=0)."""
+"""Sequence parallelism of one image's step on 2, 4 or 8 GPUs (one process each): every rank runs the blocks on
+its share of the rows, attention exchanges heads all-to-all, through the peer-memory exchange kernel
+(we_peer_exchange) or NCCL (we_all_to_all), both on the library's communicator (comm.Comm); the velocity must equal
+the one-GPU step's. 80 tokens (8 text + 72 image), so rank 0's shard holds text and image rows and the others
+image rows only. The peer case also checks the exchange itself bit for bit: scattering each rank's q rows and
+gathering them back through an identity "attention" returns them unchanged, and every rank receives exactly its
+heads of every rank's rows. Skipped when fewer GPUs are visible. NVLS is off (NCCL_NVLS_ENABLE=0)."""
 import os
 import sys
 
 import numpy as np
 import pytest
 
-from test_gpu_multi import _free_port
+from test_gpu_multi import gpu_count, run_ranks
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _rank_main(rank, world, port, peer, errq):
+def _rank_main(rank, world, port, errq, peer):
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "tests"))
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-        from datetime import timedelta
-
-        import torch
-        import torch.distributed as dist
-
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
         from conftest import load_package
         from util import bf16, bf16_round, make_step, randn
 
-        torch.cuda.set_device(rank)
-        dev = torch.device("cuda", rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
         we = load_package()
         g = we.Graph(rank)
-        st = torch.cuda.Stream(device=dev)
-        torch.cuda.set_stream(st)
-        g.set_stream(st.cuda_stream)
+        uid = we.comm.rendezvous(rank, world, "127.0.0.1", port)
+        comm = we.comm.Comm(g, rank, world, uid, timeout_ms=60000)
         T = we.transformer
-        bc = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=2, head_dim=128, mlp_act="gelu",
-                                   attn_gate=False)
+        heads, kvh = (4, 2) if world == 2 else (world, world)  # GQA where the heads split over the ranks
+        bc = we.blocks.BlockConfig(hidden=heads * 128, mlp=heads * 512, heads=heads, kv_heads=kvh, head_dim=128,
+                                   mlp_act="gelu", attn_gate=False)
         scfg = T.StepConfig(block=bc, double=1, single=2, ctx_dim=256)
         h, w, text = 16, 18, 8
         _, wts = make_step(we, g, scfg, 1200, per_channel=True)  # same seeds on every rank: the same model
@@ -48,7 +40,7 @@ def _rank_main(rank, world, port, peer, errq):
         inp = T.StepInputs(g.buffer(bf16(lat)), h, w, 0.37, g.buffer(bf16(ctx)), text)
         v1, _ = T.transformer(g, wts, scfg, inp, dtype="bf16")
         one = g.read(v1, 16 * h * w * 4, np.float32).copy()
-        sp = we.sequence.SequenceParallel(peer=peer)
+        sp = we.sequence.SequenceParallel(comm, peer=peer)
         v2, _ = T.transformer(g, wts, scfg, inp, dtype="bf16", sp=sp)
         got = g.read(v2, 16 * h * w * 4, np.float32).copy()
         err = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
@@ -60,7 +52,7 @@ def _rank_main(rank, world, port, peer, errq):
             assert np.array_equal(g.read(v3, 16 * h * w * 4, np.float32), got), "captured SP step differs"
             sgr.destroy()
         if peer:  # the exchange alone, bit for bit
-            t, heads, kvh, hb = 40, 4, 2, 256
+            t, heads, kvh, hb = 40, 2 * world, world, 256
             rows = [np.random.default_rng(70 + r).integers(0, 65536, t * heads * 128, dtype=np.uint16)
                     for r in range(world)]
             kv = [np.random.default_rng(80 + r).integers(0, 65536, t * kvh * 128, dtype=np.uint16)
@@ -71,7 +63,7 @@ def _rank_main(rank, world, port, peer, errq):
             def identity(qh, kh, vh, oh):  # copies the received q block into the output
                 seen["q"] = g.read(qh, world * t * heads // world * hb, np.uint16).copy()
                 seen["k"] = g.read(kh, world * t * kvh // world * hb, np.uint16).copy()
-                g.copy(qh, 0, oh.data_ptr(), 0, world * t * heads // world * hb)
+                g.copy(qh, 0, oh, 0, world * t * heads // world * hb)
 
             o = sp.exchange_heads(g, qb, kb, kb, t, heads, kvh, hb, identity)
             back = g.read(o, t * heads * hb, np.uint16)
@@ -82,31 +74,17 @@ def _rank_main(rank, world, port, peer, errq):
             assert np.array_equal(seen["q"], want_q) and np.array_equal(seen["k"], want_k)
         assert g.device_error() == 0
         sp.destroy()
+        comm.barrier()
+        comm.destroy()
         g.destroy()
-        dist.barrier()
-        dist.destroy_process_group()
     except BaseException as exc:  # noqa: BLE001
         errq.put(f"rank {rank}: {type(exc).__name__}: {exc}")
         raise
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("peer", [True, False], ids=["peer", "nccl"])
-def test_sequence_parallel_step_on_two_gpus(peer):
-    torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    mp = torch.multiprocessing.get_context("spawn")
-    errq = mp.SimpleQueue()
-    world, port = 2, _free_port()
-    procs = [mp.Process(target=_rank_main, args=(r, world, port, peer, errq)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    alive = [p for p in procs if p.is_alive()]
-    for p in alive:
-        p.kill()
-    errors = []
-    while not errq.empty():
-        errors.append(errq.get())
-    assert not alive and not errors and all(p.exitcode == 0 for p in procs), errors
+def test_sequence_parallel_step(peer, world):
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_ranks(_rank_main, world, peer)

@@ -12,9 +12,10 @@ from . import block as blocks
 from . import transformer
 from . import weights
 from . import sequence
+from . import comm
 
 __all__ = ["Graph", "Buffer", "Binding", "Linear", "Mod", "Rope", "linear", "linear_host", "norm", "no_mod", "rotate",
-           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "weights", "sequence", "build"]
+           "qk_norm_rotate", "k_split_for", "kernels", "blocks", "transformer", "parallel", "Streamer", "weights", "sequence", "comm", "build"]
 
 
 def build(verbose: bool = False) -> str:

@@ -17,6 +17,8 @@ F32, BF16, FP8, INT4G64, F16 = 0, 1, 2, 3, 4
 MM_ACCUMULATE, MM_FP8_FAST, MM_FORCE_SIMT, NOALLOC_SYNC = 1, 2, 4, 8
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 STREAM_HOST_PINNED = 1
+COMM_ID_BYTES = 128
+REDUCE_SUM, REDUCE_MAX = 0, 1
 ROPE_INTERLEAVED, ROPE_HALF = 0, 1
 EW = {"swiglu": 0, "sigmoid_gate": 1, "gated_add": 2, "add_bias": 3, "gelu_tanh": 4, "add": 5, "silu": 6}
 ACTS = {None: 0, "none": 0, "gelu_tanh": 1, "silu": 2}
@@ -179,6 +181,18 @@ _SIGS = {
     "we_peer_destroy": (C.c_int, [_P]),
     "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
                                         C.c_uint32, C.c_char_p, C.c_size_t]),
+    "we_comm_unique_id": (C.c_int, [_P]),
+    "we_comm_init": (C.c_int, [_P, C.c_int32, C.c_int32, _P, C.c_uint64, C.POINTER(C.c_void_p)]),
+    "we_comm_destroy": (C.c_int, [_P]),
+    "we_comm_abort": (C.c_int, [_P]),
+    "we_comm_rank": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "we_comm_last_error": (C.c_char_p, [_P]),
+    "we_all_gather": (C.c_int, [_P, _P, _P, C.c_size_t]),
+    "we_reduce_scatter": (C.c_int, [_P, _P, _P, C.c_size_t, C.c_int32]),
+    "we_all_reduce": (C.c_int, [_P, _P, _P, C.c_size_t, C.c_int32, C.c_int32]),
+    "we_all_to_all": (C.c_int, [_P, _P, _P, C.c_size_t]),
+    "we_comm_barrier": (C.c_int, [_P]),
+    "we_comm_wait": (C.c_int, [_P]),
 }
 
 _lib = None

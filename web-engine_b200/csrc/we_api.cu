@@ -213,6 +213,7 @@ bool act_dtype_ok(int dt) { return dt == WE_F32 || dt == WE_BF16; }
 // helpers shared with the other translation units of the library (we_stream.cu)
 int we_ctx_fail(we_ctx* ctx, int code, const std::string& msg) { return fail(ctx, code, msg); }
 cudaStream_t we_ctx_stream(we_ctx* ctx) { return ctx->stream; }
+int we_ctx_device(we_ctx* ctx) { return ctx->device; }
 uint32_t* we_ctx_dev_err(we_ctx* ctx) { return ctx->dev_err; }
 void we_ctx_count_launch(we_ctx* ctx) { ctx->stats.launches++; }
 bool we_ctx_capturing(const we_ctx* ctx) { return ctx->capturing; }

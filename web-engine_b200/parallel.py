@@ -1,7 +1,8 @@
 """Multi-GPU execution of the linear layers: tensor-parallel shards and data-parallel replicas.
 
-One process per GPU; torch.distributed (NCCL over NVLink/NVSwitch on B200, gloo on CPU for the
-host-logic tests) carries the collectives. The compute of every shard is the single-GPU operator
+One process per GPU; the collectives run on a communicator with comm.Comm's interface: the library's NCCL
+communicator over NVLink/NVSwitch on B200 (we_all_gather / we_reduce_scatter through the C ABI), or, in the CPU
+tests of the host logic, an adapter over gloo. The compute of every shard is the single-GPU operator
 (``ops.linear``), so each rank runs the same kernels as one GPU does.
 
 Tensor parallelism follows the Megatron + sequence-parallel layout of a DiT block (each block has four
@@ -77,61 +78,44 @@ def shard_row(weight: np.ndarray, dtype: str, n: int, k: int, world: int, rank: 
 
 
 class TensorParallel:
-    """The collective steps of a TP linear pair on top of a torch.distributed process group.
+    """The collective steps of a TP linear pair on a communicator (comm.Comm on GPUs).
 
-    `matmul(x, shard, m) -> y` is the single-device linear (``ops.linear`` on a GPU; the tests pass
-    the CPU oracle). Activations are torch tensors on the rank's device."""
+    comm: all_gather(src, dst, nbytes) and reduce_scatter(src, dst, count, dtype) on buffers, rank and world;
+    alloc(nbytes): a new buffer (graph.buffer on a GPU). matmul(x, shard, m) -> y is the single-device linear
+    (``ops.linear`` on a GPU; the CPU tests pass the oracle); add_bias(y, bias, rows, n) -> y adds a full-width
+    bias once after a reduction."""
 
-    def __init__(self, group=None):
-        import torch.distributed as dist
+    def __init__(self, comm, alloc):
+        self.comm, self.alloc = comm, alloc
+        self.world, self.rank = comm.world, comm.rank
 
-        self.dist = dist
-        self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
-
-    def all_gather_tokens(self, x_local):
-        """[T/world, K] per rank -> [T, K] on every rank (equal shards)."""
-        import torch
-
-        out = torch.empty((self.world * x_local.shape[0],) + tuple(x_local.shape[1:]), dtype=x_local.dtype,
-                          device=x_local.device)
-        self.dist.all_gather_into_tensor(out, x_local.contiguous(), group=self.group)
+    def all_gather_tokens(self, x_local, rows: int, row_bytes: int):
+        """[rows, row_bytes] per rank -> [world * rows, row_bytes] on every rank (equal shards, rank order)."""
+        out = self.alloc(self.world * rows * row_bytes)
+        self.comm.all_gather(x_local, out, rows * row_bytes)
         return out
 
-    def reduce_scatter_tokens(self, partial):
-        """[T, N] partial sums per rank -> this rank's [T/world, N] of the sum."""
-        import torch
-
-        t = partial.shape[0]
-        if t % self.world:
-            raise ValueError(f"{t} tokens do not split over {self.world} ranks")
-        out = torch.empty((t // self.world,) + tuple(partial.shape[1:]), dtype=partial.dtype, device=partial.device)
-        self.dist.reduce_scatter_tensor(out, partial.contiguous(), group=self.group)
+    def reduce_scatter_tokens(self, partial, rows: int, n: int, dtype: str = "f32"):
+        """[rows, n] partial sums per rank -> this rank's [rows / world, n] of their sum."""
+        if rows % self.world:
+            raise ValueError(f"{rows} tokens do not split over {self.world} ranks")
+        esz = 4 if dtype == "f32" else 2
+        out = self.alloc(rows // self.world * n * esz)
+        self.comm.reduce_scatter(partial, out, rows // self.world * n, dtype)
         return out
 
-    def column_linear(self, matmul, x_local, shard: Shard):
-        """Column-parallel: gather the token shards, multiply by this rank's output channels."""
-        x = self.all_gather_tokens(x_local)
-        return matmul(x, shard, x.shape[0])
+    def column_linear(self, matmul, x_local, rows: int, row_bytes: int, shard: Shard):
+        """Column-parallel: gather the token shards ([rows, row_bytes] here), multiply by this rank's output
+        channels."""
+        x = self.all_gather_tokens(x_local, rows, row_bytes)
+        return matmul(x, shard, self.world * rows)
 
-    def row_linear(self, matmul, x_cols, shard: Shard, bias=None):
-        """Row-parallel: this rank's K slice of the activations times its K slice of W, summed over ranks
-        and scattered over tokens. `bias` (full [N]) is added once, after the reduction."""
-        partial = matmul(x_cols, shard, x_cols.shape[0])
-        y = self.reduce_scatter_tokens(partial)
+    def row_linear(self, matmul, x_cols, rows: int, shard: Shard, bias=None, add_bias=None):
+        """Row-parallel: this rank's K slice of the activations ([rows, shard.k]) times its K slice of W, summed
+        over ranks and scattered over tokens (f32 partials). `bias` (full [N]) is added once, after the
+        reduction."""
+        partial = matmul(x_cols, shard, rows)
+        y = self.reduce_scatter_tokens(partial, rows, shard.n)
         if bias is not None:
-            y = y + bias
+            y = add_bias(y, bias, rows // self.world, shard.n)
         return y
-
-
-def max_over_ranks(value: float, device=None, group=None) -> float:
-    """The largest `value` over all ranks (timings are reported as the max over ranks)."""
-    import torch
-    import torch.distributed as dist
-
-    if not dist.is_initialized() or dist.get_world_size(group) == 1:
-        return float(value)
-    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-    return float(t.item())

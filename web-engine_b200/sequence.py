@@ -19,33 +19,32 @@ Two ways to run the exchange:
     in the same memory; the output comes back the same way. Three launches per block, no collective library on
     the data path, and the step can be captured in a CUDA graph. The regions alternate between even and odd
     blocks (a rank can never be two exchanges ahead of another).
-  * nccl: we_head_groups to regroup the rows, then NCCL all_to_all_single through torch.distributed.
+  * nccl: we_head_groups to regroup the rows, then an NCCL all-to-all (we_all_to_all).
+Both run over a comm.Comm (the library's NCCL communicator): the peer path uses it to pass the exchange regions'
+handles, the nccl path for the all-to-all itself. No framework is involved.
 """
 from __future__ import annotations
 
 import ctypes as C
 
 from . import _lib as L
-from .graph import Graph, addr
+from .graph import Buffer, Graph, addr
 
 
 class PeerExchange:
     """This rank's exchange region in peer memory and every other rank's, opened once (we_peer_create / export /
-    open; the handles travel through torch.distributed). exchange() runs one we_peer_exchange kernel."""
+    open; the handles travel through the communicator). exchange() runs one we_peer_exchange kernel."""
 
-    def __init__(self, graph: Graph, nbytes: int, group=None):
-        import torch.distributed as dist
-
+    def __init__(self, graph: Graph, nbytes: int, comm):
         self.graph = graph
-        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.rank, self.world = comm.rank, comm.world
         self.nbytes = nbytes
         h = C.c_void_p()
         L.check(graph.ctx, L.lib().we_peer_create(graph.ctx, self.rank, self.world, nbytes, C.byref(h)))
         self.handle = h
         blob = (C.c_ubyte * L.PEER_HANDLE_BYTES)()
         L.check(graph.ctx, L.lib().we_peer_export(h, blob))
-        blobs = [None] * self.world
-        dist.all_gather_object(blobs, bytes(blob), group=group)
+        blobs = comm.all_gather_bytes(bytes(blob))
         allb = (C.c_ubyte * (L.PEER_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(blobs))
         L.check(graph.ctx, L.lib().we_peer_open(h, allb))
         self.region = L.lib().we_peer_region(h)
@@ -95,37 +94,39 @@ def _chunk(nbytes: int, limit: int = 4096) -> int:
 
 
 class SequenceParallel:
-    def __init__(self, group=None, device=None, peer: bool = True):
-        import torch
-        import torch.distributed as dist
+    """One image's rows split over the ranks of `comm` (a comm.Comm on the step's graph). peer: the peer-memory
+    exchange kernel (default), else NCCL all-to-all. Buffers that live across blocks (the head blocks of the NCCL
+    path and the attention output) are kept in a private library context, outside the step's mark / release
+    scopes."""
 
-        self.torch, self.dist = torch, dist
-        self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
-        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self._bufs: dict = {}
+    def __init__(self, comm, peer: bool = True):
+        self.comm = comm
+        self.rank, self.world = comm.rank, comm.world
         self.peer = peer
+        self._store = Graph(comm.graph.device)  # persistent buffers only; no kernel runs on its stream
+        self._bufs: dict = {}
         self._px: dict = {}  # PeerExchange per use ("heads", "rows"), grown collectively when a call needs more
         self._parity = 0
+        self._rows_parity = 0
 
     def _exchange(self, graph: Graph, key: str, nbytes: int) -> PeerExchange:
         px = self._px.get(key)
         if px is None or px.nbytes < nbytes or px.graph is not graph:
             if px is not None:
                 px.destroy()
-            px = PeerExchange(graph, nbytes, self.group)
+            px = PeerExchange(graph, nbytes, self.comm)
             self._px[key] = px
         return px
 
     def destroy(self) -> None:
         """Frees the peer regions once every rank is done with them (a collective: every rank calls it)."""
         if self._px:
-            self.torch.cuda.synchronize(self.device)
-            self.dist.barrier(group=self.group)
+            self.comm.barrier()
         for px in self._px.values():
             px.destroy()
         self._px.clear()
+        self._bufs.clear()
+        self._store.destroy()
 
     def prepare(self, graph: Graph, local_tokens: int, heads: int, kv_heads: int, head_bytes: int) -> None:
         """Creates the exchange region and buffers that exchange_heads needs for this geometry now (a collective),
@@ -160,7 +161,7 @@ class SequenceParallel:
                      scatter_copy(addr(v).value, t, kv_heads, head_bytes, w, off_v)])
         oh = self.buffer("o_heads", qb)
         attend(px.region + off_q, px.region + off_k, px.region + off_v, oh)
-        px.exchange([gather_copy(oh.data_ptr(), t, heads, head_bytes, w, off_o)])
+        px.exchange([gather_copy(oh.ptr, t, heads, head_bytes, w, off_o)])
         return px.region + off_o
 
     def shard(self, tokens: int) -> tuple:
@@ -170,47 +171,52 @@ class SequenceParallel:
         n = tokens // self.world
         return self.rank * n, n
 
-    def buffer(self, key: str, nbytes: int):
-        """A torch uint8 device buffer of at least nbytes, kept across blocks under `key`."""
+    def buffer(self, key: str, nbytes: int) -> Buffer:
+        """A device buffer of at least nbytes, kept across blocks under `key` (in the private context)."""
         b = self._bufs.get(key)
-        if b is None or b.numel() < nbytes:
-            b = self.torch.empty(nbytes, dtype=self.torch.uint8, device=self.device)
+        if b is None or b.size < nbytes:
+            if b is not None:
+                self._store.free(b)
+            b = self._store.buffer(nbytes)
+            self._store.sync()  # its zero fill ran on the private stream: done before the step's stream uses it
             self._bufs[key] = b
-        return b[:nbytes]
+        return b
 
     def scatter_heads(self, graph: Graph, rows, local_tokens: int, heads: int, head_bytes: int, out_key: str):
         """rows [local_tokens, heads, head_bytes] of this rank -> [world * local_tokens, heads / world, head_bytes]
-        (every token, this rank's heads); returns the torch buffer holding it."""
+        (every token, this rank's heads); returns the buffer holding it."""
         if heads % self.world:
             raise ValueError(f"{heads} heads do not split over {self.world} ranks")
         gbytes = heads // self.world * head_bytes
         nbytes = local_tokens * heads * head_bytes
         send = self.buffer("send_" + out_key, nbytes)
         recv = self.buffer(out_key, nbytes)
-        L.check(graph.ctx, L.lib().we_head_groups(graph.ctx, addr(rows), C.c_void_p(send.data_ptr()), local_tokens,
+        L.check(graph.ctx, L.lib().we_head_groups(graph.ctx, addr(rows), C.c_void_p(send.ptr), local_tokens,
                                                   self.world, gbytes, 1))
-        self.dist.all_to_all_single(recv, send, group=self.group)
+        self.comm.all_to_all(send, recv, nbytes // self.world)
         return recv
 
     def gather_heads(self, graph: Graph, heads_buf, local_tokens: int, heads: int, head_bytes: int, rows) -> None:
-        """heads_buf (a torch buffer from `buffer`): [world * local_tokens, heads / world, head_bytes], every token
-        with this rank's heads -> rows [local_tokens, heads, head_bytes] of this rank."""
+        """heads_buf (a buffer from `buffer`): [world * local_tokens, heads / world, head_bytes], every token with
+        this rank's heads -> rows [local_tokens, heads, head_bytes] of this rank."""
         gbytes = heads // self.world * head_bytes
         nbytes = local_tokens * heads * head_bytes
         recv = self.buffer("gather_recv", nbytes)
-        self.dist.all_to_all_single(recv, heads_buf[:nbytes], group=self.group)
-        L.check(graph.ctx, L.lib().we_head_groups(graph.ctx, addr(rows), C.c_void_p(recv.data_ptr()), local_tokens,
+        self.comm.all_to_all(heads_buf, recv, nbytes // self.world)
+        L.check(graph.ctx, L.lib().we_head_groups(graph.ctx, addr(rows), C.c_void_p(recv.ptr), local_tokens,
                                                   self.world, gbytes, 0))
 
     def all_gather_rows(self, graph: Graph, local, local_bytes: int):
-        """Every rank's `local_bytes` in rank order: a device address (peer path) or a torch buffer (nccl) of
+        """Every rank's `local_bytes` in rank order: a device address (valid until the call after next) of
         world * local_bytes."""
         if self.peer:
-            px = self._exchange(graph, "rows", self.world * local_bytes)
-            px.exchange([rows_copy(addr(local).value, local_bytes)])
-            return px.region
-        src = self.buffer("ag_src", local_bytes)
-        graph.copy(local, 0, src.data_ptr(), 0, local_bytes)
+            # two halves used in turn, like the head exchange: a rank may start the next call's copies into a
+            # region that another rank still reads from this call's result
+            px = self._exchange(graph, "rows", 2 * self.world * local_bytes)
+            off = self._rows_parity * self.world * local_bytes
+            self._rows_parity ^= 1
+            px.exchange([rows_copy(addr(local).value, local_bytes, off)])
+            return px.region + off
         out = self.buffer("ag_out", local_bytes * self.world)
-        self.dist.all_gather_into_tensor(out, src, group=self.group)
-        return out
+        self.comm.all_gather(local, out, local_bytes)
+        return out.ptr
