@@ -172,7 +172,7 @@ PAIR_SHAPES = [(256, 256, 128), (37, 70, 128), (300, 520, 384), (130, 65, 144), 
 
 @pytest.mark.parametrize("m,n,k", PAIR_SHAPES)
 @pytest.mark.parametrize("terms", [2, 1])
-@pytest.mark.parametrize("pair_bt", ["256", "128"])
+@pytest.mark.parametrize("pair_bt", ["256", "192", "128"])
 def test_tc_pair_kernel_fp8(we, graph, force_pair_kernel, monkeypatch, m, n, k, terms, pair_bt):
     monkeypatch.setenv("WE_TC_PAIR_BT", pair_bt)  # 256 or 128 tokens per pair tile
     x = bf16_round(randn(m * k, 21))
@@ -187,7 +187,7 @@ def test_tc_pair_kernel_fp8(we, graph, force_pair_kernel, monkeypatch, m, n, k, 
 
 
 @pytest.mark.parametrize("m,n,k", [(256, 256, 64), (200, 300, 264), (512, 512, 3072)])
-@pytest.mark.parametrize("pair_bt", ["256", "128"])
+@pytest.mark.parametrize("pair_bt", ["256", "192", "128"])
 def test_tc_pair_kernel_bf16_and_epilogue(we, graph, force_pair_kernel, monkeypatch, m, n, k, pair_bt):
     monkeypatch.setenv("WE_TC_PAIR_BT", pair_bt)
     x = bf16_round(randn(m * k, 23))
@@ -348,3 +348,36 @@ def test_int4_packed_weights_at_any_alignment(we, graph, offset):
     graph.release(mark)
     want = O.matmul(x, O.INT4G64, packed, m, n, k, gscale=scales, threads=0)
     assert O.rel_error(got, want) < EXACT_REL
+
+
+@pytest.mark.parametrize("m,n,k", [(576, 384, 3072), (200, 260, 256), (1000, 520, 512)])
+@pytest.mark.parametrize("form", ["1sm", "pair"])
+def test_token_tile_widths_give_the_same_bits(we, graph, monkeypatch, m, n, k, form):
+    """Every token tile width of a kernel form (1-SM: 64, 96, 128, 256 tokens; pair: 128, 192, 256) gives the same
+    output bits on ragged shapes with the fused epilogue (bias, GELU, bf16 out): each output value is the same
+    K-ordered sum. The 96- and 192-token tiles serve 576-row sequence-parallel shards."""
+    x = bf16_round(randn(m * k, 71))
+    w = fast_fp8(n * k, 72)
+    cs = (np.abs(randn(n, 73, 0.004)) + np.float32(1e-3)).astype(np.float32)
+    bias = randn(n, 74)
+    mark = graph.mark()
+    xb, wb, csb, bb = graph.buffer(bf16(x)), graph.buffer(w), graph.buffer(cs), graph.buffer(bias)
+    outs = {}
+    widths = ["64", "96", "128", "256"] if form == "1sm" else ["128", "192", "256"]
+    monkeypatch.setenv("WE_TC_2SM", "0" if form == "1sm" else "2")
+    for bt in widths:
+        monkeypatch.setenv("WE_TC_BT" if form == "1sm" else "WE_TC_PAIR_BT", bt)
+        y = graph.buffer(m * n * 2)
+        t0 = graph.stats["tcGemms"]
+        we.kernels.matmul(graph, xb, wb, y, m, n, k, 1.0, x_dtype="bf16", w_dtype="fp8", y_dtype="bf16",
+                          chan_scale=csb, bias=bb, act="gelu_tanh")
+        assert graph.stats["tcGemms"] == t0 + 1
+        outs[bt] = graph.read(y, m * n * 2).copy()
+    assert graph.device_error() == 0
+    graph.release(mark)
+    for bt in widths[1:]:
+        assert np.array_equal(outs[bt], outs[widths[0]]), bt
+    want = O.matmul(x, O.FP8, w, m, n, k, chan_scale=cs).reshape(m, n) + bias.astype(np.float64)
+    want = 0.5 * want * (1.0 + np.tanh(0.7978845608028654 * (want + 0.044715 * want ** 3)))
+    got = O.bf16_to_f32(outs[widths[0]].view(np.uint16)).reshape(m, n)
+    assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -7 + 1e-3 * np.abs(want).max())

@@ -115,6 +115,13 @@ __device__ __forceinline__ YOut y_out(const Params& p, int64_t ch_base) {
   return YOut{p.ys[s], lo, p.seg_end[s] - lo};
 }
 
+// TMEM columns for two accumulators of BT columns: tcgen05.alloc takes a power of two of at least 32
+__host__ __device__ constexpr uint32_t tmem_cols(int bt) {
+  uint32_t c = 32;
+  while (c < 2u * (uint32_t)bt) c *= 2;
+  return c;
+}
+
 template <int BT, int TERMS>
 struct Layout {
   static constexpr int W_BYTES = BM * KB_BYTES;
@@ -312,7 +319,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   using L = Layout<BT, TERMS>;
   constexpr int STAGES = L::STAGES;
   constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;
-  constexpr uint32_t TMEM_COLS = 2 * BT;
+  constexpr uint32_t TMEM_COLS = tmem_cols(BT);
   constexpr uint32_t IDESC = make_idesc<BT, F16>();
   constexpr int MMAS_PER_KB = KB_BYTES / 32;  // 32 bytes of K per tcgen05.mma
 
@@ -532,7 +539,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   using L = Layout2<BT, TERMS, ATOMS>;
   constexpr int STAGES = L::STAGES;
   constexpr int KB_ELEMS = F16 ? KB_BYTES / 2 : KB_BYTES;  // K elements per atom
-  constexpr uint32_t TMEM_COLS = 2 * BT;
+  constexpr uint32_t TMEM_COLS = tmem_cols(BT);
   constexpr uint32_t IDESC = make_idesc_pair<BT, F16>();
   constexpr int MMAS_PER_KB = KB_BYTES / 32;
   const int num_stages = (p.num_kb + ATOMS - 1) / ATOMS;  // a K atom past the end loads as zeros
@@ -806,7 +813,7 @@ __global__ void __launch_bounds__(192 + 32 * CW, 1)
   using L = Layout<BT, 1>;
   constexpr int STAGES = L::STAGES;
   constexpr int KB_ELEMS = KB_BYTES / 2;
-  constexpr uint32_t TMEM_COLS = 2 * BT;
+  constexpr uint32_t TMEM_COLS = tmem_cols(BT);
   constexpr uint32_t IDESC = make_idesc<BT, true>();
   constexpr int MMAS_PER_KB = KB_BYTES / 32;
 
@@ -1181,16 +1188,37 @@ bool gemm_tc_supported(const TcGemmArgs& a) {
   return true;
 }
 
-// The largest token tile (of 256 / 128 / 64) that every segment boundary of a two-weight-set GEMM is a multiple of
-// (256 without segments); 0 if none.
-static int seg_tile(const TcGemmArgs& a) {
-  int bt = 256;
+// Whether every inner segment boundary of a two-weight-set GEMM is a multiple of a token tile of c rows (token tiles
+// may not straddle two weight sets).
+static bool segments_fit(const TcGemmArgs& a, int c) {
   for (int i = 0; i + 1 < a.nseg; i++)
-    while (bt >= 64 && a.row_end[i] % bt) bt /= 2;
-  return bt >= 64 ? bt : 0;
+    if (a.row_end[i] % c) return false;
+  return true;
 }
 
-// Token tile: the largest of 256 / 128 / 64 that still gives every SM a tile, else 64.
+template <int TERMS, bool F16>
+static cudaError_t run_1sm(const TcGemmArgs& a, int bt, int sms, cudaStream_t st) {
+  switch (bt) {
+    case 256: return tc::run<256, TERMS, F16>(a, sms, st);
+    case 128: return tc::run<128, TERMS, F16>(a, sms, st);
+    case 96: return tc::run<96, TERMS, F16>(a, sms, st);
+    default: return tc::run<64, TERMS, F16>(a, sms, st);
+  }
+}
+template <int TERMS, bool F16>
+static cudaError_t run_2sm(const TcGemmArgs& a, int bt, int sms, cudaStream_t st) {
+  switch (bt) {
+    case 128: return tc::run_pair<128, TERMS, F16>(a, sms, st);
+    case 192: return tc::run_pair<192, TERMS, F16>(a, sms, st);
+    default: return tc::run_pair<256, TERMS, F16>(a, sms, st);
+  }
+}
+
+// Kernel and token tile by a cost model of waves x per-SM tile cost: a 1-SM tile (128 channels x c tokens) costs
+// 1.2 c + 96 token-units, a pair tile (256 channels x c tokens on two SMs, half the shared-memory bytes per FLOP)
+// c + 96. Fitted on 576 to 4608 tokens x N 3072 / 9216 / 12288 with c of 64 / 128 / 256; the 96- and 192-token
+// tiles serve token counts that are multiples of 96 (a sequence-parallel rank's 576 rows: 6 x 96 or 3 x 192, where
+// 64 / 128 / 256 leave a ragged last tile or a ragged last wave).
 cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (!gemm_tc_supported(a)) return cudaErrorNotSupported;
   if (a.int4) {
@@ -1198,23 +1226,22 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
       if (atoi(env) == 4) return tc::run_i4<256, 4>(a, sms, st);
     return tc::run_i4<256, 8>(a, sms, st);
   }
-  const int max_bt = seg_tile(a);  // token tiles may not straddle two weight sets
-  if (max_bt == 0) return cudaErrorNotSupported;
-  // Kernel and token tile by a cost model of waves x per-SM tile cost: a 1-SM tile (128 channels x bt tokens) costs
-  // 1.2 bt + 96 token-units, a pair tile (256 channels x 256 tokens on two SMs, half the shared-memory bytes per
-  // FLOP) 256 + 96. Fitted on 576 to 4608 tokens x N 3072 / 9216 / 12288: it picks the measured fastest choice, e.g.
-  // 576 x 3072 x 12288: 128-token 1-SM tiles, 65 us (64-token tiles 103 us, pairs 85 us).
   const int64_t tn = (a.n + tc::BM - 1) / tc::BM;
   auto waves = [&](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
   double best_cost = -1.0;
   bool pair = false;
-  int bt = 64;
-  if (max_bt == 256) {
-    best_cost = (double)waves(((a.n + 255) / 256) * ((a.m + 255) / 256), sms / 2) * (256.0 + 96.0);
-    pair = true;
+  int bt = 0;
+  for (int c : {256, 192}) {
+    if (!segments_fit(a, c)) continue;
+    const double cost = (double)waves(((a.n + 255) / 256) * ((a.m + c - 1) / c), sms / 2) * (c + 96.0);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      pair = true;
+      bt = c;
+    }
   }
-  for (int c = 256; c >= 64; c /= 2) {
-    if (c > max_bt) continue;
+  for (int c : {256, 128, 96, 64}) {
+    if (!segments_fit(a, c)) continue;
     const double cost = (double)waves(tn * ((a.m + c - 1) / c), sms) * (1.2 * c + 96.0);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
@@ -1222,45 +1249,42 @@ cudaError_t launch_gemm_tc(const TcGemmArgs& a, int sms, cudaStream_t st) {
       bt = c;
     }
   }
+  if (bt == 0) return cudaErrorNotSupported;  // no token tile fits the segments
   if (const char* env = getenv("WE_TC_2SM")) {  // tuning / test override: 0 never, 2 always (where tiles allow)
     const int v = atoi(env);
-    pair = v == 2 ? max_bt == 256 : (v == 0 ? false : pair);
+    if (v == 2 && segments_fit(a, 256)) {
+      pair = true;
+      bt = 256;
+    } else if (v == 0 && pair) {
+      pair = false;
+      bt = 64;
+      for (int c : {256, 128, 96})
+        if (segments_fit(a, c) && c <= a.m) {
+          bt = c;
+          break;
+        }
+    }
   }
   if (pair) {
-    // 256 tokens per pair tile. 128 fills the last wave better on some shapes (2304 tokens x 3072 channels:
-    // 2.92 waves of 74 pairs against 1.46) but halves each tile's reuse of W from L2 and measured slower on every
-    // shape tried (2304 x 3072 x 3072: 61.4 against 58.1 us; 4608 x 3072 x 3072: 100.7 against 73.4 us).
-    int pbt = 256;
-    if (const char* env = getenv("WE_TC_PAIR_BT")) {  // tuning / test override: 128 or 256 tokens per pair tile
+    // A 128-token pair tile fills the last wave better on some shapes (2304 tokens x 3072 channels: 2.92 waves of
+    // 74 pairs against 1.46) but halves each tile's reuse of W from L2 and measured slower on every shape tried
+    // (2304 x 3072 x 3072: 61.4 against 58.1 us; 4608 x 3072 x 3072: 100.7 against 73.4 us), so it is left to the
+    // override.
+    if (const char* env = getenv("WE_TC_PAIR_BT")) {  // tuning / test override: 128, 192 or 256 tokens per pair tile
       const int v = atoi(env);
-      if (v == 128 || v == 256) pbt = v;
+      if ((v == 128 || v == 192 || v == 256) && segments_fit(a, v)) bt = v;
     }
-    if (pbt == 128) {
-      if (a.kind_f16) return tc::run_pair<128, 1, true>(a, sms, st);
-      if (a.terms > 1) return tc::run_pair<128, 2, false>(a, sms, st);
-      return tc::run_pair<128, 1, false>(a, sms, st);
-    }
-    if (a.kind_f16) return tc::run_pair<256, 1, true>(a, sms, st);
-    if (a.terms > 1) return tc::run_pair<256, 2, false>(a, sms, st);
-    return tc::run_pair<256, 1, false>(a, sms, st);
+    if (a.kind_f16) return run_2sm<1, true>(a, bt, sms, st);
+    if (a.terms > 1) return run_2sm<2, false>(a, bt, sms, st);
+    return run_2sm<1, false>(a, bt, sms, st);
   }
-  if (const char* env = getenv("WE_TC_BT")) {  // tuning override: 64, 128 or 256 tokens per tile
+  if (const char* env = getenv("WE_TC_BT")) {  // tuning / test override: 64, 96, 128 or 256 tokens per tile
     const int v = atoi(env);
-    if (v == 64 || v == 128 || v == 256) bt = v;
+    if ((v == 64 || v == 96 || v == 128 || v == 256) && segments_fit(a, v)) bt = v;
   }
-  if (a.kind_f16) {
-    if (bt == 256) return tc::run<256, 1, true>(a, sms, st);
-    if (bt == 128) return tc::run<128, 1, true>(a, sms, st);
-    return tc::run<64, 1, true>(a, sms, st);
-  }
-  if (a.terms > 1) {
-    if (bt == 256) return tc::run<256, 2, false>(a, sms, st);
-    if (bt == 128) return tc::run<128, 2, false>(a, sms, st);
-    return tc::run<64, 2, false>(a, sms, st);
-  }
-  if (bt == 256) return tc::run<256, 1, false>(a, sms, st);
-  if (bt == 128) return tc::run<128, 1, false>(a, sms, st);
-  return tc::run<64, 1, false>(a, sms, st);
+  if (a.kind_f16) return run_1sm<1, true>(a, bt, sms, st);
+  if (a.terms > 1) return run_1sm<2, false>(a, bt, sms, st);
+  return run_1sm<1, false>(a, bt, sms, st);
 }
 
 }  // namespace we
