@@ -286,3 +286,41 @@ def test_sampling_loop_matches_the_float64_loop(we, graph):
             x = O.euler_step(x, v, sig[s], sig[s + 1])
         c = O.compare(got[i], x)
         assert c["cosine"] > 0.99999 and c["relativeError"] < 1e-4, c
+
+
+@pytest.mark.parametrize("slots", [2, 3])
+def test_streamed_weights_step_equals_the_resident_step(we, graph, slots):
+    """Block weights streamed from pinned host memory one layer ahead (StreamedBlocks over we_streamer: 2 or 3 device
+    slots, layers larger than a slot's share refilled while earlier blocks run) give the resident step's velocity
+    bit for bit, for a batch of 2 images and for a 2-step sampling loop; every step copies every layer."""
+    T = we.transformer
+    bc = we.blocks.BlockConfig(hidden=512, mlp=2048, heads=4, kv_heads=4, head_dim=128, mlp_act="gelu",
+                               attn_gate=False)
+    scfg = T.StepConfig(block=bc, double=2, single=3, ctx_dim=256)
+    h, w, text = 16, 16, 8
+    _, wts = make_step(we, graph, scfg, 900, per_channel=True)
+    lats = [bf16_round(randn(16 * h * w, 910 + i)) for i in range(2)]
+    ctxs = [bf16_round(randn(text * 256, 920 + i)) for i in range(2)]
+    mark = graph.mark()
+    inputs = [T.StepInputs(graph.buffer(bf16(l)), h, w, 0.55, graph.buffer(bf16(c)), text) for l, c in zip(lats, ctxs)]
+    vel, _ = T.transformer(graph, wts, scfg, inputs, dtype="bf16")
+    want = [graph.read(v, 16 * h * w * 4, np.float32).copy() for v in vel]
+    st = T.StreamedBlocks(graph, wts, slots=slots)
+    try:
+        for _ in range(2):  # a second pass wraps around the layers again
+            vel, _ = T.transformer(graph, wts, scfg, inputs, dtype="bf16", streamed=st)
+            got = [graph.read(v, 16 * h * w * 4, np.float32).copy() for v in vel]
+            assert all(np.array_equal(a, b) for a, b in zip(got, want))
+        noise = [graph.buffer(randn(16 * h * w, 930 + i)) for i in range(2)]
+        ctxb = [graph.buffer(bf16(c)) for c in ctxs]
+        res = T.sample(graph, wts, scfg, noise, ctxb, h, w, text, steps=2, dtype="bf16")
+        stm = T.sample(graph, wts, scfg, noise, ctxb, h, w, text, steps=2, dtype="bf16", streamed=st)
+        for a, b in zip(res, stm):
+            assert np.array_equal(graph.read(a, 16 * h * w * 4, np.float32), graph.read(b, 16 * h * w * 4, np.float32))
+        layers = scfg.double + scfg.single
+        # 4 passes over 5 layers: every layer is copied in every pass except those still in a slot from the pass before
+        assert st.stats["copies"] >= 4 * layers - slots
+    finally:
+        st.close()
+    assert graph.device_error() == 0
+    graph.release(mark)

@@ -19,6 +19,7 @@ the residual stream stays f32.
 """
 from __future__ import annotations
 
+import dataclasses
 import functools
 import math
 from dataclasses import dataclass, field
@@ -30,6 +31,7 @@ from . import kernels as K
 from . import ops
 from .block import BlockConfig, BlockWeights, Part, block_flops, buffers_of, joint_block
 from .graph import Buffer, Graph, addr
+from .stream import Streamer
 
 LATENT_CHANNELS = 16
 TIME_DIM = 256
@@ -147,6 +149,74 @@ def _layers(w: TransformerWeights, images: int, T: int, Lt: int, image: int, r0:
     return layers + [clip(0, R, bw) for bw in w.single]
 
 
+def _streamed_linears(w: BlockWeights) -> list:
+    """The fp8 linears of a block that the bf16 path reads (q/k/v fused when fuse_qkv made them so)."""
+    names = ["wqkv"] if w.wqkv is not None else ["wq", "wk", "wv"]
+    names += ["wo", "mlp_up", "mlp_down"]
+    names += [nm for nm in ("gate", "mlp_gate") if getattr(w, nm) is not None]
+    return names
+
+
+class StreamedBlocks:
+    """The blocks' fp8 linear weights in pinned host memory, copied to HBM one layer (a block: both parts of a double
+    block) at a time by a streamer (we_streamer: cudaMemcpyAsync on a side stream into `slots` device slots, the
+    following layers prefetched while a block runs). This is loadTransformer's per-block upload (src/model/
+    weights.ts:94-131) made per step, for models larger than HBM or a memory budget that keeps only a few blocks
+    resident: per-channel scales, biases, norms and modulation tables (a few KB a block) stay resident.
+
+    Built from a model whose weights are on the device (their bytes are read back once into host blobs); the device
+    copies are the caller's to keep or free. transformer(..., streamed=...) then runs every block on its slot."""
+
+    def __init__(self, graph: Graph, w: TransformerWeights, slots: int = 3, align: int = 1024):
+        self.graph = graph
+        self.layers = [list(pair) for pair in w.double] + [[bw] for bw in w.single]
+        self.entries = []  # per layer: [(part index, linear name, byte offset)]
+        blobs = []
+        for ws in self.layers:
+            entries, off = [], 0
+            for wi, bw in enumerate(ws):
+                for name in _streamed_linears(bw):
+                    lin = getattr(bw, name)
+                    if lin.dtype != "fp8":
+                        raise ValueError("streaming takes the blocks' fp8 linears")
+                    off = -(-off // align) * align
+                    entries.append((wi, name, off))
+                    off += lin.n * lin.k
+            blob = np.empty(off, np.uint8)
+            for wi, name, o in entries:
+                lin = getattr(ws[wi], name)
+                blob[o:o + lin.n * lin.k] = graph.read(lin.buffer, lin.n * lin.k)
+            self.entries.append(entries)
+            blobs.append(blob)
+        self.host_bytes = sum(b.nbytes for b in blobs)
+        self.streamer = Streamer(graph, blobs, slots=slots)
+
+    def bind(self, i: int) -> dict:
+        """Layer i's weights on the device: {id(original BlockWeights): a copy whose streamed linears point into the
+        layer's slot}. Work queued after this call on the graph's stream sees the copied bytes."""
+        base = self.streamer.acquire(i)
+        out = {}
+        for wi, bw in enumerate(self.layers[i]):
+            repl = {}
+            for wj, name, o in self.entries[i]:
+                if wj == wi:
+                    lin = getattr(bw, name)
+                    repl[name] = dataclasses.replace(lin, buffer=base + o)
+            out[id(bw)] = dataclasses.replace(bw, **repl)
+        return out
+
+    def release(self, i: int) -> None:
+        """Layer i's work is queued: its slot may be refilled once that work has run."""
+        self.streamer.release(i)
+
+    @property
+    def stats(self) -> dict:
+        return self.streamer.stats
+
+    def close(self) -> None:
+        self.streamer.close()
+
+
 class StepGraph:
     """The blocks of a step (all 57 for config 4), recorded once as a CUDA graph for one geometry and replayed
     each step: the host issues one launch instead of about 1000, so a step no longer depends on how fast Python
@@ -202,7 +272,8 @@ class StepGraph:
 
 
 def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype: str = "f32", velocity=None,
-                on_block=None, sp=None, captured: StepGraph | None = None) -> tuple:
+                on_block=None, sp=None, captured: StepGraph | None = None,
+                streamed: StreamedBlocks | None = None) -> tuple:
     """One denoising step (transformer.ts:134-176) of one image (`inp` a StepInputs) or of a batch of images (a list
     of StepInputs with the same geometry and timestep). The batch runs as one token stream: every linear is one
     GEMM over all images' rows, attention runs per image.
@@ -214,7 +285,10 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     runs the blocks on T / world consecutive rows, attention exchanges heads by all-to-all, and every rank gets the
     whole velocity.
 
-    captured: a StepGraph of this geometry; the blocks then run as its replay (on_block is not called)."""
+    captured: a StepGraph of this geometry; the blocks then run as its replay (on_block is not called).
+
+    streamed: a StreamedBlocks of w: every block's fp8 linears are copied from pinned host memory into a device slot
+    just ahead of the block (eager path only)."""
     batch = list(inp) if isinstance(inp, (list, tuple)) else [inp]
     b0 = batch[0]
     if any((b.height, b.width, b.text_tokens, b.timestep) != (b0.height, b0.width, b0.text_tokens, b0.timestep)
@@ -261,11 +335,18 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
             raise ValueError("the captured step is for another geometry, batch, dtype or sequence-parallel group")
         x = captured.run(graph, x, tvec)  # graph-owned; the last layer reads it
     else:
+        if streamed is not None and captured is not None:
+            raise ValueError("a streamed step runs eagerly")
         layers = _layers(w, B, T, Lt, image, r0, n)
         for i, parts in enumerate(layers):
+            if streamed is not None:  # this block's linears from its slot (the same BlockWeights -> the same copy)
+                bound = streamed.bind(i)
+                parts = [Part(p.row0, p.rows, bound[id(p.w)]) for p in parts]
             bm = graph.mark()
             # between blocks the output stays a Residual: the next block's first norm pass adds it
             nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp, defer=i + 1 < len(layers))
+            if streamed is not None:
+                streamed.release(i)
             graph.release(bm, buffers_of(nxt))
             for b in buffers_of(x):
                 graph.free(b)
@@ -346,7 +427,7 @@ def gaussian(n: int, seed: int) -> np.ndarray:
 
 def sample(graph: Graph, w: TransformerWeights, cfg: StepConfig, noise: list, contexts: list, height: int, width: int,
            text_tokens: int, steps: int = TURBO["steps"], mu: float = TURBO["mu"], dtype: str = "bf16",
-           on_step=None) -> list:
+           on_step=None, streamed: StreamedBlocks | None = None) -> list:
     """Flow-matching Euler sampling of a batch of images (the loop of src/pipeline/generate.ts:94-105): the text
     rows are computed once per image, each step feeds timestep = sigma_i, then x += (sigma_{i+1} - sigma_i) v.
     noise: f32 latents [C, H, W] on the device (one per image); contexts: [text_tokens, ctx_dim] of `dtype`.
@@ -357,7 +438,7 @@ def sample(graph: Graph, w: TransformerWeights, cfg: StepConfig, noise: list, co
     for i in range(steps):
         inputs = [StepInputs(xs[b], height, width, sig[i], contexts[b], text_tokens, caches[b], latent_dtype="f32")
                   for b in range(len(xs))]
-        vel, caches = transformer(graph, w, cfg, inputs, dtype)
+        vel, caches = transformer(graph, w, cfg, inputs, dtype, streamed=streamed)
         nxt = [euler_step(graph, xs[b], vel[b], sig[i], sig[i + 1], n) for b in range(len(xs))]
         for v in vel:
             graph.free(v)
