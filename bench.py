@@ -446,6 +446,10 @@ def main() -> None:
                     help="run config 3's block (bf16 path) three times, untimed, for an ncu launch list")
     ap.add_argument("--profile-case", action="store_true",
                     help="run each hot-path kernel of config 2 twice, untimed, for an ncu capture")
+    ap.add_argument("--profile-rank", type=int, default=0,
+                    help="run one sequence-parallel rank's block kernels at this many ranks' shapes (config 4: 4608 / "
+                         "N rows, 24 / N heads over 4608 tokens) three times, untimed, on one GPU, for an ncu launch "
+                         "list (the peer exchange needs every rank and is left out)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -587,6 +591,52 @@ def main() -> None:
         print("profile block done", flush=True)
         return
 
+    if args.profile_rank:
+        nr = args.profile_rank
+        T = we.transformer
+        bc = T.FLUX_BLOCK
+        mr, hl = 4608 // nr, bc.heads // nr
+        bw = random_block(we, g, torch, dev, gen, bc)
+        xr = torch.randn(mr, bc.hidden, generator=gen, device=dev)
+        ar = torch.randn(mr, bc.hidden, generator=gen, device=dev) * 0.1
+        x1 = torch.empty_like(xr)
+        hi_r = torch.empty(mr, bc.mlp, dtype=torch.uint8, device=dev)
+        lo_r, rs_r = torch.empty_like(hi_r), torch.empty(mr, device=dev)
+        qkv = [torch.empty(mr, bc.hidden, dtype=torch.bfloat16, device=dev) for _ in range(3)]
+        cos_h, sin_h, pairs = we.kernels.rope_tables(we.kernels.positions(512, 64, 64), (16, 56, 56), 1e4)
+        cs_r = torch.from_numpy(cos_h[:mr * pairs]).to(dev)
+        sn_r = torch.from_numpy(sin_h[:mr * pairs]).to(dev)
+        qa, ka, va = (torch.randn(4608, hl, 128, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3))
+        oa = torch.empty_like(qa)
+        o_r = torch.empty(mr, bc.hidden, dtype=torch.bfloat16, device=dev)
+        a_r = torch.empty(mr, bc.hidden, device=dev)
+        u_r = torch.empty(mr, bc.mlp, dtype=torch.bfloat16, device=dev)
+        dn_r = torch.empty(mr, bc.hidden, device=dev)
+        gate_v = torch.randn(bc.hidden, device=dev) * 0.1
+        for _ in range(3):
+            we.kernels.add_norm_split(g, xr, ar, x1, bw.norm1, mr, bc.hidden, hi_r, lo_r, rs_r)
+            we.kernels.gemm_fp8(g, hi_r, lo_r, rs_r, bw.wqkv.buffer, None, mr, bw.wqkv.n, bc.hidden,
+                                chan_scale=bw.wqkv.chan_scale, y_dtype="bf16",
+                                parts=[(qkv[0], bc.hidden), (qkv[1], bc.hidden), (qkv[2], bc.hidden)])
+            for t_ in qkv[:2]:
+                we.kernels.qknorm_rope(g, t_, bw.norm_q, cs_r, sn_r, mr, bc.heads, pairs, t_, x_dtype="bf16",
+                                       out_dtype="bf16")
+            we.kernels.attention(g, qa, ka, va, 4608, hl, hl, 128, oa, dtype="bf16", out_dtype="bf16")
+            we.kernels.quantize_act(g, o_r, mr, bc.hidden, hi_r, lo_r, rs_r, terms=2)
+            we.kernels.gemm_fp8(g, hi_r, lo_r, rs_r, bw.wo.buffer, a_r, mr, bc.hidden, bc.hidden,
+                                chan_scale=bw.wo.chan_scale, y_dtype="f32", gate=gate_v)
+            we.kernels.add_norm_split(g, xr, a_r, x1, bw.norm2, mr, bc.hidden, hi_r, lo_r, rs_r)
+            we.kernels.gemm_fp8(g, hi_r, lo_r, rs_r, bw.mlp_up.buffer, u_r, mr, bc.mlp, bc.hidden,
+                                chan_scale=bw.mlp_up.chan_scale, y_dtype="bf16", act="gelu_tanh")
+            we.kernels.quantize_act(g, u_r, mr, bc.mlp, hi_r, lo_r, rs_r, terms=2)
+            we.kernels.gemm_fp8(g, hi_r, lo_r, rs_r, bw.mlp_down.buffer, dn_r, mr, bc.hidden, bc.mlp,
+                                chan_scale=bw.mlp_down.chan_scale, y_dtype="f32", gate=gate_v)
+        torch.cuda.synchronize()
+        assert g.device_error() == 0
+        g.destroy()
+        print(f"profile rank done ({nr} ranks: {mr} rows, {hl} heads)", flush=True)
+        return
+
     if args.profile_case:
         # the activation split, the two-term and one-term GEMMs, the int4 decode + kind::f16 GEMM,
         # RMSNorm and q/k norm + RoPE at block size: two launches each, no timing
@@ -602,6 +652,7 @@ def main() -> None:
             we.kernels.gemm_fp8(g, hi, None, rs, wq, yk, M, N, K, chan_scale=ws, y_dtype="bf16")
             mark = g.mark()
             we.linear(g, x, lin4, M, x_dtype="bf16", y_dtype="bf16")
+            we.linear(g, x[:256], lin4, 256, x_dtype="bf16", y_dtype="bf16")  # one token tile: unpacked in the GEMM
             g.release(mark)
             we.kernels.rmsnorm(g, x, wn, M, K, xn, x_dtype="bf16", out_dtype="bf16")
             we.kernels.qknorm_rope(g, x, qn, cs_d, sn_d, M, K // 128, pairs, xn, x_dtype="bf16", out_dtype="bf16")

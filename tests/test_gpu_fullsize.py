@@ -172,14 +172,17 @@ def test_config3_block_in_full(we, graph, torch_on_graph):
     assert graph.device_error() == 0
     xh = x.cpu().numpy()
     cos_, rel = _cmp(outs["bf16"] - xh, outs["f32"] - xh)
+    print(f"config 3 block update, bf16 vs f32: cosine {cos_:.7f}, max-abs-rel {rel:.2e}")
     assert cos_ >= COS and rel < MAXREL, (cos_, rel)
     # 24 rows (text and image, first and last) of the f32 path against the float64 oracle
     sel = [0, 1, 255, 511, 512, 513, 1000, 2048, 2049, 3000, 3071, 3072, 3500, 4000, 4100, 4200, 4300, 4400, 4500,
            4550, 4600, 4605, 4606, 4607]
     want = O.block_rows_reference(xh, _host_block(bw), vars(bc), tvec.cpu().numpy(), cos, sin, sel)
     c64, rel64 = _cmp(outs["f32"][sel] - xh[sel], want - xh[sel])
+    print(f"config 3 block rows, f32 vs float64: cosine {c64:.8f}, max-abs-rel {rel64:.2e}")
     assert c64 > 0.99999 and rel64 < 1e-4, (c64, rel64)  # the reference block test's bound (block.test.ts:131-132)
     cb, relb = _cmp(outs["bf16"][sel] - xh[sel], want - xh[sel])
+    print(f"config 3 block rows, bf16 vs float64: cosine {cb:.7f}, max-abs-rel {relb:.2e}")
     assert cb >= COS and relb < MAXREL, (cb, relb)
 
 
@@ -218,5 +221,6 @@ def test_config4_step_in_full(we, graph, torch_on_graph):
     assert graph.device_error() == 0
     assert np.isfinite(vel["f32"]).all()
     cos_, rel = _cmp(vel["bf16"], vel["f32"])
+    print(f"config 4 step velocity, bf16 vs f32: cosine {cos_:.7f}, max-abs-rel {rel:.2e}")
     assert cos_ >= COS and rel < MAXREL, ("eager bf16 step vs f32 step", cos_, rel)
     assert np.array_equal(vel["graph"], vel["bf16"])  # the replay runs the same kernels on the same inputs

@@ -218,6 +218,7 @@ def test_step_bf16_matches_the_float64_step(we, graph):
     got, again, want = _step_case(we, graph, scfg, 16, 18, 8, 600, "bf16", per_channel=True)
     c = O.compare(got, want)
     rel = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    print(f"small bf16 step vs float64: cosine {c['cosine']:.7f}, max-abs-rel {rel:.2e}")
     assert c["cosine"] >= 0.9999 and rel < 2e-2, (c, rel)
     assert np.array_equal(got, again)
 
