@@ -359,16 +359,30 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
         sgr_sp.destroy()
         sp.destroy()
         sp_nccl.destroy()
+        # the same image split by tensor parallelism: every block's linears sharded over the ranks (N / K splits),
+        # activations all-gathered and partial sums reduce-scattered on the same communicator
+        tp_model = we.parallel.shard_model(g, model, scfg, world, dist.get_rank())
+        tpg = we.parallel.TPGroup(comm)
+
+        def step_tp():
+            T.transformer(g, tp_model, scfg, inp, dtype="bf16", velocity=vel, tp=tpg)
+
+        with ClockSampler(gpu) as tp_clocks:
+            tp_ms = timed(step_tp, sp_steps, 2) / sp_steps
+        del tp_model
         comm.destroy()
         out["step_config4_sequence_parallel"] = {
             "ms": sp_ms, "median_ms_this_rank": per[len(per) // 2], "steps": sp_steps, "n_gpus": world,
             "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12, "launches_per_step": sp_launches,
             "graph_ms": sp_graph_ms, "nccl_all_to_all_ms": nccl_ms, "clocks": sp_clocks.summary(),
+            "tensor_parallel_ms": tp_ms, "tensor_parallel_clocks": tp_clocks.summary(),
             "note": "one 1024x1024 image's step over all GPUs: every rank runs the blocks on 4608 / n_gpus rows; "
                     "q/k/v go to the ranks attending their heads and o comes back through the peer-memory exchange "
                     "kernel (IPC-mapped HBM of every GPU, one kernel per exchange with a flag barrier); graph_ms: this "
                     "rank's blocks replayed from a CUDA graph; nccl_all_to_all_ms: the same step with NCCL "
-                    "all_to_all_single"}
+                    "all-to-all (we_all_to_all); tensor_parallel_ms: the same image by tensor parallelism (eager): "
+                    "q/k/v and MLP up split over the ranks' heads and columns, wo and MLP down over K, the split "
+                    "activations all-gathered and the f32 partial sums reduce-scattered (NCCL through the C ABI)"}
 
     # config 5's batch: 8 images per step in total, split data-parallel across the ranks (no collective); each
     # rank runs its share as one token stream (every linear one GEMM over all its images' rows)

@@ -75,6 +75,10 @@ int we_write(we_ctx* ctx, void* dst, const void* host, size_t bytes);
 int we_read(we_ctx* ctx, const void* src, void* host, size_t bytes);
 /* Graph.copy (graph.ts:93-98): device-to-device copy, in order with the queued work. */
 int we_copy(we_ctx* ctx, const void* src, size_t src_offset, void* dst, size_t dst_offset, size_t bytes);
+/* A strided device-to-device copy (no reference counterpart): `rows` rows of `width` bytes, src rows src_pitch bytes
+   apart, dst rows dst_pitch apart, in order with the queued work. Cuts column slices out of row-major tensors (the
+   K slice of a weight for tensor parallelism). */
+int we_copy_2d(we_ctx* ctx, const void* src, size_t src_pitch, void* dst, size_t dst_pitch, size_t width, size_t rows);
 /* Graph.mark (graph.ts:122): how many buffers the context owns now. */
 size_t we_mark(we_ctx* ctx);
 /* Graph.release (graph.ts:127-132): frees every buffer made since `mark`, except `keep`. */
@@ -156,7 +160,7 @@ typedef struct {
   /* Split output (part_n[0] > 0; y and y_stride unused): the first part_n[0] channels go to y_parts[0], the next
      part_n[1] to y_parts[1], the rest (part_n[2]) to y_parts[2], each with rows part_n[i] values apart, so one
      GEMM over concatenated weights (the q, k and v projections) fills separate buffers. The parts' widths sum
-     to n; the boundaries between parts are multiples of 256; no aux operand. */
+     to n; the boundaries between parts are multiples of 32 (an epilogue warp's channels); no aux operand. */
   void* y_parts[3];
   int64_t part_n[3];
   /* Two weight sets (nseg > 0): token rows [row_end[i - 1], row_end[i]) use set row_set[i] (row_end increasing, the

@@ -165,8 +165,9 @@ def test_block_bf16_fused_path(we, graph, mlp_act, kv_heads, per_channel):
 @pytest.mark.parametrize("pair", ["0", "2"], ids=["1sm", "pair"])
 @pytest.mark.parametrize("m", [150, 1000])
 def test_gemm_split_output(we, graph, monkeypatch, pair, m):
-    """we_gemm_fp8 with a split output writes channels [0, 512), [512, 768), [768, 1024) to three buffers with rows
-    as wide as each part, bit for bit the columns of the unsplit output; bad splits are refused."""
+    """we_gemm_fp8 with a split output writes channels [0, 512), [512, 768), [768, 1024) (and [0, 384), [384, 640),
+    [640, 1024): boundaries inside a 256-channel pair tile) to three buffers with rows as wide as each part, bit for
+    bit the columns of the unsplit output; bad splits are refused."""
     monkeypatch.setenv("WE_TC_2SM", pair)
     n, k = 1024, 256
     x = bf16_round(randn(m * k, 31))
@@ -180,15 +181,17 @@ def test_gemm_split_output(we, graph, monkeypatch, pair, m):
     whole = graph.buffer(m * n * 2)
     we.kernels.gemm_fp8(graph, hi, lo, rs, wb, whole, m, n, k, chan_scale=csb, bias=bb, y_dtype="bf16")
     want = graph.read(whole, m * n * 2, np.uint16).reshape(m, n)
-    widths = (512, 256, 256)
-    parts = [(graph.buffer(m * wd * 2), wd) for wd in widths]
-    we.kernels.gemm_fp8(graph, hi, lo, rs, wb, None, m, n, k, chan_scale=csb, bias=bb, y_dtype="bf16", parts=parts)
-    c0 = 0
-    for buf, wd in parts:
-        got = graph.read(buf, m * wd * 2, np.uint16).reshape(m, wd)
-        assert np.array_equal(got, want[:, c0:c0 + wd])
-        c0 += wd
-    for bad in ([(parts[0][0], 384), (parts[1][0], 640)], [(parts[0][0], 512), (parts[1][0], 256)]):
+    for widths in ((512, 256, 256), (384, 256, 384)):
+        parts = [(graph.buffer(m * wd * 2), wd) for wd in widths]
+        we.kernels.gemm_fp8(graph, hi, lo, rs, wb, None, m, n, k, chan_scale=csb, bias=bb, y_dtype="bf16",
+                            parts=parts)
+        c0 = 0
+        for buf, wd in parts:
+            got = graph.read(buf, m * wd * 2, np.uint16).reshape(m, wd)
+            assert np.array_equal(got, want[:, c0:c0 + wd])
+            c0 += wd
+    # widths that do not sum to n, and a boundary inside an epilogue warp's 32 channels
+    for bad in ([(parts[0][0], 400), (parts[1][0], 624)], [(parts[0][0], 512), (parts[1][0], 256)]):
         with pytest.raises(we._lib.WeError, match="split output"):
             we.kernels.gemm_fp8(graph, hi, lo, rs, wb, None, m, n, k, chan_scale=csb, y_dtype="bf16", parts=bad)
     assert graph.device_error() == 0

@@ -181,6 +181,7 @@ _SIGS = {
     "we_peer_destroy": (C.c_int, [_P]),
     "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
                                         C.c_uint32, C.c_char_p, C.c_size_t]),
+    "we_copy_2d": (C.c_int, [_P, _P, C.c_size_t, _P, C.c_size_t, C.c_size_t, C.c_size_t]),
     "we_comm_unique_id": (C.c_int, [_P]),
     "we_comm_init": (C.c_int, [_P, C.c_int32, C.c_int32, _P, C.c_uint64, C.POINTER(C.c_void_p)]),
     "we_comm_destroy": (C.c_int, [_P]),

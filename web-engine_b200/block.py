@@ -98,12 +98,12 @@ def fuse_qkv(graph: Graph, w: BlockWeights) -> BlockWeights:
     (a scalar scale becomes a constant run) and biases, so the bf16 path runs one GEMM whose epilogue writes q, k
     and v to their own buffers. Three N = 3072 GEMMs fill the GPU poorly (at 2304 tokens, 108 tiles for 74 SM
     pairs: 176 us); one N = 9216 GEMM takes 107 us. Needs fp8 weights with the same K and part boundaries at
-    multiples of 256 channels; otherwise w is returned unchanged. The fused copy is extra memory (n x k bytes);
+    multiples of 32 channels; otherwise w is returned unchanged. The fused copy is extra memory (n x k bytes);
     call it where the weights are created, outside any mark / release scope."""
     lins = (w.wq, w.wk, w.wv)
     if w.wqkv is not None or any(l.dtype != "fp8" or l.k != w.wq.k or l.lora is not None for l in lins):
         return w
-    if w.wq.n % 256 or (w.wq.n + w.wk.n) % 256:
+    if w.wq.n % 32 or (w.wq.n + w.wk.n) % 32:
         return w
     k, n = w.wq.k, sum(l.n for l in lins)
     buf = graph.buffer(n * k)
@@ -172,8 +172,19 @@ def double_block(graph: Graph, txt: BlockWeights, img: BlockWeights, cfg: BlockC
                        dtype)
 
 
+@dataclass
+class TPLayer:
+    """What a tensor-parallel block needs beyond its local rows: the communicator of the group, the layer's parts
+    over all T rows of the image (global row offsets; the weights are this rank's shards) and the RoPE tables of
+    all T rows."""
+
+    comm: object
+    parts_all: list
+    rope_all: ops.Rope
+
+
 def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.Rope, dtype: str = "f32",
-                images: int = 1, sp=None, defer: bool = False):
+                images: int = 1, sp=None, defer: bool = False, tp: TPLayer | None = None):
     """Rows of `images` sequences of rope.tokens / images tokens each, stacked; each part covers a row range with its
     own weights, attention runs within each image. rope: cos/sin for all stacked rows (per image, tiled).
     sp: a sequence.SequenceParallel when the rows are this rank's shard of one image (bf16 path).
@@ -186,6 +197,10 @@ def joint_block(graph: Graph, parts: list, cfg: BlockConfig, x, tvec, rope: ops.
         raise ValueError("the rows must split evenly into images")
     if sp is not None and (dtype != "bf16" or images != 1):
         raise ValueError("a sequence-parallel block runs one image on the bf16 path")
+    if tp is not None:
+        if dtype != "bf16" or images != 1 or sp is not None:
+            raise ValueError("a tensor-parallel block runs one image on the bf16 path")
+        return _joint_bf16_tp(graph, parts, cfg, x, tvec, tp, defer)
     if dtype == "f32":
         if isinstance(x, Residual):
             x = ops.add(graph, x.x1, x.dn, rope.tokens * cfg.hidden)
@@ -417,6 +432,111 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None, defer=False
         graph.release(mark, [x1, dn])
         return Residual(x1, dn)
     out = ops.add(graph, x1, dn, t * hd)  # x1 + postgate down(m): the block's output
+    graph.release(mark, [out])
+    return out
+
+
+def _joint_bf16_tp(graph, parts, cfg, x, tvec, tp: TPLayer, defer=False):
+    """The bf16 block on this rank's token shard (parts: local rows) with its linears split over the ranks of
+    tp.comm (Megatron-style: the linears of src/model/block.ts:53-64,74-81 split along N for q/k/v, gate and MLP up,
+    along K for wo and MLP down):
+      norm1 + split on local rows -> all-gather of the e4m3 planes and row scales -> q/k/v GEMM on this rank's
+      heads (column shard) over all T rows -> q/k norm + RoPE -> attention of this rank's heads over every token ->
+      [gate] -> split of o -> wo GEMM on this rank's K slice, f32 partial sums over all rows -> reduce-scatter to the
+      local rows -> x1 = x + a fused with norm2 + split -> all-gather -> MLP up (column shard) + GELU -> split of u ->
+      MLP down on this rank's K slice -> reduce-scatter.
+    The weights in the parts are this rank's shards (parallel.shard_block). The gathered planes are the ones one GPU
+    would compute, so the column-parallel outputs equal one GPU's channel for channel; the row-parallel GEMMs sum per
+    rank partials in f32."""
+    comm = tp.comm
+    W = comm.world
+    hd, hdim = cfg.hidden, cfg.head_dim
+    if cfg.heads % W or cfg.kv_heads % W or cfg.mlp % W:
+        raise ValueError(f"heads, kv heads and MLP width must split over {W} ranks")
+    hl, kl, ml = cfg.heads // W, cfg.kv_heads // W, cfg.mlp // W
+    qw, kw = hl * hdim, kl * hdim
+    n = sum(p.rows for p in parts)
+    T = n * W
+    parts_all, rope = tp.parts_all, tp.rope_all
+    if sum(p.rows for p in parts_all) != T or rope.tokens != T:
+        raise ValueError("the layer's parts and RoPE tables must cover every rank's rows")
+    mark = graph.mark()
+    res = None
+    if isinstance(x, Residual):
+        res, x = x, graph.buffer(n * hd * 4)
+    shared: dict = {}
+    for p in parts_all:
+        if id(p.w) not in shared:
+            shared[id(p.w)] = modulation(graph, tvec, p.w.table, hd)
+    mods = [shared[id(p.w)] for p in parts]
+    plan = _weight_plan(parts_all, T)
+    loc = (graph.buffer(n * hd), graph.buffer(n * hd), graph.buffer(n * 4))
+    split = (graph.buffer(T * hd), graph.buffer(T * hd), graph.buffer(T * 4))
+
+    def gather():
+        comm.all_gather(loc[0], split[0], n * hd)
+        comm.all_gather(loc[1], split[1], n * hd)
+        comm.all_gather(loc[2], split[2], n * 4)
+
+    for p, mod in zip(parts, mods):
+        if res is None:
+            K.norm_split(graph, rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(loc, p, hd),
+                         scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
+        else:
+            K.add_norm_split(graph, rows_at(res.x1, p.row0, hd * 4), rows_at(res.dn, p.row0, hd * 4),
+                             rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(loc, p, hd),
+                             scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
+    gather()
+    q, k, v = graph.buffer(T * qw * 2), graph.buffer(T * kw * 2), graph.buffer(T * kw * 2)
+    if all(p.w.wqkv is not None for p in parts_all):
+        _gemm_all(graph, plan, parts_all, split, hd, lambda w: w.wqkv, [(q, qw), (k, kw), (v, kw)], "bf16")
+    else:
+        for name, buf, nn in (("wq", q, qw), ("wk", k, kw), ("wv", v, kw)):
+            _gemm_all(graph, plan, parts_all, split, hd, lambda w, nm=name: getattr(w, nm), [(buf, nn)], "bf16")
+    for p in parts_all:
+        qp, kp = rows_at(q, p.row0, qw * 2), rows_at(k, p.row0, kw * 2)
+        pr = part_rope(rope, p)
+        K.qknorm_rope(graph, qp, p.w.norm_q, pr.cos, pr.sin, p.rows, hl, rope.pairs, qp, eps=cfg.eps,
+                      x_dtype="bf16", out_dtype="bf16")
+        K.qknorm_rope(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, kl, rope.pairs, kp, eps=cfg.eps,
+                      x_dtype="bf16", out_dtype="bf16")
+    o = graph.buffer(T * qw * 2)
+    K.attention(graph, q, k, v, T, hl, kl, hdim, o, dtype="bf16", out_dtype="bf16")
+    if cfg.attn_gate:  # this rank's gate channels are its heads' features
+        og = graph.buffer(T * qw * 2)
+        _gemm_all(graph, plan, parts_all, split, hd, lambda w: w.gate, [(og, qw)], "bf16", aux=o, aux_row_bytes=qw * 2,
+                  aux_op="sigmoid_gate", aux_dtype="bf16")
+        o = og
+    osplit = (graph.buffer(T * qw), graph.buffer(T * qw), graph.buffer(T * 4))
+    K.quantize_act(graph, o, T, qw, *osplit, terms=2)
+    partial = graph.buffer(T * hd * 4)  # this rank's share of pregate wo(o), every row
+    _gemm_all(graph, plan, parts_all, osplit, qw, lambda w: w.wo, [(partial, hd)], "f32", shared, "pregate")
+    a = graph.buffer(n * hd * 4)
+    comm.reduce_scatter(partial, a, n * hd, "f32")
+    x1 = graph.buffer(n * hd * 4)
+    for p, mod in zip(parts, mods):
+        K.add_norm_split(graph, rows_at(x, p.row0, hd * 4), rows_at(a, p.row0, hd * 4), rows_at(x1, p.row0, hd * 4),
+                         p.w.norm2, p.rows, hd, *_split_rows(loc, p, hd), scale=mod["postscale"],
+                         shift=mod["postshift"], eps=cfg.eps)
+    gather()
+    u = graph.buffer(T * ml * 2)
+    if cfg.mlp_act == "swiglu":
+        gt = graph.buffer(T * ml * 2)
+        _gemm_all(graph, plan, parts_all, split, hd, lambda w: w.mlp_gate, [(gt, ml)], "bf16")
+        _gemm_all(graph, plan, parts_all, split, hd, lambda w: w.mlp_up, [(u, ml)], "bf16", aux=gt,
+                  aux_row_bytes=ml * 2, aux_op="swiglu", aux_dtype="bf16")
+    else:
+        _gemm_all(graph, plan, parts_all, split, hd, lambda w: w.mlp_up, [(u, ml)], "bf16", act="gelu_tanh")
+    msplit = (graph.buffer(T * ml), graph.buffer(T * ml), split[2])
+    K.quantize_act(graph, u, T, ml, *msplit, terms=2)
+    partial_dn = graph.buffer(T * hd * 4)
+    _gemm_all(graph, plan, parts_all, msplit, ml, lambda w: w.mlp_down, [(partial_dn, hd)], "f32", shared, "postgate")
+    dn = graph.buffer(n * hd * 4)
+    comm.reduce_scatter(partial_dn, dn, n * hd, "f32")
+    if defer:
+        graph.release(mark, [x1, dn])
+        return Residual(x1, dn)
+    out = ops.add(graph, x1, dn, n * hd)
     graph.release(mark, [out])
     return out
 

@@ -334,6 +334,16 @@ int we_copy(we_ctx* ctx, const void* src, size_t so, void* dst, size_t dof, size
   return WE_OK;
 }
 
+int we_copy_2d(we_ctx* ctx, const void* src, size_t src_pitch, void* dst, size_t dst_pitch, size_t width,
+               size_t rows) {
+  if (!ctx) return WE_EINVAL;
+  if (width > src_pitch || width > dst_pitch) return fail(ctx, WE_EINVAL, "we_copy_2d: a row is wider than its pitch");
+  if (!width || !rows) return WE_OK;
+  CK(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width, rows, cudaMemcpyDeviceToDevice, ctx->stream),
+     "we_copy_2d");
+  return WE_OK;
+}
+
 size_t we_mark(we_ctx* ctx) { return ctx ? ctx->owned.size() : 0; }
 
 int we_release(we_ctx* ctx, size_t mark, void* const* keep, size_t nkeep) {
@@ -545,12 +555,12 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
     for (int i = 0; i < 3; i++) {
       if (d->part_n[i] < 0) ok = false;
       if (d->part_n[i] > 0 && !d->y_parts[i]) ok = false;
-      if (i > 0 && d->part_n[i] > 0 && end % 256) ok = false;  // a boundary inside a 256-channel tile
+      if (i > 0 && d->part_n[i] > 0 && end % 32) ok = false;  // a boundary inside an epilogue warp's 32 channels
       end += d->part_n[i];
       ends[i] = end;
     }
     if (!ok || end != d->n)
-      return fail(ctx, WE_EINVAL, "split output needs parts whose widths sum to n, boundaries at multiples of 256, "
+      return fail(ctx, WE_EINVAL, "split output needs parts whose widths sum to n, boundaries at multiples of 32, "
                                   "a buffer for every part and no aux operand");
   }
   if (d->nseg < 0 || d->nseg > WE_GEMM_MAX_SEGMENTS)

@@ -113,6 +113,10 @@ class Graph:
     def copy(self, src, src_offset: int, dst, dst_offset: int, size: int) -> None:
         L.check(self.ctx, L.lib().we_copy(self.ctx, addr(src), src_offset, addr(dst), dst_offset, size))
 
+    def copy_2d(self, src, src_pitch: int, dst, dst_pitch: int, width: int, rows: int) -> None:
+        """rows x width bytes from src (rows src_pitch apart) to dst (rows dst_pitch apart), in stream order."""
+        L.check(self.ctx, L.lib().we_copy_2d(self.ctx, addr(src), src_pitch, addr(dst), dst_pitch, width, rows))
+
     def submit(self) -> None:
         """Work is already queued on the stream as it is issued; kept for API parity."""
 

@@ -119,3 +119,97 @@ class TensorParallel:
         if bias is not None:
             y = add_bias(y, bias, rows // self.world, shard.n)
         return y
+
+
+# ---------------- the tensor-parallel step: this rank's shards of a model's blocks ----------------
+def _addr(b) -> int:
+    from .graph import addr
+
+    return addr(b).value
+
+
+def shard_rows(graph, lin, r0: int, r1: int, keep_bias: bool = True):
+    """Output channels [r0, r1) of a device fp8 / bf16 Linear (column-parallel shard), as new graph buffers."""
+    from .ops import Linear
+
+    es = 2 if lin.dtype == "bf16" else 1
+    if lin.dtype not in ("fp8", "bf16"):
+        raise ValueError("tensor-parallel shards take fp8 or bf16 weights")
+    n = r1 - r0
+    buf = graph.buffer(n * lin.k * es)
+    graph.copy(lin.buffer, r0 * lin.k * es, buf, 0, n * lin.k * es)
+    cs = bias = None
+    if lin.chan_scale is not None:
+        cs = graph.buffer(n * 4)
+        graph.copy(lin.chan_scale, r0 * 4, cs, 0, n * 4)
+    if lin.bias is not None and keep_bias:
+        bias = graph.buffer(n * 4)
+        graph.copy(lin.bias, r0 * 4, bias, 0, n * 4)
+    return Linear(buf, lin.dtype, lin.scale, n, lin.k, bias=bias, chan_scale=cs)
+
+
+def shard_cols(graph, lin, c0: int, c1: int, keep_bias: bool):
+    """Input features [c0, c1) of a device fp8 / bf16 Linear (row-parallel shard: a strided copy of every row's K
+    slice). The per-channel scale is the whole layer's (it multiplies each output channel, so the sum of the ranks'
+    scaled partials is the scaled sum); the bias is kept by one rank only, so the reduction adds it once."""
+    from .ops import Linear
+
+    es = 2 if lin.dtype == "bf16" else 1
+    if lin.dtype not in ("fp8", "bf16"):
+        raise ValueError("tensor-parallel shards take fp8 or bf16 weights")
+    kk = c1 - c0
+    buf = graph.buffer(lin.n * kk * es)
+    graph.copy_2d(_addr(lin.buffer) + c0 * es, lin.k * es, buf, kk * es, kk * es, lin.n)
+    return Linear(buf, lin.dtype, lin.scale, lin.n, kk, bias=lin.bias if keep_bias else None,
+                  chan_scale=lin.chan_scale)
+
+
+def shard_block(graph, w, cfg, world: int, rank: int):
+    """This rank's shard of a block's weights (block.BlockWeights) for block._joint_bf16_tp: q / k / v (fused when
+    the block is), the attention gate and MLP gate / up split along their output channels (this rank's heads and
+    MLP columns), wo and MLP down along K; norms and the modulation table are shared. Made once, outside any
+    mark / release scope (new graph buffers)."""
+    import dataclasses
+
+    from .block import fuse_qkv
+
+    if cfg.heads % world or cfg.kv_heads % world or cfg.mlp % world:
+        raise ValueError(f"heads, kv heads and MLP width must split over {world} ranks")
+    hd = cfg.head_dim
+    hq, hk, ml = cfg.heads // world * hd, cfg.kv_heads // world * hd, cfg.mlp // world
+    q0, k0, m0 = rank * hq, rank * hk, rank * ml
+    first = rank == 0
+    out = dict(wq=shard_rows(graph, w.wq, q0, q0 + hq), wk=shard_rows(graph, w.wk, k0, k0 + hk),
+               wv=shard_rows(graph, w.wv, k0, k0 + hk), wo=shard_cols(graph, w.wo, q0, q0 + hq, first),
+               mlp_up=shard_rows(graph, w.mlp_up, m0, m0 + ml), mlp_down=shard_cols(graph, w.mlp_down, m0, m0 + ml, first),
+               gate=shard_rows(graph, w.gate, q0, q0 + hq) if w.gate is not None else None,
+               mlp_gate=shard_rows(graph, w.mlp_gate, m0, m0 + ml) if w.mlp_gate is not None else None, wqkv=None)
+    local = dataclasses.replace(w, **out)
+    return fuse_qkv(graph, local) if w.wqkv is not None else local
+
+
+def shard_model(graph, model, cfg, world: int, rank: int):
+    """This rank's tensor-parallel model (transformer.TransformerWeights): every block sharded (shard_block), the
+    edge linears (time MLP, text and latent projections, last layer) and the last norm shared as they are."""
+    import dataclasses
+
+    bc = cfg.block
+    double = [(shard_block(graph, t, bc, world, rank), shard_block(graph, i, bc, world, rank)) for t, i in model.double]
+    single = [shard_block(graph, b, bc, world, rank) for b in model.single]
+    return dataclasses.replace(model, double=double, single=single)
+
+
+class TPGroup:
+    """A tensor-parallel group on a communicator (comm.Comm): transformer(..., tp=TPGroup(comm)) runs one image's
+    step with every rank holding T / world rows of the residual stream and its shard of every block's linears."""
+
+    def __init__(self, comm):
+        self.comm = comm
+        self.rank, self.world = comm.rank, comm.world
+
+    def shard(self, tokens: int) -> tuple:
+        """(first row, rows) of this rank: tokens split into equal consecutive shards."""
+        if tokens % self.world:
+            raise ValueError(f"{tokens} tokens do not split over {self.world} ranks")
+        n = tokens // self.world
+        return self.rank * n, n

@@ -29,7 +29,7 @@ import numpy as np
 from . import _lib as L
 from . import kernels as K
 from . import ops
-from .block import BlockConfig, BlockWeights, Part, block_flops, buffers_of, joint_block
+from .block import BlockConfig, BlockWeights, Part, TPLayer, block_flops, buffers_of, joint_block
 from .graph import Buffer, Graph, addr
 from .stream import Streamer
 
@@ -273,7 +273,7 @@ class StepGraph:
 
 def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype: str = "f32", velocity=None,
                 on_block=None, sp=None, captured: StepGraph | None = None,
-                streamed: StreamedBlocks | None = None) -> tuple:
+                streamed: StreamedBlocks | None = None, tp=None) -> tuple:
     """One denoising step (transformer.ts:134-176) of one image (`inp` a StepInputs) or of a batch of images (a list
     of StepInputs with the same geometry and timestep). The batch runs as one token stream: every linear is one
     GEMM over all images' rows, attention runs per image.
@@ -288,7 +288,12 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     captured: a StepGraph of this geometry; the blocks then run as its replay (on_block is not called).
 
     streamed: a StreamedBlocks of w: every block's fp8 linears are copied from pinned host memory into a device slot
-    just ahead of the block (eager path only)."""
+    just ahead of the block (eager path only).
+
+    tp: a parallel.TPGroup to split one image's step over the ranks of its communicator by tensor parallelism (bf16
+    path, eager): w is this rank's sharded model (parallel.shard_model); each rank holds T / world rows of the
+    residual stream, and every block gathers the split activations, runs this rank's heads and MLP columns over all
+    rows and reduce-scatters its K-slice partial sums back to the rows' owners. Every rank gets the whole velocity."""
     batch = list(inp) if isinstance(inp, (list, tuple)) else [inp]
     b0 = batch[0]
     if any((b.height, b.width, b.text_tokens, b.timestep) != (b0.height, b0.width, b0.text_tokens, b0.timestep)
@@ -303,7 +308,10 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     cos, sin, pairs = _tables(Lt, rows, cols, tuple(cfg.axes), float(cfg.theta))
     if sp is not None and (B != 1 or dtype != "bf16"):
         raise ValueError("sequence parallelism runs one image on the bf16 path")
-    r0, n = sp.shard(T) if sp is not None else (0, R)  # this rank's rows
+    if tp is not None and (B != 1 or dtype != "bf16" or sp is not None or captured is not None or streamed is not None):
+        raise ValueError("tensor parallelism runs one image on the bf16 path, eagerly")
+    group = sp if sp is not None else tp
+    r0, n = group.shard(T) if group is not None else (0, R)  # this rank's rows
     outs = velocity if isinstance(velocity, (list, tuple)) else [velocity] * B if velocity is not None else [None] * B
     mark = graph.mark()
     t, tvec = time(graph, w, b0.timestep, cfg.time_dim)
@@ -320,7 +328,7 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
     img = ops.linear(graph, tok, w.first, B * image, x_dtype=dtype, y_dtype="f32")
     for i in range(B):
         graph.copy(img, i * image * hid * 4, x, (i * T + Lt) * hid * 4, image * hid * 4)
-    if sp is not None:  # keep this rank's rows
+    if group is not None:  # keep this rank's rows
         xs = graph.buffer(n * hid * 4)
         graph.copy(x, r0 * hid * 4, xs, 0, n * hid * 4)
         graph.free(x)
@@ -338,13 +346,18 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
         if streamed is not None and captured is not None:
             raise ValueError("a streamed step runs eagerly")
         layers = _layers(w, B, T, Lt, image, r0, n)
+        if tp is not None:  # every layer's parts over all T rows, and the tables of all rows, for the gathered GEMMs
+            layers_all = _layers(w, B, T, Lt, image, 0, T)
+            rope_all = ops.Rope(graph.buffer(cos), graph.buffer(sin), pairs, T)
         for i, parts in enumerate(layers):
             if streamed is not None:  # this block's linears from its slot (the same BlockWeights -> the same copy)
                 bound = streamed.bind(i)
                 parts = [Part(p.row0, p.rows, bound[id(p.w)]) for p in parts]
             bm = graph.mark()
+            tpl = TPLayer(tp.comm, layers_all[i], rope_all) if tp is not None else None
             # between blocks the output stays a Residual: the next block's first norm pass adds it
-            nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp, defer=i + 1 < len(layers))
+            nxt = joint_block(graph, parts, bc, x, tvec, rope, dtype, images=B, sp=sp, defer=i + 1 < len(layers),
+                              tp=tpl)
             if streamed is not None:
                 streamed.release(i)
             graph.release(bm, buffers_of(nxt))
@@ -363,6 +376,10 @@ def transformer(graph: Graph, w: TransformerWeights, cfg: StepConfig, inp, dtype
                    w.last_linear.scale, chan_scale=w.last_linear.chan_scale, bias=w.last_linear.bias, y_dtype="f32")
         if sp is not None:  # every rank's rows of the last linear, in order
             last = sp.all_gather_rows(graph, last, n * 4 * ch * 4)
+        elif tp is not None:
+            gathered = graph.buffer(R * 4 * ch * 4)
+            tp.comm.all_gather(last, gathered, n * 4 * ch * 4)
+            last = gathered
     else:
         h = ops.norm(graph, x, w.last_norm, R, hid, ops.Mod(scale, shift), bc.eps)
         last = ops.linear(graph, h, w.last_linear, R)
