@@ -764,6 +764,9 @@ def main() -> None:
     hi8 = [torch.empty(M, K, dtype=torch.uint8, device=dev) for _ in range(NB)]
     lo8 = [torch.empty(M, K, dtype=torch.uint8, device=dev) for _ in range(NB)]
     rs8 = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(NB)]
+    xf8 = [torch.randn(M, K, generator=gen, device=dev) for _ in range(NB)]  # f32 residual stream, update, sum
+    rf8 = [torch.randn(M, K, generator=gen, device=dev) for _ in range(NB)]
+    xo8 = [torch.empty(M, K, device=dev) for _ in range(NB)]
     act_bytes = M * K * 2
     bw = {}
     for name, fn, nbytes in [
@@ -776,11 +779,18 @@ def main() -> None:
                                                       x_dtype="bf16", out_dtype="bf16"), 2 * act_bytes + 2 * M * pairs * 4),
         ("act_split_2term", lambda i: we.kernels.quantize_act(g, xs8[i], M, K, hi8[i], lo8[i], rs8[i], terms=2),
          act_bytes + 2 * M * K + M * 4),
+        # a block's first norm: the f32 residual stream -> RMSNorm + modulation -> bf16 -> two e4m3 planes
+        ("norm_split_f32", lambda i: we.kernels.norm_split(g, xf8[i], wn, M, K, hi8[i], lo8[i], rs8[i], scale=sc_v,
+                                                           shift=sh_v, x_dtype="f32"), 2 * act_bytes + 2 * M * K + M * 4),
+        # the residual form: x + r written back (f32), then the same norm + split
+        ("add_norm_split", lambda i: we.kernels.add_norm_split(g, xf8[i], rf8[i], xo8[i], wn, M, K, hi8[i], lo8[i],
+                                                               rs8[i], scale=sc_v, shift=sh_v),
+         6 * act_bytes + 2 * M * K + M * 4),
     ]:
         t_ms = timed(lambda: [fn(i) for i in range(NB)], args.steps, 2) / args.steps / NB
         bw[name] = {"ms": t_ms, "gbs": nbytes / (t_ms * 1e-3) / 1e9, "frac_hbm": nbytes / (t_ms * 1e-3) / 1e9 / hbm,
                     "bytes": nbytes, "launches_per_step": NB}
-    del xs8, xn8, hi8, lo8, rs8
+    del xs8, xn8, hi8, lo8, rs8, xf8, rf8, xo8
     roofline["bandwidth_kernels"] = bw
 
     # ---- config 3's attention (4608 tokens, 24 heads x 128, bf16): tcgen05 flash attention ----

@@ -291,7 +291,8 @@ int we_ew(we_ctx* ctx, int32_t op, const void* a, const void* b, const float* g,
           int32_t out_dtype, void** out);
 /* norm() followed by the e4m3 activation split of its bf16-rounded output, in one pass: the planes and row
    scales equal we_rmsnorm(out_dtype = bf16) then we_quantize_act up to the summation order of the row's sum of
-   squares (a 1-ulp bf16 difference in rare values). d % 8 == 0, d <= 8192, 16-byte aligned. */
+   squares and the modulation's rounding (y = fma(x inv, (offset + w)(1 + scale), shift), the product of the two
+   factors rounded once): a 1-ulp bf16 difference in rare values. d % 8 == 0, d <= 8192, 16-byte aligned. */
 int we_norm_split(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, const float* scale,
                   const float* shift, int64_t rows, int64_t d, float eps, float offset, int32_t terms, uint8_t* hi,
                   uint8_t* lo, float* row_scale);

@@ -110,6 +110,7 @@ def test_activation_split_bit_exact(we, graph, m, k, terms):
     x[1] *= np.float32(300.0)
     x[2] *= np.float32(1e-3)
     x[3] = 0
+    x[4] *= np.float32(1e-37)  # 2^-e above the largest float: the kernels' ldexpf path instead of a multiply
     x = bf16_round(x).reshape(m, k)
     mark = graph.mark()
     xb = graph.buffer(bf16(x))

@@ -6,6 +6,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "../../include/we_b200.h"
 
@@ -169,9 +170,9 @@ __device__ __forceinline__ float2 silu2(float2 v) {
 // Grid of a row-loop kernel: as many CTAs as fit on the SMs at once (each then walks its rows, and a kernel that
 // prefetches its next row keeps those loads in flight), at most one per row.
 template <typename K>
-static inline unsigned resident_grid(K kernel, int threads, int sms, int64_t rows) {
+static inline unsigned resident_grid(K kernel, int threads, int sms, int64_t rows, size_t smem = 0) {
   int per = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, 0) != cudaSuccess || per < 1) per = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess || per < 1) per = 1;
   const int64_t g = (int64_t)per * sms;
   return (unsigned)(rows < g ? rows : g);
 }
@@ -186,6 +187,77 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// ---- programmatic dependent launch (griddepcontrol) ----
+// A kernel launched by launch_pdl may begin while the kernel before it in the stream is still finishing: its CTAs
+// are placed as that kernel's CTAs leave the SMs, so the launch latency and the block scheduling overlap the
+// previous kernel's tail. Such a kernel calls pdl_wait() in every CTA before its first global memory access (read
+// or write): the wait returns once the previous kernel has completed and its writes are visible, and calling it
+// unconditionally keeps "this kernel completed" implying "every earlier kernel completed" for the next one.
+// pdl_launch_dependents() lets the next kernel's CTAs be placed once every CTA of this one has started.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// WE_PDL=0 launches the pdl kernels as ordinary stream-ordered launches (their pdl_wait then returns at once).
+static inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* env = getenv("WE_PDL");
+    return !(env && env[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                                     cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---- cp.async: a thread's own global -> shared copies, in flight without holding registers ----
+// A thread that reads back only the bytes it copied itself needs no barrier: cp.async.wait_group orders them.
+// `smem` is a shared-memory address (__cvta_generic_to_shared).
+__device__ __forceinline__ void cp_async16(uint32_t smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most N of this thread's committed groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// max over the warp's 32 lanes of |v| (sm_100a redux.sync; NaN lanes are ignored, as fmaxf does)
+__device__ __forceinline__ float warp_max_abs(float v) {
+  float r;
+  asm volatile("redux.sync.max.abs.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// Exponent e of the activation split's row scale 2^e for a row maximum |x| = amax: the smallest e with
+// amax 2^-e <= 448 when amax's mantissa is at most 1.75 (E - 9), else one more (E - 8), amax = f 2^E, f in [0.5, 1).
+// Normal amax by its bits, the rest (0, subnormal, inf, NaN) by frexpf.
+__device__ __forceinline__ int split_exponent(float amax) {
+  const uint32_t b = __float_as_uint(amax);
+  const uint32_t ex = (b >> 23) & 0xffu;
+  if (ex != 0u && ex != 0xffu && !(b >> 31)) return (int)ex - 126 - ((b & 0x7fffffu) <= 0x600000u ? 9 : 8);
+  if (!(amax > 0.f)) return 0;
+  int E;
+  const float f = frexpf(amax, &E);
+  return (2.f * f <= 1.75f) ? E - 9 : E - 8;
 }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {

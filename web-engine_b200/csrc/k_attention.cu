@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
   using namespace fa2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  pdl_launch_dependents();  // a kernel launched by launch_pdl after this one may place its CTAs as these finish
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + BAR_OFF;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + BAR_OFF + NUM_BARS * 8);

@@ -74,241 +74,232 @@ cudaError_t launch_elementwise(int op, const void* a, const void* b, const float
 }
 
 // ---------------- RMSNorm + modulation fused with the e4m3 split ----------------
-// One warp per row: the normalised, modulated row is rounded to bf16 (the value the unfused path
-// would store), then split into hi / lo e4m3 planes under the row's power-of-two scale, exactly as
-// quant_act_kernel does on that bf16 row. So the planes equal norm(bf16 out) followed by the split.
-template <int DT, int TERMS, int UMAX>
-__global__ void __launch_bounds__(128) norm_split_kernel(const void* __restrict__ x, const float* __restrict__ w,
-                                                         const float* __restrict__ sc, const float* __restrict__ sh,
-                                                         int64_t rows, int64_t d, float eps, float offset,
-                                                         uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
-                                                         float* __restrict__ row_scale) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * 4;
-  for (int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5); row < rows; row += warps) {
-    float v[UMAX][8];
-    float ss = 0.f;
+// 8 values (four pairs, already scaled by the row's 2^-e) -> their e4m3 hi (and lo = e4m3(s - hi)) terms, 8 bytes each
+template <int TERMS>
+__device__ __forceinline__ void split_store8(const float2 (&s)[4], uint8_t* hi, uint8_t* lo) {
+  uint32_t h[2], l[2];
 #pragma unroll
-    for (int c = 0; c < UMAX; c++) {
-      const int64_t i = (int64_t)(c * 32 + lane) * 8;
-      if (i < d) {
-        load8<DT>(x, row * d + i, v[c]);
-        // the summation order of rmsnorm_warp_kernel, so a bf16 row normalises to the same bits
-#pragma unroll
-        for (int j = 0; j < 4; j++) ss = fmaf(v[c][2 * j], v[c][2 * j], fmaf(v[c][2 * j + 1], v[c][2 * j + 1], ss));
-      }
-    }
-    const float inv = rsqrtf(warp_sum(ss) / (float)d + eps);
-    float amax = 0.f;
-#pragma unroll
-    for (int c = 0; c < UMAX; c++) {
-      const int64_t i = (int64_t)(c * 32 + lane) * 8;
-      if (i >= d) continue;
-      float ww[8], s8[8], h8[8];
-      load8f(w, i, ww);
-      if (sc) load8f(sc, i, s8); else for (int j = 0; j < 8; j++) s8[j] = 0.f;
-      if (sh) load8f(sh, i, h8); else for (int j = 0; j < 8; j++) h8[j] = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const float y = v[c][j] * inv * (offset + ww[j]) * (1.f + s8[j]) + h8[j];
-        v[c][j] = bf16_bits_to_f32(f32_to_bf16_bits(y));
-        amax = fmaxf(amax, fabsf(v[c][j]));
-      }
-    }
-    amax = warp_max(amax);
-    int e = 0;
-    if (amax > 0.f) {
-      int E;
-      const float f = frexpf(amax, &E);
-      e = (2.f * f <= 1.75f) ? E - 9 : E - 8;
-    }
-    if (lane == 0) row_scale[row] = ldexpf(1.0f, e);
-#pragma unroll
-    for (int c = 0; c < UMAX; c++) {
-      const int64_t i = (int64_t)(c * 32 + lane) * 8;
-      if (i >= d) continue;
-      float s[8];
-#pragma unroll
-      for (int j = 0; j < 8; j++) s[j] = ldexpf(v[c][j], -e);
-      uint32_t h2[2], l2[2];
-#pragma unroll
-      for (int j = 0; j < 2; j++) {
-        const uint16_t h0 = f32x2_to_e4m3x2(s[4 * j], s[4 * j + 1]);
-        const uint16_t h1 = f32x2_to_e4m3x2(s[4 * j + 2], s[4 * j + 3]);
-        h2[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        if (TERMS > 1) {
-          const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
-          const uint16_t l0 = f32x2_to_e4m3x2(s[4 * j] - d0.x, s[4 * j + 1] - d0.y);
-          const uint16_t l1 = f32x2_to_e4m3x2(s[4 * j + 2] - d1.x, s[4 * j + 3] - d1.y);
-          l2[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-        }
-      }
-      *reinterpret_cast<uint2*>(hi + row * d + i) = make_uint2(h2[0], h2[1]);
-      if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * d + i) = make_uint2(l2[0], l2[1]);
+  for (int j = 0; j < 2; j++) {
+    const uint16_t h0 = f32x2_to_e4m3x2(s[2 * j].x, s[2 * j].y), h1 = f32x2_to_e4m3x2(s[2 * j + 1].x, s[2 * j + 1].y);
+    h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+    if (TERMS > 1) {
+      const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+      const float2 r0 = __fadd2_rn(s[2 * j], make_float2(-d0.x, -d0.y));
+      const float2 r1 = __fadd2_rn(s[2 * j + 1], make_float2(-d1.x, -d1.y));
+      l[j] = (uint32_t)f32x2_to_e4m3x2(r0.x, r0.y) | ((uint32_t)f32x2_to_e4m3x2(r1.x, r1.y) << 16);
     }
   }
+  *reinterpret_cast<uint2*>(hi) = make_uint2(h[0], h[1]);
+  if (TERMS > 1) *reinterpret_cast<uint2*>(lo) = make_uint2(l[0], l[1]);
 }
 
-// The same, one 256-thread CTA per row for rows of 2048+ values: thread t keeps the row's 4-value chunks t,
-// t + 256, ... in registers (3 chunks at d = 3072: few registers, many rows in flight per SM, where the warp per
-// row form holds a whole row per warp and is latency-bound); the sum of squares and the maximum go through a
-// shared-memory reduction over the 8 warps in a fixed order.
-template <int DT>
-__device__ __forceinline__ void load4(const void* p, int64_t i, float v[4]) {
-  if constexpr (DT == WE_F32) {
-    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  } else {
-    const uint2 a = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
-    v[0] = __uint_as_float(a.x << 16); v[1] = __uint_as_float(a.x & 0xffff0000u);
-    v[2] = __uint_as_float(a.y << 16); v[3] = __uint_as_float(a.y & 0xffff0000u);
-  }
-}
-
-// RES: the row is x + r (f32 residual plus f32 update), written to xo before it is normalised (the residual add
-// of a block, fused with the next RMSNorm and split)
-template <int DT, int TERMS, int CH, bool RES = false>
-__global__ void __launch_bounds__(256) norm_split_row_kernel(const void* __restrict__ x, const float* __restrict__ w,
-                                                             const float* __restrict__ sc, const float* __restrict__ sh,
-                                                             int64_t rows, int64_t d, float eps, float offset,
-                                                             uint8_t* __restrict__ hi, uint8_t* __restrict__ lo,
-                                                             float* __restrict__ row_scale,
-                                                             const float* __restrict__ r = nullptr,
-                                                             float* __restrict__ xo = nullptr) {
-  __shared__ float red[2][8];
+// CTA-per-row RMSNorm + modulation + bf16 rounding + e4m3 split for rows of 2048..8192 values (d % 8 == 0). NT
+// threads; thread t owns the 8-value chunks t, t + NT, ... (CH of them) of every row and keeps its columns'
+// modulation in registers for all the rows the CTA strides over, as two factors: (offset + w)(1 + scale), rounded
+// once, and the shift, so y = fma(x inv, (offset + w)(1 + scale), shift) (one f32 rounding from the product order
+// of rmsnorm.ts:42-46). The rows are staged through shared memory by cp.async, S - 1 rows ahead of the one being
+// reduced: each thread copies exactly the chunks it later reads, so the ring needs no barrier, and the loads in
+// flight hold no registers. Per row: sum of squares (warp shuffle, then the NT / 32 warps in a fixed order), y
+// rounded to bf16, the row's |y| max (warp redux, then the warps), the power-of-two row scale, the e4m3 planes; the
+// arithmetic runs two values at a time (packed f32x2). Many values per thread keep the per-row reductions a small
+// share of the instructions.
+// RES: the row is x + r (f32 residual plus f32 update), written to xo before it is normalised (the residual add of a
+// block, fused with the next RMSNorm and split); both inputs are staged.
+template <int DT, int TERMS, int NT, int CH, int S, bool RES = false>
+__global__ void __launch_bounds__(NT, 512 / NT) norm_split_row_kernel(
+    const void* __restrict__ x, const float* __restrict__ w, const float* __restrict__ sc,
+    const float* __restrict__ sh, int64_t rows, int64_t d, float eps, float offset, uint8_t* __restrict__ hi,
+    uint8_t* __restrict__ lo, float* __restrict__ row_scale, const float* __restrict__ r = nullptr,
+    float* __restrict__ xo = nullptr) {
+  constexpr int NW = NT / 32;
+  constexpr int ES = DT == WE_F32 ? 4 : 2;  // bytes per value of x
+  constexpr int XB = 8 * ES;                 // bytes of one 8-value chunk of x
+  constexpr int XSTAGE = CH * NT * XB, RSTAGE = CH * NT * 32;
+  extern __shared__ __align__(16) uint8_t ring[];  // [S][CH][NT] chunks of x, then (RES) [S][CH][NT] of r
+  __shared__ __align__(16) float red[2][NW];
+  pdl_wait();  // launched by launch_pdl: the previous kernel's outputs (x, r, the modulation) are complete
+  pdl_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
-  float wo[CH][4], g1[CH][4], sf[CH][4];  // offset + w, 1 + scale, shift of this thread's columns, once per CTA
+  const int dd = (int)d;
+  float2 mw[CH][4], sf[CH][4];  // (offset + w)(1 + scale) and shift of this thread's columns, once per CTA
 #pragma unroll
   for (int c = 0; c < CH; c++) {
-    const int64_t i = (int64_t)(c * 256 + tid) * 4;
-    const bool live = i < d;
-    const float4 ww = live ? *reinterpret_cast<const float4*>(w + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 s4 = live && sc ? *reinterpret_cast<const float4*>(sc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 h4 = live && sh ? *reinterpret_cast<const float4*>(sh + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float wv[4] = {ww.x, ww.y, ww.z, ww.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+    const int i = (c * NT + tid) * 8;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      wo[c][j] = offset + wv[j];
-      g1[c][j] = 1.f + sv[j];
-      sf[c][j] = hv[j];
+    for (int h = 0; h < 2; h++) {
+      const bool live = i < dd;
+      const float4 ww = live ? *reinterpret_cast<const float4*>(w + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 s4 = live && sc ? *reinterpret_cast<const float4*>(sc + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 h4 = live && sh ? *reinterpret_cast<const float4*>(sh + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      mw[c][2 * h] = make_float2((offset + ww.x) * (1.f + s4.x), (offset + ww.y) * (1.f + s4.y));
+      mw[c][2 * h + 1] = make_float2((offset + ww.z) * (1.f + s4.z), (offset + ww.w) * (1.f + s4.w));
+      sf[c][2 * h] = make_float2(h4.x, h4.y);
+      sf[c][2 * h + 1] = make_float2(h4.z, h4.w);
     }
   }
-  // software-pipelined over rows: the next row's loads are in flight while this row is reduced and stored
-  float nx[CH][4], nr[CH][4];
-  auto fetch = [&](int64_t row) {
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+  auto issue = [&](int64_t row, int s) {  // this thread's chunks of `row` into stage s (an empty group past the end)
+    if (row < rows) {
+      const uint8_t* xr = static_cast<const uint8_t*>(x) + row * d * ES;
+      const float* rr = RES ? r + row * d : nullptr;
 #pragma unroll
-    for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i < d && row < rows) {
-        load4<DT>(x, row * d + i, nx[c]);
-        if (RES) {
-          const float4 u = *reinterpret_cast<const float4*>(r + row * d + i);
-          nr[c][0] = u.x; nr[c][1] = u.y; nr[c][2] = u.z; nr[c][3] = u.w;
+      for (int c = 0; c < CH; c++) {
+        const int i = (c * NT + tid) * 8;
+        if (i >= dd) continue;
+        const uint32_t xa = ring_s + s * XSTAGE + (c * NT + tid) * XB;
+#pragma unroll
+        for (int q = 0; q < XB / 16; q++) cp_async16(xa + 16 * q, xr + i * ES + 16 * q);
+        if constexpr (RES) {
+          const uint32_t ra = ring_s + S * XSTAGE + s * RSTAGE + (c * NT + tid) * 32;
+          cp_async16(ra, rr + i);
+          cp_async16(ra + 16, rr + i + 4);
         }
       }
     }
+    cp_async_commit();
   };
-  fetch(blockIdx.x);
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[CH][4];
-    float ss = 0.f;
+  const int64_t G = gridDim.x;
+  int64_t row = blockIdx.x;
+#pragma unroll
+  for (int s = 0; s < S - 1; s++) issue(row + s * G, s);
+  int s = 0, sn = S - 1;  // stage of this row, stage the next issue fills (the one read one row ago)
+  for (; row < rows; row += G) {
+    issue(row + (S - 1) * G, sn);
+    cp_async_wait<S - 1>();  // this row's group has landed
+    float2 v[CH][4];
+    float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < CH; c++) {
+      const int i = (c * NT + tid) * 8;
 #pragma unroll
-      for (int j = 0; j < 4; j++) v[c][j] = RES ? nx[c][j] + nr[c][j] : nx[c][j];
-    }
-    fetch(row + gridDim.x);
+      for (int j = 0; j < 4; j++) v[c][j] = make_float2(0.f, 0.f);
+      if (i >= dd) continue;
+      const uint8_t* xs = ring + s * XSTAGE + (c * NT + tid) * XB;
+      if constexpr (DT == WE_F32) {
+        const float4 a = *reinterpret_cast<const float4*>(xs), b = *reinterpret_cast<const float4*>(xs + 16);
+        v[c][0] = make_float2(a.x, a.y); v[c][1] = make_float2(a.z, a.w);
+        v[c][2] = make_float2(b.x, b.y); v[c][3] = make_float2(b.z, b.w);
+      } else {
+        const uint4 a = *reinterpret_cast<const uint4*>(xs);
+        const uint32_t u[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-    for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i < d) {
-        if (RES) *reinterpret_cast<float4*>(xo + row * d + i) = make_float4(v[c][0], v[c][1], v[c][2], v[c][3]);
-        ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
-        ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
+        for (int j = 0; j < 4; j++) v[c][j] = make_float2(__uint_as_float(u[j] << 16), __uint_as_float(u[j] & 0xffff0000u));
       }
+      if constexpr (RES) {
+        const uint8_t* rs = ring + S * XSTAGE + s * RSTAGE + (c * NT + tid) * 32;
+        const float4 a = *reinterpret_cast<const float4*>(rs), b = *reinterpret_cast<const float4*>(rs + 16);
+        v[c][0] = __fadd2_rn(v[c][0], make_float2(a.x, a.y)); v[c][1] = __fadd2_rn(v[c][1], make_float2(a.z, a.w));
+        v[c][2] = __fadd2_rn(v[c][2], make_float2(b.x, b.y)); v[c][3] = __fadd2_rn(v[c][3], make_float2(b.z, b.w));
+        float* xor_ = xo + row * d + i;
+        *reinterpret_cast<float4*>(xor_) = make_float4(v[c][0].x, v[c][0].y, v[c][1].x, v[c][1].y);
+        *reinterpret_cast<float4*>(xor_ + 4) = make_float4(v[c][2].x, v[c][2].y, v[c][3].x, v[c][3].y);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) ss2 = __ffma2_rn(v[c][j], v[c][j], ss2);
     }
-    ss = warp_sum(ss);
+    s = s + 1 == S ? 0 : s + 1;
+    sn = sn + 1 == S ? 0 : sn + 1;
+    const float ss = warp_sum(ss2.x + ss2.y);
     if (lane == 0) red[0][wp] = ss;
     __syncthreads();
-    const float tot = ((red[0][0] + red[0][1]) + (red[0][2] + red[0][3])) + ((red[0][4] + red[0][5]) + (red[0][6] + red[0][7]));
-    const float inv = rsqrtf(tot / (float)d + eps);
+    float tot = red[0][0];
+#pragma unroll
+    for (int k = 1; k < NW; k++) tot += red[0][k];
+    const float inv = rsqrtf(tot / (float)dd + eps);
+    const float2 inv2 = make_float2(inv, inv);
     float amax = 0.f;
 #pragma unroll
     for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i >= d) continue;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const float y = v[c][j] * inv * wo[c][j] * g1[c][j] + sf[c][j];
-        v[c][j] = bf16_bits_to_f32(f32_to_bf16_bits(y));
-        amax = fmaxf(amax, fabsf(v[c][j]));
+        const float2 p = __ffma2_rn(__fmul2_rn(v[c][j], inv2), mw[c][j], sf[c][j]);
+        const uint32_t b = pack_bf16x2(p.x, p.y);
+        v[c][j] = make_float2(__uint_as_float(b << 16), __uint_as_float(b & 0xffff0000u));
+        amax = fmaxf(amax, fmaxf(fabsf(v[c][j].x), fabsf(v[c][j].y)));  // chunks past d are 0
       }
     }
-    amax = warp_max(amax);
+    amax = warp_max_abs(amax);
     if (lane == 0) red[1][wp] = amax;
     __syncthreads();
-    amax = fmaxf(fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3])),
-                 fmaxf(fmaxf(red[1][4], red[1][5]), fmaxf(red[1][6], red[1][7])));
-    int e = 0;
-    if (amax > 0.f) {
-      int E;
-      const float f = frexpf(amax, &E);
-      e = (2.f * f <= 1.75f) ? E - 9 : E - 8;
-    }
+    amax = red[1][0];
+#pragma unroll
+    for (int k = 1; k < NW; k++) amax = fmaxf(amax, red[1][k]);
+    const int e = split_exponent(amax);
     if (tid == 0) row_scale[row] = ldexpf(1.0f, e);
+    uint8_t* const hr = hi + row * d;
+    uint8_t* const lr = TERMS > 1 ? lo + row * d : nullptr;
+    // 2^-e is uniform over the row: one branch per row; the usual case (2^-e a normal float) scales by packed
+    // multiplies (exact, as ldexpf), ldexpf only for rows whose scale is outside that range
+    const int b = 127 - e;
+    if (b >= 1 && b <= 254) {
+      const float2 mul2 = make_float2(__int_as_float(b << 23), __int_as_float(b << 23));
 #pragma unroll
-    for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i >= d) continue;
-      float s[4];
+      for (int c = 0; c < CH; c++) {
+        const int i = (c * NT + tid) * 8;
+        if (i >= dd) continue;
+        float2 t[4];
 #pragma unroll
-      for (int j = 0; j < 4; j++) s[j] = ldexpf(v[c][j], -e);
-      const uint16_t h0 = f32x2_to_e4m3x2(s[0], s[1]), h1 = f32x2_to_e4m3x2(s[2], s[3]);
-      *reinterpret_cast<uint32_t*>(hi + row * d + i) = (uint32_t)h0 | ((uint32_t)h1 << 16);
-      if (TERMS > 1) {
-        const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
-        const uint16_t l0 = f32x2_to_e4m3x2(s[0] - d0.x, s[1] - d0.y), l1 = f32x2_to_e4m3x2(s[2] - d1.x, s[3] - d1.y);
-        *reinterpret_cast<uint32_t*>(lo + row * d + i) = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        for (int j = 0; j < 4; j++) t[j] = __fmul2_rn(v[c][j], mul2);
+        split_store8<TERMS>(t, hr + i, lr + i);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < CH; c++) {
+        const int i = (c * NT + tid) * 8;
+        if (i >= dd) continue;
+        float2 t[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) t[j] = make_float2(ldexpf(v[c][j].x, -e), ldexpf(v[c][j].y, -e));
+        split_store8<TERMS>(t, hr + i, lr + i);
       }
     }
     // red[0] was read before the second barrier and red[1] is next written after the next row's first one
   }
+  cp_async_wait<0>();  // nothing is left in flight (every row issued was consumed); kept as the exit rule
 }
 
-template <int DT, int TERMS>
-static bool norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
-                           float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs, int sms, cudaStream_t st) {
-  const int64_t ch = (d / 4 + 255) / 256;
-#define WE_NS(CH)                                                                                              \
-  {                                                                                                            \
-    auto k = norm_split_row_kernel<DT, TERMS, CH>;                                                             \
-    k<<<resident_grid(k, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, nullptr, \
-                                                         nullptr);                                             \
-  }
-  if (ch <= 2) WE_NS(2)
-  else if (ch <= 3) WE_NS(3)
-  else if (ch <= 4) WE_NS(4)
-  else if (ch <= 6) WE_NS(6)
-  else if (ch <= 8) WE_NS(8)
-  else return false;
+// The ring of the row kernel: as many stages (2..4) of one row as fit in 36 KB (72 KB with the residual's rows too),
+// two or three rows in flight per CTA. Deeper rings measured slower: every CTA requests most of its rows at once
+// and the first row of each waits behind all of them.
+template <int DT, bool RES, int NT, int CH>
+constexpr size_t norm_ring_stage_bytes() {
+  return (size_t)CH * NT * (8 * (DT == WE_F32 ? 4 : 2) + (RES ? 32 : 0));
+}
+template <int DT, bool RES, int NT, int CH>
+constexpr int norm_ring_stages() {
+  constexpr size_t n = (RES ? 72 * 1024 : 36 * 1024) / norm_ring_stage_bytes<DT, RES, NT, CH>();
+  return n < 2 ? 2 : n > 4 ? 4 : (int)n;
+}
+
+template <int DT, int TERMS, int NT, int CH, bool RES>
+static cudaError_t launch_norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
+                                         int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs,
+                                         const float* r, float* xo, int sms, cudaStream_t st) {
+  constexpr int S = norm_ring_stages<DT, RES, NT, CH>();
+  constexpr size_t smem = S * norm_ring_stage_bytes<DT, RES, NT, CH>();
+  auto k = norm_split_row_kernel<DT, TERMS, NT, CH, S, RES>;
+  // the ring plus the kernel's static reductions can pass the 48 KB a launch gets without this opt-in
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k, resident_grid(k, NT, sms, rows, smem), NT, smem, st, x, w, sc, sh, rows, d, eps, offset, hi, lo,
+                    rs, r, xo);
+}
+
+// d % 8 == 0, d <= 8192: 128 threads x up to 3 chunks (d <= 3072), else 256 threads x up to 4
+template <int DT, int TERMS, bool RES>
+static cudaError_t norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
+                                  int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs,
+                                  const float* r, float* xo, int sms, cudaStream_t st) {
+  const int64_t chunks = d / 8;
+#define WE_NS(NT, CH) \
+  return launch_norm_split_row<DT, TERMS, NT, CH, RES>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo, sms, st)
+  if (chunks <= 128 * 2) WE_NS(128, 2);
+  if (chunks <= 128 * 3) WE_NS(128, 3);
+  if (chunks <= 256 * 2) WE_NS(256, 2);
+  if (chunks <= 256 * 3) WE_NS(256, 3);
+  if (chunks <= 256 * 4) WE_NS(256, 4);
 #undef WE_NS
-  return true;
-}
-
-template <int DT, int TERMS>
-static bool norm_split_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
-                                int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs, int sms,
-                                cudaStream_t st) {
-  if (d >= 2048 && norm_split_row<DT, TERMS>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st)) return true;
-  int64_t g = (rows + 3) / 4;
-  if (g > (int64_t)sms * 16) g = (int64_t)sms * 16;
-  if (d <= 256 * 4) norm_split_kernel<DT, TERMS, 4><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (d <= 256 * 8) norm_split_kernel<DT, TERMS, 8><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (d <= 256 * 12) norm_split_kernel<DT, TERMS, 12><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (d <= 256 * 16) norm_split_kernel<DT, TERMS, 16><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else if (d <= 256 * 24) norm_split_kernel<DT, TERMS, 24><<<(unsigned)g, 128, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs);
-  else return false;
-  return true;
+  return cudaErrorNotSupported;
 }
 
 cudaError_t launch_add_norm_split(const float* x, const float* r, float* xo, const float* w, const float* sc,
@@ -318,40 +309,28 @@ cudaError_t launch_add_norm_split(const float* x, const float* r, float* xo, con
   if (d % 8 || d > 8192 || !al(x) || !al(r) || !al(xo) || !al(w) || (sc && !al(sc)) || (sh && !al(sh)) ||
       ((uintptr_t)hi & 7) || (lo && ((uintptr_t)lo & 7)))
     return cudaErrorNotSupported;
-  const int64_t ch = (d / 4 + 255) / 256;
-#define WE_ANS(CH)                                                                                                  \
-  {                                                                                                                 \
-    if (terms > 1) {                                                                                                \
-      auto k = norm_split_row_kernel<WE_F32, 2, CH, true>;                                                          \
-      k<<<resident_grid(k, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo);   \
-    } else {                                                                                                        \
-      auto k = norm_split_row_kernel<WE_F32, 1, CH, true>;                                                          \
-      k<<<resident_grid(k, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo);   \
-    }                                                                                                               \
-  }
-  if (ch <= 2) WE_ANS(2)
-  else if (ch <= 3) WE_ANS(3)
-  else if (ch <= 4) WE_ANS(4)
-  else if (ch <= 6) WE_ANS(6)
-  else WE_ANS(8)
-#undef WE_ANS
-  return cudaGetLastError();
+  const cudaError_t e = terms > 1 ? norm_split_row<WE_F32, 2, true>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo, sms, st)
+                                  : norm_split_row<WE_F32, 1, true>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo, sms, st);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_norm_split(const void* x, int xdt, const float* w, const float* sc, const float* sh, int64_t rows,
                               int64_t d, float eps, float offset, int terms, uint8_t* hi, uint8_t* lo, float* rs,
                               int sms, cudaStream_t st) {
   auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
-  if (d % 8 || !al(x) || !al(w) || (sc && !al(sc)) || (sh && !al(sh)) || ((uintptr_t)hi & 7) ||
+  if (d % 8 || d > 8192 || !al(x) || !al(w) || (sc && !al(sc)) || (sh && !al(sh)) || ((uintptr_t)hi & 7) ||
       (lo && ((uintptr_t)lo & 7)))
     return cudaErrorNotSupported;
-  bool ok;
-  if (xdt == WE_BF16) ok = terms > 1 ? norm_split_dispatch<WE_BF16, 2>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st)
-                                     : norm_split_dispatch<WE_BF16, 1>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st);
-  else ok = terms > 1 ? norm_split_dispatch<WE_F32, 2>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st)
-                      : norm_split_dispatch<WE_F32, 1>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, sms, st);
-  if (!ok) return cudaErrorNotSupported;
-  return cudaGetLastError();
+  // every width takes the CTA-per-row kernel, so norm + split of x equals the residual form's on x = x1 + dn bit
+  // for bit
+  cudaError_t e;
+  if (xdt == WE_BF16)
+    e = terms > 1 ? norm_split_row<WE_BF16, 2, false>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, nullptr, nullptr, sms, st)
+                  : norm_split_row<WE_BF16, 1, false>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, nullptr, nullptr, sms, st);
+  else
+    e = terms > 1 ? norm_split_row<WE_F32, 2, false>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, nullptr, nullptr, sms, st)
+                  : norm_split_row<WE_F32, 1, false>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, nullptr, nullptr, sms, st);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace we

@@ -325,6 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  pdl_launch_dependents();  // a kernel launched by launch_pdl after this one may place its CTAs as these finish
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::BAR_OFFSET;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::BAR_OFFSET + L::NUM_BARS * 8);
@@ -546,6 +547,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  pdl_launch_dependents();  // a kernel launched by launch_pdl after this one may place its CTAs as these finish
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::BAR_OFFSET;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::BAR_OFFSET + L::NUM_BARS * 8);
@@ -819,6 +821,7 @@ __global__ void __launch_bounds__(192 + 32 * CW, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  pdl_launch_dependents();  // a kernel launched by launch_pdl after this one may place its CTAs as these finish
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::BAR_OFFSET;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::BAR_OFFSET + L::NUM_BARS * 8);

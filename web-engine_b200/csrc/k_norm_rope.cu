@@ -162,89 +162,118 @@ __global__ void __launch_bounds__(128) rmsnorm_warp_kernel(const uint16_t* __res
   }
 }
 
-// CTA-per-row RMSNorm for rows of 2048..8192 values (16-byte aligned, d % 4 == 0): 256 threads, thread t owns
-// the 4-value chunks t, t + 256, ... of every row. Its weight / scale / shift values are loaded once per CTA and
-// kept in registers across the rows the CTA strides over (a warp-per-row form reloads those three f32 vectors,
-// six times the row's own bytes, for every row). Sum of squares: warp shuffle, then the 8 warps in a fixed order.
-template <int DT, int OT, int CH>
-__global__ void __launch_bounds__(256) rmsnorm_row_kernel(const void* __restrict__ x, const float* __restrict__ w,
-                                                          const float* __restrict__ sc, const float* __restrict__ sh,
-                                                          int64_t rows, int64_t d, float eps, float offset,
-                                                          void* __restrict__ out) {
-  __shared__ float red[8];
+// CTA-per-row RMSNorm for rows of 2048..8192 values (16-byte aligned, d % 8 == 0): NT threads, thread t owns the
+// 8-value chunks t, t + NT, ... (CH of them) of every row and keeps its columns' modulation in registers across the
+// rows the CTA strides over (a warp-per-row form reloads those f32 vectors, six times the row's own bytes, for every
+// row), as two factors: (offset + w)(1 + scale), rounded once, and the shift, so y = fma(x inv, (offset + w)(1 +
+// scale), shift) (one f32 rounding from the product order of rmsnorm.ts:42-46). The rows are staged through shared
+// memory by cp.async, S - 1 rows ahead: each thread copies the chunks it later reads (no barrier on the ring) and the
+// loads in flight hold no registers. Sum of squares: warp shuffle, then the warps in a fixed order; the per-value
+// arithmetic runs two values at a time (packed f32x2); offsets within a row are 32-bit (d <= 8192).
+template <int DT, int OT, int NT, int CH, int S>
+__global__ void __launch_bounds__(NT, NT == 192 ? 4 : 512 / NT) rmsnorm_row_kernel(
+    const void* __restrict__ x, const float* __restrict__ w, const float* __restrict__ sc,
+    const float* __restrict__ sh, int64_t rows, int64_t d, float eps, float offset, void* __restrict__ out) {
+  constexpr int NW = NT / 32;
+  constexpr int ES = DT == WE_F32 ? 4 : 2;  // bytes per value of x
+  constexpr int XB = 8 * ES;                 // bytes of one 8-value chunk
+  constexpr int XSTAGE = CH * NT * XB;
+  extern __shared__ __align__(16) uint8_t ring[];  // [S][CH][NT] chunks
+  __shared__ __align__(16) float red[NW];
+  pdl_wait();  // launched by launch_pdl: the previous kernel's outputs (x, the modulation) are complete
+  pdl_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
-  float wo[CH][4], g1[CH][4], sf[CH][4];  // offset + w, 1 + scale, shift of this thread's columns
+  const int dd = (int)d;
+  float2 mw[CH][4], sf[CH][4];  // (offset + w)(1 + scale) and shift of this thread's columns
 #pragma unroll
   for (int c = 0; c < CH; c++) {
-    const int64_t i = (int64_t)(c * 256 + tid) * 4;
-    const bool live = i < d;
-    const float4 ww = live ? *reinterpret_cast<const float4*>(w + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 s4 = live && sc ? *reinterpret_cast<const float4*>(sc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 h4 = live && sh ? *reinterpret_cast<const float4*>(sh + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float wv[4] = {ww.x, ww.y, ww.z, ww.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w}, hv[4] = {h4.x, h4.y, h4.z, h4.w};
+    const int i = (c * NT + tid) * 8;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      wo[c][j] = offset + wv[j];
-      g1[c][j] = 1.f + sv[j];
-      sf[c][j] = hv[j];
+    for (int h = 0; h < 2; h++) {
+      const bool live = i < dd;
+      const float4 ww = live ? *reinterpret_cast<const float4*>(w + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 s4 = live && sc ? *reinterpret_cast<const float4*>(sc + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 h4 = live && sh ? *reinterpret_cast<const float4*>(sh + i + 4 * h) : make_float4(0.f, 0.f, 0.f, 0.f);
+      mw[c][2 * h] = make_float2((offset + ww.x) * (1.f + s4.x), (offset + ww.y) * (1.f + s4.y));
+      mw[c][2 * h + 1] = make_float2((offset + ww.z) * (1.f + s4.z), (offset + ww.w) * (1.f + s4.w));
+      sf[c][2 * h] = make_float2(h4.x, h4.y);
+      sf[c][2 * h + 1] = make_float2(h4.z, h4.w);
     }
   }
-  // software-pipelined over rows: the next row's chunks are loaded (raw words) while this row is reduced and stored
-  using Raw = typename std::conditional<DT == WE_F32, float4, uint2>::type;
-  Raw nx[CH];
-  auto fetch = [&](int64_t row) {
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+  auto issue = [&](int64_t row, int s) {  // this thread's chunks of `row` into stage s (an empty group past the end)
+    if (row < rows) {
+      const uint8_t* xr = static_cast<const uint8_t*>(x) + row * d * ES;
 #pragma unroll
-    for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i < d && row < rows) {
-        if constexpr (DT == WE_F32) nx[c] = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + row * d + i);
-        else nx[c] = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + row * d + i);
+      for (int c = 0; c < CH; c++) {
+        const int i = (c * NT + tid) * 8;
+        if (i >= dd) continue;
+        const uint32_t xa = ring_s + s * XSTAGE + (c * NT + tid) * XB;
+#pragma unroll
+        for (int q = 0; q < XB / 16; q++) cp_async16(xa + 16 * q, xr + i * ES + 16 * q);
       }
     }
+    cp_async_commit();
   };
-  fetch(blockIdx.x);
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[CH][4];
-    float ss = 0.f;
+  const int64_t G = gridDim.x;
+  int64_t row = blockIdx.x;
+#pragma unroll
+  for (int s = 0; s < S - 1; s++) issue(row + s * G, s);
+  int s = 0, sn = S - 1;  // stage of this row, stage the next issue fills (the one read one row ago)
+  for (; row < rows; row += G) {
+    issue(row + (S - 1) * G, sn);
+    cp_async_wait<S - 1>();  // this row's group has landed
+    float2 v[CH][4];
+    float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < CH; c++) {
+      const int i = (c * NT + tid) * 8;
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[c][j] = make_float2(0.f, 0.f);
+      if (i >= dd) continue;
+      const uint8_t* xs = ring + s * XSTAGE + (c * NT + tid) * XB;
       if constexpr (DT == WE_F32) {
-        v[c][0] = nx[c].x; v[c][1] = nx[c].y; v[c][2] = nx[c].z; v[c][3] = nx[c].w;
+        const float4 a = *reinterpret_cast<const float4*>(xs), b = *reinterpret_cast<const float4*>(xs + 16);
+        v[c][0] = make_float2(a.x, a.y); v[c][1] = make_float2(a.z, a.w);
+        v[c][2] = make_float2(b.x, b.y); v[c][3] = make_float2(b.z, b.w);
       } else {
-        v[c][0] = __uint_as_float(nx[c].x << 16); v[c][1] = __uint_as_float(nx[c].x & 0xffff0000u);
-        v[c][2] = __uint_as_float(nx[c].y << 16); v[c][3] = __uint_as_float(nx[c].y & 0xffff0000u);
-      }
-    }
-    fetch(row + gridDim.x);
+        const uint4 a = *reinterpret_cast<const uint4*>(xs);
+        const uint32_t u[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-    for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i < d) {
-        ss = fmaf(v[c][0], v[c][0], fmaf(v[c][1], v[c][1], ss));
-        ss = fmaf(v[c][2], v[c][2], fmaf(v[c][3], v[c][3], ss));
+        for (int j = 0; j < 4; j++) v[c][j] = make_float2(__uint_as_float(u[j] << 16), __uint_as_float(u[j] & 0xffff0000u));
       }
+#pragma unroll
+      for (int j = 0; j < 4; j++) ss2 = __ffma2_rn(v[c][j], v[c][j], ss2);
     }
-    ss = warp_sum(ss);
+    s = s + 1 == S ? 0 : s + 1;
+    sn = sn + 1 == S ? 0 : sn + 1;
+    const float ss = warp_sum(ss2.x + ss2.y);
     if (lane == 0) red[wp] = ss;
     __syncthreads();
-    const float inv = rsqrtf((((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]))) /
-                                 (float)d + eps);
+    float tot = red[0];
+#pragma unroll
+    for (int k = 1; k < NW; k++) tot += red[k];
+    const float inv = rsqrtf(tot / (float)dd + eps);
     __syncthreads();  // red is rewritten by the next row
+    const float2 inv2 = make_float2(inv, inv);
+    uint8_t* const orow = static_cast<uint8_t*>(out) + row * d * (OT == WE_F32 ? 4 : 2);
 #pragma unroll
     for (int c = 0; c < CH; c++) {
-      const int64_t i = (int64_t)(c * 256 + tid) * 4;
-      if (i >= d) continue;
-      float y[4];
+      const int i = (c * NT + tid) * 8;
+      if (i >= dd) continue;
+      float2 y[4];
 #pragma unroll
-      for (int j = 0; j < 4; j++) y[j] = v[c][j] * inv * wo[c][j] * g1[c][j] + sf[c][j];  // rmsnorm.ts:42-46 order
+      for (int j = 0; j < 4; j++) y[j] = __ffma2_rn(__fmul2_rn(v[c][j], inv2), mw[c][j], sf[c][j]);
       if constexpr (OT == WE_F32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(out) + row * d + i) = make_float4(y[0], y[1], y[2], y[3]);
+        *reinterpret_cast<float4*>(orow + i * 4) = make_float4(y[0].x, y[0].y, y[1].x, y[1].y);
+        *reinterpret_cast<float4*>(orow + i * 4 + 16) = make_float4(y[2].x, y[2].y, y[3].x, y[3].y);
       } else {
-        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + row * d + i) =
-            make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+        *reinterpret_cast<uint4*>(orow + i * 2) = make_uint4(pack_bf16x2(y[0].x, y[0].y), pack_bf16x2(y[1].x, y[1].y),
+                                                             pack_bf16x2(y[2].x, y[2].y), pack_bf16x2(y[3].x, y[3].y));
       }
     }
   }
+  cp_async_wait<0>();  // nothing is left in flight (every row issued was consumed); kept as the exit rule
 }
 
 // q/k norm + RoPE for 128-wide heads (NORM false: RoPE alone): 16 lanes per head row, 8 values (16 bytes of
@@ -258,6 +287,8 @@ __global__ void __launch_bounds__(256, TOK ? 3 : 2) qknorm_rope128_kernel(const 
                                                              const float* __restrict__ sn, int64_t tokens,
                                                              int64_t heads, void* __restrict__ out) {
   constexpr int D = 128, P = 64, R = 4;
+  pdl_wait();  // launched by launch_pdl: the previous kernel's outputs (q or k) are complete
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4;
   const int64_t rows = tokens * heads;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -456,20 +487,27 @@ static int capped(int64_t want, int sms, int per_sm) {
 template <int DT, int OT>
 static void rmsnorm_dispatch(const void* x, const float* w, const float* sc, const float* sh, int64_t rows, int64_t d,
                              float eps, float offset, void* out, bool vec, int sms, cudaStream_t st) {
-  if (vec && d >= 2048 && d % 4 == 0 && d <= 8192) {  // CTA per row, weights held across rows
-    const int64_t ch = (d / 4 + 255) / 256;
-#define WE_RNR(CH)                                                                                  \
-  {                                                                                                 \
-    auto kern = rmsnorm_row_kernel<DT, OT, CH>;                                                     \
-    kern<<<resident_grid(kern, 256, sms, rows), 256, 0, st>>>(x, w, sc, sh, rows, d, eps, offset, out); \
+  if (vec && d >= 2048 && d % 8 == 0 && d <= 8192) {  // CTA per row, modulation held across rows
+    // 2 chunks of 8 a thread on 128 or 192 threads up to d = 3072 (six warps measured 7 % faster there than four
+    // warps with 3 chunks each), else 256 threads x up to 4; a ring of as many stages (2..4) as fit in 36 KB
+    // (deeper rings measured slower: the first row of every CTA waits behind all the others)
+#define WE_RNR(NT, CH)                                                                                        \
+  {                                                                                                           \
+    constexpr size_t per = (size_t)CH * NT * 8 * (DT == WE_F32 ? 4 : 2);                                      \
+    constexpr int S = 36 * 1024 / per < 2 ? 2 : 36 * 1024 / per > 4 ? 4 : (int)(36 * 1024 / per);            \
+    auto kern = rmsnorm_row_kernel<DT, OT, NT, CH, S>;                                                        \
+    /* the ring plus the static reduction can pass the 48 KB a launch gets without this opt-in */             \
+    (void)cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(per * S));           \
+    (void)launch_pdl(kern, resident_grid(kern, NT, sms, rows, per * S), NT, per * S, st, x, w, sc, sh, rows, d, eps, \
+                     offset, out);                                                                            \
+    return;                                                                                                   \
   }
-    if (ch <= 2) WE_RNR(2)
-    else if (ch <= 3) WE_RNR(3)
-    else if (ch <= 4) WE_RNR(4)
-    else if (ch <= 6) WE_RNR(6)
-    else WE_RNR(8)
+    const int64_t chunks = d / 8;
+    if (chunks <= 128 * 2) WE_RNR(128, 2)
+    if (chunks <= 192 * 2) WE_RNR(192, 2)
+    if (chunks <= 256 * 3) WE_RNR(256, 3)
+    WE_RNR(256, 4)
 #undef WE_RNR
-    return;
   }
   if constexpr (DT == WE_BF16) {
     if (vec && d <= 256 * 24) {
@@ -521,8 +559,8 @@ static void launch_qk128(const void* x, const float* w, float eps, float offset,
 #define WE_QK(PAIR, TOK)                                                                                       \
   {                                                                                                            \
     auto kern = qknorm_rope128_kernel<DT, OT, PAIR, NORM, TOK>;                                                \
-    kern<<<resident_grid(kern, 256, sms, (groups + 7) / 8), 256, 0, st>>>(x, w, eps, offset, cs, sn, tokens,   \
-                                                                          heads, out);                          \
+    (void)launch_pdl(kern, resident_grid(kern, 256, sms, (groups + 7) / 8), 256, 0, st, x, w, eps, offset, cs, sn, \
+                     tokens, heads, out);                                                                      \
   }
   const bool tok = tok_ok && heads % 8 == 0;
   if (pairing == WE_ROPE_INTERLEAVED) {

@@ -320,12 +320,34 @@ __global__ void __launch_bounds__(128, 6) quant_act_warp_kernel(const uint16_t* 
 // keeps the row's 16-byte chunks t, t + 256, ... in registers (few registers: many rows in flight per SM); the
 // row max is a warp shuffle then a shared-memory reduction over the 8 warps. PF: the next row's chunks are
 // loaded while this row is split (pays for short rows; at 6+ chunks the doubled registers cost more than it gains).
+// 8 scaled values -> their e4m3 hi (and lo = e4m3(s - hi)) terms, 8 bytes per term
+template <int TERMS>
+__device__ __forceinline__ void split_store8(const float2 (&s)[4], uint8_t* hi, uint8_t* lo) {
+  uint32_t h[2], l[2];
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const uint16_t h0 = f32x2_to_e4m3x2(s[2 * j].x, s[2 * j].y);
+    const uint16_t h1 = f32x2_to_e4m3x2(s[2 * j + 1].x, s[2 * j + 1].y);
+    h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+    if (TERMS > 1) {
+      const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
+      const float2 r0 = __fadd2_rn(s[2 * j], make_float2(-d0.x, -d0.y));
+      const float2 r1 = __fadd2_rn(s[2 * j + 1], make_float2(-d1.x, -d1.y));
+      l[j] = (uint32_t)f32x2_to_e4m3x2(r0.x, r0.y) | ((uint32_t)f32x2_to_e4m3x2(r1.x, r1.y) << 16);
+    }
+  }
+  *reinterpret_cast<uint2*>(hi) = make_uint2(h[0], h[1]);
+  if (TERMS > 1) *reinterpret_cast<uint2*>(lo) = make_uint2(l[0], l[1]);
+}
+
 template <int TERMS, int CH, int NT = 256, bool PF = false>
 __global__ void __launch_bounds__(NT) quant_act_row_kernel(const uint16_t* __restrict__ x, int64_t m, int64_t k,
                                                            int64_t stride, uint8_t* __restrict__ hi,
                                                            uint8_t* __restrict__ lo, float* __restrict__ row_scale) {
   constexpr int NW = NT / 32;
   __shared__ float red[8];
+  pdl_wait();  // launched by launch_pdl: the previous kernel's output (x) is complete
+  pdl_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
   uint4 nv[CH];
   auto fetch = [&](int64_t row) {
@@ -362,33 +384,33 @@ __global__ void __launch_bounds__(NT) quant_act_row_kernel(const uint16_t* __res
     const int e = act_exponent(amax);
     if (tid == 0) row_scale[row] = ldexpf(1.0f, e);
     const float mul = pow2_neg(e);  // exact: scaling by a power of two
+    // The multiplier is uniform over the row: one branch per row, and in the usual case (2^-e a normal float) the
+    // values are scaled two at a time by packed multiplies; ldexpf only for rows whose scale is outside that range.
+    if (mul != 0.f) {
+      const float2 mul2 = make_float2(mul, mul);
 #pragma unroll
-    for (int c = 0; c < CH; c++) {
-      const int64_t t = (int64_t)(c * NT + tid) * 8;
-      if (t >= k) continue;
-      const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-      float s[8];
+      for (int c = 0; c < CH; c++) {
+        const int64_t t = (int64_t)(c * NT + tid) * 8;
+        if (t >= k) continue;
+        const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+        float2 s[4];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
-        s[2 * j] = mul != 0.f ? a * mul : ldexpf(a, -e);
-        s[2 * j + 1] = mul != 0.f ? b * mul : ldexpf(b, -e);
+        for (int j = 0; j < 4; j++)
+          s[j] = __fmul2_rn(make_float2(__uint_as_float(u[j] << 16), __uint_as_float(u[j] & 0xffff0000u)), mul2);
+        split_store8<TERMS>(s, hi + row * k + t, lo + row * k + t);
       }
-      uint32_t h[2], l[2];
+    } else {
 #pragma unroll
-      for (int j = 0; j < 2; j++) {
-        const uint16_t h0 = f32x2_to_e4m3x2(s[4 * j], s[4 * j + 1]);
-        const uint16_t h1 = f32x2_to_e4m3x2(s[4 * j + 2], s[4 * j + 3]);
-        h[j] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        if (TERMS > 1) {
-          const float2 d0 = e4m3x2_to_f32x2(h0), d1 = e4m3x2_to_f32x2(h1);
-          const uint16_t l0 = f32x2_to_e4m3x2(s[4 * j] - d0.x, s[4 * j + 1] - d0.y);
-          const uint16_t l1 = f32x2_to_e4m3x2(s[4 * j + 2] - d1.x, s[4 * j + 3] - d1.y);
-          l[j] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-        }
+      for (int c = 0; c < CH; c++) {
+        const int64_t t = (int64_t)(c * NT + tid) * 8;
+        if (t >= k) continue;
+        const uint32_t u[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+        float2 s[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          s[j] = make_float2(ldexpf(__uint_as_float(u[j] << 16), -e), ldexpf(__uint_as_float(u[j] & 0xffff0000u), -e));
+        split_store8<TERMS>(s, hi + row * k + t, lo + row * k + t);
       }
-      *reinterpret_cast<uint2*>(hi + row * k + t) = make_uint2(h[0], h[1]);
-      if (TERMS > 1) *reinterpret_cast<uint2*>(lo + row * k + t) = make_uint2(l[0], l[1]);
     }
   }
 }
@@ -402,7 +424,7 @@ static bool quant_act_row(const uint16_t* x, int64_t m, int64_t k, int64_t strid
     constexpr bool pf = NT == 128;                                                                       \
     auto kern = quant_act_row_kernel<TERMS, CH, NT, pf>;                                                 \
     const int g = pf ? resident_grid(kern, NT, sms, m) : (int)std::min<int64_t>(m, (int64_t)sms * 8);    \
-    kern<<<g, NT, 0, st>>>(x, m, k, stride, hi, lo, rs);                                                 \
+    (void)launch_pdl(kern, g, NT, 0, st, x, m, k, stride, hi, lo, rs);                                   \
   }
   if (k <= 128 * 8 * 4) {  // up to 4096 values: 128 threads, every thread busy at k = 3072
     const int64_t ch = (k / 8 + 127) / 128;
