@@ -209,10 +209,10 @@ static inline bool pdl_enabled() {
 }
 
 template <typename... KArgs, typename... Args>
-static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem,
                                      cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -222,6 +222,12 @@ static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, un
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// the programmatic-serialization attribute for a launch that sets its own other attributes
+static inline void pdl_attribute(cudaLaunchAttribute& a) {
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
 }
 
 // ---- cp.async: a thread's own global -> shared copies, in flight without holding registers ----

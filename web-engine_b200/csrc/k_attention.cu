@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(fa2::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // launched by launch_pdl: q, k and v are complete before any global access
 
   if (warp == 0) {
     if (lane == 0) {
@@ -510,6 +511,8 @@ template <int OT>
 __global__ void __launch_bounds__(256) flash_combine_kernel(const float* __restrict__ part_o,
                                                             const float* __restrict__ part_ml, int splits,
                                                             int64_t rows, void* __restrict__ out) {
+  pdl_wait();  // launched by launch_pdl: the splits' partial rows are complete (every CTA waits, even an idle one)
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -617,16 +620,15 @@ cudaError_t launch_flash_attention(const AttnArgs& a, int splits, void* scratch,
   cudaError_t e = cudaFuncSetAttribute(flash_attn2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa2::ALLOC);
   if (e != cudaSuccess) return e;
   dim3 grid(blocks, (unsigned)a.heads, (unsigned)splits);
-  flash_attn2_kernel<<<grid, fa2::THREADS, fa2::ALLOC, st>>>(mq, mk, mv, p);
-  e = cudaGetLastError();
+  e = launch_pdl(flash_attn2_kernel, grid, fa2::THREADS, fa2::ALLOC, st, mq, mk, mv, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess || splits == 1) return e;
   const int64_t rows = a.tokens * a.heads;
   const unsigned cb = (unsigned)((rows + 7) / 8);
-  if (a.out_dtype == WE_BF16)
-    flash_combine_kernel<WE_BF16><<<cb, 256, 0, st>>>(p.part_o, p.part_ml, splits, rows, a.out);
-  else
-    flash_combine_kernel<WE_F32><<<cb, 256, 0, st>>>(p.part_o, p.part_ml, splits, rows, a.out);
-  return cudaGetLastError();
+  e = a.out_dtype == WE_BF16
+          ? launch_pdl(flash_combine_kernel<WE_BF16>, dim3(cb), 256, 0, st, p.part_o, p.part_ml, splits, rows, a.out)
+          : launch_pdl(flash_combine_kernel<WE_F32>, dim3(cb), 256, 0, st, p.part_o, p.part_ml, splits, rows, a.out);
+  return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 cudaError_t launch_attention_simt(const AttnArgs& a, int sms, cudaStream_t st) {

@@ -356,6 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // launched by launch_pdl: the previous kernel's outputs are complete before any global access
 
   const int64_t tiles_n = (p.n + BM - 1) / BM;
   const int64_t tiles_m = (p.m + BT - 1) / BT;
@@ -581,6 +582,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   cluster_sync_all();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // launched by launch_pdl: the previous kernel's outputs are complete before any global access
 
   const int64_t tiles_n = (p.n + 2 * BM - 1) / (2 * BM);  // pair tiles of 256 weight rows
   const int64_t tiles_m = (p.m + BT - 1) / BT;
@@ -852,6 +854,7 @@ __global__ void __launch_bounds__(192 + 32 * CW, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // launched by launch_pdl: the previous kernel's outputs are complete before any global access
 
   const int64_t tiles_n = (p.n + BM - 1) / BM;
   const int64_t tiles_m = (p.m + BT - 1) / BT;
@@ -1108,8 +1111,8 @@ static cudaError_t run(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int64_t tiles = ((a.n + BM - 1) / BM) * ((a.m + BT - 1) / BT);
   const int grid = (int)(tiles < sms ? tiles : sms);
-  kern<<<grid, THREADS, L::ALLOC, st>>>(mw, mx0, mx1, mw2, p);
-  return cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), THREADS, L::ALLOC, st, mw, mx0, mx1, mw2, p);
+  return e == cudaSuccess ? cudaGetLastError() : e;
 }
 
 
@@ -1131,16 +1134,17 @@ static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  pdl_attribute(attr[1]);  // the kernel waits (griddepcontrol.wait) before its first global access
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // the occupancy query below sees the cluster shape only
   const int64_t tiles = ((a.n + 2 * BM - 1) / (2 * BM)) * ((a.m + BT - 1) / BT);
   int clusters = sms / 2;
   cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
@@ -1150,6 +1154,7 @@ static cudaError_t run_pair(const TcGemmArgs& a, int sms, cudaStream_t st) {
     clusters = max_clusters;
   if (tiles < clusters) clusters = (int)tiles;
   cfg.gridDim = dim3((unsigned)(2 * clusters), 1, 1);
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, mw, mx0, mx1, mw2, p);
   return e == cudaSuccess ? cudaGetLastError() : e;
 }
@@ -1165,8 +1170,8 @@ static cudaError_t run_i4(const TcGemmArgs& a, int sms, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   const int64_t tiles = ((a.n + BM - 1) / BM) * ((a.m + BT - 1) / BT);
   const int grid = (int)(tiles < sms ? tiles : sms);
-  kern<<<grid, 192 + 32 * CW, L::ALLOC, st>>>(mx0, p);
-  return cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), 192 + 32 * CW, L::ALLOC, st, mx0, p);
+  return e == cudaSuccess ? cudaGetLastError() : e;
 }
 }  // namespace tc
 
