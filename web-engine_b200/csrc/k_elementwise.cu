@@ -106,7 +106,7 @@ __device__ __forceinline__ void split_store8(const float2 (&s)[4], uint8_t* hi, 
 // RES: the row is x + r (f32 residual plus f32 update), written to xo before it is normalised (the residual add of a
 // block, fused with the next RMSNorm and split); both inputs are staged.
 template <int DT, int TERMS, int NT, int CH, int S, bool RES = false>
-__global__ void __launch_bounds__(NT, 512 / NT) norm_split_row_kernel(
+__global__ void __launch_bounds__(NT, NT == 192 ? 4 : 512 / NT) norm_split_row_kernel(
     const void* __restrict__ x, const float* __restrict__ w, const float* __restrict__ sc,
     const float* __restrict__ sh, int64_t rows, int64_t d, float eps, float offset, uint8_t* __restrict__ hi,
     uint8_t* __restrict__ lo, float* __restrict__ row_scale, const float* __restrict__ r = nullptr,
@@ -258,34 +258,34 @@ __global__ void __launch_bounds__(NT, 512 / NT) norm_split_row_kernel(
   cp_async_wait<0>();  // nothing is left in flight (every row issued was consumed); kept as the exit rule
 }
 
-// The ring of the row kernel: as many stages (2..4) of one row as fit in 36 KB (72 KB with the residual's rows too),
-// two or three rows in flight per CTA. Deeper rings measured slower: every CTA requests most of its rows at once
-// and the first row of each waits behind all of them.
+// Bytes of one stage of the row ring: a row of x (and of r).
 template <int DT, bool RES, int NT, int CH>
 constexpr size_t norm_ring_stage_bytes() {
   return (size_t)CH * NT * (8 * (DT == WE_F32 ? 4 : 2) + (RES ? 32 : 0));
 }
-template <int DT, bool RES, int NT, int CH>
-constexpr int norm_ring_stages() {
-  constexpr size_t n = (RES ? 72 * 1024 : 36 * 1024) / norm_ring_stage_bytes<DT, RES, NT, CH>();
-  return n < 2 ? 2 : n > 4 ? 4 : (int)n;
-}
 
+// Ring depth and grid, measured at 4608 x 3072 on B200 over thread shapes, ring depths and CTAs per SM: two stages
+// (one row ahead) beat three or four in every form; the plain form runs best with every resident CTA (192 threads:
+// 17.5 us, 0.76 of measured HBM for f32 rows), the residual form with two CTAs per SM (36.5 us, 0.85; three or four
+// per SM 39-45 us). The thread shape sets the order of the sum of squares, so both forms share it and stay
+// bit-identical; the ring depth and grid do not change the arithmetic.
 template <int DT, int TERMS, int NT, int CH, bool RES>
 static cudaError_t launch_norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
                                          int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs,
                                          const float* r, float* xo, int sms, cudaStream_t st) {
-  constexpr int S = norm_ring_stages<DT, RES, NT, CH>();
+  constexpr int S = 2;
   constexpr size_t smem = S * norm_ring_stage_bytes<DT, RES, NT, CH>();
   auto k = norm_split_row_kernel<DT, TERMS, NT, CH, S, RES>;
   // the ring plus the kernel's static reductions can pass the 48 KB a launch gets without this opt-in
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(k, resident_grid(k, NT, sms, rows, smem), NT, smem, st, x, w, sc, sh, rows, d, eps, offset, hi, lo,
-                    rs, r, xo);
+  unsigned grid = resident_grid(k, NT, sms, rows, smem);
+  if (RES && grid > 2u * (unsigned)sms) grid = 2u * (unsigned)sms;
+  return launch_pdl(k, dim3(grid), NT, smem, st, x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo);
 }
 
-// d % 8 == 0, d <= 8192: 128 threads x up to 3 chunks (d <= 3072), else 256 threads x up to 4
+// d % 8 == 0, d <= 8192: 2 chunks of 8 a thread on 128 or 192 threads up to d = 3072 (six warps measured faster at
+// d = 3072 than four warps with 3 chunks each, or twelve with one), else 256 threads x up to 4
 template <int DT, int TERMS, bool RES>
 static cudaError_t norm_split_row(const void* x, const float* w, const float* sc, const float* sh, int64_t rows,
                                   int64_t d, float eps, float offset, uint8_t* hi, uint8_t* lo, float* rs,
@@ -294,8 +294,7 @@ static cudaError_t norm_split_row(const void* x, const float* w, const float* sc
 #define WE_NS(NT, CH) \
   return launch_norm_split_row<DT, TERMS, NT, CH, RES>(x, w, sc, sh, rows, d, eps, offset, hi, lo, rs, r, xo, sms, st)
   if (chunks <= 128 * 2) WE_NS(128, 2);
-  if (chunks <= 128 * 3) WE_NS(128, 3);
-  if (chunks <= 256 * 2) WE_NS(256, 2);
+  if (chunks <= 192 * 2) WE_NS(192, 2);
   if (chunks <= 256 * 3) WE_NS(256, 3);
   if (chunks <= 256 * 4) WE_NS(256, 4);
 #undef WE_NS
