@@ -441,6 +441,28 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
     return out
 
 
+def numa_local_cpus(torch, local: int) -> dict:
+    """Bind this process to the CPUs of its GPU's NUMA node (sysfs local_cpulist of the GPU's PCI function), so that
+    the pinned host buffers it allocates afterwards (first touch) sit in that node's memory and its DMA does not
+    cross sockets. Returns what was done, for the bench line."""
+    try:
+        p = torch.cuda.get_device_properties(local)
+        dev = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        base = f"/sys/bus/pci/devices/{dev}"
+        node = int(open(f"{base}/numa_node").read().strip())
+        cpus = set()
+        for part in open(f"{base}/local_cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return {"numa_node": node, "bound": False, "why": "no allowed CPU on the GPU's node", "pci": dev}
+        os.sched_setaffinity(0, cpus)
+        return {"numa_node": node, "bound": True, "cpus": len(cpus), "pci": dev}
+    except Exception as exc:  # noqa: BLE001 - a host without the sysfs entries keeps its affinity
+        return {"bound": False, "why": f"{type(exc).__name__}: {exc}"[:120]}
+
+
 def config_dict(args) -> dict:
     return {"workload": "config 2: dequant-GEMM M=4608 K=3072 N=12288, bf16 activations ~N(0,1), fp8 e4m3 weights "
                         "~N(0,0.02) with per-output-channel absmax scales, exact two-term e4m3 activation split",
@@ -477,7 +499,10 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
+    # Several ranks on one host share its memory and PCIe root complexes: each binds to its GPU's NUMA node before
+    # it allocates pinned buffers (one rank keeps every core, for the CPU baseline).
     torch.cuda.set_device(local)
+    numa = numa_local_cpus(torch, local) if world > 1 else {"bound": False, "why": "one rank"}
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -899,6 +924,10 @@ def main() -> None:
     serial_ms = timed(step_serial, max(3, args.steps // 2), 2) / max(3, args.steps // 2)
     e2e["serial_ms_per_step"] = serial_ms
     e2e["pcie_gbs_estimate"] = (M * K * 2 + M * N * 2) / (serial_ms - ms) / 1e6 if serial_ms > ms else None
+    # host traffic of the end-to-end step: per rank, and for all ranks together (the slowest rank's time)
+    e2e["host_gbs_per_rank"] = (M * K * 2 + M * N * 2) / (e2e_ms * 1e-3) / 1e9
+    e2e["host_gbs_all_ranks"] = world * e2e["host_gbs_per_rank"]
+    e2e["numa"] = numa
 
     line = None
     if rank == 0:
