@@ -357,6 +357,16 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
 
         sp_graph_ms = timed(step_sp_graph, sp_steps, 2) / sp_steps
         sgr_sp.destroy()
+        # the same with the q/k/v scatter fused into its producers' stores (no copy kernel after them)
+        sp_fused = we.sequence.SequenceParallel(comm, fused=True)
+        sgr_fu = T.StepGraph(g, model, scfg, side, side, text_tokens, dtype="bf16", sp=sp_fused)
+
+        def step_fused_graph():
+            T.transformer(g, model, scfg, inp, dtype="bf16", velocity=vel, sp=sp_fused, captured=sgr_fu)
+
+        sp_fused_graph_ms = timed(step_fused_graph, sp_steps, 2) / sp_steps
+        sgr_fu.destroy()
+        sp_fused.destroy()
         sp.destroy()
         sp_nccl.destroy()
         # the same image split by tensor parallelism: every block's linears sharded over the ranks (N / K splits),
@@ -374,12 +384,16 @@ def bench_model(we, g, torch, dev, gen, timed, interleaved, steps: int, bf16_pea
         out["step_config4_sequence_parallel"] = {
             "ms": sp_ms, "median_ms_this_rank": per[len(per) // 2], "steps": sp_steps, "n_gpus": world,
             "one_gpu_ms": st_ms, "tflops": sf["total"] / (sp_ms * 1e-3) / 1e12, "launches_per_step": sp_launches,
-            "graph_ms": sp_graph_ms, "nccl_all_to_all_ms": nccl_ms, "clocks": sp_clocks.summary(),
+            "graph_ms": sp_graph_ms, "graph_ms_fused_exchange": sp_fused_graph_ms, "nccl_all_to_all_ms": nccl_ms,
+            "clocks": sp_clocks.summary(),
             "tensor_parallel_ms": tp_ms, "tensor_parallel_clocks": tp_clocks.summary(),
             "note": "one 1024x1024 image's step over all GPUs: every rank runs the blocks on 4608 / n_gpus rows; "
                     "q/k/v go to the ranks attending their heads and o comes back through the peer-memory exchange "
                     "kernel (IPC-mapped HBM of every GPU, one kernel per exchange with a flag barrier); graph_ms: this "
-                    "rank's blocks replayed from a CUDA graph; nccl_all_to_all_ms: the same step with NCCL "
+                    "rank's blocks replayed from a CUDA graph; graph_ms_fused_exchange: the same with q/k/v stored "
+                    "into the attending ranks' memory by the kernels that produce them (the q/k/v GEMM's epilogue "
+                    "for v, q/k norm + RoPE for q and k) and a flag barrier instead of the copy; "
+                    "nccl_all_to_all_ms: the same step with NCCL "
                     "all-to-all (we_all_to_all); tensor_parallel_ms: the same image by tensor parallelism (eager): "
                     "q/k/v and MLP up split over the ranks' heads and columns, wo and MLP down over K, the split "
                     "activations all-gathered and the f32 partial sums reduce-scattered (NCCL through the C ABI)"}

@@ -85,6 +85,9 @@ size_t we_mark(we_ctx* ctx);
 int we_release(we_ctx* ctx, size_t mark, void* const* keep, size_t nkeep);
 /* Graph.free (graph.ts:135-139): frees one buffer made by we_buffer. */
 int we_free(we_ctx* ctx, void* buf);
+/* the largest group of ranks that share memory (peer exchange, peer outputs) */
+#define WE_PEER_MAX 8
+
 /* Graph.stats (graph.ts:33): buffers created vs taken from the pool, bytes created; plus the number of
    kernels this context launched, and how many matmuls ran on the tcgen05 and CUDA-core kernels. */
 typedef struct {
@@ -176,6 +179,19 @@ typedef struct {
   int32_t nseg;
   int64_t row_end[WE_GEMM_MAX_SEGMENTS];
   int32_t row_set[WE_GEMM_MAX_SEGMENTS];
+  /* Peer output (peer_world > 0; no counterpart in the reference, which runs on one GPU): the channels of part
+     peer_part (of the whole output without a split; that part's y_parts entry is then not used) are heads of 128,
+     and head h goes straight into the memory of rank o = h / hl, hl = the part's width / (128 peer_world): row r
+     of this GEMM to peer_dst[o] + ((peer_row0 + r) hl + h % hl) 128 values, i.e. rank o's [every rank's tokens,
+     hl heads, 128] block (sequence parallelism: the GEMM's epilogue does the head scatter over NVLink, tile by
+     tile, while the other tiles are computed). bf16 y, no aux operand, no WE_MM_ACCUMULATE, the part's width a
+     multiple of 128 peer_world and its first channel of 128, peer_dst[0 .. peer_world) 16-byte aligned (from
+     we_peer_remote). The stores are fenced at system scope; a flag barrier after the kernel (we_peer_exchange with
+     no copies) makes them visible to the other ranks. */
+  void* peer_dst[WE_PEER_MAX];
+  int32_t peer_world;
+  int32_t peer_part;
+  int64_t peer_row0;
 } we_gemm_fp8_desc;
 int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* desc);
 /* kSplitFor (src/model/ops.ts:42-45). */
@@ -242,6 +258,16 @@ int we_rope_apply(we_ctx* ctx, const void* x, int32_t x_dtype, const float* cos,
 int we_qknorm_rope(we_ctx* ctx, const void* x, int32_t x_dtype, const float* weight, float eps, float offset,
                    const float* cos, const float* sin, int64_t tokens, int64_t heads, int64_t pairs,
                    int32_t pairing, void* out, int32_t out_dtype);
+/* we_qknorm_rope for sequence parallelism, with the head scatter done by the kernel's own stores (no reference
+   counterpart: the reference runs on one GPU). x: this rank's bf16 rows [tokens, heads, 128] (interleaved or half
+   pairing); the normalised, rotated bf16 row of (token t, head h) is written straight into the memory of the rank
+   that attends head h, o = h / (heads / world), at dst[o] + ((dst_row0 + t) (heads / world) + h % (heads / world))
+   128 values: dst[r] is rank r's q (or k) block in its exchange region (we_peer_remote + offset), laid out
+   [world x tokens, heads / world, 128]. The stores are fenced at system scope; a flag barrier after the kernel
+   (we_peer_exchange with no copies) makes them visible to the other ranks. */
+int we_qknorm_rope_peers(we_ctx* ctx, const void* x, const float* weight, float eps, float offset, const float* cos,
+                         const float* sin, int64_t tokens, int64_t heads, int32_t pairing, void* const* dst,
+                         int32_t world, int64_t dst_row0);
 /* ropeTables (src/kernels/rope.ts:20-36) on the host in float64: pos [tokens, naxes], axes (even),
    cos/sin [tokens, pairs] f32. Returns pairs, or -1 ("Every RoPE axis needs an even number of dims"). */
 int64_t we_rope_tables(const int64_t* pos, int64_t tokens, int32_t naxes, const int64_t* axes, double theta,
@@ -377,7 +403,6 @@ int we_streamer_destroy(we_streamer* s);
    timeout_ns (0: 2 s); on timeout the kernel sets the context's device error word (we_device_error) and returns.
    Sources, chunks and strides must be multiples of 16 bytes; a copy may not run past the region. The kernel
    can be captured in a CUDA graph (its epoch lives on the device). */
-#define WE_PEER_MAX 8
 #define WE_PEER_HANDLE_BYTES 128
 typedef struct we_peer we_peer;
 typedef struct {
@@ -391,6 +416,10 @@ int we_peer_create(we_ctx* ctx, int32_t rank, int32_t world, size_t bytes, we_pe
 int we_peer_export(const we_peer* peer, void* handle);
 int we_peer_open(we_peer* peer, const void* handles);
 void* we_peer_region(const we_peer* peer);
+/* Rank `rank`'s exchange region as this process maps it (its own region for rank == this rank; NULL before
+   we_peer_open or for a rank outside the group): the destination of kernels that store straight into a peer's
+   region (we_qknorm_rope_peers, the peer output of we_gemm_fp8). */
+void* we_peer_remote(const we_peer* peer, int32_t rank);
 int we_peer_exchange(we_ctx* ctx, we_peer* peer, const we_peer_copy* copies, int32_t ncopies, uint64_t timeout_ns);
 int we_peer_destroy(we_peer* peer);
 

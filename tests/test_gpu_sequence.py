@@ -1,7 +1,9 @@
 """Sequence parallelism of one image's step on 2, 4 or 8 GPUs (one process each): every rank runs the blocks on
-its share of the rows, attention exchanges heads all-to-all, through the peer-memory exchange kernel
-(we_peer_exchange) or NCCL (we_all_to_all), both on the library's communicator (comm.Comm); the velocity must equal
-the one-GPU step's. 80 tokens (8 text + 72 image), so rank 0's shard holds text and image rows and the others
+its share of the rows, attention exchanges heads all-to-all, through peer memory or NCCL (we_all_to_all), both on the
+library's communicator (comm.Comm); the velocity must equal the one-GPU step's. Peer memory in two forms: "fused",
+the kernels that produce q, k and v store them straight into the attending ranks' regions (the q/k/v GEMM's epilogue
+for v, we_qknorm_rope_peers for q and k) and a flag barrier follows; "copy", one exchange kernel copies them after
+their producers (we_peer_exchange). 80 tokens (8 text + 72 image), so rank 0's shard holds text and image rows and the others
 image rows only. The peer case also checks the exchange itself bit for bit: scattering each rank's q rows and
 gathering them back through an identity "attention" returns them unchanged, and every rank receives exactly its
 heads of every rank's rows. Skipped when fewer GPUs are visible. NVLS is off (NCCL_NVLS_ENABLE=0)."""
@@ -17,7 +19,8 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _rank_main(rank, world, port, errq, peer):
+def _rank_main(rank, world, port, errq, mode):
+    peer = mode != "nccl"
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -40,7 +43,7 @@ def _rank_main(rank, world, port, errq, peer):
         inp = T.StepInputs(g.buffer(bf16(lat)), h, w, 0.37, g.buffer(bf16(ctx)), text)
         v1, _ = T.transformer(g, wts, scfg, inp, dtype="bf16")
         one = g.read(v1, 16 * h * w * 4, np.float32).copy()
-        sp = we.sequence.SequenceParallel(comm, peer=peer)
+        sp = we.sequence.SequenceParallel(comm, peer=peer, fused=mode == "fused")
         v2, _ = T.transformer(g, wts, scfg, inp, dtype="bf16", sp=sp)
         got = g.read(v2, 16 * h * w * 4, np.float32).copy()
         err = float(np.max(np.abs(got - one)) / np.max(np.abs(one)))
@@ -83,8 +86,8 @@ def _rank_main(rank, world, port, errq, peer):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("peer", [True, False], ids=["peer", "nccl"])
-def test_sequence_parallel_step(peer, world):
+@pytest.mark.parametrize("mode", ["fused", "copy", "nccl"])
+def test_sequence_parallel_step(mode, world):
     if gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    run_ranks(_rank_main, world, peer)
+    run_ranks(_rank_main, world, mode)

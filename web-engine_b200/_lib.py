@@ -64,7 +64,8 @@ class GemmFp8Desc(C.Structure):
                 ("flags", C.c_uint32), ("epi", Epilogue), ("y_parts", C.c_void_p * 3), ("part_n", C.c_int64 * 3),
                 ("w2", C.c_void_p), ("scale2", C.c_float), ("chan_scale2", C.c_void_p), ("bias2", C.c_void_p),
                 ("gate2", C.c_void_p), ("nseg", C.c_int32), ("row_end", C.c_int64 * GEMM_MAX_SEGMENTS),
-                ("row_set", C.c_int32 * GEMM_MAX_SEGMENTS)]
+                ("row_set", C.c_int32 * GEMM_MAX_SEGMENTS), ("peer_dst", C.c_void_p * 8), ("peer_world", C.c_int32),
+                ("peer_part", C.c_int32), ("peer_row0", C.c_int64)]
 
 
 class LinearDesc(C.Structure):
@@ -178,6 +179,9 @@ _SIGS = {
     "we_peer_open": (C.c_int, [_P, _P]),
     "we_peer_region": (C.c_void_p, [_P]),
     "we_peer_exchange": (C.c_int, [_P, _P, _P, C.c_int32, C.c_uint64]),
+    "we_peer_remote": (C.c_void_p, [_P, C.c_int32]),
+    "we_qknorm_rope_peers": (C.c_int, [_P, _P, _P, C.c_float, C.c_float, _P, _P, _I64, _I64, C.c_int32, _P, C.c_int32,
+                                       _I64]),
     "we_peer_destroy": (C.c_int, [_P]),
     "we_matmul_fp8_noalloc": (C.c_int, [_P, _P, _I64, _I64, _I64, _P, _I64, C.c_float, _P, _P, _P, _I64, C.c_int32,
                                         C.c_uint32, C.c_char_p, C.c_size_t]),

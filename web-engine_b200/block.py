@@ -330,18 +330,21 @@ def _weight_plan(parts, t: int):
 
 
 def _gemm_all(graph, plan, parts, split, width: int, lin, outs, y_dtype: str, mods=None, gate_key=None, aux=None,
-              aux_row_bytes: int = 0, **epi):
+              aux_row_bytes: int = 0, peer=None, **epi):
     """The linear lin(w) of every part, over all rows: split holds the e4m3 planes of rows [0, t) (width values a
     row), outs = [(buffer, channels), ...] the output rows (one buffer, or the q / k / v parts of a split output),
-    mods[id(w)][gate_key] the per-channel gate of a weight set, aux an epilogue operand over all rows."""
+    mods[id(w)][gate_key] the per-channel gate of a weight set, aux an epilogue operand over all rows. peer =
+    dict(dst=, part=, row0=): that output part goes to the ranks that attend its heads (gemm_fp8's peer), row 0 of
+    these rows at row row0 of their blocks."""
     es = 2 if y_dtype == "bf16" else 4
 
-    def call(sr, rows, w, ys, aux_p, **more):
+    def call(sr, rows, w, ys, aux_p, row_ofs=0, **more):
         ln = lin(w)
         gate = mods[id(w)][gate_key] if gate_key else None
         y, pt = (ys[0][0], None) if len(ys) == 1 else (None, ys)
+        pe = dict(peer, row0=peer["row0"] + row_ofs) if peer else None
         K.gemm_fp8(graph, *sr, ln.buffer, y, rows, ln.n, ln.k, ln.scale, chan_scale=ln.chan_scale, bias=ln.bias,
-                   y_dtype=y_dtype, gate=gate, aux=aux_p, parts=pt, **epi, **more)
+                   y_dtype=y_dtype, gate=gate, aux=aux_p, parts=pt, peer=pe, **epi, **more)
 
     if plan is not None and plan[0] == "one":
         call(split, parts[-1].row0 + parts[-1].rows, plan[1], outs, aux)
@@ -354,7 +357,7 @@ def _gemm_all(graph, plan, parts, split, width: int, lin, outs, y_dtype: str, mo
     else:
         for p in parts:
             call(_split_rows(split, p, width), p.rows, p.w, [(rows_at(b, p.row0, n * es), n) for b, n in outs],
-                 rows_at(aux, p.row0, aux_row_bytes) if aux is not None else None)
+                 rows_at(aux, p.row0, aux_row_bytes) if aux is not None else None, p.row0)
 
 
 def _split_rows(split, p: Part, width: int):
@@ -386,14 +389,28 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None, defer=False
             K.add_norm_split(graph, rows_at(res.x1, p.row0, hd * 4), rows_at(res.dn, p.row0, hd * 4),
                              rows_at(x, p.row0, hd * 4), p.w.norm1, p.rows, hd, *_split_rows(split, p, hd),
                              scale=mod["prescale"], shift=mod["preshift"], eps=cfg.eps)
+    # sequence parallelism, fused exchange: the q/k/v GEMM's epilogue stores v, and q / k norm + RoPE store q and k,
+    # straight into the regions of the ranks that attend their heads (no copy kernel after them)
+    tg = None
+    if sp is not None and sp.fused and hdim == 128:
+        tg = sp.head_targets(graph, t, cfg.heads, cfg.kv_heads, hdim * 2)
+    vpeer = dict(dst=tg["v"], row0=tg["row0"]) if tg else None
     if all(p.w.wqkv is not None for p in parts):  # one GEMM, its epilogue writing q, k and v
-        _gemm_all(graph, plan, parts, split, hd, lambda w: w.wqkv, [(q, qw), (k, kw), (v, kw)], "bf16")
+        _gemm_all(graph, plan, parts, split, hd, lambda w: w.wqkv, [(q, qw), (k, kw), (v, kw)], "bf16",
+                  peer=dict(vpeer, part=2) if vpeer else None)
     else:
         for name, buf, n in (("wq", q, qw), ("wk", k, kw), ("wv", v, kw)):
-            _gemm_all(graph, plan, parts, split, hd, lambda w, nm=name: getattr(w, nm), [(buf, n)], "bf16")
+            _gemm_all(graph, plan, parts, split, hd, lambda w, nm=name: getattr(w, nm), [(buf, n)], "bf16",
+                      peer=dict(vpeer, part=0) if vpeer and name == "wv" else None)
     for p in parts:
         qp, kp = rows_at(q, p.row0, qw * 2), rows_at(k, p.row0, kw * 2)
         pr = part_rope(rope, p)
+        if tg:
+            K.qknorm_rope_peers(graph, qp, p.w.norm_q, pr.cos, pr.sin, p.rows, cfg.heads, tg["q"], tg["row0"] + p.row0,
+                                eps=cfg.eps)
+            K.qknorm_rope_peers(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, cfg.kv_heads, tg["k"],
+                                tg["row0"] + p.row0, eps=cfg.eps)
+            continue
         K.qknorm_rope(graph, qp, p.w.norm_q, pr.cos, pr.sin, p.rows, cfg.heads, rope.pairs, qp, eps=cfg.eps,
                       x_dtype="bf16", out_dtype="bf16")
         K.qknorm_rope(graph, kp, p.w.norm_k, pr.cos, pr.sin, p.rows, cfg.kv_heads, rope.pairs, kp, eps=cfg.eps,
@@ -401,6 +418,13 @@ def _joint_bf16(graph, parts, cfg, x, tvec, rope, images=1, sp=None, defer=False
     if sp is None:
         o = graph.buffer(t * hd * 2)
         _attend_images(graph, q, k, v, o, t, cfg, images, "bf16")
+    elif tg:
+        hl, kl, T = cfg.heads // sp.world, cfg.kv_heads // sp.world, t * sp.world
+
+        def attend(qh, kh, vh, oh):
+            K.attention(graph, qh, kh, vh, T, hl, kl, hdim, oh, dtype="bf16", out_dtype="bf16")
+
+        o = sp.finish_heads(graph, t, cfg.heads, hdim * 2, attend)
     else:
         o = _attend_sp(graph, sp, q, k, v, t, cfg)
     if cfg.attn_gate:  # og = o * sigmoid(gate h), in the gate GEMM's epilogue

@@ -65,6 +65,10 @@ struct Params {
   const uint8_t* w4;
   const uint16_t* w4_scale;
   int64_t k;
+  // peer output (peer_part >= 0): that part's heads go to the ranks that attend them (TcGemmArgs::peer)
+  int peer_part;
+  int64_t peer_row0, peer_hl;
+  void* peer_dst[WE_PEER_MAX];
 };
 
 // The token tile of the i-th tile in schedule order. With two weight sets the tiles of set 0 come first, then those
@@ -108,10 +112,17 @@ struct YOut {
   void* y;
   int64_t cofs, stride;
 };
+// The peer part (peer_part) goes head by head (128 channels, one or more epilogue warps' channels) to rank
+// o = h / hl's memory, rows [peer_row0, ...) of its [tokens of every rank, hl heads, 128] block.
 __device__ __forceinline__ YOut y_out(const Params& p, int64_t ch_base) {
-  if (!p.ys[0]) return YOut{p.y, 0, p.y_stride};
-  const int s = (ch_base >= p.seg_end[0]) + (ch_base >= p.seg_end[1]);
+  const int s = p.ys[0] ? (ch_base >= p.seg_end[0]) + (ch_base >= p.seg_end[1]) : 0;
   const int64_t lo = s ? p.seg_end[s - 1] : 0;
+  if (s == p.peer_part) {
+    const int64_t h = (ch_base - lo) >> 7, o = h / p.peer_hl;
+    return YOut{static_cast<uint16_t*>(p.peer_dst[o]) + (p.peer_row0 * p.peer_hl + h - o * p.peer_hl) * 128,
+                lo + h * 128, p.peer_hl * 128};
+  }
+  if (!p.ys[0]) return YOut{p.y, 0, p.y_stride};
   return YOut{p.ys[s], lo, p.seg_end[s] - lo};
 }
 
@@ -486,6 +497,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   }
+  // peer output: this thread's stores to other GPUs are visible system-wide before the kernel ends
+  if (p.peer_part >= 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -719,6 +732,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   }
+  // peer output: this thread's stores to other GPUs are visible system-wide before the kernel ends
+  if (p.peer_part >= 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // neither CTA frees TMEM or exits while its peer may still signal it
@@ -1006,6 +1021,8 @@ __global__ void __launch_bounds__(192 + 32 * CW, 1)
       }
     }
   }
+  // peer output: this thread's stores to other GPUs are visible system-wide before the kernel ends
+  if (p.peer_part >= 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1086,6 +1103,15 @@ static Params make_params(const TcGemmArgs& a) {
     p.row_set[i] = i < a.nseg ? (uint8_t)a.row_set[i] : 0;
   }
   p.err = a.dev_err;
+  p.peer_part = a.peer ? a.peer_part : -1;
+  p.peer_row0 = a.peer_row0;
+  p.peer_hl = 1;
+  if (a.peer) {
+    const int64_t lo = a.ys[0] && a.peer_part ? a.seg_end[a.peer_part - 1] : 0;
+    const int64_t hi = a.ys[0] ? a.seg_end[a.peer_part] : a.n;
+    p.peer_hl = (hi - lo) / (128 * a.peer_world);
+    for (int r = 0; r < WE_PEER_MAX; r++) p.peer_dst[r] = r < a.peer_world ? a.peer_dst[r] : nullptr;
+  }
   p.w4 = a.int4 ? static_cast<const uint8_t*>(a.w) : nullptr;
   p.w4_scale = a.int4 ? a.group_scale : nullptr;
   p.k = a.k;

@@ -281,11 +281,20 @@ __global__ void __launch_bounds__(NT, NT == 192 ? 4 : 512 / NT) rmsnorm_row_kern
 // before any arithmetic, so each warp keeps R x 48 bytes per lane in flight. Interleaved pairs stay in a lane;
 // half pairing exchanges with lane ^ 8. TOK (heads % 8 == 0): a step's 8 rows are 8 heads of one token, so the
 // token's cos/sin values are loaded once per step instead of once per row (they are twice a row's own bytes).
-template <int DT, int OT, int PAIRING, bool NORM, bool TOK = false>
+// PEER: row (token t, head h) goes to rank o = h / hl's exchange region instead of out: to
+// dst[o] + ((row0 + t) hl + h - o hl) 128 values, i.e. [every rank's tokens, rank o's hl heads, 128] with this rank's
+// tokens from row0 (sequence parallelism: the head scatter done by the stores themselves, over NVLink).
+struct PeerRows {
+  void* dst[WE_PEER_MAX];
+  int64_t row0, hl;
+};
+
+template <int DT, int OT, int PAIRING, bool NORM, bool TOK = false, bool PEER = false>
 __global__ void __launch_bounds__(256, TOK ? 3 : 2) qknorm_rope128_kernel(const void* __restrict__ x, const float* __restrict__ w,
                                                              float eps, float offset, const float* __restrict__ cs,
                                                              const float* __restrict__ sn, int64_t tokens,
-                                                             int64_t heads, void* __restrict__ out) {
+                                                             int64_t heads, void* __restrict__ out,
+                                                             const PeerRows peer = PeerRows{}) {
   constexpr int D = 128, P = 64, R = 4;
   pdl_wait();  // launched by launch_pdl: the previous kernel's outputs (q or k) are complete
   pdl_launch_dependents();
@@ -375,9 +384,19 @@ __global__ void __launch_bounds__(256, TOK ? 3 : 2) qknorm_rope128_kernel(const 
           o8[e] = first ? v[r][e] * c[r][e] - partner * sv[r][e] : v[r][e] * c[r][e] + partner * sv[r][e];
         }
       }
-      if (live[r]) store8<OT>(out, base[r], o8);
+      if (live[r]) {
+        if constexpr (PEER) {
+          const int64_t row = base[r] / D, t = row / heads, h = row - t * heads, o = h / peer.hl;
+          store8<OT>(peer.dst[o], ((peer.row0 + t) * peer.hl + h - o * peer.hl) * D + sub * 8, o8);
+        } else {
+          store8<OT>(out, base[r], o8);
+        }
+      }
     }
   }
+  // the stores to other GPUs' memory are visible system-wide before this thread ends, so the flag barrier that
+  // follows on the stream (a later kernel) publishes them
+  if constexpr (PEER) __threadfence_system();
 }
 
 // RoPE, interleaved pairs (2j, 2j+1) or half pairs (j, j+P). One thread per (token, group of G pairs),
@@ -560,7 +579,7 @@ static void launch_qk128(const void* x, const float* w, float eps, float offset,
   {                                                                                                            \
     auto kern = qknorm_rope128_kernel<DT, OT, PAIR, NORM, TOK>;                                                \
     (void)launch_pdl(kern, resident_grid(kern, 256, sms, (groups + 7) / 8), 256, 0, st, x, w, eps, offset, cs, sn, \
-                     tokens, heads, out);                                                                      \
+                     tokens, heads, out, PeerRows{});                                                          \
   }
   const bool tok = tok_ok && heads % 8 == 0;
   if (pairing == WE_ROPE_INTERLEAVED) {
@@ -633,6 +652,34 @@ static bool qk_dispatch(const void* x, const float* w, float eps, float offset, 
 
 // Returns cudaErrorNotSupported when the head size has no fused variant (the caller then runs
 // rmsnorm + rope as two passes).
+cudaError_t launch_qknorm_rope_peers(const void* x, const float* w, float eps, float offset, const float* cs,
+                                     const float* sn, int64_t tokens, int64_t heads, int pairing, void* const* dst,
+                                     int world, int64_t row0, int sms, cudaStream_t st) {
+  if (world < 1 || world > WE_PEER_MAX || heads % world || !al16(x) || ((uintptr_t)cs & 15) || ((uintptr_t)sn & 15))
+    return cudaErrorNotSupported;
+  PeerRows pr{};
+  for (int r = 0; r < world; r++) {
+    if (!dst[r] || ((uintptr_t)dst[r] & 15)) return cudaErrorNotSupported;
+    pr.dst[r] = dst[r];
+  }
+  pr.row0 = row0;
+  pr.hl = heads / world;
+  const int64_t groups = (tokens * heads + 7) / 8;
+  const bool tok = heads % 8 == 0;
+#define WE_QKP(PAIR, TOK)                                                                                      \
+  {                                                                                                            \
+    auto kern = qknorm_rope128_kernel<WE_BF16, WE_BF16, PAIR, true, TOK, true>;                                \
+    return launch_pdl(kern, resident_grid(kern, 256, sms, (groups + 7) / 8), 256, 0, st, x, w, eps, offset, cs, sn, \
+                      tokens, heads, (void*)nullptr, pr);                                                      \
+  }
+  if (pairing == WE_ROPE_INTERLEAVED) {
+    if (tok) WE_QKP(WE_ROPE_INTERLEAVED, true) else WE_QKP(WE_ROPE_INTERLEAVED, false)
+  } else {
+    if (tok) WE_QKP(WE_ROPE_HALF, true) else WE_QKP(WE_ROPE_HALF, false)
+  }
+#undef WE_QKP
+}
+
 cudaError_t launch_qknorm_rope(const void* x, int xdt, const float* w, float eps, float offset, const float* cs,
                                const float* sn, int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out,
                                int odt, int sms, cudaStream_t st) {

@@ -68,6 +68,15 @@ struct TcGemmArgs {
   // group_scale f16 [n, k / 64]; k % 64 == 0, one weight set
   int int4;
   const uint16_t* group_scale;
+  // peer output (peer = 1): split-output part peer_part (the whole output without a split) is stored into other
+  // GPUs' memory, head by head (128 channels): head h of the part goes to rank o = h / hl, hl = part width /
+  // (128 peer_world), at peer_dst[o] + ((peer_row0 + row) hl + h - o hl) 128 values (bf16 y only, no aux, no
+  // accumulate); the kernel fences its stores at system scope before it ends
+  int peer;
+  int peer_part;
+  int peer_world;
+  int64_t peer_row0;
+  void* peer_dst[WE_PEER_MAX];
 };
 // Returns cudaErrorNotSupported when the layout cannot go through TMA (alignment) so the caller can
 // use the CUDA-core kernel instead.
@@ -89,6 +98,11 @@ cudaError_t launch_rmsnorm(const void* x, int xdt, const float* w, const float* 
                            int64_t d, float eps, float offset, void* out, int odt, int sms, cudaStream_t st);
 cudaError_t launch_rope(const void* x, int xdt, const float* cs, const float* sn, int64_t tokens, int64_t heads,
                         int64_t pairs, int pairing, void* out, int odt, int sms, cudaStream_t st);
+// bf16 rows of 128-wide heads, norm + RoPE, each row stored into the exchange region of the rank that attends its
+// head (dst[rank], [world x tokens, heads / world, 128], this rank's tokens from row0)
+cudaError_t launch_qknorm_rope_peers(const void* x, const float* w, float eps, float offset, const float* cs,
+                                     const float* sn, int64_t tokens, int64_t heads, int pairing, void* const* dst,
+                                     int world, int64_t row0, int sms, cudaStream_t st);
 cudaError_t launch_qknorm_rope(const void* x, int xdt, const float* w, float eps, float offset, const float* cs,
                                const float* sn, int64_t tokens, int64_t heads, int64_t pairs, int pairing, void* out,
                                int odt, int sms, cudaStream_t st);

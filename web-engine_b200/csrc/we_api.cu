@@ -576,12 +576,32 @@ int we_gemm_fp8(we_ctx* ctx, const we_gemm_fp8_desc* d) {
       return fail(ctx, WE_EINVAL, "row segments must increase to m, name set 0 or 1, have w2 for set 1, and give "
                                   "gate2 iff epi.gate");
   }
+  if (d->peer_world != 0) {
+    const int pp = d->peer_part;
+    bool ok = d->peer_world > 0 && d->peer_world <= WE_PEER_MAX && d->y_dtype == WE_BF16 && !d->epi.aux_op &&
+              !(d->flags & WE_MM_ACCUMULATE) && pp >= 0 && pp < (split ? 3 : 1);
+    if (ok) {
+      const int64_t lo = split && pp ? ends[pp - 1] : 0, hi = split ? ends[pp] : d->n;
+      ok = hi > lo && lo % 128 == 0 && (hi - lo) % (128 * (int64_t)d->peer_world) == 0 && d->peer_row0 >= 0;
+      for (int r = 0; ok && r < d->peer_world; r++) ok = d->peer_dst[r] && (uintptr_t)d->peer_dst[r] % 16 == 0;
+    }
+    if (!ok)
+      return fail(ctx, WE_EINVAL, "peer output needs bf16 y, no aux operand or accumulate, a part of heads of 128 "
+                                  "that split over 1 to 8 ranks, and a 16-byte aligned destination per rank");
+  }
   if (d->m == 0 || d->n == 0) return WE_OK;
   we::TcGemmArgs t{};
   t.m = d->m;
   t.n = d->n;
   t.k = d->k;
   t.kind_f16 = 0;
+  if (d->peer_world > 0) {
+    t.peer = 1;
+    t.peer_part = d->peer_part;
+    t.peer_world = d->peer_world;
+    t.peer_row0 = d->peer_row0;
+    for (int r = 0; r < d->peer_world; r++) t.peer_dst[r] = d->peer_dst[r];
+  }
   if (d->nseg > 0) {
     t.w2 = d->w2 ? d->w2 : d->w;
     t.scale2 = d->scale2;
@@ -865,6 +885,24 @@ int we_qknorm_rope(we_ctx* ctx, const void* x, int32_t x_dtype, const float* wei
     return WE_OK;
   }
   CK(e, "qknorm_rope");
+  ctx->stats.launches++;
+  return WE_OK;
+}
+
+int we_qknorm_rope_peers(we_ctx* ctx, const void* x, const float* weight, float eps, float offset, const float* cos,
+                         const float* sin, int64_t tokens, int64_t heads, int32_t pairing, void* const* dst,
+                         int32_t world, int64_t dst_row0) {
+  if (!ctx) return WE_EINVAL;
+  if (!x || !weight || !cos || !sin || !dst) return fail(ctx, WE_EINVAL, "qk norm + RoPE to peers: missing buffer");
+  if (pairing != WE_ROPE_INTERLEAVED && pairing != WE_ROPE_HALF) return fail(ctx, WE_EINVAL, "unknown pairing");
+  if (world < 1 || world > WE_PEER_MAX || heads % world)
+    return fail(ctx, WE_EINVAL, "the heads must split evenly over 1 to 8 ranks");
+  if (tokens == 0 || heads == 0) return WE_OK;
+  cudaError_t e = we::launch_qknorm_rope_peers(x, weight, eps, offset, cos, sin, tokens, heads, pairing, dst, world,
+                                               dst_row0, ctx->sms, ctx->stream);
+  if (e == cudaErrorNotSupported)
+    return fail(ctx, WE_EINVAL, "qk norm + RoPE to peers needs 16-byte aligned rows, tables and destinations");
+  CK(e, "qknorm_rope_peers");
   ctx->stats.launches++;
   return WE_OK;
 }

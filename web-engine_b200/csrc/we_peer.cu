@@ -176,6 +176,9 @@ int we_peer_open(we_peer* p, const void* handles) {
 }
 
 void* we_peer_region(const we_peer* p) { return p ? p->region : nullptr; }
+void* we_peer_remote(const we_peer* p, int32_t rank) {
+  return p && rank >= 0 && rank < p->world ? p->base[rank] : nullptr;
+}
 
 int we_peer_exchange(we_ctx* ctx, we_peer* p, const we_peer_copy* copies, int32_t ncopies, uint64_t timeout_ns) {
   if (!ctx || !p || (ncopies > 0 && !copies)) return WE_EINVAL;

@@ -199,6 +199,17 @@ def qknorm_rope(graph: Graph, x, weight, cos, sin, tokens: int, heads: int, pair
                                               L.DTYPES[out_dtype]))
 
 
+def qknorm_rope_peers(graph: Graph, x, weight, cos, sin, tokens: int, heads: int, dst: list, row0: int, eps=1e-5,
+                      offset=1.0, pairing="interleaved") -> None:
+    """qknorm_rope on bf16 rows of 128-wide heads, each output row stored straight into the memory of the rank that
+    attends its head (we_qknorm_rope_peers): dst[r] is rank r's [world x tokens, heads / world, 128] block (a device
+    address), this rank's rows starting at row row0 of it."""
+    p = L.ROPE_HALF if pairing == "half" else L.ROPE_INTERLEAVED
+    table = (C.c_void_p * len(dst))(*dst)
+    L.check(graph.ctx, L.lib().we_qknorm_rope_peers(graph.ctx, addr(x), addr(weight), eps, offset, addr(cos),
+                                                    addr(sin), tokens, heads, p, table, len(dst), row0))
+
+
 def quantize_fp8(graph: Graph, w, n: int, k: int, q, scales, per_channel: bool = True, w_dtype="f32") -> None:
     L.check(graph.ctx, L.lib().we_quantize_fp8(graph.ctx, addr(w), L.DTYPES[w_dtype], n, k, int(per_channel), addr(q),
                                                addr(scales)))
@@ -218,11 +229,12 @@ def quantize_act(graph: Graph, x, m: int, k: int, hi, lo, row_scale, terms: int 
 def gemm_fp8(graph: Graph, x_hi, x_lo, row_scale, w, y, m: int, n: int, k: int, scale: float = 1.0,
              chan_scale=None, bias=None, y_dtype="f32", y_stride: int = 0, accumulate: bool = False,
              act=None, aux_op=None, aux=None, aux_dtype="f32", gate=None, parts=None, set2=None,
-             segments=None) -> None:
+             segments=None, peer=None) -> None:
     """The tcgen05 GEMM on an already-split activation (we_gemm_fp8); x_lo None = one term. parts: a split output,
     [(buffer, width), ...] taking the channels in order (y is then unused). set2 / segments: a second weight set,
     set2 = dict(w=, scale=, chan_scale=, bias=, gate=) used by the row segments marked 1 in segments =
-    [(row_end, set), ...]."""
+    [(row_end, set), ...]. peer = dict(dst=[address per rank], part=i, row0=r): part i (the whole output without
+    parts) goes head by head straight into the ranks that attend its heads (we_gemm_fp8_desc.peer_dst)."""
     d = L.GemmFp8Desc(m, n, k, addr(x_hi).value, addr(x_lo).value, addr(row_scale).value, addr(w).value, scale,
                       addr(chan_scale).value, addr(bias).value, addr(y).value, y_stride, L.DTYPES[y_dtype],
                       L.MM_ACCUMULATE if accumulate else 0, epilogue(act, aux_op, aux, aux_dtype, gate))
@@ -237,6 +249,10 @@ def gemm_fp8(graph: Graph, x_hi, x_lo, row_scale, w, y, m: int, n: int, k: int, 
         d.nseg = len(segments)
         for i, (end, st) in enumerate(segments):
             d.row_end[i], d.row_set[i] = end, st
+    if peer:
+        for r, a in enumerate(peer["dst"]):
+            d.peer_dst[r] = a
+        d.peer_world, d.peer_part, d.peer_row0 = len(peer["dst"]), peer.get("part", 0), peer["row0"]
     L.check(graph.ctx, L.lib().we_gemm_fp8(graph.ctx, C.byref(d)))
 
 
