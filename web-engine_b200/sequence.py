@@ -104,8 +104,9 @@ class SequenceParallel:
         self.rank, self.world = comm.rank, comm.world
         self.peer = peer
         # fused: the producers of q, k and v store them into the attending ranks' regions (head_targets /
-        # finish_heads) instead of a copy kernel after them (exchange_heads). Measured at 2 ranks (config 4, from a
-        # CUDA graph): 45.3 ms fused against 44.7 ms with the copy kernel, so the copy kernel is the default.
+        # finish_heads) instead of a copy kernel after them (exchange_heads). Measured on config 4 from a CUDA graph:
+        # 45.3 ms fused against 44.7 ms with the copy kernel at 2 ranks, 20.5 against 19.45 ms at 8, so the copy
+        # kernel is the default.
         self.fused = peer and fused
         self._pending = None
         self._store = Graph(comm.graph.device)  # persistent buffers only; no kernel runs on its stream
