@@ -6,8 +6,8 @@
   reference block test's tolerance (cosine > 0.99999, relErr < 1e-4), bf16 with the bf16 block test's
   (update cosine >= 0.9999, max-abs-rel < 1e-2).
 - whole steps against oracle.step_reference: f32 on a tiny model (cosine > 0.99999, relErr < 1e-4); bf16 on a
-  small model with 128-wide heads (velocity cosine >= 0.9999, max-abs-rel < 2e-2: bf16 activations at every GEMM
-  input across 4 blocks, against float64).
+  small model with 128-wide heads (velocity cosine >= 0.9999, max-abs-rel < 1e-2, the north star's bound; measured
+  2.0e-3 with bf16 activations at every GEMM input across 4 blocks, against float64).
 - the text cache gives the same velocity bit for bit; the device Euler step equals the f32 formula.
 """
 import numpy as np
@@ -219,7 +219,7 @@ def test_step_bf16_matches_the_float64_step(we, graph):
     c = O.compare(got, want)
     rel = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
     print(f"small bf16 step vs float64: cosine {c['cosine']:.7f}, max-abs-rel {rel:.2e}")
-    assert c["cosine"] >= 0.9999 and rel < 2e-2, (c, rel)
+    assert c["cosine"] >= 0.9999 and rel < 1e-2, (c, rel)
     assert np.array_equal(got, again)
 
 
